@@ -1,0 +1,81 @@
+// gemm.cu -- level-3 entry points: gen9blas_gemm / _gemm_batched / _hgemm / _sgemm and the kernel dispatch.
+//
+// Host flow of the reference (lib/src/gemm.c:5-74, 177-184): type check, empty dimensions return 0, a small M or N
+// (min(M, N) <= skinny threshold, single matrix) goes to the skinny kernels (gemm.c:11-12), everything else to the
+// main GEMM. What differs on B200: there is no pack / pad / epilogue pipeline and no launch banding
+// (gemm.c:15-55, 119-164); one kernel reads the strided operands through TMA or predicated 16-byte loads and applies
+// alpha/beta in its epilogue.
+#include "internal.h"
+
+namespace g9 {
+
+int launch_hgemm_tc(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, long long sA,
+                    const void *B, int ldb, long long sB, double beta, void *C, int ldc, long long sC, int count,
+                    cudaStream_t st);
+int launch_gemm_simt(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, long long sA,
+                     const void *B, int ldb, long long sB, double beta, void *C, int ldc, long long sC, int count,
+                     cudaStream_t st);
+
+static int elem_size(int type) { return type == GEN9BLAS_S ? 4 : type == GEN9BLAS_D ? 8 : 2; }
+
+int launch_gemm(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, long long sA,
+                const void *B, int ldb, long long sB, double beta, void *C, int ldc, long long sC, int count,
+                cudaStream_t st) {
+    if (count == 1 && (M < N ? M : N) <= skinny_threshold(type))
+        return launch_skinny(type, tA, tB, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, st);
+    if (type == GEN9BLAS_H || type == GEN9BLAS_HS)
+        return launch_hgemm_tc(type, tA, tB, M, N, K, alpha, A, lda, sA, B, ldb, sB, beta, C, ldc, sC, count, st);
+    return launch_gemm_simt(type, tA, tB, M, N, K, alpha, A, lda, sA, B, ldb, sB, beta, C, ldc, sC, count, st);
+}
+
+}  // namespace g9
+
+using namespace g9;
+
+extern "C" {
+
+GEN9BLAS_API int gen9blas_gemm_batched(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda,
+                                       int64_t sA, const void *B, int ldb, int64_t sB, double beta, void *C, int ldc,
+                                       int64_t sC, int count) {
+    if (int e = begin_op()) return e;
+    if (type < 0 || type > 3) return fail(GEN9BLAS_ERR_UNSUPPORTED, "type %d unavailable", type);
+    if (M <= 0 || N <= 0 || K <= 0 || count <= 0) return 0;
+    tA = tA ? 1 : 0;
+    tB = tB ? 1 : 0;
+    const size_t es = elem_size(type), c1 = count - 1;
+    const size_t bA = (c1 * sA + (tA ? (size_t)(K - 1) * lda + M : (size_t)(M - 1) * lda + K)) * es;
+    const size_t bB = (c1 * sB + (tB ? (size_t)(N - 1) * ldb + K : (size_t)(K - 1) * ldb + N)) * es;
+    const size_t bC = (c1 * sC + (size_t)(M - 1) * ldc + N) * es;
+    timer_start();
+    Operand op[3];
+    G9_TRY(map_operand(op[0], A, bA, 0, true, false));
+    G9_TRY(map_operand(op[1], B, bB, 1, true, false));
+    // C is read when beta != 0; it is also copied in when its region has gaps (row pitch or batch stride larger
+    // than the data), so that the copy back leaves the caller's bytes between rows untouched.
+    const bool c_gaps = ldc != N || (count > 1 && sC != (int64_t)M * ldc);
+    G9_TRY(map_operand(op[2], C, bC, 2, beta != 0.0 || c_gaps, true));
+    G.last_zc = op[0].zc | op[1].zc << 1 | op[2].zc << 2;
+    timer_kernel();
+    G9_TRY(launch_gemm(type, tA, tB, M, N, K, alpha, op[0].dptr, lda, sA, op[1].dptr, ldb, sB, beta, op[2].dptr, ldc, sC,
+                       count, stream()));
+    int r = finish_op(op, 3);
+    timer_stop();
+    return r;
+}
+
+GEN9BLAS_API int gen9blas_gemm(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda,
+                               const void *B, int ldb, double beta, void *C, int ldc) {
+    return gen9blas_gemm_batched(type, tA, tB, M, N, K, alpha, A, lda, 0, B, ldb, 0, beta, C, ldc, 0, 1);
+}
+
+GEN9BLAS_API int gen9blas_hgemm(int M, int N, int K, double alpha, const uint16_t *A, int lda, const uint16_t *B, int ldb,
+                                double beta, uint16_t *C, int ldc) {
+    return gen9blas_gemm(GEN9BLAS_H, 0, 0, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc);
+}
+
+GEN9BLAS_API int gen9blas_sgemm(int M, int N, int K, double alpha, const float *A, int lda, const float *B, int ldb,
+                                double beta, float *C, int ldc) {
+    return gen9blas_gemm(GEN9BLAS_S, 0, 0, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc);
+}
+
+}  // extern "C"

@@ -1,0 +1,404 @@
+// hgemm_tc.cu -- FP16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), sm_100a.
+//
+// Computes C = alpha·op(A)·op(B) + beta·C for GEN9BLAS_H (FP16 accumulator in TMEM: the tensor core rounds the
+// running sum to FP16 after every K=16 step, the B200 counterpart of the reference's FP16-accumulate hgemm_v,
+// lib/kernels/hgemm.cl:838-868) and GEN9BLAS_HS (FP32 accumulator for the whole K, strictly more accurate than the
+// reference's FP16 chunks of 32 summed into FP32, hgemm.cl:869-898). The epilogue applies alpha/beta in FP32 and
+// rounds once to FP16 (the reference rounds to FP16 first and runs gen9blas_epilog_b, hgemm.cl:557-564).
+//
+// There is no packing step: TMA reads op(A) and op(B) straight from the row-major operands. A transposed operand
+// is an MN-major UMMA operand (transpose bit of the instruction descriptor), so all four transA/transB combinations
+// run the same kernel. Operands whose strides break the TMA rules (16-byte aligned base and row pitch) are first
+// copied into an aligned scratch layout by a small repack kernel.
+//
+// Kernel structure (persistent, one CTA per SM, 192 threads):
+//   warp 0      TMA producer: 4-stage ring of (A 128×64, B 256×64) FP16 tiles, 128-byte swizzle, mbarrier tx counts;
+//   warp 1      MMA issuer: one thread issues tcgen05.mma 128×256×16 into one of two TMEM accumulators
+//               (2 × 256 columns), tcgen05.commit frees smem stages and hands finished accumulators to the epilogue;
+//   warps 2-5   epilogue: tcgen05.ld 32 lanes × 32 columns, alpha/beta, FP16 stores, then release the accumulator.
+// Tiles are visited in groups of 16 M-tiles so that the CTAs working at the same time share A and B in L2.
+// Every mbarrier wait is bounded (4 s of global time); a wait that gives up sets the mapped error word and all
+// roles leave their loops, drain their in-flight copies / MMAs (bounded) and free TMEM.
+#include "common.cuh"
+#include "internal.h"
+#include "sm100.cuh"
+#include <cudaTypedefs.h>
+
+namespace g9 {
+using namespace sm100;
+
+constexpr int TC_BM = 128, TC_BN = 256, TC_BK = 64, TC_STAGES = 4;
+constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;   // 16 KiB
+constexpr int TC_B_BYTES = TC_BN * TC_BK * 2;   // 32 KiB
+constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;
+constexpr int TC_THREADS = 192;
+constexpr int TC_GROUP_M = 16;
+constexpr uint32_t TC_TMEM_COLS = 512;           // two 128×256 FP32 accumulators
+constexpr int TC_SMEM = TC_STAGES * TC_STAGE_BYTES + 1024 /*alignment*/ + 256 /*barriers*/;
+constexpr uint64_t TC_WAIT_NS = 4000000000ull;
+
+struct TcParams {
+    int M, N, K, count;
+    int tiles_m, tiles_n, total_tiles;
+    int a_mn, b_mn;           // 1: operand is MN-major in memory (transposed)
+    float alpha, beta;
+    int plain;                // alpha == 1 && beta == 0
+    __half *C;
+    long long ldc, sC;
+    int c_vec;                // C base 16-byte aligned and ldc % 8 == 0
+    unsigned *err;
+};
+
+__device__ __forceinline__ void tile_coords(const TcParams &p, int tile, int &b, int &mb, int &nb) {
+    const int per_batch = p.tiles_m * p.tiles_n;
+    b = tile / per_batch;
+    const int r = tile - b * per_batch;
+    const int group_span = TC_GROUP_M * p.tiles_n;
+    const int group = r / group_span;
+    const int first_m = group * TC_GROUP_M;
+    const int gsz = min(p.tiles_m - first_m, TC_GROUP_M);
+    const int in_group = r - group * group_span;
+    mb = first_m + in_group % gsz;
+    nb = in_group / gsz;
+}
+
+__device__ __forceinline__ void report_timeout(const TcParams &p, volatile int *abort) {
+    *abort = 1;
+    *(volatile unsigned *)p.err = kDevErrWaitTimeout;
+    __threadfence_system();
+}
+
+// Epilogue of one 32-column chunk of one row: v = alpha·acc + beta·C, rounded once to FP16.
+template <bool F16ACC>
+__device__ __forceinline__ void store_chunk(const TcParams &p, const uint32_t *r, __half *crow, int col0, bool row_ok) {
+    if (!row_ok) return;
+    float v[32];
+    if (F16ACC) {
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            __half2 h = *reinterpret_cast<const __half2 *>(&r[j]);
+            float2 f = __half22float2(h);
+            v[2 * j] = f.x;
+            v[2 * j + 1] = f.y;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+    }
+    const bool full = col0 + 32 <= p.N;
+    __half *c = crow + col0;
+    if (full && p.c_vec) {
+        uint4 *c4 = reinterpret_cast<uint4 *>(c);
+        if (F16ACC && p.plain) {
+#pragma unroll
+            for (int q = 0; q < 4; q++) c4[q] = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+            return;
+        }
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            float o[8];
+            if (p.beta != 0.0f) {
+                uint4 old = c4[q];
+                const __half2 *oh = reinterpret_cast<const __half2 *>(&old);
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    float2 f = __half22float2(oh[e]);
+                    o[2 * e] = __fmaf_rn(p.beta, f.x, p.alpha * v[8 * q + 2 * e]);
+                    o[2 * e + 1] = __fmaf_rn(p.beta, f.y, p.alpha * v[8 * q + 2 * e + 1]);
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; e++) o[e] = p.alpha * v[8 * q + e];
+            }
+            uint4 u;
+            __half2 *uh = reinterpret_cast<__half2 *>(&u);
+#pragma unroll
+            for (int e = 0; e < 4; e++) uh[e] = __floats2half2_rn(o[2 * e], o[2 * e + 1]);
+            c4[q] = u;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            if (col0 + j < p.N) {
+                float o = p.alpha * v[j];
+                if (p.beta != 0.0f) o = __fmaf_rn(p.beta, __half2float(c[j]), o);
+                c[j] = __float2half_rn(o);
+            }
+        }
+    }
+}
+
+template <bool F16ACC>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    hgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const TcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t *smem = smem_raw + (((raw + 1023) & ~1023u) - raw);
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + TC_STAGES * TC_A_BYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + TC_STAGES * TC_STAGE_BYTES);
+    uint64_t *full = bars;                     // [STAGES] TMA -> MMA
+    uint64_t *empty = bars + TC_STAGES;        // [STAGES] MMA -> TMA
+    uint64_t *tfull = bars + 2 * TC_STAGES;    // [2] MMA -> epilogue
+    uint64_t *tempty = bars + 2 * TC_STAGES + 2;   // [2] epilogue -> MMA
+    uint64_t *drain = bars + 2 * TC_STAGES + 4;    // MMA teardown
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * TC_STAGES + 5);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < TC_STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 128);
+        }
+        mbar_init(drain, 1);
+        *abort = 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, TC_TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int nk = (p.K + TC_BK - 1) / TC_BK;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- TMA producer
+        int stage = 0;
+        uint32_t phase = 0;
+        long long issued = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
+            int b, mb, nb;
+            tile_coords(p, tile, b, mb, nb);
+            const int m0 = mb * TC_BM, n0 = nb * TC_BN;
+            for (int kb = 0; kb < nk; kb++) {
+                if (!mbar_wait(&empty[stage], phase ^ 1, abort, TC_WAIT_NS)) { ok = false; break; }
+                mbar_arrive_expect_tx(&full[stage], TC_STAGE_BYTES);
+                uint8_t *a = sA + stage * TC_A_BYTES;
+                uint8_t *bb = sB + stage * TC_B_BYTES;
+                const int k0 = kb * TC_BK;
+                if (!p.a_mn) {
+                    tma_load_3d(a, &tmA, &full[stage], k0, m0, b);
+                } else {
+                    tma_load_3d(a, &tmA, &full[stage], m0, k0, b);
+                    tma_load_3d(a + 8192, &tmA, &full[stage], m0 + 64, k0, b);
+                }
+                if (!p.b_mn) {
+                    tma_load_3d(bb, &tmB, &full[stage], k0, n0, b);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 4; j++) tma_load_3d(bb + 8192 * j, &tmB, &full[stage], n0 + 64 * j, k0, b);
+                }
+                issued++;
+                if (++stage == TC_STAGES) { stage = 0; phase ^= 1; }
+            }
+        }
+        if (!ok) {
+            report_timeout(p, abort);
+            // Let the copies already issued land before the CTA exits (bounded).
+            const int outstanding = (int)(issued < TC_STAGES ? issued : TC_STAGES);
+            for (int i = 1; i <= outstanding; i++) {
+                int s = stage - i;
+                uint32_t ph = phase;
+                if (s < 0) { s += TC_STAGES; ph ^= 1; }
+                volatile int no_abort = 0;
+                mbar_wait(&full[s], ph, &no_abort, 100000000ull);
+            }
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ---------------- MMA issuer
+        const uint32_t idesc = idesc_f16(F16ACC ? 0 : 1, p.a_mn, p.b_mn, TC_BM, TC_BN);
+        int stage = 0;
+        uint32_t phase = 0;
+        int local = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, local++) {
+            const int buf = local & 1;
+            const uint32_t acc_phase = (local >> 1) & 1;
+            if (!mbar_wait(&tempty[buf], acc_phase ^ 1, abort, TC_WAIT_NS)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + buf * TC_BN;
+            for (int kb = 0; kb < nk; kb++) {
+                if (!mbar_wait(&full[stage], phase, abort, TC_WAIT_NS)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t a_base = smem_u32(sA + stage * TC_A_BYTES);
+                const uint32_t b_base = smem_u32(sB + stage * TC_B_BYTES);
+#pragma unroll
+                for (int k = 0; k < TC_BK / 16; k++) {
+                    // K-major: the 16-element K slice is 32 bytes into each 128-byte swizzled row.
+                    // MN-major: the slice is 16 K-rows of 128 bytes; MN atoms of 64 elements are 8 KiB apart.
+                    const uint64_t ad = p.a_mn ? smem_desc_sw128(a_base + k * 2048, 8192, 1024)
+                                               : smem_desc_sw128(a_base + k * 32, 16, 1024);
+                    const uint64_t bd = p.b_mn ? smem_desc_sw128(b_base + k * 2048, 8192, 1024)
+                                               : smem_desc_sw128(b_base + k * 32, 16, 1024);
+                    umma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0);
+                }
+                umma_commit(&empty[stage]);
+                if (++stage == TC_STAGES) { stage = 0; phase ^= 1; }
+            }
+            if (!ok) break;
+            umma_commit(&tfull[buf]);
+        }
+        if (!ok) report_timeout(p, abort);
+        // Wait (bounded) until every MMA issued by this thread has finished before TMEM is freed.
+        umma_commit(drain);
+        volatile int no_abort = 0;
+        mbar_wait(drain, 0, &no_abort, 100000000ull);
+    } else if (warp >= 2) {
+        // ---------------- epilogue: 128 threads, thread = one accumulator row (TMEM lane)
+        const int q = warp & 3;                 // TMEM lane quarter this warp may access
+        const int row_in_tile = q * 32 + lane;
+        int local = 0;
+        for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, local++) {
+            int b, mb, nb;
+            tile_coords(p, tile, b, mb, nb);
+            const int buf = local & 1;
+            const uint32_t acc_phase = (local >> 1) & 1;
+            if (!mbar_wait(&tfull[buf], acc_phase, abort, TC_WAIT_NS)) {
+                report_timeout(p, abort);
+                break;
+            }
+            tc_fence_after();
+            const int row = mb * TC_BM + row_in_tile;
+            const bool row_ok = row < p.M;
+            __half *crow = p.C + (long long)b * p.sC + (long long)(row_ok ? row : 0) * p.ldc;
+            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + buf * TC_BN;
+#pragma unroll 1
+            for (int c = 0; c < TC_BN / 32; c++) {
+                const int col0 = nb * TC_BN + c * 32;
+                uint32_t r[32];
+                if (F16ACC) tmem_ld_32x32_pack16(t_row + c * 32, r);
+                else tmem_ld_32x32(t_row + c * 32, r);
+                tmem_ld_wait();
+                if (col0 < p.N) store_chunk<F16ACC>(p, r, crow, col0, row_ok);
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[buf]);
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TC_TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ repack
+// Copies a rows × cols FP16 matrix (row pitch ld, batch stride s) into a dense layout with a row pitch that is a
+// multiple of 8 elements (16 bytes), so that TMA can read it. Used only when the caller's strides are not TMA-legal.
+__global__ void repack_f16(const __half *__restrict__ src, long long ld, long long s, int rows, int cols, __half *dst,
+                           long long dld, long long ds, int count) {
+    const long long n = (long long)rows * cols;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n * count; i += (long long)gridDim.x * blockDim.x) {
+        const long long b = i / n, r = (i % n) / cols, c = i % cols;
+        dst[b * ds + r * dld + c] = src[b * s + r * ld + c];
+    }
+}
+
+static int encode_map(CUtensorMap *m, const void *base, long long inner, long long outer, long long ld, long long count,
+                      long long bstride, int box_inner, int box_outer) {
+    auto enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(tensor_map_encoder());
+    if (!enc) return fail(GEN9BLAS_ERR, "cuTensorMapEncodeTiled is not available from the driver");
+    cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)outer, (cuuint64_t)count};
+    cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)bstride * 2};
+    cuuint32_t box[3] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(GEN9BLAS_ERR, "cuTensorMapEncodeTiled failed (%d): inner %lld outer %lld ld %lld count %lld", (int)r,
+                    inner, outer, ld, count);
+    return 0;
+}
+
+static bool tma_ok(const void *p, long long ld, long long s, int count) {
+    return ((uintptr_t)p & 15) == 0 && (ld * 2) % 16 == 0 && (count == 1 || (s * 2) % 16 == 0);
+}
+
+int launch_hgemm_tc(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, long long sA,
+                    const void *B, int ldb, long long sB, double beta, void *C, int ldc, long long sC, int count,
+                    cudaStream_t st) {
+    DevState *d = dev_state();
+    if (!d) return G.status;
+    // Stored shapes: A is rowsA × colsA with pitch lda (tA: K × M, else M × K); B is rowsB × colsB (tB: N × K, else K × N).
+    const long long rowsA = tA ? K : M, colsA = tA ? M : K;
+    const long long rowsB = tB ? N : K, colsB = tB ? K : N;
+    const void *a = A, *b = B;
+    long long la = lda, lb = ldb, xa = sA, xb = sB;
+    if (!tma_ok(A, lda, sA, count) || !tma_ok(B, ldb, sB, count)) {
+        const long long pa = (colsA + 7) / 8 * 8, pb = (colsB + 7) / 8 * 8;
+        const long long bytesA = tma_ok(A, lda, sA, count) ? 0 : ((rowsA * pa * count * 2 + 255) / 256 * 256);
+        const long long bytesB = tma_ok(B, ldb, sB, count) ? 0 : rowsB * pb * count * 2;
+        void *scr = nullptr;
+        G9_TRY(scratch((size_t)(bytesA + bytesB), &scr));
+        if (bytesA) {
+            repack_f16<<<d->sm_count * 8, 256, 0, st>>>((const __half *)A, lda, sA, (int)rowsA, (int)colsA, (__half *)scr, pa,
+                                                       rowsA * pa, count);
+            G9_TRY(launched("repack_f16"));
+            a = scr; la = pa; xa = rowsA * pa;
+        }
+        if (bytesB) {
+            __half *dstB = (__half *)((char *)scr + bytesA);
+            repack_f16<<<d->sm_count * 8, 256, 0, st>>>((const __half *)B, ldb, sB, (int)rowsB, (int)colsB, dstB, pb,
+                                                       rowsB * pb, count);
+            G9_TRY(launched("repack_f16"));
+            b = dstB; lb = pb; xb = rowsB * pb;
+        }
+    }
+    if (count == 1) {   // a batch stride is still required by the 3-D map; any legal value works
+        xa = (rowsA * la + 7) / 8 * 8;
+        xb = (rowsB * lb + 7) / 8 * 8;
+    }
+    CUtensorMap mA, mB;
+    // K-major operands: box 64 (K) × rows; MN-major operands: box 64 (M or N) × 64 (K).
+    if (!tA) G9_TRY(encode_map(&mA, a, K, M, la, count, xa, TC_BK, TC_BM));
+    else G9_TRY(encode_map(&mA, a, M, K, la, count, xa, 64, TC_BK));
+    if (tB) G9_TRY(encode_map(&mB, b, K, N, lb, count, xb, TC_BK, TC_BN));
+    else G9_TRY(encode_map(&mB, b, N, K, lb, count, xb, 64, TC_BK));
+
+    TcParams p;
+    p.M = M; p.N = N; p.K = K; p.count = count;
+    p.tiles_m = (M + TC_BM - 1) / TC_BM;
+    p.tiles_n = (N + TC_BN - 1) / TC_BN;
+    p.total_tiles = p.tiles_m * p.tiles_n * count;
+    p.a_mn = tA ? 1 : 0;
+    p.b_mn = tB ? 0 : 1;
+    p.alpha = (float)alpha;
+    p.beta = (float)beta;
+    p.plain = alpha == 1.0 && beta == 0.0;
+    p.C = (__half *)C;
+    p.ldc = ldc;
+    p.sC = sC;
+    p.c_vec = ((uintptr_t)C & 15) == 0 && (ldc % 8) == 0 && (count == 1 || (sC % 8) == 0);
+    p.err = d->err_dev;
+    const int grid = p.total_tiles < d->sm_count ? p.total_tiles : d->sm_count;
+    if (type == GEN9BLAS_H) {
+        static bool attr = false;
+        if (!attr) {
+            G9_CU(cudaFuncSetAttribute(hgemm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM));
+            attr = true;
+        }
+        hgemm_tc_kernel<true><<<grid, TC_THREADS, TC_SMEM, st>>>(mA, mB, p);
+    } else {
+        static bool attr = false;
+        if (!attr) {
+            G9_CU(cudaFuncSetAttribute(hgemm_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM));
+            attr = true;
+        }
+        hgemm_tc_kernel<false><<<grid, TC_THREADS, TC_SMEM, st>>>(mA, mB, p);
+    }
+    return launched("hgemm_tc");
+}
+
+}  // namespace g9

@@ -1,0 +1,125 @@
+// internal.h -- state and helpers shared by the translation units of libgen9blas.so (B200 build). Not installed.
+//
+// The reference keeps an OpenCL context, a queue, USM work buffers and per-type kernel tables
+// (lib/src/internal.h:22-60, lib/src/core.c:114-203). Here the runtime is the CUDA runtime: one state block per CUDA
+// device (stream, staging buffers, scratch, a mapped error word for bounded device-side waits), selected by
+// gen9blas_set_device. Everything in this header has hidden visibility.
+#pragma once
+#include "gen9blas.h"
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+#pragma GCC visibility push(hidden)
+namespace g9 {
+
+constexpr int kMaxDevices = 16;
+constexpr int kStageSlots = 3;   // staged operands per call (A, B, C or x, y, A)
+
+// Device-side error codes written into DevState::err_host by kernels whose waits gave up.
+enum : unsigned { kDevErrNone = 0, kDevErrWaitTimeout = 1, kDevErrTmemAlloc = 2 };
+
+struct DevState {
+    bool ready = false;
+    int dev = -1;
+    int sm_count = 0;
+    int cc_major = 0, cc_minor = 0;
+    cudaStream_t own_stream = nullptr;
+    void *stage[kStageSlots] = {nullptr, nullptr, nullptr};   // device copies of staged host operands
+    size_t stage_n[kStageSlots] = {0, 0, 0};
+    void *scratch = nullptr;                                   // partial sums, packed operands
+    size_t scratch_n = 0;
+    double *result_host = nullptr;                             // pinned: scalar results of reductions
+    unsigned *err_host = nullptr;                              // mapped pinned word: device-side error code
+    unsigned *err_dev = nullptr;                               // its device address
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+};
+
+// Process-wide call state (the caller serialises calls, as for the reference).
+struct CallState {
+    int status = 0;
+    char err[1200] = {0};
+    double last_ms = 0;
+    int last_zc = 0;
+    bool profile = false;
+    bool nowait = false;
+    cudaStream_t user_stream = nullptr;
+    bool user_stream_set = false;
+    int cur_dev = -1;
+    long long launches = 0;
+};
+extern CallState G;
+
+// Current device state; initialises it on first use. nullptr on failure (status set).
+DevState *dev_state();
+cudaStream_t stream();
+
+int fail(int code, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
+int cuda_fail(cudaError_t e, const char *what, const char *file, int line);
+#define G9_CU(x)                                                                  \
+    do {                                                                          \
+        cudaError_t e_ = (x);                                                     \
+        if (e_ != cudaSuccess) return ::g9::cuda_fail(e_, #x, __FILE__, __LINE__); \
+    } while (0)
+#define G9_FAIL(code, ...) return ::g9::fail((code), __VA_ARGS__)
+#define G9_TRY(x)            \
+    do {                     \
+        int r_ = (x);        \
+        if (r_ < 0) return r_; \
+    } while (0)
+
+// Starts an operation: resets the status, initialises the library and the device. Returns 0 or an error.
+int begin_op();
+// Records one kernel launch (checks the launch error).
+int launched(const char *name);
+
+// One operand of a call: a region [host, host + bytes) the caller passed and the pointer the kernels use.
+struct Operand {
+    const void *user = nullptr;   // caller's pointer (lowest address of the region)
+    void *dptr = nullptr;         // pointer for the kernels (user itself when zero-copy)
+    size_t bytes = 0;
+    bool zc = true;               // used in place (device or managed memory)
+    bool written = false;         // copied back at the end when staged
+};
+// Maps an operand: device / managed memory in place, any other memory staged into slot (copy_in: with its contents).
+int map_operand(Operand &op, const void *p, size_t bytes, int slot, bool copy_in, bool written);
+// Ends a call: waits for the stream (unless no-wait applies), copies staged written operands back, checks the
+// device error word. ops may be empty.
+int finish_op(Operand *ops, int n);
+// Scratch buffer of at least `bytes` on the current device (grow-only). Waits for queued work before growing.
+int scratch(size_t bytes, void **p);
+// Call timing: timer_start at entry (wall clock), timer_kernel right before the main kernels (GEN9BLAS_PROFILE=1:
+// CUDA event), timer_stop at the end: last_time_ms is the kernel time with profiling, else the whole call.
+void timer_start();
+void timer_kernel();
+void timer_stop();
+
+// cuTensorMapEncodeTiled from the driver (resolved once through cudaGetDriverEntryPoint).
+void *tensor_map_encoder();
+
+// Elements of a strided vector region and offset of element 0 (inc < 0: pointer is the lowest address).
+inline size_t vec_span(int n, int inc) { return (size_t)(n - 1) * (size_t)(inc < 0 ? -(long long)inc : inc) + 1; }
+inline long long vec_off(int n, int inc) { return inc < 0 ? (long long)(n - 1) * (long long)(-inc) : 0; }
+
+// ---- kernel entry points implemented in the other translation units (host-side launchers) ----
+// All pointers are device-addressable; they enqueue on `st` and return 0 or a negative status.
+int launch_axpy(int type, int n, double a, const void *x, long long ox, long long ix, void *y, long long oy, long long iy,
+                cudaStream_t st);
+int launch_reduce(int type, int mode, int n, const void *x, long long ox, long long ix, const void *y, long long oy,
+                  long long iy, double *result_dev, cudaStream_t st);
+int launch_iamax(int type, int n, const void *x, long long ox, long long ix, long long *result_dev, cudaStream_t st);
+int launch_gemv(int type, int trans, int M, int N, double alpha, const void *A, int lda, const void *x, long long ox,
+                long long ix, double beta, void *y, long long oy, long long iy, cudaStream_t st);
+int launch_ger(int type, int M, int N, double alpha, const void *x, long long ox, long long ix, const void *y,
+               long long oy, long long iy, void *A, int lda, cudaStream_t st);
+// Dense GEMM on device pointers (batched, strided). Dispatches to tcgen05 (H/HS), FFMA (S) or FP64 (D) kernels.
+int launch_gemm(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, long long sA,
+                const void *B, int ldb, long long sB, double beta, void *C, int ldc, long long sC, int count,
+                cudaStream_t st);
+// Skinny GEMM (min(M, N) small) on device pointers.
+int launch_skinny(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, const void *B,
+                  int ldb, double beta, void *C, int ldc, cudaStream_t st);
+int skinny_threshold(int type);
+
+}  // namespace g9
+#pragma GCC visibility pop

@@ -1,0 +1,364 @@
+// runtime.cu -- initialisation, status, memory and the host/device boundary of libgen9blas.so (B200 build).
+//
+// Replaces the reference runtime lib/src/core.c (init 114-219, has 222-236, wait_gpu 240-258, alloc 288-297,
+// get_obj 328-340, to_host 363-367, getters 385-392) and its i915 layer lib/kcl.c. The design differs where the
+// hardware differs:
+// - "zero-copy" operands are device memory (cudaMalloc, torch tensors) and managed memory (gen9blas_alloc), used in
+//   place; any other host pointer is staged through grow-only device buffers (the reference copies into USM buffers);
+// - the wait is a stream synchronisation, then a check of a mapped error word that device-side bounded waits set
+//   (the reference polls GEM_WAIT with a 60 s limit, kcl.c:361-372);
+// - the state is per CUDA device so that one process per GPU (or one process switching devices) works.
+#include "internal.h"
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <pthread.h>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <ctime>
+
+namespace g9 {
+
+CallState G;
+static DevState g_dev[kMaxDevices];
+static pthread_once_t g_once = PTHREAD_ONCE_INIT;
+static int g_init_status = -1;
+static char g_init_err[sizeof(G.err)];
+
+int fail(int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(G.err, sizeof G.err, fmt, ap);
+    va_end(ap);
+    G.status = code;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what, const char *file, int line) {
+    int code = e == cudaErrorMemoryAllocation ? GEN9BLAS_ERR_OUT_OF_MEMORY : GEN9BLAS_ERR;
+    const char *base = strrchr(file, '/');
+    return fail(code, "%s:%d: %s = %s (%s)", base ? base + 1 : file, line, what, cudaGetErrorName(e),
+                cudaGetErrorString(e));
+}
+
+static double now_s() {
+    timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return ts.tv_sec + ts.tv_nsec * 1e-9;
+}
+
+// Once per process: find an sm_100 device. A failure is final, as in the reference (core.c:205-219).
+static void init_run() {
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        snprintf(g_init_err, sizeof g_init_err, "no CUDA device (%s)", e != cudaSuccess ? cudaGetErrorString(e) : "count 0");
+        g_init_status = GEN9BLAS_ERR_NO_DEVICE;
+        return;
+    }
+    int cur = 0;
+    cudaGetDevice(&cur);
+    int major = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, cur);
+    if (major != 10) {
+        snprintf(g_init_err, sizeof g_init_err, "device %d has compute capability %d.x; this build runs sm_100a kernels only",
+                 cur, major);
+        g_init_status = GEN9BLAS_ERR_NO_DEVICE;
+        return;
+    }
+    const char *p = getenv("GEN9BLAS_PROFILE");
+    G.profile = p && *p && strcmp(p, "0") != 0;
+    G.cur_dev = cur;
+    g_init_status = 0;
+}
+
+static int device_setup(DevState &d, int dev) {
+    int prev = -1;
+    cudaGetDevice(&prev);
+    if (prev != dev) G9_CU(cudaSetDevice(dev));
+    d.dev = dev;
+    G9_CU(cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev));
+    G9_CU(cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev));
+    G9_CU(cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev));
+    if (d.cc_major != 10) G9_FAIL(GEN9BLAS_ERR_NO_DEVICE, "device %d is not sm_100 (cc %d.%d)", dev, d.cc_major, d.cc_minor);
+    G9_CU(cudaStreamCreateWithFlags(&d.own_stream, cudaStreamNonBlocking));
+    G9_CU(cudaHostAlloc((void **)&d.result_host, 4096, cudaHostAllocDefault));
+    G9_CU(cudaHostAlloc((void **)&d.err_host, 64, cudaHostAllocMapped));
+    *d.err_host = kDevErrNone;
+    G9_CU(cudaHostGetDevicePointer((void **)&d.err_dev, d.err_host, 0));
+    G9_CU(cudaEventCreate(&d.ev0));
+    G9_CU(cudaEventCreate(&d.ev1));
+    d.ready = true;
+    return 0;
+}
+
+DevState *dev_state() {
+    int dev = G.cur_dev;
+    if (dev < 0 || dev >= kMaxDevices) {
+        fail(GEN9BLAS_ERR_INVALID_ARG, "device %d out of range", dev);
+        return nullptr;
+    }
+    DevState &d = g_dev[dev];
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != dev && cudaSetDevice(dev) != cudaSuccess) {
+        cudaGetLastError();
+        fail(GEN9BLAS_ERR, "cudaSetDevice(%d) failed", dev);
+        return nullptr;
+    }
+    if (!d.ready && device_setup(d, dev) < 0) return nullptr;
+    return &d;
+}
+
+cudaStream_t stream() {
+    if (G.user_stream_set) return G.user_stream;
+    DevState *d = dev_state();
+    return d ? d->own_stream : nullptr;
+}
+
+int begin_op() {
+    G.status = 0;
+    G.err[0] = 0;
+    pthread_once(&g_once, init_run);
+    if (g_init_status) return fail(GEN9BLAS_ERR_NO_DEVICE, "%s", g_init_err);
+    if (!dev_state()) return G.status ? G.status : GEN9BLAS_ERR;
+    return 0;
+}
+
+int launched(const char *name) {
+    G.launches++;
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(GEN9BLAS_ERR, "launch of %s failed: %s", name, cudaGetErrorString(e));
+    return 0;
+}
+
+static int ensure_dev_buf(void **p, size_t *n, size_t bytes) {
+    if (*n >= bytes) return 0;
+    if (*p) {
+        G9_CU(cudaStreamSynchronize(stream()));
+        G9_CU(cudaFree(*p));
+        *p = nullptr;
+        *n = 0;
+    }
+    size_t want = bytes < 4096 ? 4096 : (bytes + 0xFFFFF) & ~(size_t)0xFFFFF;   // round to 1 MiB
+    G9_CU(cudaMalloc(p, want));
+    *n = want;
+    return 0;
+}
+
+int scratch(size_t bytes, void **p) {
+    DevState *d = dev_state();
+    if (!d) return G.status;
+    G9_TRY(ensure_dev_buf(&d->scratch, &d->scratch_n, bytes));
+    *p = d->scratch;
+    return 0;
+}
+
+int map_operand(Operand &op, const void *p, size_t bytes, int slot, bool copy_in, bool written) {
+    op.user = p;
+    op.bytes = bytes;
+    op.written = written;
+    DevState *d = dev_state();
+    if (!d) return G.status;
+    if (!p) return fail(GEN9BLAS_ERR_INVALID_ARG, "NULL operand");
+    cudaPointerAttributes a;
+    cudaError_t e = cudaPointerGetAttributes(&a, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        a.type = cudaMemoryTypeUnregistered;
+    }
+    if (a.type == cudaMemoryTypeDevice) {
+        if (a.device != d->dev)
+            return fail(GEN9BLAS_ERR_INVALID_ARG, "operand is memory of device %d, the current device is %d", a.device, d->dev);
+        op.dptr = const_cast<void *>(p);
+        op.zc = true;
+        return 0;
+    }
+    if (a.type == cudaMemoryTypeManaged) {
+        op.dptr = const_cast<void *>(p);
+        op.zc = true;
+#if CUDART_VERSION >= 12020
+        cudaMemLocation loc;
+        loc.type = cudaMemLocationTypeDevice;
+        loc.id = d->dev;
+        if (cudaMemPrefetchAsync(p, bytes, loc, 0, stream()) != cudaSuccess) cudaGetLastError();
+#endif
+        return 0;
+    }
+    // Host memory (pageable or pinned): stage through the slot's device buffer.
+    G9_TRY(ensure_dev_buf(&d->stage[slot], &d->stage_n[slot], bytes));
+    op.dptr = d->stage[slot];
+    op.zc = false;
+    if (copy_in) G9_CU(cudaMemcpyAsync(op.dptr, p, bytes, cudaMemcpyHostToDevice, stream()));
+    return 0;
+}
+
+static int check_dev_err(DevState *d) {
+    unsigned v = *(volatile unsigned *)d->err_host;
+    if (v != kDevErrNone) {
+        *(volatile unsigned *)d->err_host = kDevErrNone;
+        if (v == kDevErrWaitTimeout)
+            return fail(GEN9BLAS_ERR, "a device-side wait gave up (bounded mbarrier wait timed out); results are invalid");
+        return fail(GEN9BLAS_ERR, "device-side error code %u", v);
+    }
+    return 0;
+}
+
+int finish_op(Operand *ops, int n) {
+    DevState *d = dev_state();
+    if (!d) return G.status;
+    cudaStream_t st = stream();
+    bool all_zc = true;
+    for (int i = 0; i < n; i++) all_zc = all_zc && ops[i].zc;
+    if (G.nowait && all_zc) return 0;
+    for (int i = 0; i < n; i++)
+        if (ops[i].written && !ops[i].zc)
+            G9_CU(cudaMemcpyAsync(const_cast<void *>(ops[i].user), ops[i].dptr, ops[i].bytes, cudaMemcpyDeviceToHost, st));
+    G9_CU(cudaStreamSynchronize(st));
+    return check_dev_err(d);
+}
+
+static double g_t0;
+void timer_start() { g_t0 = now_s(); }
+void timer_kernel() {
+    if (G.profile) {
+        DevState *d = dev_state();
+        if (d) cudaEventRecord(d->ev0, stream());
+    }
+}
+void timer_stop() {
+    if (G.profile && !G.nowait) {
+        DevState *d = dev_state();
+        if (d) {
+            cudaEventRecord(d->ev1, stream());
+            cudaEventSynchronize(d->ev1);
+            float ms = 0;
+            cudaEventElapsedTime(&ms, d->ev0, d->ev1);
+            G.last_ms = ms;
+            return;
+        }
+    }
+    G.last_ms = (now_s() - g_t0) * 1e3;
+}
+
+void *tensor_map_encoder() {
+    static void *fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            fn = nullptr;
+        }
+    }
+    return fn;
+}
+
+}  // namespace g9
+
+using namespace g9;
+
+extern "C" {
+
+GEN9BLAS_API int gen9blas_version(void) { return GEN9BLAS_VERSION; }
+
+GEN9BLAS_API int gen9blas_init(void) {
+    pthread_once(&g_once, init_run);
+    if (g_init_status) return fail(GEN9BLAS_ERR_NO_DEVICE, "%s", g_init_err);
+    return 0;
+}
+
+GEN9BLAS_API int gen9blas_device_gen(void) {
+    if (gen9blas_init()) return 0;
+    DevState *d = dev_state();
+    return d ? d->cc_major * 10 + d->cc_minor : 0;
+}
+
+GEN9BLAS_API int gen9blas_has(int f) {
+    if (gen9blas_init()) return 0;
+    switch (f) {
+    case GEN9BLAS_FEAT_FP16:
+    case GEN9BLAS_FEAT_FP32:
+    case GEN9BLAS_FEAT_FP64: return 1;
+    default: return 0;
+    }
+}
+
+GEN9BLAS_API const char *gen9blas_error(void) { return G.err; }
+GEN9BLAS_API int gen9blas_last_status(void) { return G.status; }
+GEN9BLAS_API double gen9blas_last_time_ms(void) { return G.last_ms; }
+GEN9BLAS_API int gen9blas_last_zero_copy(void) { return G.last_zc; }
+GEN9BLAS_API long long gen9blas_kernel_launches(void) { return G.launches; }
+
+GEN9BLAS_API void *gen9blas_alloc(size_t bytes) {
+    if (begin_op()) return nullptr;
+    void *p = nullptr;
+    cudaError_t e = cudaMallocManaged(&p, bytes ? bytes : 1, cudaMemAttachGlobal);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        fail(GEN9BLAS_ERR_OUT_OF_MEMORY, "cudaMallocManaged(%zu) = %s", bytes, cudaGetErrorName(e));
+        return nullptr;
+    }
+    return p;
+}
+
+GEN9BLAS_API void gen9blas_free(void *p) {
+    if (!p || gen9blas_init()) return;
+    cudaDeviceSynchronize();
+    if (cudaFree(p) != cudaSuccess) cudaGetLastError();
+}
+
+GEN9BLAS_API int gen9blas_is_usm(const void *p, size_t bytes) {
+    if (!p || gen9blas_init()) return 0;
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (a.type != cudaMemoryTypeManaged) return 0;
+    // The CUDA runtime reports the allocation range through the driver only; the end check uses the last byte.
+    if (bytes > 1) {
+        cudaPointerAttributes b;
+        if (cudaPointerGetAttributes(&b, (const char *)p + bytes - 1) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        return b.type == cudaMemoryTypeManaged;
+    }
+    return 1;
+}
+
+GEN9BLAS_API int gen9blas_set_device(int device) {
+    if (gen9blas_init()) return G.status;
+    int n = 0;
+    cudaGetDeviceCount(&n);
+    if (device < 0 || device >= n || device >= kMaxDevices)
+        return fail(GEN9BLAS_ERR_INVALID_ARG, "device %d out of range (%d devices)", device, n);
+    G.cur_dev = device;
+    G.user_stream_set = false;
+    G.user_stream = nullptr;
+    return dev_state() ? 0 : G.status;
+}
+
+GEN9BLAS_API int gen9blas_get_device(void) { return gen9blas_init() ? -1 : G.cur_dev; }
+
+GEN9BLAS_API int gen9blas_set_stream(void *s) {
+    if (gen9blas_init()) return G.status;
+    G.user_stream = (cudaStream_t)s;
+    G.user_stream_set = s != nullptr;
+    return 0;
+}
+
+GEN9BLAS_API void gen9blas_set_nowait(int on) { G.nowait = on != 0; }
+
+GEN9BLAS_API int gen9blas_flush(void) {
+    if (begin_op()) return G.status;
+    G9_CU(cudaStreamSynchronize(stream()));
+    return check_dev_err(dev_state());
+}
+
+}  // extern "C"

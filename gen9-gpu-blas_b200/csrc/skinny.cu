@@ -1,0 +1,397 @@
+// skinny.cu -- GEMM with a small dimension (min(M, N) <= 16 by default): C = alpha·a·wᵀ + beta·C, where the small
+// operand a has Mc rows and the large "weights" operand w has Nc rows of length K.
+//
+// Replaces the reference's gemm_skinny (lib/src/gemm.c:191-263) and its kernels skinny_k1/k4/k8, skinny_r4/r8
+// (weights contiguous along K, lib/kernels/level12.cl:646-801) and skinny_n4 + skinny_n2 (weights contiguous along N,
+// level12.cl:803-862). The host logic is the same: the operand roles swap when N is the small side
+// (Cᵀ = op(B)ᵀ·op(A)ᵀ, C written with swapped strides, gemm.c:213-221), and accumulation is FP32 (FP64 never takes
+// this path, gemm.c:191-199).
+//
+// B200 kernels:
+// - wk_f16_mma: weights FP16, contiguous along K. A CTA owns 16 weight rows; its 8 warps split K. Each lane streams
+//   16-byte loads of two weight rows (ld.global.nc, deep unroll) and feeds them to mma.sync m16n8k16 (FP16 in, FP32
+//   accumulate) with the weight rows as the MMA's M side and up to 16 tokens as N. The K order inside a 32-wide step
+//   is permuted identically for weights and tokens (a dot product does not depend on it), so every lane's 16-byte
+//   load is directly an MMA fragment. Warp partial sums are combined in shared memory in a fixed order.
+// - wk_f32: weights FP32, contiguous along K, FFMA: a CTA owns 4 rows, 8 warps split K, lanes read float4, warp
+//   shuffle reduction, fixed-order combination across warps.
+// - wn_partial + wn_final: weights contiguous along N: split-K partial sums P[part][m][n] in FP32, then a fixed-order
+//   sum with the alpha/beta epilogue (deterministic, no atomics).
+// - generic: any other layout (unaligned rows, K not a multiple of 8): one warp per weight row, scalar loads.
+#include "common.cuh"
+#include "internal.h"
+#include <cstdlib>
+
+namespace g9 {
+
+int skinny_threshold(int type) {
+    static int forced = -2;
+    if (forced == -2) {
+        const char *e = getenv("GEN9BLAS_SKINNY");
+        forced = e ? atoi(e) : -1;
+    }
+    if (type == GEN9BLAS_D) return 0;
+    if (forced >= 0) return forced;
+    return 16;
+}
+
+struct SkinnyArgs {
+    int Mc, Nc, K;
+    float alpha, beta;
+    const void *a;   // a[m*sam + k*sak]
+    long long sam, sak;
+    const void *w;   // w[n*swn + k*swk]
+    long long swn, swk;
+    void *C;         // C[m*scm + n*scn]
+    long long scm, scn;
+};
+
+template <typename T>
+__device__ __forceinline__ void skinny_store(const SkinnyArgs &p, int m, int n, float s) {
+    T *c = (T *)p.C + (long long)m * p.scm + (long long)n * p.scn;
+    float v = p.alpha * s;
+    if (p.beta != 0.0f) v = __fmaf_rn(p.beta, to_r(*c), v);
+    *c = from_r<T>(v);
+}
+
+// ------------------------------------------------------------------------------------------------ FP16, K-contiguous
+constexpr int WK_WARPS = 8;
+constexpr int WK_UNROLL = 4;   // 32-wide K steps per batch of loads
+
+__device__ __forceinline__ void mma_16816(float *d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                          uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint4 ldg_nc16(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t word(const uint4 &v, int i) {
+    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+// Requirements (checked on the host): K % 8 == 0, weight rows and token rows contiguous along K with 16-byte aligned
+// starts. grid = (ceil(Nc / 16), ceil(Mc / 16)).
+template <bool TWO_NTILES>
+__global__ void __launch_bounds__(WK_WARPS * 32) wk_f16_mma(const SkinnyArgs p) {
+    __shared__ float red[WK_WARPS][16][17];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int r0 = blockIdx.x * 16, t0 = blockIdx.y * 16;
+    const __half *W = (const __half *)p.w;
+    const __half *A = (const __half *)p.a;
+    // Rows beyond the edges are clamped (valid addresses); their results are never stored.
+    const int wr0 = min(r0 + g, p.Nc - 1), wr1 = min(r0 + g + 8, p.Nc - 1);
+    const int ta0 = min(t0 + g, p.Mc - 1), ta1 = min(t0 + g + 8, p.Mc - 1);
+    const __half *w0 = W + (long long)wr0 * p.swn;
+    const __half *w1 = W + (long long)wr1 * p.swn;
+    const __half *a0 = A + (long long)ta0 * p.sam;
+    const __half *a1 = A + (long long)ta1 * p.sam;
+
+    const int steps = (p.K + 31) / 32;
+    const int per_warp = (steps + WK_WARPS - 1) / WK_WARPS;
+    const int s_beg = warp * per_warp, s_end = min(steps, s_beg + per_warp);
+    float d0[4] = {0, 0, 0, 0}, d1[4] = {0, 0, 0, 0};
+    for (int s = s_beg; s < s_end; s += WK_UNROLL) {
+        uint4 wv0[WK_UNROLL], wv1[WK_UNROLL], av0[WK_UNROLL], av1[WK_UNROLL];
+#pragma unroll
+        for (int u = 0; u < WK_UNROLL; u++) {
+            const int k = (s + u) * 32 + 8 * t;
+            const bool in = s + u < s_end && k < p.K;
+            wv0[u] = in ? ldg_nc16(w0 + k) : make_uint4(0, 0, 0, 0);
+            wv1[u] = in ? ldg_nc16(w1 + k) : make_uint4(0, 0, 0, 0);
+            av0[u] = in ? __ldg(reinterpret_cast<const uint4 *>(a0 + k)) : make_uint4(0, 0, 0, 0);
+            if (TWO_NTILES) av1[u] = in ? __ldg(reinterpret_cast<const uint4 *>(a1 + k)) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < WK_UNROLL; u++) {
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const uint32_t A0 = word(wv0[u], 2 * j), A1 = word(wv1[u], 2 * j);
+                const uint32_t A2 = word(wv0[u], 2 * j + 1), A3 = word(wv1[u], 2 * j + 1);
+                mma_16816(d0, A0, A1, A2, A3, word(av0[u], 2 * j), word(av0[u], 2 * j + 1));
+                if (TWO_NTILES) mma_16816(d1, A0, A1, A2, A3, word(av1[u], 2 * j), word(av1[u], 2 * j + 1));
+            }
+        }
+    }
+    // D fragment: d[0..1] = (row g, tokens 2t, 2t+1), d[2..3] = (row g+8, tokens 2t, 2t+1).
+    red[warp][g][2 * t] = d0[0];
+    red[warp][g][2 * t + 1] = d0[1];
+    red[warp][g + 8][2 * t] = d0[2];
+    red[warp][g + 8][2 * t + 1] = d0[3];
+    if (TWO_NTILES) {
+        red[warp][g][8 + 2 * t] = d1[0];
+        red[warp][g][8 + 2 * t + 1] = d1[1];
+        red[warp][g + 8][8 + 2 * t] = d1[2];
+        red[warp][g + 8][8 + 2 * t + 1] = d1[3];
+    } else {
+        red[warp][g][8 + 2 * t] = 0;
+        red[warp][g][8 + 2 * t + 1] = 0;
+        red[warp][g + 8][8 + 2 * t] = 0;
+        red[warp][g + 8][8 + 2 * t + 1] = 0;
+    }
+    __syncthreads();
+    const int row = threadIdx.x >> 4, tok = threadIdx.x & 15;
+    const int n = r0 + row, m = t0 + tok;
+    if (n < p.Nc && m < p.Mc) {
+        float s = 0;
+#pragma unroll
+        for (int w = 0; w < WK_WARPS; w++) s += red[w][row][tok];
+        skinny_store<__half>(p, m, n, s);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ FP32, K-contiguous
+constexpr int WKF_ROWS = 4;
+
+// Requirements: K % 4 == 0, rows 16-byte aligned. grid = (ceil(Nc / 4), ceil(Mc / MT)).
+template <int MT>
+__global__ void __launch_bounds__(WK_WARPS * 32) wk_f32(const SkinnyArgs p) {
+    __shared__ float red[WK_WARPS][WKF_ROWS][MT];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r0 = blockIdx.x * WKF_ROWS, t0 = blockIdx.y * MT;
+    const float *W = (const float *)p.w;
+    const float *A = (const float *)p.a;
+    const int nv = p.K / 4;
+    const int per_warp = (nv + WK_WARPS - 1) / WK_WARPS;
+    const int v_beg = warp * per_warp, v_end = min(nv, v_beg + per_warp);
+    float acc[WKF_ROWS][MT];
+#pragma unroll
+    for (int r = 0; r < WKF_ROWS; r++)
+#pragma unroll
+        for (int m = 0; m < MT; m++) acc[r][m] = 0;
+    const float *wrow[WKF_ROWS];
+#pragma unroll
+    for (int r = 0; r < WKF_ROWS; r++) wrow[r] = W + (long long)min(r0 + r, p.Nc - 1) * p.swn;
+    const float *arow[MT];
+#pragma unroll
+    for (int m = 0; m < MT; m++) arow[m] = A + (long long)min(t0 + m, p.Mc - 1) * p.sam;
+    for (int v = v_beg + lane; v < v_end; v += 32) {
+        float4 wv[WKF_ROWS];
+#pragma unroll
+        for (int r = 0; r < WKF_ROWS; r++) {
+            uint4 u = ldg_nc16(wrow[r] + 4 * v);
+            wv[r] = make_float4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z), __uint_as_float(u.w));
+        }
+#pragma unroll
+        for (int m = 0; m < MT; m++) {
+            const float4 av = __ldg(reinterpret_cast<const float4 *>(arow[m] + 4 * v));
+#pragma unroll
+            for (int r = 0; r < WKF_ROWS; r++) {
+                acc[r][m] = __fmaf_rn(wv[r].x, av.x, acc[r][m]);
+                acc[r][m] = __fmaf_rn(wv[r].y, av.y, acc[r][m]);
+                acc[r][m] = __fmaf_rn(wv[r].z, av.z, acc[r][m]);
+                acc[r][m] = __fmaf_rn(wv[r].w, av.w, acc[r][m]);
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < WKF_ROWS; r++)
+#pragma unroll
+        for (int m = 0; m < MT; m++) {
+            float s = acc[r][m];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            if (lane == 0) red[warp][r][m] = s;
+        }
+    __syncthreads();
+    for (int i = threadIdx.x; i < WKF_ROWS * MT; i += blockDim.x) {
+        const int r = i / MT, m = i % MT;
+        const int n = r0 + r, mm = t0 + m;
+        if (n < p.Nc && mm < p.Mc) {
+            float s = 0;
+#pragma unroll
+            for (int w = 0; w < WK_WARPS; w++) s += red[w][r][m];
+            skinny_store<float>(p, mm, n, s);
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ N-contiguous
+constexpr int WN_THREADS = 256, WN_COLS = 4, WN_MT = 16, WN_KC = 64;
+
+// P[part][m][n] = Σ_{k in part} a[m][k]·w[k][n] for 16 tokens (blockIdx.z) and 4 columns per thread.
+template <typename T>
+__global__ void __launch_bounds__(WN_THREADS) wn_partial(const SkinnyArgs p, int kpp, float *P) {
+    __shared__ float as[WN_MT][WN_KC];
+    const int n = (blockIdx.x * WN_THREADS + threadIdx.x) * WN_COLS;
+    const int part = blockIdx.y, t0 = blockIdx.z * WN_MT;
+    const int kb = part * kpp, ke = min(p.K, kb + kpp);
+    const T *W = (const T *)p.w;
+    const T *A = (const T *)p.a;
+    float acc[WN_MT][WN_COLS];
+#pragma unroll
+    for (int m = 0; m < WN_MT; m++)
+#pragma unroll
+        for (int c = 0; c < WN_COLS; c++) acc[m][c] = 0;
+    for (int k0 = kb; k0 < ke; k0 += WN_KC) {
+        const int kn = min(WN_KC, ke - k0);
+        __syncthreads();
+        for (int i = threadIdx.x; i < WN_MT * WN_KC; i += WN_THREADS) {
+            const int m = i / WN_KC, k = i % WN_KC;
+            as[m][k] = (t0 + m < p.Mc && k < kn) ? to_r(A[(long long)(t0 + m) * p.sam + (long long)(k0 + k) * p.sak]) : 0.0f;
+        }
+        __syncthreads();
+        if (n < p.Nc) {
+            for (int k = 0; k < kn; k++) {
+                const T *wp = W + (long long)(k0 + k) * p.swk + n;
+                float wv[WN_COLS];
+#pragma unroll
+                for (int c = 0; c < WN_COLS; c++) wv[c] = n + c < p.Nc ? to_r(__ldg(wp + c)) : 0.0f;
+#pragma unroll
+                for (int m = 0; m < WN_MT; m++) {
+                    const float av = as[m][k];
+#pragma unroll
+                    for (int c = 0; c < WN_COLS; c++) acc[m][c] = __fmaf_rn(av, wv[c], acc[m][c]);
+                }
+            }
+        }
+    }
+    if (n >= p.Nc) return;
+#pragma unroll
+    for (int m = 0; m < WN_MT; m++) {
+        if (t0 + m >= p.Mc) break;
+        float *out = P + ((long long)part * p.Mc + t0 + m) * p.Nc + n;
+#pragma unroll
+        for (int c = 0; c < WN_COLS; c++)
+            if (n + c < p.Nc) out[c] = acc[m][c];
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) wn_final(const SkinnyArgs p, int parts, const float *P) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= (long long)p.Mc * p.Nc) return;
+    const int m = (int)(i / p.Nc), n = (int)(i % p.Nc);
+    float s = 0;
+    for (int q = 0; q < parts; q++) s += P[((long long)q * p.Mc + m) * p.Nc + n];
+    skinny_store<T>(p, m, n, s);
+}
+
+// ------------------------------------------------------------------------------------------------ generic
+// One warp per weight row n, tokens in groups of 8, lanes stride K. Any strides.
+template <typename T>
+__global__ void __launch_bounds__(256) skinny_generic(const SkinnyArgs p) {
+    const int lane = threadIdx.x & 31;
+    const long long n = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+    if (n >= p.Nc) return;
+    const T *W = (const T *)p.w + n * p.swn;
+    const T *A = (const T *)p.a;
+    for (int m0 = 0; m0 < p.Mc; m0 += 8) {
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int k = lane; k < p.K; k += 32) {
+            const float wv = to_r(W[(long long)k * p.swk]);
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+                if (m0 + j < p.Mc) acc[j] = __fmaf_rn(wv, to_r(A[(long long)(m0 + j) * p.sam + (long long)k * p.sak]), acc[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            float s = acc[j];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            if (lane == 0 && m0 + j < p.Mc) skinny_store<T>(p, m0 + j, (int)n, s);
+        }
+    }
+}
+
+// Dense K-contiguous copy of the small operand (Mc × K, row pitch Kp = K rounded up to 8) for the fast kernels.
+template <typename T>
+__global__ void repack_small(const T *__restrict__ a, long long sam, long long sak, int Mc, int K, int Kp, T *dst) {
+    const long long n = (long long)Mc * Kp;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const int m = (int)(i / Kp), k = (int)(i % Kp);
+        dst[i] = k < K ? a[(long long)m * sam + (long long)k * sak] : T(0);
+    }
+}
+
+template <typename T>
+static int skinny_t(SkinnyArgs p, cudaStream_t st) {
+    DevState *d = dev_state();
+    if (!d) return G.status;
+    const int es = sizeof(T);
+    if (p.swk == 1) {
+        // Fast path when the weight rows allow 16-byte loads; the small operand is repacked when it does not.
+        const int kq = 16 / es;   // elements per 16-byte load
+        const bool w_ok = ((uintptr_t)p.w & 15) == 0 && (p.swn * es) % 16 == 0 && p.K % kq == 0;
+        if (w_ok) {
+            const bool a_ok = p.sak == 1 && ((uintptr_t)p.a & 15) == 0 && (p.sam * es) % 16 == 0;
+            if (!a_ok) {
+                void *scr = nullptr;
+                G9_TRY(scratch((size_t)p.Mc * p.K * es + 256, &scr));
+                repack_small<T><<<d->sm_count * 4, 256, 0, st>>>((const T *)p.a, p.sam, p.sak, p.Mc, p.K, p.K, (T *)scr);
+                G9_TRY(launched("repack_small"));
+                p.a = scr;
+                p.sam = p.K;
+                p.sak = 1;
+            }
+            if (sizeof(T) == 2) {
+                dim3 grid((p.Nc + 15) / 16, (p.Mc + 15) / 16);
+                if (p.Mc > 8) wk_f16_mma<true><<<grid, WK_WARPS * 32, 0, st>>>(p);
+                else wk_f16_mma<false><<<grid, WK_WARPS * 32, 0, st>>>(p);
+                return launched("skinny_wk_f16_mma");
+            }
+            const int mt = p.Mc <= 1 ? 1 : p.Mc <= 4 ? 4 : p.Mc <= 8 ? 8 : 16;
+            dim3 grid((p.Nc + WKF_ROWS - 1) / WKF_ROWS, (p.Mc + mt - 1) / mt);
+            if (mt == 1) wk_f32<1><<<grid, WK_WARPS * 32, 0, st>>>(p);
+            else if (mt == 4) wk_f32<4><<<grid, WK_WARPS * 32, 0, st>>>(p);
+            else if (mt == 8) wk_f32<8><<<grid, WK_WARPS * 32, 0, st>>>(p);
+            else wk_f32<16><<<grid, WK_WARPS * 32, 0, st>>>(p);
+            return launched("skinny_wk_f32");
+        }
+        const long long warps = p.Nc;
+        skinny_generic<T><<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(p);
+        return launched("skinny_generic");
+    }
+    // Weights contiguous along N: split K into parts so that the grid covers the GPU, then a fixed-order sum.
+    const int col_blocks = (p.Nc + WN_THREADS * WN_COLS - 1) / (WN_THREADS * WN_COLS);
+    const int mtiles = (p.Mc + WN_MT - 1) / WN_MT;
+    int parts = (d->sm_count * 4 + col_blocks * mtiles - 1) / (col_blocks * mtiles);
+    const int max_parts = (p.K + WN_KC - 1) / WN_KC;
+    if (parts > max_parts) parts = max_parts;
+    if (parts < 1) parts = 1;
+    int kpp = (p.K + parts - 1) / parts;
+    kpp = (kpp + WN_KC - 1) / WN_KC * WN_KC;
+    parts = (p.K + kpp - 1) / kpp;
+    void *P = nullptr;
+    G9_TRY(scratch((size_t)parts * p.Mc * p.Nc * sizeof(float), &P));
+    dim3 grid(col_blocks, parts, mtiles);
+    wn_partial<T><<<grid, WN_THREADS, 0, st>>>(p, kpp, (float *)P);
+    G9_TRY(launched("skinny_wn_partial"));
+    const long long outs = (long long)p.Mc * p.Nc;
+    wn_final<T><<<(unsigned)((outs + 255) / 256), 256, 0, st>>>(p, parts, (const float *)P);
+    return launched("skinny_wn_final");
+}
+
+int launch_skinny(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, const void *B,
+                  int ldb, double beta, void *C, int ldc, cudaStream_t st) {
+    SkinnyArgs p;
+    p.K = K;
+    p.alpha = (float)alpha;
+    p.beta = (float)beta;
+    p.C = C;
+    // Role choice of the reference (gemm.c:213-221): the smaller of M and N is the token side.
+    if (M <= N) {
+        p.Mc = M; p.Nc = N; p.a = A; p.w = B; p.scm = ldc; p.scn = 1;
+        p.sam = tA ? 1 : lda; p.sak = tA ? lda : 1;   // op(A)[m][k]
+        p.swn = tB ? ldb : 1; p.swk = tB ? 1 : ldb;   // op(B)[k][n]
+    } else {
+        p.Mc = N; p.Nc = M; p.a = B; p.w = A; p.scm = 1; p.scn = ldc;
+        p.sam = tB ? ldb : 1; p.sak = tB ? 1 : ldb;   // op(B)ᵀ[n][k]
+        p.swn = tA ? 1 : lda; p.swk = tA ? lda : 1;   // op(A)ᵀ[k][m]
+    }
+    if (p.swk != 1 && p.swn != 1) return fail(GEN9BLAS_ERR_INVALID_ARG, "skinny GEMM: weights have no contiguous dimension");
+    if (type == GEN9BLAS_S) return skinny_t<float>(p, st);
+    return skinny_t<__half>(p, st);
+}
+
+}  // namespace g9

@@ -1,0 +1,337 @@
+"""gen9blas -- NumPy module over libgen9blas.so, the B200 (sm_100a) build of gen9blas.
+
+    import numpy as np, gen9blas
+    C = gen9blas.hgemm(A, B)                      # float16, FP16 accumulation; accurate=True: FP32 accumulation
+    C = gen9blas.sgemm(A.T, B, alpha=2.0)         # float32; transposed views and row slices without a copy
+    C = gen9blas.gemm_batched(A3, B3)             # (count, M, K) · (count, K, N) -> (count, M, N)
+    X = gen9blas.empty((n, n), np.float16)        # managed memory: used in place by the GPU, writable by the CPU
+    gen9blas.axpy(0.5, x, y); d = gen9blas.dot(x, y); i = gen9blas.iamax(x)
+    y = gen9blas.gemv(A, x); gen9blas.ger(1.0, x, y, A)
+
+Same function names, argument meaning and error behaviour as the reference module lib/gen9blas.py of
+kprzybys/gen9-gpu-blas (gemm/hgemm/sgemm/gemm_batched 168-204, empty/free_pool 60-115, axpy..ger 335-419): the type
+follows the dtype, views map to leading dimensions and transpose flags (lib/gen9blas.py:316-328), errors raise
+RuntimeError with gen9blas_error(). Plain NumPy arrays are staged through device buffers by the library; arrays from
+gen9blas.empty() live in CUDA managed memory and are used in place.
+"""
+import ctypes
+import os
+import weakref
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.realpath(__file__))
+
+
+def _find(name):
+    p = os.path.join(_HERE, name)
+    return p if os.path.exists(p) else name
+
+
+_lib = ctypes.CDLL(os.environ.get("GEN9BLAS_LIB") or _find("libgen9blas.so"))
+_i, _f, _p, _l, _d = ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_int64, ctypes.c_double
+_lib.gen9blas_init.argtypes = []
+_lib.gen9blas_gemm.argtypes = [_i, _i, _i, _i, _i, _i, _d, _p, _i, _p, _i, _d, _p, _i]
+_lib.gen9blas_gemm_batched.argtypes = [_i, _i, _i, _i, _i, _i, _d, _p, _i, _l, _p, _i, _l, _d, _p, _i, _l, _i]
+_lib.gen9blas_last_time_ms.restype = ctypes.c_double
+_lib.gen9blas_alloc.argtypes = [ctypes.c_size_t]
+_lib.gen9blas_alloc.restype = ctypes.c_void_p
+_lib.gen9blas_free.argtypes = [ctypes.c_void_p]
+_lib.gen9blas_error.restype = ctypes.c_char_p
+_lib.gen9blas_axpy.argtypes = [_i, _i, _d, _p, _i, _p, _i]
+_lib.gen9blas_dot.argtypes = [_i, _i, _p, _i, _p, _i, ctypes.POINTER(_d)]
+_lib.gen9blas_asum.argtypes = [_i, _i, _p, _i, ctypes.POINTER(_d)]
+_lib.gen9blas_nrm2.argtypes = [_i, _i, _p, _i, ctypes.POINTER(_d)]
+_lib.gen9blas_iamax.argtypes = [_i, _i, _p, _i, ctypes.POINTER(_l)]
+_lib.gen9blas_gemv.argtypes = [_i, _i, _i, _i, _d, _p, _i, _p, _i, _d, _p, _i]
+_lib.gen9blas_ger.argtypes = [_i, _i, _i, _d, _p, _i, _p, _i, _p, _i]
+_lib.gen9blas_set_device.argtypes = [_i]
+_lib.gen9blas_set_stream.argtypes = [_p]
+_lib.gen9blas_set_nowait.argtypes = [_i]
+_lib.gen9blas_kernel_launches.restype = ctypes.c_longlong
+GEN9BLAS_H, GEN9BLAS_S, GEN9BLAS_HS, GEN9BLAS_D = 0, 1, 2, 3
+FEAT_FP16, FEAT_FP32, FEAT_FP64 = 0, 1, 2
+_lib.gen9blas_version.restype = ctypes.c_int
+if _lib.gen9blas_version() // 100 != 2:   # 0.2.x: the API this module is written for
+    raise ImportError(f"gen9blas.py expects libgen9blas 0.2.x, loaded {_lib.gen9blas_version()}")
+_ready = False
+
+
+def _init():
+    global _ready
+    if not _ready:
+        if _lib.gen9blas_init() != 0:
+            raise RuntimeError(_lib.gen9blas_error().decode())
+        _ready = True
+
+
+def _check(w):
+    if w != 0:
+        raise RuntimeError(_lib.gen9blas_error().decode())
+
+
+# Managed-memory pool: released blocks wait for the next gen9blas.empty of the same rounded size.
+_pool = {}
+_pool_bytes = 0
+POOL_MAX = 1 << 30
+
+
+def _block_size(n):
+    return max(4096, (n + 65535) // 65536 * 65536 if n > 65536 else (n + 4095) // 4096 * 4096)
+
+
+def _release(p, n):
+    global _pool_bytes
+    if _pool_bytes + n <= POOL_MAX:
+        _pool.setdefault(n, []).append(p)
+        _pool_bytes += n
+    else:
+        _lib.gen9blas_free(p)
+
+
+def free_pool():
+    """Returns the blocks waiting in the pool (arrays still in use stay allocated)."""
+    global _pool_bytes
+    for blocks in _pool.values():
+        for p in blocks:
+            _lib.gen9blas_free(p)
+    _pool.clear()
+    _pool_bytes = 0
+
+
+def empty(shape, dtype=np.float16):
+    """C-contiguous array in CUDA managed memory: the GPU uses it in place (views and slices too), the CPU reads and
+    writes it directly. When every view is gone the block returns to the pool (up to POOL_MAX bytes)."""
+    global _pool_bytes
+    _init()
+    dtype = np.dtype(dtype)
+    n = int(np.prod(shape)) * dtype.itemsize
+    nb = _block_size(n)
+    if _pool.get(nb):
+        p = _pool[nb].pop()
+        _pool_bytes -= nb
+    else:
+        p = _lib.gen9blas_alloc(nb)
+        if not p:
+            raise MemoryError(_lib.gen9blas_error().decode())
+    raw = (ctypes.c_char * nb).from_address(p)
+    f = weakref.finalize(raw, _release, p, nb)
+    f.atexit = False
+    return np.frombuffer(raw, dtype=np.uint8, count=n).view(dtype).reshape(shape)
+
+
+def available(dt, accurate=False):
+    """Whether the type can be used on this GPU."""
+    _init()
+    k = _kind(dt, accurate)
+    return bool(_lib.gen9blas_has(FEAT_FP32 if k == GEN9BLAS_S else FEAT_FP64 if k == GEN9BLAS_D else FEAT_FP16))
+
+
+def _kind(dt, accurate):
+    if np.dtype(dt) == np.float32:
+        return GEN9BLAS_S
+    if np.dtype(dt) == np.float64:
+        return GEN9BLAS_D
+    if np.dtype(dt) == np.float16:
+        return GEN9BLAS_HS if accurate else GEN9BLAS_H
+    raise TypeError("supported types: float16, float32, float64")
+
+
+def _mat(A, dt, write=False):
+    """(array, pointer, rows, columns, ld, trans) for a row-major matrix with a leading dimension; a transposed
+    view is used without a copy (trans = 1)."""
+    if A.ndim != 2:
+        raise ValueError("expected a 2-D matrix")
+    e = A.itemsize
+    if A.dtype == dt and A.strides[1] == e and A.strides[0] >= A.shape[1] * e and A.strides[0] % e == 0:
+        return A, A.ctypes.data, A.shape[0], A.shape[1], A.strides[0] // e, 0
+    if not write and A.dtype == dt and A.strides[0] == e and A.strides[1] >= A.shape[0] * e and A.strides[1] % e == 0:
+        return A, A.ctypes.data, A.shape[1], A.shape[0], A.strides[1] // e, 1
+    if write:
+        raise TypeError(f"the result must be a {np.dtype(dt).name} matrix with contiguous rows")
+    A = np.ascontiguousarray(A, dtype=dt)
+    return A, A.ctypes.data, A.shape[0], A.shape[1], A.shape[1], 0
+
+
+def _m3(X, dt, write=False):
+    X, p, _, _, ld, tr = _mat(X, dt, write)
+    return X, p, ld, tr
+
+
+def _c(X, dt):
+    return np.ascontiguousarray(X, dtype=dt)
+
+
+def _output(C, shape, dt):
+    """(C, given, ldc): a new C from gen9blas.empty or the supplied C with contiguous rows (any row stride)."""
+    if C is None:
+        return empty(shape, dt), False, shape[-1]
+    if C.shape != tuple(shape) or C.dtype != dt or C.strides[-1] != C.itemsize:
+        raise ValueError(f"C must have shape {tuple(shape)}, type {np.dtype(dt).name} and contiguous rows")
+    if C.ndim == 2:
+        return C, True, _mat(C, dt, True)[4]
+    if not C.flags.c_contiguous:
+        raise ValueError("C (batch) must be C-contiguous")
+    return C, True, shape[-1]
+
+
+def gemm(A, B, alpha=1.0, beta=0.0, C=None, accurate=False):
+    """C = alpha·A·B + beta·C (type from A: float16, float32 or float64)."""
+    _init()
+    dt = A.dtype if A.dtype in (np.float16, np.float32, np.float64) else np.float32
+    (M, K), (K2, N) = A.shape, B.shape
+    if K != K2:
+        raise ValueError(f"incompatible dimensions: {A.shape} · {B.shape}")
+    a, pa, lda, ta = _m3(A, dt)
+    b, pb, ldb, tb = _m3(B, dt)
+    C, given, ldc = _output(C, (M, N), dt)
+    _check(_lib.gen9blas_gemm(_kind(dt, accurate), ta, tb, M, N, K, alpha, pa, lda, pb, ldb,
+                              beta if given else 0.0, C.ctypes.data, ldc))
+    return C
+
+
+def hgemm(A, B, alpha=1.0, beta=0.0, C=None, accurate=False):
+    return gemm(A if A.dtype == np.float16 else A.astype(np.float16),
+                B if B.dtype == np.float16 else B.astype(np.float16), alpha, beta, C, accurate)
+
+
+def sgemm(A, B, alpha=1.0, beta=0.0, C=None):
+    return gemm(A if A.dtype == np.float32 else A.astype(np.float32),
+                B if B.dtype == np.float32 else B.astype(np.float32), alpha, beta, C)
+
+
+def dgemm(A, B, alpha=1.0, beta=0.0, C=None):
+    return gemm(A if A.dtype == np.float64 else A.astype(np.float64),
+                B if B.dtype == np.float64 else B.astype(np.float64), alpha, beta, C)
+
+
+def gemm_batched(A, B, alpha=1.0, beta=0.0, C=None, accurate=False):
+    """Batch: A (count, M, K), B (count, K, N) -> C (count, M, N), one kernel launch."""
+    _init()
+    dt = A.dtype if A.dtype in (np.float16, np.float32, np.float64) else np.float32
+    a, b = _c(A, dt), _c(B, dt)
+    (cnt, M, K), (cnt2, K2, N) = a.shape, b.shape
+    if K != K2 or cnt != cnt2:
+        raise ValueError(f"incompatible dimensions: {a.shape} · {b.shape}")
+    C, given, _ = _output(C, (cnt, M, N), dt)
+    _check(_lib.gen9blas_gemm_batched(_kind(dt, accurate), 0, 0, M, N, K, alpha, a.ctypes.data, K, M * K,
+                                      b.ctypes.data, N, K * N, beta if given else 0.0, C.ctypes.data, N, M * N, cnt))
+    return C
+
+
+def last_time_ms():
+    """GEN9BLAS_PROFILE=1: kernel time of the last call; otherwise the whole call."""
+    return _lib.gen9blas_last_time_ms()
+
+
+def last_zero_copy():
+    """Bits 1 = A, 2 = B, 4 = C used in place (device or managed memory) by the last call."""
+    return _lib.gen9blas_last_zero_copy()
+
+
+# ---------------- levels 1-2 ----------------
+
+def _dtype_of(*X):
+    """Compute type from the first array: float16, float64 or (anything else) float32."""
+    return np.float16 if X[0].dtype == np.float16 else np.float64 if X[0].dtype == np.float64 else np.float32
+
+
+def _vec(x, dt, write=False):
+    """(array, pointer to the lowest address, n, inc) of a 1-D vector; inc < 0 as in BLAS."""
+    if x.ndim != 1:
+        raise ValueError("expected a 1-D vector")
+    if x.dtype != dt or x.strides[0] % x.itemsize or x.strides[0] == 0:
+        if write:
+            raise TypeError(f"the result must be a {np.dtype(dt).name} vector with a stride that is a multiple of the "
+                            "element size")
+        x = np.ascontiguousarray(x, dtype=dt)
+    n, inc = x.shape[0], x.strides[0] // x.itemsize
+    return x, x.ctypes.data + (min(inc, 0) * (n - 1) * x.itemsize if n else 0), n, inc
+
+
+def _kind_basic(dt):
+    return GEN9BLAS_S if dt == np.float32 else GEN9BLAS_D if dt == np.float64 else GEN9BLAS_H
+
+
+def axpy(a, x, y):
+    """y = a·x + y (in place); returns y."""
+    _init()
+    t = _dtype_of(y)
+    y, py, n, iy = _vec(y, t, True)
+    x, px, nx, ix = _vec(x, t)
+    if nx != n:
+        raise ValueError("lengths differ")
+    _check(_lib.gen9blas_axpy(_kind_basic(t), n, a, px, ix, py, iy))
+    return y
+
+
+def dot(x, y):
+    _init()
+    t = _dtype_of(x)
+    x, px, n, ix = _vec(x, t)
+    y, py, ny, iy = _vec(y, t)
+    if ny != n:
+        raise ValueError("lengths differ")
+    w = _d()
+    _check(_lib.gen9blas_dot(_kind_basic(t), n, px, ix, py, iy, ctypes.byref(w)))
+    return w.value
+
+
+def asum(x):
+    _init()
+    t = _dtype_of(x)
+    x, px, n, ix = _vec(x, t)
+    w = _d()
+    _check(_lib.gen9blas_asum(_kind_basic(t), n, px, ix, ctypes.byref(w)))
+    return w.value
+
+
+def nrm2(x):
+    _init()
+    t = _dtype_of(x)
+    x, px, n, ix = _vec(x, t)
+    w = _d()
+    _check(_lib.gen9blas_nrm2(_kind_basic(t), n, px, ix, ctypes.byref(w)))
+    return w.value
+
+
+def iamax(x):
+    """Index (0-based) of the first largest |x|; -1 for an empty vector."""
+    _init()
+    t = _dtype_of(x)
+    x, px, n, ix = _vec(x, t)
+    w = _l()
+    _check(_lib.gen9blas_iamax(_kind_basic(t), n, px, ix, ctypes.byref(w)))
+    return w.value
+
+
+def gemv(A, x, alpha=1.0, beta=0.0, y=None, trans=False):
+    """y = alpha·op(A)·x + beta·y; without y a new array. An A.T view is used without a copy."""
+    _init()
+    t = _dtype_of(A)
+    A, pa, M, N, lda, tr = _mat(A, t)
+    tr ^= int(trans)
+    x, px, nx, ix = _vec(x, t)
+    ny = N if tr else M
+    if nx != (M if tr else N):
+        raise ValueError("length of x does not match A")
+    if y is None:
+        y, beta = empty((ny,), t), 0.0
+    y, py, n, iy = _vec(y, t, True)
+    if n != ny:
+        raise ValueError("length of y does not match A")
+    _check(_lib.gen9blas_gemv(_kind_basic(t), tr, M, N, alpha, pa, lda, px, ix, beta, py, iy))
+    return y
+
+
+def ger(alpha, x, y, A):
+    """A = alpha·x·yᵀ + A (in place); returns A."""
+    _init()
+    t = _dtype_of(A)
+    A, pa, M, N, lda, _ = _mat(A, t, True)
+    x, px, nx, ix = _vec(x, t)
+    y, py, ny, iy = _vec(y, t)
+    if nx != M or ny != N:
+        raise ValueError("lengths of x, y do not match A")
+    _check(_lib.gen9blas_ger(_kind_basic(t), M, N, alpha, px, ix, py, iy, pa, lda))
+    return A

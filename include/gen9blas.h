@@ -1,0 +1,175 @@
+/* gen9blas.h -- public C ABI of the B200 (sm_100a) build of gen9blas.
+ *
+ * This header is the drop-in boundary: every function, enum value and argument order below matches the interface
+ * of the reference library (lib/gen9blas.h of kprzybys/gen9-gpu-blas, version 0.2), so programs and bindings
+ * written against that library (ctypes module, CBLAS shim, Rust FFI) link against libgen9blas.so unchanged.
+ * Each declaration cites the reference line it replaces as "ref: lib/gen9blas.h:<line>".
+ *
+ * Conventions (same as the reference):
+ * - Matrices are row-major; element types are uint16_t (IEEE FP16), float or double, passed as void*.
+ *   Strides (lda, inc, sA...) are in elements.
+ * - Result codes: 0 success, < 0 an error (text in gen9blas_error()), GEN9BLAS_DECLINED = 1 "not handled, nothing
+ *   written". Functions returning a pointer return NULL on error; gen9blas_last_status() then holds the code.
+ * - Operands may live anywhere the CPU or the GPU can address: device memory (cudaMalloc, torch tensors) and
+ *   managed memory (gen9blas_alloc) are used in place; any other host pointer is staged through device work
+ *   buffers. Calls are synchronous unless gen9blas_set_nowait(1) is on and every operand is device-resident.
+ * - The library keeps process-wide state (work buffers, last error, current device). The caller serialises calls;
+ *   gen9blas_error() stays valid until the next call.
+ * - Vectors hold n elements spaced inc apart; inc != 0; a negative inc means the pointer is the lowest address
+ *   (element 0 is the last one in memory), as in reference BLAS.
+ */
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GEN9BLAS_VERSION_MAJOR 0
+#define GEN9BLAS_VERSION_MINOR 2
+#define GEN9BLAS_VERSION_PATCH 0
+#define GEN9BLAS_VERSION (GEN9BLAS_VERSION_MAJOR * 10000 + GEN9BLAS_VERSION_MINOR * 100 + GEN9BLAS_VERSION_PATCH)
+#ifndef GEN9BLAS_API
+#define GEN9BLAS_API __attribute__((visibility("default")))
+#endif
+
+/* Element / accumulation kinds (ref: lib/gen9blas.h:28-32). */
+enum { GEN9BLAS_H = 0,    /* FP16 in and out, FP16 accumulation (tcgen05 f16 accumulator in TMEM) */
+       GEN9BLAS_S = 1,    /* FP32 */
+       GEN9BLAS_HS = 2,   /* FP16 in and out, FP32 accumulation ("accurate") */
+       GEN9BLAS_D = 3 };  /* FP64 */
+#define GEN9BLAS_KC 32    /* chunk length of the reference's HS accumulation; the B200 HS accumulates all of K in FP32 */
+enum { GEN9BLAS_NO_TRANS = 0, GEN9BLAS_TRANS = 1 };   /* ref: lib/gen9blas.h:34 */
+enum { GEN9BLAS_LEFT = 0, GEN9BLAS_RIGHT = 1 };       /* ref: lib/gen9blas.h:35 */
+enum { GEN9BLAS_LOWER = 0, GEN9BLAS_UPPER = 1 };      /* ref: lib/gen9blas.h:36 */
+enum { GEN9BLAS_NON_UNIT = 0, GEN9BLAS_UNIT = 1 };    /* ref: lib/gen9blas.h:37 */
+
+/* Status codes (ref: lib/gen9blas.h:38-46). */
+typedef enum {
+    GEN9BLAS_OK = 0,
+    GEN9BLAS_DECLINED = 1,               /* not handled; nothing was written */
+    GEN9BLAS_ERR = -1,                   /* CUDA launch / execution error, device wait timeout */
+    GEN9BLAS_ERR_UNSUPPORTED = -2,       /* type or entry point not available in this build */
+    GEN9BLAS_ERR_INVALID_ARG = -3,       /* invalid arguments (leading dimension, increment 0, ...) */
+    GEN9BLAS_ERR_OUT_OF_MEMORY = -4,     /* device or host allocation failed */
+    GEN9BLAS_ERR_NO_DEVICE = -5,         /* initialisation failed: no usable sm_100 GPU (final for the process) */
+} gen9blas_status;
+
+/* ---- Library (ref: lib/gen9blas.h:48-78) ---- */
+GEN9BLAS_API int gen9blas_version(void);                 /* ref: lib/gen9blas.h:50 */
+GEN9BLAS_API int gen9blas_init(void);                    /* ref: lib/gen9blas.h:53; once per process, failure is final */
+GEN9BLAS_API int gen9blas_device_gen(void);              /* ref: lib/gen9blas.h:55; B200 build: 100 (sm_100), 0 = none */
+enum {
+    GEN9BLAS_FEAT_FP16 = 0,
+    GEN9BLAS_FEAT_FP32,
+    GEN9BLAS_FEAT_FP64,
+    GEN9BLAS_FEAT_SKINNY_PB,
+    GEN9BLAS_FEAT_EPILOG_EXT,
+    GEN9BLAS_FEAT_NORM_PACK,
+    GEN9BLAS_FEAT_ROPE_MULTI,
+    GEN9BLAS_FEAT_CPY,
+    GEN9BLAS_FEAT_SET_ROWS,
+};                                                        /* ref: lib/gen9blas.h:56-66 */
+GEN9BLAS_API int gen9blas_has(int feature);              /* ref: lib/gen9blas.h:68; 1 for FP16/FP32/FP64, else 0 */
+GEN9BLAS_API const char *gen9blas_error(void);           /* ref: lib/gen9blas.h:69 */
+GEN9BLAS_API int gen9blas_last_status(void);             /* ref: lib/gen9blas.h:70 */
+GEN9BLAS_API double gen9blas_last_time_ms(void);         /* ref: lib/gen9blas.h:71; GEN9BLAS_PROFILE=1: kernel time */
+GEN9BLAS_API int gen9blas_last_zero_copy(void);          /* ref: lib/gen9blas.h:72; bits 1 A, 2 B, 4 C used in place */
+/* Managed memory (cudaMallocManaged, 4096-byte aligned): CPU-writable and used in place by every kernel
+ * (ref: lib/gen9blas.h:76-78, USM host memory there). */
+GEN9BLAS_API void *gen9blas_alloc(size_t bytes);
+GEN9BLAS_API void gen9blas_free(void *p);
+GEN9BLAS_API int gen9blas_is_usm(const void *p, size_t bytes);  /* 1: [p, p+bytes) inside one gen9blas_alloc block */
+
+/* ---- Level 3 (ref: lib/gen9blas.h:80-117) ---- */
+/* C = alpha·op(A)·op(B) + beta·C; op(A) M×K (transA: A stored K×M), op(B) K×N (transB: B stored N×K).
+ * beta = 0: C is not read. ref: lib/gen9blas.h:82-83 */
+GEN9BLAS_API int gen9blas_gemm(int type, int transA, int transB, int M, int N, int K, double alpha, const void *A, int lda,
+                               const void *B, int ldb, double beta, void *C, int ldc);
+/* Strided batch: matrix b uses A + b·sA, B + b·sB, C + b·sC (elements). ref: lib/gen9blas.h:86-88 */
+GEN9BLAS_API int gen9blas_gemm_batched(int type, int transA, int transB, int M, int N, int K, double alpha,
+                                       const void *A, int lda, int64_t sA, const void *B, int ldb, int64_t sB,
+                                       double beta, void *C, int ldc, int64_t sC, int count);
+/* Constant packed weights (ref: lib/gen9blas.h:94-98): not built in this tier, return UNSUPPORTED / NULL. */
+typedef struct gen9blas_packed_b gen9blas_packed_b;
+GEN9BLAS_API gen9blas_packed_b *gen9blas_pack_b(int type, int transB, int K, int N, const void *B, int ldb);
+GEN9BLAS_API int gen9blas_gemm_pb(int transA, int M, double alpha, const void *A, int lda, const gen9blas_packed_b *Bp,
+                                  double beta, void *C, int ldc);
+GEN9BLAS_API void gen9blas_packed_b_free(gen9blas_packed_b *Bp);
+/* Level-3 derived operations (ref: lib/gen9blas.h:100-113): not built in this tier, return UNSUPPORTED. */
+GEN9BLAS_API int gen9blas_symm(int type, int side, int uplo, int M, int N, double alpha, const void *A, int lda,
+                               const void *B, int ldb, double beta, void *C, int ldc);
+GEN9BLAS_API int gen9blas_syrk(int type, int uplo, int trans, int N, int K, double alpha, const void *A, int lda,
+                               double beta, void *C, int ldc);
+GEN9BLAS_API int gen9blas_syr2k(int type, int uplo, int trans, int N, int K, double alpha, const void *A, int lda,
+                                const void *B, int ldb, double beta, void *C, int ldc);
+GEN9BLAS_API int gen9blas_trmm(int type, int side, int uplo, int transA, int diag, int M, int N, double alpha,
+                               const void *A, int lda, void *B, int ldb);
+GEN9BLAS_API int gen9blas_trsm(int type, int side, int uplo, int transA, int diag, int M, int N, double alpha,
+                               const void *A, int lda, void *B, int ldb);
+/* Shortcuts without transposes. ref: lib/gen9blas.h:114-117 */
+GEN9BLAS_API int gen9blas_hgemm(int M, int N, int K, double alpha, const uint16_t *A, int lda, const uint16_t *B, int ldb,
+                                double beta, uint16_t *C, int ldc);
+GEN9BLAS_API int gen9blas_sgemm(int M, int N, int K, double alpha, const float *A, int lda, const float *B, int ldb,
+                                double beta, float *C, int ldc);
+
+/* ---- Levels 1-2 (ref: lib/gen9blas.h:119-148). type: GEN9BLAS_S, _D or _H (_HS = _H). FP16 is computed in FP32,
+ * reductions accumulate in FP64. ---- */
+GEN9BLAS_API int gen9blas_axpy(int type, int n, double a, const void *x, int incx, void *y, int incy);   /* :121 */
+GEN9BLAS_API int gen9blas_scal(int type, int n, double a, void *x, int incx);                            /* :122 */
+GEN9BLAS_API int gen9blas_copy(int type, int n, const void *x, int incx, void *y, int incy);            /* :123 */
+GEN9BLAS_API int gen9blas_swap(int type, int n, void *x, int incx, void *y, int incy);                  /* :124 */
+GEN9BLAS_API int gen9blas_rot(int type, int n, void *x, int incx, void *y, int incy, double c, double s); /* :125 */
+GEN9BLAS_API int gen9blas_rotm(int type, int n, void *x, int incx, void *y, int incy, const double *param); /* :126 */
+GEN9BLAS_API void gen9blas_rotg(float *a, float *b, float *c, float *s);                                 /* :127 */
+GEN9BLAS_API void gen9blas_rotmg(float *d1, float *d2, float *x1, float y1, float *param);               /* :128 */
+GEN9BLAS_API int gen9blas_dot(int type, int n, const void *x, int incx, const void *y, int incy, double *result); /* :129 */
+GEN9BLAS_API int gen9blas_asum(int type, int n, const void *x, int incx, double *result);               /* :130 */
+GEN9BLAS_API int gen9blas_nrm2(int type, int n, const void *x, int incx, double *result);               /* :131 */
+GEN9BLAS_API int gen9blas_iamax(int type, int n, const void *x, int incx, int64_t *result);             /* :132 */
+/* y = alpha·op(A)·x + beta·y, A M×N (trans: x has length M, y length N); beta = 0: y not read. :133-135 */
+GEN9BLAS_API int gen9blas_gemv(int type, int trans, int M, int N, double alpha, const void *A, int lda, const void *x, int incx,
+                               double beta, void *y, int incy);
+GEN9BLAS_API int gen9blas_symv(int type, int uplo, int n, double alpha, const void *A, int lda, const void *x, int incx,
+                               double beta, void *y, int incy);                                           /* :137 */
+GEN9BLAS_API int gen9blas_trmv(int type, int uplo, int trans, int diag, int n, const void *A, int lda, void *x, int incx);
+GEN9BLAS_API int gen9blas_trsv(int type, int uplo, int trans, int diag, int n, const void *A, int lda, void *x, int incx);
+GEN9BLAS_API int gen9blas_syr(int type, int uplo, int n, double alpha, const void *x, int incx, void *A, int lda);
+GEN9BLAS_API int gen9blas_syr2(int type, int uplo, int n, double alpha, const void *x, int incx, const void *y, int incy,
+                               void *A, int lda);
+/* A = alpha·x·yᵀ + A, A M×N. ref: lib/gen9blas.h:147-148 */
+GEN9BLAS_API int gen9blas_ger(int type, int M, int N, double alpha, const void *x, int incx, const void *y, int incy,
+                              void *A, int lda);
+/* Banded and packed level 2 (ref: lib/gen9blas.h:150-168): not built in this tier, return UNSUPPORTED. */
+GEN9BLAS_API int gen9blas_gbmv(int type, int trans, int M, int N, int KL, int KU, double alpha, const void *A, int lda,
+                               const void *x, int incx, double beta, void *y, int incy);
+GEN9BLAS_API int gen9blas_sbmv(int type, int uplo, int N, int K, double alpha, const void *A, int lda, const void *x, int incx,
+                               double beta, void *y, int incy);
+GEN9BLAS_API int gen9blas_tbmv(int type, int uplo, int trans, int diag, int N, int K, const void *A, int lda, void *x, int incx);
+GEN9BLAS_API int gen9blas_tbsv(int type, int uplo, int trans, int diag, int N, int K, const void *A, int lda, void *x, int incx);
+GEN9BLAS_API int gen9blas_spmv(int type, int uplo, int N, double alpha, const void *Ap, const void *x, int incx, double beta,
+                               void *y, int incy);
+GEN9BLAS_API int gen9blas_tpmv(int type, int uplo, int trans, int diag, int N, const void *Ap, void *x, int incx);
+GEN9BLAS_API int gen9blas_tpsv(int type, int uplo, int trans, int diag, int N, const void *Ap, void *x, int incx);
+GEN9BLAS_API int gen9blas_spr(int type, int uplo, int N, double alpha, const void *x, int incx, void *Ap);
+GEN9BLAS_API int gen9blas_spr2(int type, int uplo, int N, double alpha, const void *x, int incx, const void *y, int incy,
+                               void *Ap);
+
+/* ---- Additions of the B200 build (no counterpart in lib/gen9blas.h; the reference is single-device) ---- */
+/* Selects the CUDA device used by later calls (one process per GPU: call once after start-up). Default: the device
+ * current when gen9blas_init ran. Returns 0 or GEN9BLAS_ERR_INVALID_ARG. */
+GEN9BLAS_API int gen9blas_set_device(int device);
+GEN9BLAS_API int gen9blas_get_device(void);
+/* Launches later calls on the given cudaStream_t (NULL: the library's own non-blocking stream of the device). */
+GEN9BLAS_API int gen9blas_set_stream(void *cuda_stream);
+/* No-wait mode (same names and meaning as lib/gen9blas_ml.h:61,69 of the reference): while on, a call whose operands
+ * are all device-resident returns right after its kernels are queued; results are ready after gen9blas_flush()
+ * (or any synchronisation of the stream). Calls with host operands still wait. */
+GEN9BLAS_API void gen9blas_set_nowait(int on);
+GEN9BLAS_API int gen9blas_flush(void);
+/* Number of kernels this library launched since the process started (launch accounting for benchmarks). */
+GEN9BLAS_API long long gen9blas_kernel_launches(void);
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,66 @@
+"""CPU checks of the drop-in boundary: libgen9blas.so loads without a GPU, exports every function that
+include/gen9blas.h declares (the reference's lib/gen9blas.h set plus the B200 additions), keeps the 0.2.x version
+gate of the NumPy module, and fails initialisation cleanly (GEN9BLAS_ERR_NO_DEVICE) where there is no GPU."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from conftest import PKG, ROOT
+
+HEADER = os.path.join(ROOT, "include", "gen9blas.h")
+LIB = os.path.join(PKG, "libgen9blas.so")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"GEN9BLAS_API\s+[^;(]*?\b(gen9blas_\w+)\s*\(", text)))
+
+
+def exported(path):
+    out = subprocess.run(["nm", "-D", "--defined-only", path], capture_output=True, text=True, check=True).stdout
+    return {line.split()[-1] for line in out.splitlines() if " T " in line}
+
+
+def test_header_declares_reference_surface():
+    names = declared_functions()
+    # the 51 entry points of the reference's lib/gen9blas.h plus the additions of this build
+    for must in ("gen9blas_gemm", "gen9blas_gemm_batched", "gen9blas_hgemm", "gen9blas_sgemm", "gen9blas_axpy",
+                 "gen9blas_dot", "gen9blas_nrm2", "gen9blas_asum", "gen9blas_iamax", "gen9blas_gemv", "gen9blas_ger",
+                 "gen9blas_init", "gen9blas_error", "gen9blas_alloc", "gen9blas_spr2", "gen9blas_set_device"):
+        assert must in names
+    assert len(names) == 57
+
+
+def test_library_exports_every_declared_function():
+    syms = exported(LIB)
+    missing = [n for n in declared_functions() if n not in syms]
+    assert not missing, missing
+    # nothing else leaks: hidden visibility for the internals
+    extra = sorted(s for s in syms if not s.startswith("gen9blas_"))
+    assert not extra, extra[:10]
+
+
+def test_version_gate(lib):
+    assert lib.version() // 100 == 2   # lib/gen9blas.py:48-49 accepts 0.2.x
+
+
+def test_only_sm100a_code_in_library():
+    out = subprocess.run(["/usr/local/cuda/bin/cuobjdump", "--list-elf", LIB], capture_output=True, text=True)
+    if out.returncode != 0:
+        pytest.skip("cuobjdump unavailable")
+    arches = set(re.findall(r"sm_(\d+a?)", out.stdout))
+    assert arches == {"100a"}, arches
+
+
+def test_init_without_gpu_is_clean(lib):
+    if lib.init() == 0:
+        pytest.skip("a GPU is present")
+    assert lib.init() == -5                       # GEN9BLAS_ERR_NO_DEVICE, final for the process
+    assert lib.last_status() == -5
+    assert lib.error()                            # an explanation is set
+    assert lib.has(0) == 0 and lib.device_gen() == 0
+    x = (ctypes.c_float * 4)()
+    assert lib.axpy(1, 4, 1.0, ctypes.addressof(x), 1, ctypes.addressof(x), 1) == -5

@@ -1,0 +1,168 @@
+"""GPU parity of dense GEMM (tcgen05 HGEMM fast/accurate, FFMA SGEMM, FP64 DGEMM) with the cases and error metric of
+the reference's lib/test_basic.py:4-79 (sizes, alpha/beta, all four transposes, managed vs plain unaligned memory),
+lib/test_level3.py:48-53 (batched) and lib/test_long_launch.py (large sizes, sampled rows), against FP64 NumPy on the
+same FP16/FP32/FP64-rounded inputs and against the CPU oracle."""
+import ctypes
+
+import numpy as np
+import pytest
+
+import abi
+from conftest import gemm_error
+
+pytestmark = pytest.mark.gpu
+
+# (name, dtype, accurate, mean limit, max limit): reference limits (test_basic.py:5-8, test_level3.py:5) with the
+# maximum tightened to the build's targets (HGEMM fast 1e-3).
+KINDS = [("hgemm", np.float16, False, 4.9e-4, 1e-3), ("hgemm acc.", np.float16, True, 4.9e-4, 1e-3),
+         ("sgemm", np.float32, False, 1e-6, 1e-5), ("dgemm", np.float64, False, 1e-14, 1e-13)]
+SIZES = [(1, 1, 1, 1, 0), (17, 33, 15, 1, 0), (100, 70, 300, 2.0, 0), (64, 96, 48, 0.5, 1.0),
+         (333, 129, 1000, 1, -1.0), (1000, 1024, 777, 1, 0.5)]
+
+
+def new_array(g9, shape, dt, zc):
+    """zc=1: gen9blas.empty (managed memory, used in place); zc=0: plain NumPy array, deliberately unaligned."""
+    if zc:
+        return g9.empty(shape, dt)
+    t = np.zeros(shape[0] * shape[1] + 64, dt)
+    off = 32 if (t.ctypes.data % 4096) == 0 else 0
+    return t[off:off + shape[0] * shape[1]].reshape(shape)
+
+
+def case(g9, dt, accurate, M, N, K, al, be, ta, tb, zc, seed=0):
+    rng = np.random.default_rng(seed)
+    a = new_array(g9, (K, M) if ta else (M, K), dt, zc)
+    a[...] = rng.uniform(-1, 1, a.shape)
+    b = new_array(g9, (N, K) if tb else (K, N), dt, zc)
+    b[...] = rng.uniform(-1, 1, b.shape)
+    A, B = (a.T if ta else a), (b.T if tb else b)
+    C0 = rng.uniform(-1, 1, (M, N)).astype(dt)
+    C = new_array(g9, (M, N), dt, zc)
+    C[...] = C0 if be else 0
+    W = g9.gemm(A, B, al, be, C, accurate=accurate)
+    a64, b64 = A.astype(np.float64), B.astype(np.float64)
+    ref = al * a64 @ b64 + (be * C0.astype(np.float64) if be else 0)
+    scale = abs(al) * np.abs(a64) @ np.abs(b64) + (abs(be) * np.abs(C0.astype(np.float64)) if be else 0)
+    return gemm_error(W, ref, scale) + (g9.last_zero_copy(),)
+
+
+@pytest.mark.parametrize("name,dt,accurate,tol_avg,tol_max", KINDS)
+def test_reference_cases(g9, name, dt, accurate, tol_avg, tol_max):
+    worst = []
+    for (M, N, K, al, be) in SIZES:
+        for ta, tb in [(0, 0), (1, 0), (0, 1), (1, 1)]:
+            for zc in (0, 1):
+                avg, mx, z = case(g9, dt, accurate, M, N, K, al, be, ta, tb, zc)
+                if accurate and K >= 256:
+                    ok = avg <= 1e-4 and mx <= 1e-3
+                else:
+                    ok = avg <= tol_avg and mx <= tol_max
+                assert ok, f"{name} M={M} N={N} K={K} a={al} b={be} tA={ta} tB={tb} zc={zc}: avg {avg:.2e} max {mx:.2e}"
+                assert z == (7 if zc else 0), z
+                worst.append(mx)
+    print(f"{name}: worst max error {max(worst):.2e}")
+
+
+@pytest.mark.parametrize("t,dt", [(abi.S, np.float32), (abi.D, np.float64)])
+def test_close_to_oracle(gpu_lib, oracle, t, dt):
+    """FP32/FP64 results next to the oracle's FMA chain (same products, different summation order)."""
+    rng = np.random.default_rng(5)
+    for (M, N, K, ta, tb) in ((131, 67, 200, 0, 0), (64, 160, 33, 1, 1), (250, 130, 129, 0, 1)):
+        A = rng.uniform(-1, 1, (K, M) if ta else (M, K)).astype(dt)
+        B = rng.uniform(-1, 1, (N, K) if tb else (K, N)).astype(dt)
+        C0 = rng.uniform(-1, 1, (M, N)).astype(dt)
+        Cg, Co = C0.copy(), C0.copy()
+        args = (t, ta, tb, M, N, K, 0.75, A.ctypes.data, A.shape[1], B.ctypes.data, B.shape[1], -0.5)
+        assert gpu_lib.gemm(*args, Cg.ctypes.data, N) == 0
+        assert oracle.gemm(*args, Co.ctypes.data, N) == 0
+        a64 = (A.T if ta else A).astype(np.float64)
+        b64 = (B.T if tb else B).astype(np.float64)
+        scale = 0.75 * np.abs(a64) @ np.abs(b64) + 0.5 * np.abs(C0.astype(np.float64))
+        assert (np.abs(Cg.astype(np.float64) - Co) / scale).max() <= (2e-6 if t == abi.S else 2e-13)
+
+
+@pytest.mark.parametrize("t,dt", [(abi.H, np.float16), (abi.HS, np.float16), (abi.S, np.float32), (abi.D, np.float64)])
+def test_beta_zero_ignores_c_and_slice_untouched(gpu_lib, t, dt):
+    """beta = 0 never reads C (NaN there stays out of the result, sgemm.cl:196 / level12.cl:280 semantics), and a C
+    that is a slice of a larger array leaves everything outside the slice unchanged."""
+    rng = np.random.default_rng(9)
+    for (M, N, K) in ((5, 300, 70), (200, 300, 64), (129, 257, 40)):
+        A = rng.uniform(-1, 1, (M, K)).astype(dt)
+        B = rng.uniform(-1, 1, (K, N)).astype(dt)
+        big = np.full((M + 3, N + 11), np.nan, dt)
+        C = big[1:M + 1, 3:N + 3]
+        outside = np.ones(big.shape, bool)
+        outside[1:M + 1, 3:N + 3] = False
+        assert gpu_lib.gemm(t, 0, 0, M, N, K, 1.0, A.ctypes.data, K, B.ctypes.data, N, 0.0,
+                            C.ctypes.data, big.shape[1]) == 0
+        assert np.isfinite(C).all()
+        assert np.isnan(big[outside]).all()
+        ref = A.astype(np.float64) @ B.astype(np.float64)
+        scale = np.abs(A.astype(np.float64)) @ np.abs(B.astype(np.float64))
+        assert gemm_error(C, ref, scale)[1] <= (1e-3 if dt == np.float16 else 1e-5)
+
+
+@pytest.mark.parametrize("name,dt,accurate,tol_avg,tol_max", KINDS)
+def test_batched(g9, name, dt, accurate, tol_avg, tol_max):
+    rng = np.random.default_rng(3)
+    for cnt, M, N, K in ((1, 96, 112, 80), (7, 64, 40, 100), (33, 17, 33, 65)):
+        A = rng.uniform(-1, 1, (cnt, M, K)).astype(dt)
+        B = rng.uniform(-1, 1, (cnt, K, N)).astype(dt)
+        C0 = rng.uniform(-1, 1, (cnt, M, N)).astype(dt)
+        C = C0.copy()
+        g9.gemm_batched(A, B, 1.5, 0.5, C, accurate=accurate)
+        a64, b64, c64 = A.astype(np.float64), B.astype(np.float64), C0.astype(np.float64)
+        ref = 1.5 * a64 @ b64 + 0.5 * c64
+        scale = 1.5 * np.abs(a64) @ np.abs(b64) + 0.5 * np.abs(c64)
+        avg, mx = gemm_error(C, ref, scale)
+        assert avg <= tol_avg and mx <= tol_max, (name, cnt, avg, mx)
+
+
+def test_hgemm_unaligned_leading_dimensions(gpu_lib):
+    """Leading dimensions that are not multiples of 8 FP16 elements (TMA needs 16-byte pitches): repack path."""
+    rng = np.random.default_rng(4)
+    for t in (abi.H, abi.HS):
+        for (M, N, K, lda, ldb, ldc, ta, tb) in ((70, 90, 45, 47, 93, 91, 0, 0), (33, 40, 17, 35, 19, 41, 1, 1),
+                                                  (129, 257, 65, 67, 261, 259, 0, 1)):
+            A = rng.uniform(-1, 1, ((K if ta else M), lda)).astype(np.float16)
+            B = rng.uniform(-1, 1, ((N if tb else K), ldb)).astype(np.float16)
+            C = np.zeros((M, ldc), np.float16)
+            assert gpu_lib.gemm(t, ta, tb, M, N, K, 1.0, A.ctypes.data, lda, B.ctypes.data, ldb, 0.0,
+                                C.ctypes.data, ldc) == 0
+            a64 = (A[:, :M].T if ta else A[:, :K]).astype(np.float64)
+            b64 = (B[:, :K].T if tb else B[:, :N]).astype(np.float64)
+            ref = a64 @ b64
+            avg, mx = gemm_error(C[:, :N], ref, np.abs(a64) @ np.abs(b64))
+            assert mx <= 1e-3, (t, M, N, K, mx)
+            assert not C[:, N:].any()
+
+
+@pytest.mark.parametrize("accurate,limit", [(False, 1e-3), (True, 1e-4)])
+def test_hgemm_headline_config(g9, accurate, limit):
+    """n = 4096, A, B iid N(0,1)/sqrt(n) in FP16, C = A·B; north-star limits on the max error
+    (fast 1e-3, accurate 1e-4), checked on 256 sampled rows against FP64."""
+    n = 4096
+    rng = np.random.default_rng(1)
+    A = (rng.standard_normal((n, n)) / np.sqrt(n)).astype(np.float16)
+    B = (rng.standard_normal((n, n)) / np.sqrt(n)).astype(np.float16)
+    C = g9.hgemm(A, B, accurate=accurate)
+    rows = rng.choice(n, 256, replace=False)
+    a64, b64 = A[rows].astype(np.float64), B.astype(np.float64)
+    avg, mx = gemm_error(C[rows], a64 @ b64, np.abs(a64) @ np.abs(b64))
+    print(f"hgemm n=4096 accurate={accurate}: mean {avg:.2e} max {mx:.2e}")
+    assert mx <= limit
+
+
+@pytest.mark.parametrize("name,dt,accurate,tol_avg,tol_max", KINDS)
+def test_large_sampled_rows(g9, name, dt, accurate, tol_avg, tol_max):
+    """Long launches (lib/test_long_launch.py): n = 8192 (FP64: 4096), rows sampled against FP64."""
+    n = 4096 if dt == np.float64 else 8192
+    rng = np.random.default_rng(2)
+    A = rng.uniform(-1, 1, (n, n)).astype(dt)
+    B = rng.uniform(-1, 1, (n, n)).astype(dt)
+    C = g9.gemm(A, B, accurate=accurate)
+    rows = rng.choice(n, 64, replace=False)
+    a64, b64 = A[rows].astype(np.float64), B.astype(np.float64)
+    avg, mx = gemm_error(C[rows], a64 @ b64, np.abs(a64) @ np.abs(b64))
+    lim_max = 1e-3 if dt == np.float16 else tol_max
+    assert mx <= lim_max and avg <= (1e-4 if accurate else tol_avg), (name, avg, mx)

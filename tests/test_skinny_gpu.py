@@ -1,0 +1,57 @@
+"""GPU parity of the skinny GEMM (min(M, N) <= 16): the cases of the reference's lib/test_skinny.py:43-63 (both weight
+layouts, transposes, small-N role swap, alpha/beta with C as a slice, M around the tiles, K tails) with its error
+metric max|C − ref| / max|ref| (4e-3 FP16, 2e-6 FP32), plus the 7B decoder shapes of BASELINE configs[2]."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+TOL = {np.float16: 4e-3, np.float32: 2e-6}
+rng = np.random.default_rng(7)
+
+
+def tab(g9, shape, dt, usm):
+    X = g9.empty(shape, dt) if usm else np.empty(shape, dt)
+    X[...] = rng.uniform(-1, 1, shape).astype(dt)
+    return X
+
+
+def err(result, ref):
+    return float(np.max(np.abs(result.astype(np.float64) - ref)) / max(1e-30, np.max(np.abs(ref))))
+
+
+@pytest.mark.parametrize("dt", [np.float16, np.float32])
+@pytest.mark.parametrize("usm", [True, False])
+def test_reference_skinny_cases(g9, dt, usm):
+    fn = g9.hgemm if dt == np.float16 else g9.sgemm
+    for M, N, K in [(1, 1000, 777), (3, 517, 1029), (4, 2048, 128), (5, 64, 9), (8, 333, 4096), (9, 1500, 1500),
+                    (16, 4096, 1000), (17, 130, 257), (1, 8, 3), (2, 7, 2000), (16, 16, 16)]:
+        for tA in (False, True):
+            for tB in (False, True):
+                A = tab(g9, (K, M), dt, usm).T if tA else tab(g9, (M, K), dt, usm)
+                B = tab(g9, (N, K), dt, usm).T if tB else tab(g9, (K, N), dt, usm)
+                Ad, Bd = A.astype(np.float64), B.astype(np.float64)
+                desc = f"M={M} N={N} K={K} tA={tA} tB={tB}"
+                assert err(fn(A, B), Ad @ Bd) <= TOL[dt], desc
+                assert err(fn(B.T, A.T), Bd.T @ Ad.T) <= TOL[dt], desc + " (small N)"
+        A = tab(g9, (M, K), dt, usm)
+        W = tab(g9, (N, K), dt, usm)
+        big = tab(g9, (M + 2, N + 5), dt, usm)
+        C = big[1:M + 1, 2:N + 2]
+        C0 = C.astype(np.float64)
+        D0 = big.copy()
+        fn(A, W.T, alpha=0.75, beta=-1.5, C=C)
+        assert err(C, 0.75 * A.astype(np.float64) @ W.astype(np.float64).T - 1.5 * C0) <= TOL[dt]
+        mask = np.ones(big.shape, bool)
+        mask[1:M + 1, 2:N + 2] = False
+        assert np.array_equal(big[mask], D0[mask]), "change outside the slice of C"
+
+
+@pytest.mark.parametrize("M", [1, 2, 4, 8, 16])
+def test_decoder_shapes(g9, M):
+    """W FP16 N(0,0.02) of the 7B shapes, A FP16 N(0,1); C = A·Wᵀ."""
+    for N, K in ((4096, 4096), (12288, 4096), (11008, 4096), (4096, 11008)):
+        W = (rng.standard_normal((N, K)) * 0.02).astype(np.float16)
+        A = rng.standard_normal((M, K)).astype(np.float16)
+        C = g9.hgemm(A, W.T)
+        ref = A.astype(np.float64) @ W.astype(np.float64).T
+        assert err(C, ref) <= 4e-3, (M, N, K)
