@@ -1,0 +1,422 @@
+"""bench.py -- headline benchmark of the B200 gen9blas hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload auto|hgemm4096|scaleout]
+
+Workloads:
+- hgemm4096 (default at N = 1, configs[1]): HGEMM FP16 n = 4096, row-major, A, B iid N(0,1)/sqrt(n), C = A·B with
+  FP16 accumulation (GEN9BLAS_H); one step = one gen9blas_gemm call. The FP32-accumulate mode (GEN9BLAS_HS) is timed
+  the same way and reported under "modes".
+- scaleout (default at N > 1, configs[4]): HGEMM n = 32768 with B and C column-sharded over the N ranks, A
+  replicated, C all-gathered over NVLink (NCCL); one step = local GEMM of the rank's column block + all-gather +
+  re-layout into the row-major C. Strong scaling (total work fixed).
+value: whole-job TFLOP/s from CUDA events on the launching stream (max over ranks), inputs resident in HBM, buffer
+sets rotated so that the inputs of consecutive steps exceed L2. e2e: the same metric through the public C ABI with
+pinned host buffers (host->device copies of A and B and the device->host copy of C inside the timed region).
+--impl reference: the reference's own CPU path (its CBLAS layer lib/src/cblas.c in CPU mode over OpenBLAS, built by
+oracle/Makefile into oracle/_ref/) on the same config: cblas_sgemm on the FP16 inputs converted to FP32 (OpenBLAS has
+no FP16 GEMM), all host threads.
+"""
+import argparse
+import ctypes
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "gen9-gpu-blas_b200")
+METRIC = "HGEMM/SGEMM/DGEMM TFLOPS at n=4096/8192; skinny GEMM µs & HBM GB/s at M=1..16"
+OPENBLAS_DIR = "/opt/prime-rl/.venv/lib/python3.12/site-packages/opencv_python_headless.libs"
+OPENBLAS = os.path.join(OPENBLAS_DIR, "libopenblasp-r0-59ffcd50.3.15.so")
+H, S, HS, D = 0, 1, 2, 3
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=0)
+    ap.add_argument("--warmup", type=int, default=0)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="auto", choices=["auto", "hgemm4096", "scaleout"])
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) measurement")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample (profiling runs)")
+    return ap.parse_args()
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+# --------------------------------------------------------------------------------------------- clocks during the run
+class ClockSampler:
+    """nvidia-smi samples (every 100 ms) of one GPU while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS,
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            p = [x.strip() for x in ln.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx = float(p[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, p[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        loaded = [v for v in sm if mx and v > 0.3 * mx] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------------------------- reference CPU path
+def load_reference_cblas():
+    """The reference's CBLAS layer in CPU mode (oracle/_ref) over OpenBLAS; None if it was not built here."""
+    so = os.path.join(ROOT, "oracle", "_ref", "libgen9blas_blas_ref.so")
+    if not os.path.exists(so) or not os.path.exists(OPENBLAS):
+        return None, "port"
+    os.environ["GEN9BLAS_BLAS"] = "cpu"
+    os.environ["GEN9BLAS_BLAS_CPU"] = OPENBLAS
+    os.environ.setdefault("OPENBLAS_NUM_THREADS", str(os.cpu_count()))
+    for dep in ("libquadmath-2284e583.so.0.0.0", "libgfortran-83c28eba.so.5.0.0"):
+        ctypes.CDLL(os.path.join(OPENBLAS_DIR, dep), mode=ctypes.RTLD_GLOBAL)
+    L = ctypes.CDLL(so)
+    L.cblas_sgemm.argtypes = [ctypes.c_int] * 6 + [ctypes.c_float, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
+                                                   ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_int]
+    return L, "reference"
+
+
+def cpu_sgemm_sample(n, max_seconds=20.0, min_calls=2, max_calls=5):
+    """Times cblas_sgemm(RowMajor, n³) of the reference layer on FP32-converted FP16 inputs (the HGEMM stand-in):
+    one untimed call, then calls until max_seconds or max_calls. Returns (TFLOP/s best, kind, calls, threads)."""
+    L, kind = load_reference_cblas()
+    rng = np.random.default_rng(1)
+    A = (rng.standard_normal((n, n)) / np.sqrt(n)).astype(np.float16).astype(np.float32)
+    B = (rng.standard_normal((n, n)) / np.sqrt(n)).astype(np.float16).astype(np.float32)
+    C = np.empty((n, n), np.float32)
+    threads = int(os.environ.get("OPENBLAS_NUM_THREADS", os.cpu_count()))
+    if L is None:   # oracle port: the naive restatement is too slow for n³, time a row block and scale
+        sys.path.insert(0, os.path.join(ROOT, "tests"))
+        import abi
+        subprocess.run(["make", "-C", os.path.join(ROOT, "oracle"), "all"], check=True, capture_output=True)
+        O = abi.bind(ctypes.CDLL(os.path.join(ROOT, "oracle", "liboracle.so")), "oracle_")
+        rows = 16
+        t0 = time.perf_counter()
+        O.gemm(S, 0, 0, rows, n, n, 1.0, A.ctypes.data, n, B.ctypes.data, n, 0.0, C.ctypes.data, n)
+        dt = time.perf_counter() - t0
+        return 2.0 * rows * n * n / dt / 1e12, "port", 1, 1, f"{rows} rows of the n={n} product with the scalar oracle"
+
+    def call():
+        L.cblas_sgemm(101, 111, 111, n, n, n, 1.0, A.ctypes.data, n, B.ctypes.data, n, 0.0, C.ctypes.data, n)
+
+    call()
+    times, t_start = [], time.perf_counter()
+    while len(times) < max_calls and (len(times) < min_calls or time.perf_counter() - t_start < max_seconds):
+        t0 = time.perf_counter()
+        call()
+        times.append(time.perf_counter() - t0)
+    return (2.0 * n ** 3 / min(times) / 1e12, kind, len(times), threads,
+            f"{len(times)} cblas_sgemm calls n={n} (FP32 stand-in for FP16), best of them")
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    n = 4096
+    steps = args.steps or 3
+    warm = args.warmup or 1
+    L, kind = load_reference_cblas()
+    rng = np.random.default_rng(1)
+    A = (rng.standard_normal((n, n)) / np.sqrt(n)).astype(np.float16).astype(np.float32)
+    B = (rng.standard_normal((n, n)) / np.sqrt(n)).astype(np.float16).astype(np.float32)
+    C = np.empty((n, n), np.float32)
+    threads = int(os.environ.get("OPENBLAS_NUM_THREADS", os.cpu_count()))
+    if L is None:
+        v, kind, calls, threads, sample = cpu_sgemm_sample(n)
+        ms = 2.0 * n ** 3 / (v * 1e12) * 1e3
+    else:
+        for _ in range(warm):
+            L.cblas_sgemm(101, 111, 111, n, n, n, 1.0, A.ctypes.data, n, B.ctypes.data, n, 0.0, C.ctypes.data, n)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            L.cblas_sgemm(101, 111, 111, n, n, n, 1.0, A.ctypes.data, n, B.ctypes.data, n, 0.0, C.ctypes.data, n)
+        ms = (time.perf_counter() - t0) / steps * 1e3
+        v = 2.0 * n ** 3 / (ms * 1e-3) / 1e12
+        sample = f"{steps} timed cblas_sgemm calls n={n} after {warm} warm-up (FP32 stand-in for FP16)"
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "TFLOP/s", "n_gpus": args.gpus,
+            "steps": steps, "warmup": warm, "ms_per_step": round(ms, 3), "higher_is_better": True,
+            "scaling": "strong" if args.gpus > 1 else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "hgemm4096: reference CBLAS layer (lib/src/cblas.c, CPU mode) -> OpenBLAS "
+                                   "cblas_sgemm, n=4096 row-major, FP16 N(0,1)/sqrt(n) inputs converted to FP32",
+                       "n": n},
+            "cpu_baseline": {"value": round(v, 4), "unit": "TFLOP/s", "cores": threads, "kind": kind,
+                             "sample": sample},
+            "e2e": {"value": round(v, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------------------------------- our path
+def load_lib():
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import abi
+    path = os.path.join(PKG, "libgen9blas.so")
+    if not os.path.exists(path):
+        raise SystemExit("libgen9blas.so is not built (run __graft_entry__.build())")
+    L = abi.bind(ctypes.CDLL(path), "gen9blas_")
+    if L.init() != 0:
+        raise SystemExit("gen9blas_init failed: " + L.error().decode())
+    return L
+
+
+def profile_traffic(name):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary (profiles/<name>.txt)."""
+    p = os.path.join(ROOT, "profiles", name + ".txt")
+    if not os.path.exists(p):
+        return None
+    m = re.search(r"traffic_bytes_per_launch\s*[=:]\s*([0-9.eE+]+)", open(p).read())
+    return float(m.group(1)) if m else None
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("bf16_tflops"), d.get("hbm_gbs"), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def run_ours(args):
+    import torch
+    rank, world, local = dist_env()
+    workload = args.workload if args.workload != "auto" else ("hgemm4096" if world == 1 else "scaleout")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    L = load_lib()
+    assert L.set_device(local) == 0, L.error()
+    stream = torch.cuda.Stream()
+    assert L.set_stream(ctypes.c_void_p(stream.cuda_stream)) == 0
+    L.set_nowait(1)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+            torch.cuda.synchronize()
+
+    rng = torch.Generator(device="cuda")
+    rng.manual_seed(1 + rank)
+    if workload == "hgemm4096":
+        n = 4096
+        steps = args.steps or 4000
+        warm = max(args.warmup or 20, 3)
+        sets = 4   # 4 × (A, B, C) × 32 MiB = 384 MiB > 126 MB L2: each step reads inputs that are not L2-resident
+        A = [torch.randn(n, n, device="cuda", generator=rng).div_(n ** 0.5).half() for _ in range(sets)]
+        B = [torch.randn(n, n, device="cuda", generator=rng).div_(n ** 0.5).half() for _ in range(sets)]
+        C = [torch.empty(n, n, device="cuda", dtype=torch.float16) for _ in range(sets)]
+        flops = 2.0 * n ** 3
+
+        def step(i, kind=H):
+            j = i % sets
+            r = L.gemm(kind, 0, 0, n, n, n, 1.0, A[j].data_ptr(), n, B[j].data_ptr(), n, 0.0, C[j].data_ptr(), n)
+            if r:
+                raise RuntimeError(L.error().decode())
+
+        def timed(kind, k, w):
+            with torch.cuda.stream(stream):
+                for i in range(w):
+                    step(i, kind)
+                barrier()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                l0 = L.kernel_launches()
+                e0.record(stream)
+                for i in range(k):
+                    step(i, kind)
+                e1.record(stream)
+                e1.synchronize()
+                launches = L.kernel_launches() - l0
+                barrier()
+            return e0.elapsed_time(e1), launches
+
+        clocks = ClockSampler(local)
+        clocks.start()
+        ms_total, launches = timed(H, steps, warm)
+        clk = clocks.stop()
+        ms_hs, _ = timed(HS, max(steps // 2, 1), warm)
+        ms_step = ms_total / steps
+        value = flops * steps / (ms_total * 1e-3) / 1e12
+        value_hs = flops * max(steps // 2, 1) / (ms_hs * 1e-3) / 1e12
+        # e2e through the public API with pinned host buffers (library stages H2D, computes, copies C back)
+        e2e = None
+        if not args.no_e2e:
+            hA = A[0].cpu().pin_memory()
+            hB = B[0].cpu().pin_memory()
+            hC = torch.empty((n, n), dtype=torch.float16).pin_memory()
+            L.set_nowait(0)
+            e2e_steps = max(min(steps // 20, 100), 5)
+            for _ in range(3):
+                L.gemm(H, 0, 0, n, n, n, 1.0, hA.data_ptr(), n, hB.data_ptr(), n, 0.0, hC.data_ptr(), n)
+            t0 = time.perf_counter()
+            for _ in range(e2e_steps):
+                r = L.gemm(H, 0, 0, n, n, n, 1.0, hA.data_ptr(), n, hB.data_ptr(), n, 0.0, hC.data_ptr(), n)
+                if r:
+                    raise RuntimeError(L.error().decode())
+            dt = time.perf_counter() - t0
+            L.set_nowait(1)
+            e2e = {"value": round(flops * e2e_steps / dt / 1e12, 3), "unit": "TFLOP/s",
+                   "h2d_bytes_per_step": 2 * n * n * 2, "d2h_bytes_per_step": n * n * 2,
+                   "steps": e2e_steps, "path": "gen9blas_gemm(GEN9BLAS_H) on pinned host pointers"}
+        peak_t, _, peak_kind = measured_peaks()
+        traffic = profile_traffic("hgemm_tc_n4096")
+        roof = {"bound": "tensor", "achieved": round(value, 2), "peak": peak_t, "unit": "TFLOP/s",
+                "frac": round(value / peak_t, 4), "traffic": traffic, "kernel": "hgemm_tc_kernel<true>",
+                "algorithmic": f"2*n^3 = {flops:.4g} FLOP per launch, one launch per step",
+                "peak_kind": f"{peak_kind} bf16 dense (burst; kernel timed alone), MEASURED_PEAKS.json"}
+        cpu = None
+        if rank == 0 and world == 1 and not args.no_cpu:
+            v, kind, calls, threads, sample = cpu_sgemm_sample(n)
+            cpu = {"value": round(v, 4), "unit": "TFLOP/s", "cores": threads, "kind": kind, "sample": sample}
+        line = {"metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": steps,
+                "warmup": warm, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+                "config": {"workload": "hgemm4096: BASELINE configs[1], HGEMM FP16 n=4096 row-major NN, "
+                                       "A,B iid N(0,1)/sqrt(n), C=A*B, FP16 accumulation (GEN9BLAS_H)",
+                           "n": n, "l2": "inputs larger than L2: 4 rotating (A,B,C) sets = 384 MiB"},
+                "modes": {"fp16_accumulate_tflops": round(value, 3), "fp32_accumulate_tflops": round(value_hs, 3)},
+                "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clk}
+    else:
+        line = run_scaleout(args, L, torch, stream, barrier, rank, world, local)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def run_scaleout(args, L, torch, stream, barrier, rank, world, local):
+    """HGEMM n = 32768, B/C column-sharded, A replicated, C all-gathered (NCCL) and re-laid out."""
+    n = 32768
+    steps = args.steps or 5
+    warm = max(args.warmup or 3, 3)
+    nb = n // world
+    chunks = 4 if world > 1 else 1
+    cw = nb // chunks
+    g = torch.Generator(device="cuda")
+    g.manual_seed(7)   # same A on every rank
+    A = torch.randn(n, n, device="cuda", generator=g, dtype=torch.float16).div_(n ** 0.5)
+    g.manual_seed(100 + rank)
+    Bs = torch.randn(n, nb, device="cuda", generator=g, dtype=torch.float16).div_(n ** 0.5)   # this rank's columns
+    C = torch.empty(n, n, device="cuda", dtype=torch.float16)
+    # local result, chunk-major (N = 1 writes straight into C)
+    Cs = torch.empty(chunks, n, cw, device="cuda", dtype=torch.float16) if world > 1 else None
+    Cg = torch.empty(chunks, world, n, cw, device="cuda", dtype=torch.float16) if world > 1 else None
+    comm = torch.cuda.Stream()
+    flops = 2.0 * n * n * n
+
+    def step():
+        with torch.cuda.stream(stream):
+            for c in range(chunks):
+                dst, ldc = (Cs[c].data_ptr(), cw) if world > 1 else (C.data_ptr(), n)
+                r = L.gemm(H, 0, 0, n, cw, n, 1.0, A.data_ptr(), n, Bs[:, c * cw:].data_ptr(), nb, 0.0, dst, ldc)
+                if r:
+                    raise RuntimeError(L.error().decode())
+                if world > 1:
+                    ev = torch.cuda.Event()
+                    ev.record(stream)
+                    comm.wait_event(ev)
+                    with torch.cuda.stream(comm):
+                        torch.distributed.all_gather_into_tensor(Cg[c], Cs[c])
+        if world > 1:
+            stream.wait_stream(comm)
+            with torch.cuda.stream(stream):
+                # column block (rank q, chunk c) -> C[:, q*nb + c*cw : ... + cw]
+                C.view(n, world, chunks, cw).copy_(Cg.permute(2, 1, 0, 3))
+
+    for _ in range(warm):
+        step()
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0 = L.kernel_launches()
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    e1.synchronize()
+    launches = L.kernel_launches() - l0
+    clk = clocks.stop()
+    ms = torch.tensor([e0.elapsed_time(e1)], device="cuda")
+    if world > 1:
+        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+    barrier()
+    ms_total = float(ms.item())
+    value = flops * steps / (ms_total * 1e-3) / 1e12
+    peak_t, _, peak_kind = measured_peaks()
+    return {"metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": steps,
+            "warmup": warm, "ms_per_step": round(ms_total / steps, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "scaleout: BASELINE configs[4], HGEMM FP16 n=32768, A replicated, B/C column-"
+                                   f"sharded over {world} GPU(s), C all-gathered with NCCL in {chunks} chunk(s) "
+                                   "overlapped with the GEMM of the next chunk, then re-laid out row-major",
+                       "n": n, "l2": "inputs larger than L2 (A alone 2 GiB)"},
+            "roofline": {"bound": "tensor", "achieved": round(value / world, 2), "peak": peak_t, "unit": "TFLOP/s",
+                         "frac": round(value / world / peak_t, 4), "traffic": None,
+                         "peak_kind": f"{peak_kind} bf16 dense per GPU; achieved = whole step per GPU incl. gather"},
+            "cpu_baseline": None, "e2e": None, "gpu_launches": launches, "clocks": clk}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())
