@@ -605,3 +605,124 @@ GEN9BLAS_API int gen9blas_ger(int type, int M, int N, double alpha, const void *
 }
 
 }  // extern "C"
+
+// ================================================================================================ allocation-free gemv
+// gen9blas_gemv_noalloc: the gemv entry point for callers that must not allocate GPU memory. The transposed product
+// needs scratch for its split-row partial sums; here that scratch is a fixed array in the library's own device image
+// instead of the grow-only buffer of gen9blas_gemv. See include/gen9blas.h for the contract.
+namespace g9 {
+
+constexpr size_t kNoAllocScratchBytes = 8u << 20;   // 8 MiB per GPU that loads the library, held until exit
+
+// Partial sums of the transposed product. Device code could name it directly; host code needs its device address,
+// which noalloc_scratch() obtains once per device with cudaGetSymbolAddress (the array's name in host code is only a
+// host-side stand-in, not a device address).
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+static void *g_noalloc_ptr[kMaxDevices];
+
+static int noalloc_scratch(int dev, void **p) {
+    if (!g_noalloc_ptr[dev]) {
+        void *ptr = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return fail(GEN9BLAS_ERR, "cudaGetSymbolAddress of the no-allocation scratch failed on device %d: %s", dev,
+                        cudaGetErrorString(e));
+        }
+        g_noalloc_ptr[dev] = ptr;
+    }
+    *p = g_noalloc_ptr[dev];
+    return 0;
+}
+
+static bool device_resident(const void *p, int dev) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return (a.type == cudaMemoryTypeDevice && a.device == dev) || a.type == cudaMemoryTypeManaged;
+}
+
+template <typename T>
+static int gemv_noalloc_t(int trans, int M, int N, double alpha, const T *A, int lda, const T *x, long long ix,
+                          double beta, T *y, long long iy, int sm_count, void *P, cudaStream_t st) {
+    using R = typename Compute<T>::R;
+    if (!trans) {   // the untransposed product uses no scratch: same kernel as gen9blas_gemv
+        const bool vec = ix == 1 && (((uintptr_t)A | (uintptr_t)x) & 15) == 0 && ((long long)lda * sizeof(T)) % 16 == 0;
+        const long long warps = (M + kRowsN - 1) / kRowsN;
+        const int blocks = (int)((warps * 32 + kThreads - 1) / kThreads);
+        if (vec) gemv_n_kernel<T, true><<<blocks, kThreads, 0, st>>>(M, N, (R)alpha, A, lda, x, ix, (R)beta, y, iy);
+        else gemv_n_kernel<T, false><<<blocks, kThreads, 0, st>>>(M, N, (R)alpha, A, lda, x, ix, (R)beta, y, iy);
+        return launched("gemv_n");
+    }
+    const size_t row_bytes = (size_t)N * sizeof(R);   // one part of the partial sums
+    if (row_bytes > kNoAllocScratchBytes)
+        return fail(GEN9BLAS_ERR_INVALID_ARG,
+                    "gen9blas_gemv_noalloc: trans with N = %d needs %zu bytes of scratch per row part; the fixed "
+                    "scratch holds %zu bytes (N <= %zu for this type)", N, row_bytes, kNoAllocScratchBytes,
+                    kNoAllocScratchBytes / sizeof(R));
+    const bool vec = (((uintptr_t)A) & 15) == 0 && ((long long)lda * sizeof(T)) % 16 == 0;
+    const int w = vec ? V16<T>::W : 1;
+    const int col_blocks = (int)(((long long)N + (long long)kThreads * w - 1) / ((long long)kThreads * w));
+    int parts = (sm_count * 8 + col_blocks - 1) / col_blocks;   // the split of gen9blas_gemv ...
+    const long long fit = (long long)(kNoAllocScratchBytes / row_bytes);
+    if (parts > fit) parts = (int)fit;                          // ... capped by the fixed scratch
+    if (parts > M) parts = M;
+    if (parts > 65535) parts = 65535;
+    if (parts < 1) parts = 1;
+    const int rpp = (M + parts - 1) / parts;
+    parts = (M + rpp - 1) / rpp;
+    dim3 grid(col_blocks, parts);
+    if (vec) gemv_t_partial<T, true><<<grid, kThreads, 0, st>>>(M, N, rpp, A, lda, x, ix, (R *)P);
+    else gemv_t_partial<T, false><<<grid, kThreads, 0, st>>>(M, N, rpp, A, lda, x, ix, (R *)P);
+    G9_TRY(launched("gemv_t_partial"));
+    gemv_t_final<T><<<(N + kThreads - 1) / kThreads, kThreads, 0, st>>>(N, parts, (const R *)P, (R)alpha, (R)beta, y, iy);
+    return launched("gemv_t_final");
+}
+
+}  // namespace g9
+
+extern "C" GEN9BLAS_API int gen9blas_gemv_noalloc(int type, int trans, int M, int N, double alpha, const void *A, int lda,
+                                                  const void *x, int incx, double beta, void *y, int incy) {
+    G.status = 0;
+    G.err[0] = 0;
+    if (int e = gen9blas_init()) return e;
+    const int es = l12_es(type);
+    if (!es) return fail(GEN9BLAS_ERR_UNSUPPORTED, "type %d unavailable", type);
+    if ((M < N ? M : N) <= 0) return 0;
+    if (!incx || !incy) return fail(GEN9BLAS_ERR_INVALID_ARG, "vector increment 0");
+    if (lda < N) return fail(GEN9BLAS_ERR_INVALID_ARG, "lda < N");
+    const int dev = G.cur_dev;
+    int cur = -1;
+    G9_CU(cudaGetDevice(&cur));
+    if (cur != dev) G9_CU(cudaSetDevice(dev));
+    if (!device_resident(A, dev) || !device_resident(x, dev) || !device_resident(y, dev))
+        return fail(GEN9BLAS_ERR_INVALID_ARG,
+                    "gen9blas_gemv_noalloc takes device or managed memory of the current device only (no staging)");
+    void *P = nullptr;
+    G9_TRY(noalloc_scratch(dev, &P));
+    int sm_count = 0;
+    G9_CU(cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev));
+    cudaStream_t st = G.user_stream_set ? G.user_stream : cudaStreamPerThread;
+    const int nx = trans ? M : N, ny = trans ? N : M;
+    const long long ox = vec_off(nx, incx), oy = vec_off(ny, incy);
+    int r;
+    switch (l12_type(type)) {
+    case GEN9BLAS_S:
+        r = gemv_noalloc_t<float>(trans ? 1 : 0, M, N, alpha, (const float *)A, lda, (const float *)x + ox, incx, beta,
+                                  (float *)y + oy, incy, sm_count, P, st);
+        break;
+    case GEN9BLAS_D:
+        r = gemv_noalloc_t<double>(trans ? 1 : 0, M, N, alpha, (const double *)A, lda, (const double *)x + ox, incx, beta,
+                                   (double *)y + oy, incy, sm_count, P, st);
+        break;
+    default:
+        r = gemv_noalloc_t<__half>(trans ? 1 : 0, M, N, alpha, (const __half *)A, lda, (const __half *)x + ox, incx, beta,
+                                   (__half *)y + oy, incy, sm_count, P, st);
+    }
+    if (r < 0) return r;
+    if (!G.nowait) G9_CU(cudaStreamSynchronize(st));
+    return 0;
+}

@@ -1,0 +1,88 @@
+"""gen9blas_gemv_noalloc: the gemv entry point for callers that must not allocate GPU memory (graph capture, loops
+that cannot take the device-wide synchronisation of cudaMalloc/cudaFree, processes that hand all device memory to
+their own pool). Its transposed product keeps the split-row partial sums in a fixed 8 MiB array of the library's
+device image instead of the grow-only scratch buffer that gen9blas_gemv uses.
+
+Checked through the C ABI on device-resident operands: two calls in a row, each equal (within the level-2
+tolerances) to the output of the existing gen9blas_gemv; no growth of device memory use across calls that would
+need more scratch; oversize N rejected with a clear error before any launch. This file sorts last so that a run
+that stops at the first failure has already run every other test; it also passes alone in a fresh process."""
+import ctypes
+
+import numpy as np
+import pytest
+
+import abi
+
+pytestmark = pytest.mark.gpu
+TOL = {abi.S: 1e-6, abi.H: 2e-3, abi.D: 1e-13}
+
+
+@pytest.fixture(scope="module")
+def torch():
+    return pytest.importorskip("torch")
+
+
+def scaled_error(got, ref, scale):
+    return float((np.abs(got.astype(np.float64) - ref.astype(np.float64)) / np.maximum(scale, 1e-30)).max())
+
+
+@pytest.mark.parametrize("t,dtname", [(abi.S, "float32"), (abi.H, "float16"), (abi.D, "float64")])
+def test_noalloc_matches_gemv_twice(gpu_lib, torch, t, dtname):
+    dt = getattr(torch, dtname)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(31)
+    for (M, N, trans, incx, incy, beta) in ((1000, 3000, 1, 1, 1, 0.0), (3001, 513, 1, 2, -1, 0.5),
+                                            (700, 900, 0, 1, 1, -1.0), (32768, 4096, 1, 1, 1, 0.0)):
+        lda = N + 3
+        A = torch.empty(M, lda, device="cuda", dtype=torch.float64).uniform_(-1, 1, generator=gen).to(dt)
+        nx, ny = (M, N) if trans else (N, M)
+        x = torch.empty(nx * incx, device="cuda", dtype=torch.float64).uniform_(-1, 1, generator=gen).to(dt)
+        y0 = torch.empty(ny * abs(incy), device="cuda", dtype=torch.float64).uniform_(-1, 1, generator=gen).to(dt)
+        y_ref, y1, y2 = y0.clone(), y0.clone(), y0.clone()
+        torch.cuda.synchronize()
+        args = (t, trans, M, N, 0.75, A.data_ptr(), lda, x.data_ptr(), incx, beta)
+        assert gpu_lib.gemv(*args, y_ref.data_ptr(), incy) == 0, gpu_lib.error()
+        assert gpu_lib.gemv_noalloc(*args, y1.data_ptr(), incy) == 0, gpu_lib.error()
+        assert gpu_lib.gemv_noalloc(*args, y2.data_ptr(), incy) == 0, gpu_lib.error()
+        torch.cuda.synchronize()
+        Ad = A[:, :N].double().cpu().numpy()
+        xs = x.double().cpu().numpy()[::incx]
+        scale = 0.75 * (np.abs(Ad.T if trans else Ad) @ np.abs(xs))   # logical order of y
+        if incy < 0:
+            scale = scale[::-1]                                           # memory order (element 0 is last)
+        scale = scale + abs(beta) * np.abs(y0.double().cpu().numpy()[::abs(incy)])
+        ref = y_ref.cpu().numpy()[::abs(incy)]
+        for got in (y1, y2):
+            g = got.cpu().numpy()[::abs(incy)]
+            assert scaled_error(g, ref, scale) <= TOL[t], (t, M, N, trans)
+
+
+def test_noalloc_uses_no_new_device_memory(gpu_lib, torch):
+    """After the first call (which loads the library's device image, fixed array included) larger transposed
+    problems, which would grow gen9blas_gemv's scratch, leave the free device memory unchanged."""
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(5)
+    A = torch.empty(8192, 60000, device="cuda", dtype=torch.float32).uniform_(-1, 1, generator=gen)
+    x = torch.empty(8192, device="cuda", dtype=torch.float32).uniform_(-1, 1, generator=gen)
+    y = torch.zeros(60000, device="cuda", dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert gpu_lib.gemv_noalloc(abi.S, 1, 64, 1000, 1.0, A.data_ptr(), 60000, x.data_ptr(), 1, 0.0, y.data_ptr(), 1) == 0
+    free0 = torch.cuda.mem_get_info()[0]
+    for N in (30000, 60000):
+        assert gpu_lib.gemv_noalloc(abi.S, 1, 8192, N, 1.0, A.data_ptr(), 60000, x.data_ptr(), 1, 0.0, y.data_ptr(), 1) == 0
+    assert torch.cuda.mem_get_info()[0] == free0
+
+
+def test_noalloc_rejects_oversize_and_host_memory(gpu_lib, torch):
+    A = torch.zeros(2, 3_000_000, device="cuda", dtype=torch.float32)
+    x = torch.zeros(2, device="cuda", dtype=torch.float32)
+    y = torch.zeros(3_000_000, device="cuda", dtype=torch.float32)
+    torch.cuda.synchronize()
+    launches = gpu_lib.kernel_launches()
+    r = gpu_lib.gemv_noalloc(abi.S, 1, 2, 3_000_000, 1.0, A.data_ptr(), 3_000_000, x.data_ptr(), 1, 0.0, y.data_ptr(), 1)
+    assert r == -3 and b"scratch" in gpu_lib.error()
+    assert gpu_lib.kernel_launches() == launches           # rejected before any launch
+    h = np.zeros(16, np.float32)
+    r = gpu_lib.gemv_noalloc(abi.S, 0, 4, 4, 1.0, h.ctypes.data, 4, h.ctypes.data, 1, 0.0, h.ctypes.data, 1)
+    assert r == -3 and b"device" in gpu_lib.error()
