@@ -70,23 +70,30 @@ def build_core(force=False, ptxas_verbose=False):
 
 def build_shim(force=False):
     """libgen9blas_blas.so: own CBLAS/BLAS symbols over libgen9blas.so, every other BLAS symbol forwarded."""
-    if not os.path.isdir(SHIM):
-        return None
-    srcs = sorted(glob.glob(os.path.join(SHIM, "*.c")))
+    src = os.path.join(SHIM, "cblas_shim.c")
     gen = os.path.join(SHIM, "gen_forward.py")
     syms = os.path.join(SHIM, "blas_symbols.txt")
-    if not srcs or not os.path.exists(gen):
+    if not os.path.exists(src):
         return None
-    fwd = os.path.join(OBJ, "cblas_forward.c")
     os.makedirs(OBJ, exist_ok=True)
-    if force or _newer(fwd, srcs + [gen, syms]):
-        out = _run([sys.executable, gen, syms] + srcs).stdout
+    inc = ["-I", os.path.join(ROOT, "include")]
+    obj = os.path.join(OBJ, "cblas_shim.o")
+    own = os.path.join(OBJ, "shim_own_symbols.txt")
+    fwd = os.path.join(OBJ, "cblas_forward.c")
+    hdr = os.path.join(ROOT, "include", "gen9blas.h")
+    if force or _newer(obj, [src, hdr]):
+        _run(["gcc", "-O2", "-fPIC", "-fvisibility=hidden", "-c"] + inc + [src, "-o", obj])
+    if force or _newer(fwd, [obj, gen, syms]):
+        nm = _run(["nm", "--defined-only", "-g", obj]).stdout
+        names = sorted({ln.split()[-1] for ln in nm.splitlines() if ln.split() and ln.split()[-2] in ("T", "D", "R", "B")})
+        with open(own, "w") as f:
+            f.write("\n".join(n for n in names if not n.startswith("g9_")) + "\n")
+        out = _run([sys.executable, gen, syms, own]).stdout
         with open(fwd, "w") as f:
             f.write(out)
-    deps = srcs + [fwd, LIB, os.path.join(ROOT, "include", "gen9blas.h")]
-    if force or _newer(SHIM_LIB, deps):
-        _run(["gcc", "-O2", "-fPIC", "-shared", "-fvisibility=hidden", "-I", os.path.join(ROOT, "include"), "-o", SHIM_LIB]
-             + srcs + [fwd, "-L", HERE, "-lgen9blas", "-Wl,-rpath,$ORIGIN", "-ldl", "-lpthread"])
+    if force or _newer(SHIM_LIB, [obj, fwd, LIB]):
+        _run(["gcc", "-O2", "-fPIC", "-shared", "-o", SHIM_LIB, obj, fwd, "-L", HERE, "-lgen9blas",
+              "-Wl,-rpath,$ORIGIN", "-ldl", "-lpthread"])
     return SHIM_LIB
 
 

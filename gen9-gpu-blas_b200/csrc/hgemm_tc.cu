@@ -401,4 +401,33 @@ int launch_hgemm_tc(int type, int tA, int tB, int M, int N, int K, double alpha,
     return launched("hgemm_tc");
 }
 
+// ------------------------------------------------------------------------------------------------ wait self-test
+// One thread waits on an mbarrier that nothing arrives on, through the same bounded wait the GEMM roles use; after
+// limit_ns it gives up, sets the mapped error word and returns. Exercises the timeout path without any GPU fault.
+__global__ void wait_probe_kernel(unsigned *err, unsigned long long limit_ns) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && !mbar_wait(&bar, 0, &abort_flag, limit_ns)) {
+        *(volatile unsigned *)err = kDevErrWaitTimeout;
+        __threadfence_system();
+    }
+}
+
 }  // namespace g9
+
+extern "C" GEN9BLAS_API int gen9blas_selftest_wait(double limit_ms) {
+    using namespace g9;
+    if (int e = begin_op()) return e;
+    DevState *d = dev_state();
+    if (limit_ms < 0.1) limit_ms = 0.1;
+    if (limit_ms > 1000.0) limit_ms = 1000.0;
+    wait_probe_kernel<<<1, 32, 0, stream()>>>(d->err_dev, (unsigned long long)(limit_ms * 1e6));
+    G9_TRY(launched("wait_probe"));
+    return finish_op(nullptr, 0);
+}

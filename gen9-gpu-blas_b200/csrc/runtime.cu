@@ -127,8 +127,26 @@ int begin_op() {
     return 0;
 }
 
+// Host-side fault injection for the error-path tests (no GPU fault is ever provoked): GEN9BLAS_FAULT=alloc makes
+// every device buffer allocation report out-of-memory, =launch makes every kernel launch report a launch error,
+// =wait makes every call end as if a device-side bounded wait had given up. Read once per process.
+enum { kFaultNone = 0, kFaultAlloc, kFaultLaunch, kFaultWait };
+static int fault_mode() {
+    static int m = -1;
+    if (m < 0) {
+        const char *e = getenv("GEN9BLAS_FAULT");
+        m = !e ? kFaultNone : !strcmp(e, "alloc") ? kFaultAlloc : !strcmp(e, "launch") ? kFaultLaunch
+            : !strcmp(e, "wait") ? kFaultWait : kFaultNone;
+    }
+    return m;
+}
+
 int launched(const char *name) {
     G.launches++;
+    if (fault_mode() == kFaultLaunch) {
+        cudaGetLastError();
+        return fail(GEN9BLAS_ERR, "launch of %s failed: injected fault (GEN9BLAS_FAULT=launch)", name);
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(GEN9BLAS_ERR, "launch of %s failed: %s", name, cudaGetErrorString(e));
     return 0;
@@ -143,6 +161,8 @@ static int ensure_dev_buf(void **p, size_t *n, size_t bytes) {
         *n = 0;
     }
     size_t want = bytes < 4096 ? 4096 : (bytes + 0xFFFFF) & ~(size_t)0xFFFFF;   // round to 1 MiB
+    if (fault_mode() == kFaultAlloc)
+        return fail(GEN9BLAS_ERR_OUT_OF_MEMORY, "cudaMalloc(%zu): injected fault (GEN9BLAS_FAULT=alloc)", want);
     G9_CU(cudaMalloc(p, want));
     *n = want;
     return 0;
@@ -196,6 +216,7 @@ int map_operand(Operand &op, const void *p, size_t bytes, int slot, bool copy_in
 }
 
 static int check_dev_err(DevState *d) {
+    if (fault_mode() == kFaultWait) *(volatile unsigned *)d->err_host = kDevErrWaitTimeout;
     unsigned v = *(volatile unsigned *)d->err_host;
     if (v != kDevErrNone) {
         *(volatile unsigned *)d->err_host = kDevErrNone;

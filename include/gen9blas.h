@@ -169,6 +169,10 @@ GEN9BLAS_API void gen9blas_set_nowait(int on);
 GEN9BLAS_API int gen9blas_flush(void);
 /* Number of kernels this library launched since the process started (launch accounting for benchmarks). */
 GEN9BLAS_API long long gen9blas_kernel_launches(void);
+/* Diagnostic of the bounded device-side waits: runs a kernel whose mbarrier wait can never complete; the wait gives
+ * up after limit_ms (clamped to 0.1 .. 1000 ms), records the timeout in the error word and the kernel returns. The
+ * call then returns GEN9BLAS_ERR with the timeout message and the device stays usable. No GPU fault is involved. */
+GEN9BLAS_API int gen9blas_selftest_wait(double limit_ms);
 
 /* GEMV that allocates nothing: same arguments, results and error codes as gen9blas_gemv, for callers that must not
  * allocate GPU memory -- code recording or replaying a CUDA graph, a latency-critical loop that cannot afford the

@@ -1,0 +1,155 @@
+"""Child process for the LD_PRELOAD-library tests: loads libgen9blas_blas.so the way a program linked against
+libblas.so.3 would see it (its CPU BLAS, OpenBLAS, chosen by GEN9BLAS_BLAS_CPU), runs one group of CBLAS / Fortran BLAS
+calls and prints a JSON report. The environment (GEN9BLAS_BLAS, GEN9BLAS_BLAS_INFO) is set by the parent test.
+
+    python tests/shim_child.py <group>
+"""
+import ctypes
+import json
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+sys.path.insert(0, os.path.join(HERE, "golden"))
+from make_golden import GEMM_CASES, ColMajor, NoTrans, RowMajor, Trans, gemm_inputs, vec_inputs  # noqa: E402
+
+OPENBLAS_DIR = "/opt/prime-rl/.venv/lib/python3.12/site-packages/opencv_python_headless.libs"
+for dep in ("libquadmath-2284e583.so.0.0.0", "libgfortran-83c28eba.so.5.0.0"):
+    ctypes.CDLL(os.path.join(OPENBLAS_DIR, dep), mode=ctypes.RTLD_GLOBAL)
+os.environ.setdefault("GEN9BLAS_BLAS_CPU", os.path.join(OPENBLAS_DIR, "libopenblasp-r0-59ffcd50.3.15.so"))
+L = ctypes.CDLL(os.path.join(ROOT, "gen9-gpu-blas_b200", "libgen9blas_blas.so"))
+I, P = ctypes.c_int, ctypes.c_void_p
+REF = np.load(os.path.join(HERE, "golden", "ref_cblas_outputs.npz"))
+
+
+def rel(got, want, scale):
+    return float((np.abs(np.asarray(got, np.float64) - np.asarray(want, np.float64)) / scale).max())
+
+
+def group_cblas_gemm():
+    """Row/column-major, all transposes, alpha/beta: compared with the reference CBLAS layer's own outputs."""
+    out = {}
+    for tag, F in (("s", ctypes.c_float), ("d", ctypes.c_double)):
+        f = getattr(L, f"cblas_{tag}gemm")
+        f.argtypes = [I, I, I, I, I, I, F, P, I, P, I, F, P, I]
+        worst = 0.0
+        for order in (RowMajor, ColMajor):
+            for (M, N, K, al, be) in GEMM_CASES:
+                for ta in (NoTrans, Trans):
+                    for tb in (NoTrans, Trans):
+                        A, B, C0 = gemm_inputs(tag, order, ta, tb, M, N, K)
+                        if order == RowMajor:
+                            As, Bs, Cs = np.ascontiguousarray(A), np.ascontiguousarray(B), C0.copy()
+                            lda, ldb, ldc = A.shape[1], B.shape[1], N
+                        else:
+                            As, Bs, Cs = np.asfortranarray(A), np.asfortranarray(B), np.asfortranarray(C0.copy())
+                            lda, ldb, ldc = A.shape[0], B.shape[0], M
+                        f(order, ta, tb, M, N, K, al, As.ctypes.data, lda, Bs.ctypes.data, ldb, be, Cs.ctypes.data, ldc)
+                        a64 = A.astype(np.float64) if ta == NoTrans else A.astype(np.float64).T
+                        b64 = B.astype(np.float64) if tb == NoTrans else B.astype(np.float64).T
+                        scale = abs(al) * np.abs(a64) @ np.abs(b64) + abs(be) * np.abs(C0.astype(np.float64))
+                        want = REF[f"{tag}gemm_o{order}_t{ta}{tb}_{M}x{N}x{K}"]
+                        worst = max(worst, rel(np.ascontiguousarray(Cs), want, scale))
+        out[f"{tag}gemm_vs_ref_cblas"] = worst
+    return out
+
+
+def group_fortran_and_l12():
+    out = {}
+    rng = np.random.default_rng(3)
+    for tag, F, dt in (("s", ctypes.c_float, np.float32), ("d", ctypes.c_double, np.float64)):
+        # Fortran xGEMM_ (column-major), padded leading dimensions, all transposes
+        g = getattr(L, f"{tag}gemm_")
+        g.argtypes = [ctypes.c_char_p, ctypes.c_char_p] + [ctypes.POINTER(I)] * 3 + [ctypes.POINTER(F), P,
+                      ctypes.POINTER(I), P, ctypes.POINTER(I), ctypes.POINTER(F), P, ctypes.POINTER(I)]
+        worst = 0.0
+        for ta in "NT":
+            for tb in "nt":
+                M, N, K = 45, 38, 70
+                A = rng.uniform(-1, 1, (M, K) if ta == "N" else (K, M)).astype(dt)
+                B = rng.uniform(-1, 1, (K, N) if tb == "n" else (N, K)).astype(dt)
+                C0 = rng.uniform(-1, 1, (M, N)).astype(dt)
+                Af = np.zeros((A.shape[0] + 3, A.shape[1]), dt, order="F"); Af[:A.shape[0]] = A
+                Bf = np.zeros((B.shape[0] + 1, B.shape[1]), dt, order="F"); Bf[:B.shape[0]] = B
+                Cf = np.zeros((M + 2, N), dt, order="F"); Cf[:M] = C0
+                al, be = F(1.5), F(-0.5)
+                g(ta.encode(), tb.encode(), I(M), I(N), I(K), al, Af.ctypes.data, I(Af.shape[0]), Bf.ctypes.data,
+                  I(Bf.shape[0]), be, Cf.ctypes.data, I(Cf.shape[0]))
+                a64 = A.astype(np.float64) if ta == "N" else A.astype(np.float64).T
+                b64 = B.astype(np.float64) if tb == "n" else B.astype(np.float64).T
+                ref = 1.5 * a64 @ b64 - 0.5 * C0
+                scale = 1.5 * np.abs(a64) @ np.abs(b64) + 0.5 * np.abs(C0)
+                worst = max(worst, rel(Cf[:M], ref, scale))
+                assert not Cf[M:].any()
+        out[f"{tag}gemm_fortran"] = worst
+        # cblas gemv (both orders, negative increments), ger, level 1 against FP64 NumPy
+        gv = getattr(L, f"cblas_{tag}gemv")
+        gv.argtypes = [I, I, I, I, F, P, I, P, I, F, P, I]
+        worst = 0.0
+        for order in (RowMajor, ColMajor):
+            for tr in (NoTrans, Trans):
+                M, N = 301, 257
+                A = rng.uniform(-1, 1, (M, N)).astype(dt)
+                As = np.ascontiguousarray(A) if order == RowMajor else np.asfortranarray(A)
+                lda = N if order == RowMajor else M
+                nx, ny = (N, M) if tr == NoTrans else (M, N)
+                x = rng.uniform(-1, 1, 2 * nx).astype(dt)
+                y0 = rng.uniform(-1, 1, ny).astype(dt)
+                y = y0.copy()
+                gv(order, tr, M, N, 0.5, As.ctypes.data, lda, x.ctypes.data, -2, 2.0, y.ctypes.data, 1)
+                xs = x[::2][::-1].astype(np.float64)   # incx = -2: element 0 is the last in memory
+                op = A.astype(np.float64) if tr == NoTrans else A.astype(np.float64).T
+                worst = max(worst, rel(y, 0.5 * op @ xs + 2 * y0, 0.5 * np.abs(op) @ np.abs(xs) + 2 * np.abs(y0)))
+        out[f"{tag}gemv"] = worst
+        gr = getattr(L, f"cblas_{tag}ger")
+        gr.argtypes = [I, I, I, F, P, I, P, I, P, I]
+        M, N = 123, 77
+        A = rng.uniform(-1, 1, (M, N)).astype(dt)
+        x = rng.uniform(-1, 1, M).astype(dt)
+        y = rng.uniform(-1, 1, N).astype(dt)
+        Ac = np.asfortranarray(A.copy())
+        gr(ColMajor, M, N, -0.25, x.ctypes.data, 1, y.ctypes.data, 1, Ac.ctypes.data, M)
+        ref = A.astype(np.float64) - 0.25 * np.outer(x, y)
+        out[f"{tag}ger"] = rel(Ac, ref, np.abs(A) + 0.25 * np.abs(np.outer(x, y)))
+        n = 100003
+        x = vec_inputs(tag, "l1x", n)
+        yv = vec_inputs(tag, "l1y", n)
+        ax = getattr(L, f"cblas_{tag}axpy")
+        ax.argtypes = [I, F, P, I, P, I]
+        yy = yv.copy()
+        ax(n, 0.7, x.ctypes.data, 1, yy.ctypes.data, 1)
+        out[f"{tag}axpy"] = rel(yy, 0.7 * x.astype(np.float64) + yv, 0.7 * np.abs(x) + np.abs(yv))
+        dot = getattr(L, f"cblas_{tag}dot")
+        dot.argtypes, dot.restype = [I, P, I, P, I], F
+        X, Y = x.astype(np.float64), yv.astype(np.float64)
+        out[f"{tag}dot"] = abs(dot(n, x.ctypes.data, 1, yv.ctypes.data, 1) - X @ Y) / (np.abs(X) @ np.abs(Y))
+        for nm, refv in (("nrm2", np.linalg.norm(X)), ("asum", np.abs(X).sum())):
+            fn = getattr(L, f"cblas_{tag}{nm}")
+            fn.argtypes, fn.restype = [I, P, I], F
+            out[f"{tag}{nm}"] = abs(fn(n, x.ctypes.data, 1) - refv) / refv
+        im = getattr(L, f"cblas_i{tag}amax")
+        im.argtypes, im.restype = [I, P, I], ctypes.c_size_t
+        out[f"i{tag}amax_exact"] = int(im(n, x.ctypes.data, 1)) == int(np.argmax(np.abs(X)))
+    return out
+
+
+def group_forwarded():
+    """A symbol the shim does not own (complex GEMM) reaches the CPU BLAS through the jump table."""
+    f = L.cblas_zgemm
+    f.argtypes = [I] * 6 + [P, P, I, P, I, P, P, I]
+    rng = np.random.default_rng(1)
+    A = (rng.standard_normal((5, 7)) + 1j * rng.standard_normal((5, 7))).astype(np.complex128)
+    B = (rng.standard_normal((7, 3)) + 1j * rng.standard_normal((7, 3))).astype(np.complex128)
+    C = np.zeros((5, 3), np.complex128)
+    one, zero = np.array(1 + 0j), np.array(0j)
+    f(RowMajor, NoTrans, NoTrans, 5, 3, 7, one.ctypes.data, A.ctypes.data, 7, B.ctypes.data, 3, zero.ctypes.data,
+      C.ctypes.data, 3)
+    return {"zgemm_forwarded": float(np.abs(C - A @ B).max())}
+
+
+if __name__ == "__main__":
+    groups = {"cblas_gemm": group_cblas_gemm, "fortran_l12": group_fortran_and_l12, "forwarded": group_forwarded}
+    print(json.dumps(groups[sys.argv[1]]()))

@@ -1,0 +1,60 @@
+"""The LD_PRELOAD CBLAS/BLAS library libgen9blas_blas.so (drop-in for the reference's libgen9blas_blas.so,
+lib/src/cblas.c): symbol surface and forwarding on CPU; GPU routing and parity against the reference's own CBLAS
+outputs (GEN9BLAS_BLAS_INFO log, tolerances of lib/test_blas.py / test_blas_d.py) on a GPU."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+from conftest import PKG, ROOT
+
+SHIM = os.path.join(PKG, "libgen9blas_blas.so")
+CHILD = os.path.join(ROOT, "tests", "shim_child.py")
+
+
+def child(group, **env):
+    e = dict(os.environ)
+    e.update(env)
+    r = subprocess.run([sys.executable, CHILD, group], capture_output=True, text=True, env=e, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    return json.loads(r.stdout.strip().splitlines()[-1]), r.stderr
+
+
+def test_exports_exactly_the_blas_surface():
+    syms = [s.strip() for s in open(os.path.join(PKG, "shim", "blas_symbols.txt")) if s.strip()]
+    assert len(syms) == 393
+    out = subprocess.run(["nm", "-D", "--defined-only", SHIM], capture_output=True, text=True, check=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
+    assert exported == set(syms)
+
+
+def test_cpu_mode_routes_everything_to_the_cpu_blas():
+    res, err = child("forwarded", GEN9BLAS_BLAS="cpu", GEN9BLAS_BLAS_INFO="1")
+    assert res["zgemm_forwarded"] < 1e-12
+    res, err = child("cblas_gemm", GEN9BLAS_BLAS="cpu", GEN9BLAS_BLAS_INFO="1")
+    assert res["sgemm_vs_ref_cblas"] <= 1e-6 and res["dgemm_vs_ref_cblas"] <= 1e-13
+    assert "-> GPU" not in err and "sgemm -> CPU" in err
+
+
+@pytest.mark.gpu
+def test_gpu_gemm_matches_reference_cblas():
+    res, err = child("cblas_gemm", GEN9BLAS_BLAS="gpu", GEN9BLAS_BLAS_INFO="1")
+    assert res["sgemm_vs_ref_cblas"] <= 2e-6, res
+    assert res["dgemm_vs_ref_cblas"] <= 1e-13, res
+    assert "sgemm -> GPU" in err and "dgemm -> GPU" in err and "-> CPU" not in err
+
+
+@pytest.mark.gpu
+def test_gpu_fortran_and_level12():
+    res, err = child("fortran_l12", GEN9BLAS_BLAS_INFO="1")
+    for tag, tol in (("s", 1e-5), ("d", 1e-12)):   # lib/test_blas.py:55-60, lib/test_blas_d.py:1-7
+        for k in ("gemm_fortran", "gemv", "ger", "axpy", "dot", "nrm2", "asum"):
+            assert res[tag + k] <= tol, (tag + k, res[tag + k])
+        assert res[f"i{tag}amax_exact"]
+    for f in ("sgemm_", "dgemm_", "sgemv", "dger", "saxpy", "ddot", "snrm2", "dasum", "isamax"):
+        assert f"{f} -> GPU" in err, f
+    assert "-> CPU" not in err
+    res, err = child("forwarded")
+    assert res["zgemm_forwarded"] < 1e-12
