@@ -219,11 +219,13 @@ def profile_traffic(name):
 
 
 def measured_peaks():
+    """(dense bf16 TF/s for a kernel timed inside a long power-capped run, HBM GB/s, kind). The timed loops of this
+    benchmark run for about half a second back to back, so the sustained figure is the denominator."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         d = json.load(open(p))
-        return d.get("bf16_tflops"), d.get("hbm_gbs"), "measured"
-    return 1590.0, 6650.0, "fallback"
+        return d.get("bf16_tflops_sustained") or d.get("bf16_tflops"), d.get("hbm_gbs"), "measured"
+    return 1400.0, 6650.0, "fallback"
 
 
 def run_ours(args):
@@ -315,7 +317,8 @@ def run_ours(args):
         roof = {"bound": "tensor", "achieved": round(value, 2), "peak": peak_t, "unit": "TFLOP/s",
                 "frac": round(value / peak_t, 4), "traffic": traffic, "kernel": "hgemm_tc_kernel<true>",
                 "algorithmic": f"2*n^3 = {flops:.4g} FLOP per launch, one launch per step",
-                "peak_kind": f"{peak_kind} bf16 dense (burst; kernel timed alone), MEASURED_PEAKS.json"}
+                "peak_kind": f"{peak_kind} cuBLAS bf16 dense, sustained (the timed loop runs ~0.5 s under the 1 kW "
+                             "power cap), MEASURED_PEAKS.json"}
         cpu = None
         if rank == 0 and world == 1 and not args.no_cpu:
             v, kind, calls, threads, sample = cpu_sgemm_sample(n)

@@ -23,6 +23,7 @@
 #include "internal.h"
 #include "sm100.cuh"
 #include <cudaTypedefs.h>
+#include <cstdlib>
 
 namespace g9 {
 using namespace sm100;
@@ -47,6 +48,12 @@ struct TcParams {
     long long ldc, sC;
     int c_vec;                // C base 16-byte aligned and ldc % 8 == 0
     unsigned *err;
+    // split-K tail of the pair kernel: tiles [dp_tiles, total_tiles) are split into `split` K ranges; part 0 adds
+    // the FP32 partial sums that parts 1..split-1 leave in `partial`, after their flags carry `epoch`.
+    int dp_tiles, split, units;
+    float *partial;
+    unsigned *flags;
+    unsigned epoch;
 };
 
 __device__ __forceinline__ void tile_coords(const TcParams &p, int tile, int &b, int &mb, int &nb) {
@@ -68,16 +75,12 @@ __device__ __forceinline__ void report_timeout(const TcParams &p, volatile int *
     __threadfence_system();
 }
 
-// Epilogue of one 32-column chunk of one row: v = alpha·acc + beta·C, rounded once to FP16.
-template <bool F16ACC>
-__device__ __forceinline__ void store_chunk(const TcParams &p, const uint32_t *r, __half *crow, int col0, bool row_ok) {
-    if (!row_ok) return;
-    float v[32];
+// Accumulator chunk (32 columns of one row, as loaded from TMEM) widened to FP32.
+template <bool F16ACC> __device__ __forceinline__ void acc_to_f32(const uint32_t *r, float *v) {
     if (F16ACC) {
 #pragma unroll
         for (int j = 0; j < 16; j++) {
-            __half2 h = *reinterpret_cast<const __half2 *>(&r[j]);
-            float2 f = __half22float2(h);
+            float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&r[j]));
             v[2 * j] = f.x;
             v[2 * j + 1] = f.y;
         }
@@ -85,15 +88,13 @@ __device__ __forceinline__ void store_chunk(const TcParams &p, const uint32_t *r
 #pragma unroll
         for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
     }
-    const bool full = col0 + 32 <= p.N;
+}
+
+// Stores 32 columns of one row: alpha·v + beta·C, rounded once to FP16 (beta = 0: C is not read).
+__device__ __forceinline__ void store_vals(const TcParams &p, const float *v, __half *crow, int col0) {
     __half *c = crow + col0;
-    if (full && p.c_vec) {
+    if (col0 + 32 <= p.N && p.c_vec) {
         uint4 *c4 = reinterpret_cast<uint4 *>(c);
-        if (F16ACC && p.plain) {
-#pragma unroll
-            for (int q = 0; q < 4; q++) c4[q] = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
-            return;
-        }
 #pragma unroll
         for (int q = 0; q < 4; q++) {
             float o[8];
@@ -126,6 +127,22 @@ __device__ __forceinline__ void store_chunk(const TcParams &p, const uint32_t *r
             }
         }
     }
+}
+
+// Epilogue of one 32-column chunk of one row straight from the TMEM registers. FP16 accumulators with alpha = 1,
+// beta = 0 are stored as they are (no widening).
+template <bool F16ACC>
+__device__ __forceinline__ void store_chunk(const TcParams &p, const uint32_t *r, __half *crow, int col0, bool row_ok) {
+    if (!row_ok) return;
+    if (F16ACC && p.plain && col0 + 32 <= p.N && p.c_vec) {
+        uint4 *c4 = reinterpret_cast<uint4 *>(crow + col0);
+#pragma unroll
+        for (int q = 0; q < 4; q++) c4[q] = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+        return;
+    }
+    float v[32];
+    acc_to_f32<F16ACC>(r, v);
+    store_vals(p, v, crow, col0);
 }
 
 template <bool F16ACC>
@@ -293,6 +310,313 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
 }
 
+// ------------------------------------------------------------------------------------------------ CTA-pair kernel
+// Same roles and bounded waits as hgemm_tc_kernel, on a cluster of 2 CTAs that computes 256×256 tiles with
+// tcgen05.mma.cta_group::2 (M = 256 across the pair's TMEM, N = 256). Each CTA stages only its half of the operands
+// per K-block (A: its 128 rows, B: its 128 of the 256 columns), 32 KiB per stage instead of 48 KiB for a 128×256
+// tile: half the shared-memory fill traffic per FLOP. Protocol of the pair:
+// - full[s] of the leader (rank 0) counts the TMA bytes of both CTAs (cta_group::2 loads name the leader's
+//   barrier); the leader's producer arms it with the pair's byte count;
+// - the leader's MMA thread releases a stage in both CTAs with one multicast commit to empty[s], and hands a
+//   finished accumulator to both epilogues with a multicast commit to tfull[b];
+// - every epilogue warp of both CTAs arrives (cluster scope) on the leader's tempty[b];
+// - a cluster barrier after the barrier setup and before TMEM is freed keeps both CTAs alive while the pair's MMAs
+//   read their shared memory. No TMA multicast is used.
+constexpr int T2_BM = 256;
+constexpr int T2_A_BYTES = 128 * TC_BK * 2;   // this CTA's 128 rows of A, 16 KiB
+
+// Tile width BN (256 or 128) sets the shared-memory ring and the number of TMEM accumulators (512 / BN columns).
+template <int BN> struct PairCfg {
+    static constexpr int B_BYTES = (BN / 2) * TC_BK * 2;          // this CTA's BN/2 columns of B
+    static constexpr int STAGE_BYTES = T2_A_BYTES + B_BYTES;
+    static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;   // 6 (BN 256) or 8 (BN 128)
+    static constexpr int NBUF = 512 / BN;                       // TMEM accumulators
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 512;
+};
+
+__device__ __forceinline__ void tile_coords_pair(const TcParams &p, int tile, int &b, int &mb, int &nb) {
+    const int per_batch = p.tiles_m * p.tiles_n;
+    b = tile / per_batch;
+    const int r = tile - b * per_batch;
+    const int group_span = TC_GROUP_M * p.tiles_n;
+    const int group = r / group_span;
+    const int first_m = group * TC_GROUP_M;
+    const int gsz = min(p.tiles_m - first_m, TC_GROUP_M);
+    const int in_group = r - group * group_span;
+    mb = first_m + in_group % gsz;
+    nb = in_group / gsz;
+}
+
+// One unit of work of a CTA pair: a whole tile (part -1) or one K range of a split tail tile (part 0 finishes the
+// tile, parts 1.. leave FP32 partial sums for it).
+struct PairUnit {
+    int tile, kb0, kb1, part;
+};
+__device__ __forceinline__ PairUnit pair_unit(const TcParams &p, int u, int nk) {
+    PairUnit w;
+    if (u < p.dp_tiles) {
+        w.tile = u; w.kb0 = 0; w.kb1 = nk; w.part = -1;
+    } else {
+        const int v = u - p.dp_tiles;
+        w.tile = p.dp_tiles + v / p.split;
+        w.part = v % p.split;
+        w.kb0 = (int)((long long)nk * w.part / p.split);
+        w.kb1 = (int)((long long)nk * (w.part + 1) / p.split);
+    }
+    return w;
+}
+__device__ __forceinline__ int partial_slot(const TcParams &p, int tile, int part, uint32_t rank) {
+    return ((tile - p.dp_tiles) * (p.split - 1) + (part - 1)) * 2 + (int)rank;
+}
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *a) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_gpu(unsigned *a, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ void epilogue_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+template <bool F16ACC, int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
+    hgemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const TcParams p) {
+    using Cfg = PairCfg<BN>;
+    constexpr int STAGES = Cfg::STAGES, NBUF = Cfg::NBUF;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t *smem = smem_raw + (((raw + 1023) & ~1023u) - raw);
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + STAGES * T2_A_BYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * Cfg::STAGE_BYTES);
+    uint64_t *full = bars;
+    uint64_t *empty = bars + STAGES;
+    uint64_t *tfull = bars + 2 * STAGES;
+    uint64_t *tempty = bars + 2 * STAGES + NBUF;
+    uint64_t *drain = bars + 2 * STAGES + 2 * NBUF;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < NBUF; b++) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 8);   // 4 epilogue warps in each CTA of the pair
+        }
+        mbar_init(drain, 1);
+        *abort = 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, TC_TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();   // both CTAs' barriers are initialised before any cross-CTA arrive
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int nk = (p.K + TC_BK - 1) / TC_BK;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- TMA producer (both CTAs): this CTA's halves, bytes counted on the leader's full[s]
+        int stage = 0;
+        uint32_t phase = 0;
+        long long issued = 0;
+        bool ok = true;
+        for (int u = cluster; u < p.units && ok; u += nclusters) {
+            const PairUnit w = pair_unit(p, u, nk);
+            int b, mb, nb;
+            tile_coords_pair(p, w.tile, b, mb, nb);
+            const int m0 = mb * T2_BM + 128 * rank, n0 = nb * BN + (BN / 2) * rank;
+            for (int kb = w.kb0; kb < w.kb1; kb++) {
+                if (!mbar_wait_cluster(&empty[stage], phase ^ 1, abort, TC_WAIT_NS)) { ok = false; break; }
+                if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
+                const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+                uint8_t *a = sA + stage * T2_A_BYTES;
+                uint8_t *bb = sB + stage * Cfg::B_BYTES;
+                const int k0 = kb * TC_BK;
+                if (!p.a_mn) {
+                    tma_load_3d_pair(a, &tmA, bar, k0, m0, b);
+                } else {
+                    tma_load_3d_pair(a, &tmA, bar, m0, k0, b);
+                    tma_load_3d_pair(a + 8192, &tmA, bar, m0 + 64, k0, b);
+                }
+                if (!p.b_mn) {
+                    tma_load_3d_pair(bb, &tmB, bar, k0, n0, b);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < BN / 128; j++) tma_load_3d_pair(bb + 8192 * j, &tmB, bar, n0 + 64 * j, k0, b);
+                }
+                issued++;
+                if (++stage == STAGES) { stage = 0; phase ^= 1; }
+            }
+        }
+        if (!ok) {
+            report_timeout(p, abort);
+            // Wait (bounded) until the pair's MMAs released the stages this CTA filled, so no copy is in flight.
+            const int outstanding = (int)(issued < STAGES ? issued : STAGES);
+            for (int i = 1; i <= outstanding; i++) {
+                int s = stage - i;
+                uint32_t ph = phase;
+                if (s < 0) { s += STAGES; ph ^= 1; }
+                volatile int no_abort = 0;
+                mbar_wait_cluster(&empty[s], ph, &no_abort, 100000000ull);
+            }
+        }
+    } else if (warp == 1 && lane == 0 && rank == 0) {
+        // ---------------- MMA issuer (leader CTA only)
+        const uint32_t idesc = idesc_f16(F16ACC ? 0 : 1, p.a_mn, p.b_mn, T2_BM, BN);
+        int stage = 0;
+        uint32_t phase = 0;
+        int local = 0;
+        bool ok = true;
+        for (int u = cluster; u < p.units && ok; u += nclusters, local++) {
+            const PairUnit w = pair_unit(p, u, nk);
+            const int buf = local % NBUF;
+            const uint32_t acc_phase = (local / NBUF) & 1;
+            if (!mbar_wait_cluster(&tempty[buf], acc_phase ^ 1, abort, TC_WAIT_NS)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + buf * BN;
+            for (int kb = w.kb0; kb < w.kb1; kb++) {
+                if (!mbar_wait_cluster(&full[stage], phase, abort, TC_WAIT_NS)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t a_base = smem_u32(sA + stage * T2_A_BYTES);
+                const uint32_t b_base = smem_u32(sB + stage * Cfg::B_BYTES);
+#pragma unroll
+                for (int k = 0; k < TC_BK / 16; k++) {
+                    const uint64_t ad = p.a_mn ? smem_desc_sw128(a_base + k * 2048, 8192, 1024)
+                                               : smem_desc_sw128(a_base + k * 32, 16, 1024);
+                    const uint64_t bd = p.b_mn ? smem_desc_sw128(b_base + k * 2048, 8192, 1024)
+                                               : smem_desc_sw128(b_base + k * 32, 16, 1024);
+                    umma_f16_pair(d_tmem, ad, bd, idesc, (kb > w.kb0 || k > 0) ? 1u : 0u);
+                }
+                umma_commit_pair_mc(&empty[stage], 0x3);
+                if (++stage == STAGES) { stage = 0; phase ^= 1; }
+            }
+            if (!ok) break;
+            umma_commit_pair_mc(&tfull[buf], 0x3);
+        }
+        if (!ok) report_timeout(p, abort);
+        umma_commit_pair(drain);
+        volatile int no_abort = 0;
+        mbar_wait(drain, 0, &no_abort, 100000000ull);
+    } else if (warp >= 2) {
+        // ---------------- epilogue (both CTAs): this CTA's 128 rows of the 256×BN tile
+        const int q = warp & 3;
+        const int row_local = q * 32 + lane;
+        const int row_in_tile = 128 * rank + row_local;
+        int local = 0;
+        for (int u = cluster; u < p.units; u += nclusters, local++) {
+            const PairUnit w = pair_unit(p, u, nk);
+            int b, mb, nb;
+            tile_coords_pair(p, w.tile, b, mb, nb);
+            const int buf = local % NBUF;
+            const uint32_t acc_phase = (local / NBUF) & 1;
+            if (!mbar_wait_cluster(&tfull[buf], acc_phase, abort, TC_WAIT_NS)) {
+                report_timeout(p, abort);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
+            if (w.part > 0) {
+                // contributor: FP32 partial sums of this K range to the slot of (tile, part, rank), then its flag
+                float *dst = p.partial + (size_t)partial_slot(p, w.tile, w.part, rank) * (128 * BN) + (size_t)row_local * BN;
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; c++) {
+                    uint32_t r[32];
+                    if (F16ACC) tmem_ld_32x32_pack16(t_row + c * 32, r);
+                    else tmem_ld_32x32(t_row + c * 32, r);
+                    tmem_ld_wait();
+                    float v[32];
+                    acc_to_f32<F16ACC>(r, v);
+                    float4 *d4 = reinterpret_cast<float4 *>(dst + c * 32);
+#pragma unroll
+                    for (int j = 0; j < 8; j++) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                }
+                epilogue_bar();
+                if (threadIdx.x == 64) {
+                    __threadfence();
+                    st_release_gpu(p.flags + partial_slot(p, w.tile, w.part, rank), p.epoch);
+                }
+            } else {
+                const int row = mb * T2_BM + row_in_tile;
+                const bool row_ok = row < p.M;
+                __half *crow = p.C + (long long)b * p.sC + (long long)(row_ok ? row : 0) * p.ldc;
+                bool have = true;
+                if (w.part == 0) {
+                    // finisher: wait (bounded) until every other part of this tile has left its partial sums
+                    for (int j = 1; j < p.split && have; j++) {
+                        const unsigned *f = p.flags + partial_slot(p, w.tile, j, rank);
+                        if (ld_acquire_gpu(f) != p.epoch) {
+                            const uint64_t t0 = globaltimer();
+                            while (ld_acquire_gpu(f) != p.epoch) {
+                                if (*abort || globaltimer() - t0 > TC_WAIT_NS) { have = false; break; }
+                            }
+                        }
+                    }
+                    if (!have) report_timeout(p, abort);
+                }
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; c++) {
+                    const int col0 = nb * BN + c * 32;
+                    uint32_t r[32];
+                    if (F16ACC) tmem_ld_32x32_pack16(t_row + c * 32, r);
+                    else tmem_ld_32x32(t_row + c * 32, r);
+                    tmem_ld_wait();
+                    if (!have || col0 >= p.N || !row_ok) continue;
+                    if (w.part < 0) {
+                        store_chunk<F16ACC>(p, r, crow, col0, row_ok);
+                    } else {
+                        float v[32];
+                        acc_to_f32<F16ACC>(r, v);
+                        for (int j = 1; j < p.split; j++) {
+                            const float4 *s4 = reinterpret_cast<const float4 *>(
+                                p.partial + (size_t)partial_slot(p, w.tile, j, rank) * (128 * BN) + (size_t)row_local * BN +
+                                c * 32);
+#pragma unroll
+                            for (int e = 0; e < 8; e++) {
+                                const float4 t = s4[e];
+                                v[4 * e] += t.x; v[4 * e + 1] += t.y; v[4 * e + 2] += t.z; v[4 * e + 3] += t.w;
+                            }
+                        }
+                        store_vals(p, v, crow, col0);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[buf]), 0));
+        }
+    }
+    __syncthreads();
+    cluster_sync();   // the pair's MMAs (drained by the leader) no longer read either CTA's shared memory
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, TC_TMEM_COLS);
+    }
+}
+
+template <bool F16ACC, int BN>
+static int launch_pair(const CUtensorMap &mA, const CUtensorMap &mB, const TcParams &p, int grid, cudaStream_t st) {
+    static bool attr = false;
+    if (!attr) {
+        G9_CU(cudaFuncSetAttribute(hgemm_tc2_kernel<F16ACC, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   PairCfg<BN>::SMEM));
+        attr = true;
+    }
+    hgemm_tc2_kernel<F16ACC, BN><<<grid, TC_THREADS, PairCfg<BN>::SMEM, st>>>(mA, mB, p);
+    return launched("hgemm_tc2");
+}
+
 // ------------------------------------------------------------------------------------------------ repack
 // Copies a rows × cols FP16 matrix (row pitch ld, batch stride s) into a dense layout with a row pitch that is a
 // multiple of 8 elements (16 bytes), so that TMA can read it. Used only when the caller's strides are not TMA-legal.
@@ -331,47 +655,63 @@ int launch_hgemm_tc(int type, int tA, int tB, int M, int N, int K, double alpha,
                     cudaStream_t st) {
     DevState *d = dev_state();
     if (!d) return G.status;
+    // GEN9BLAS_HGEMM_PAIR: 0 keeps the one-CTA kernel, 128 / 256 force the pair tile width (comparisons).
+    static int pair_env = -1;
+    if (pair_env < 0) {
+        const char *e = getenv("GEN9BLAS_HGEMM_PAIR");
+        pair_env = e ? atoi(e) : 1;
+    }
+    const bool pair = pair_env && M > 128;
+    const int bn = pair_env == 128 ? 128 : 256;
+    const int pairs = d->sm_count / 2;
+    const int nk = (K + TC_BK - 1) / TC_BK;
+    // Work plan of the pair kernel: whole tiles while full waves of CTA pairs remain; when the last wave would leave
+    // at least half of the pairs idle, its tiles are split along K over them (split-K tail, FP32 partials).
+    long long tiles = 0, dp = 0, units = 0;
+    int split = 1;
+    if (pair) {
+        tiles = (long long)((M + T2_BM - 1) / T2_BM) * ((N + bn - 1) / bn) * count;
+        const long long waves = tiles / pairs, tail = tiles % pairs;
+        if (tail > 0 && waves >= 1 && 2 * tail <= pairs && nk >= 4) {
+            split = (int)(pairs / tail);
+            if (split > 4) split = 4;
+            if (split > nk / 2) split = nk / 2;
+        }
+        dp = split > 1 ? tiles - tail : tiles;
+        units = dp + (tiles - dp) * split;
+    }
+    const size_t partial_bytes = pair && split > 1 ? (size_t)(tiles - dp) * (split - 1) * 2 * 128 * bn * sizeof(float) : 0;
+
     // Stored shapes: A is rowsA × colsA with pitch lda (tA: K × M, else M × K); B is rowsB × colsB (tB: N × K, else K × N).
     const long long rowsA = tA ? K : M, colsA = tA ? M : K;
     const long long rowsB = tB ? N : K, colsB = tB ? K : N;
     const void *a = A, *b = B;
     long long la = lda, lb = ldb, xa = sA, xb = sB;
-    if (!tma_ok(A, lda, sA, count) || !tma_ok(B, ldb, sB, count)) {
-        const long long pa = (colsA + 7) / 8 * 8, pb = (colsB + 7) / 8 * 8;
-        const long long bytesA = tma_ok(A, lda, sA, count) ? 0 : ((rowsA * pa * count * 2 + 255) / 256 * 256);
-        const long long bytesB = tma_ok(B, ldb, sB, count) ? 0 : rowsB * pb * count * 2;
-        void *scr = nullptr;
-        G9_TRY(scratch((size_t)(bytesA + bytesB), &scr));
-        if (bytesA) {
-            repack_f16<<<d->sm_count * 8, 256, 0, st>>>((const __half *)A, lda, sA, (int)rowsA, (int)colsA, (__half *)scr, pa,
-                                                       rowsA * pa, count);
-            G9_TRY(launched("repack_f16"));
-            a = scr; la = pa; xa = rowsA * pa;
-        }
-        if (bytesB) {
-            __half *dstB = (__half *)((char *)scr + bytesA);
-            repack_f16<<<d->sm_count * 8, 256, 0, st>>>((const __half *)B, ldb, sB, (int)rowsB, (int)colsB, dstB, pb,
-                                                       rowsB * pb, count);
-            G9_TRY(launched("repack_f16"));
-            b = dstB; lb = pb; xb = rowsB * pb;
-        }
+    const bool okA = tma_ok(A, lda, sA, count), okB = tma_ok(B, ldb, sB, count);
+    const long long pa = (colsA + 7) / 8 * 8, pb = (colsB + 7) / 8 * 8;
+    const long long bytesA = okA ? 0 : (rowsA * pa * count * 2 + 255) / 256 * 256;
+    const long long bytesB = okB ? 0 : (rowsB * pb * count * 2 + 255) / 256 * 256;
+    void *scr = nullptr;
+    if (bytesA + bytesB + (long long)partial_bytes > 0) G9_TRY(scratch((size_t)(bytesA + bytesB) + partial_bytes, &scr));
+    if (bytesA) {
+        repack_f16<<<d->sm_count * 8, 256, 0, st>>>((const __half *)A, lda, sA, (int)rowsA, (int)colsA, (__half *)scr, pa,
+                                                   rowsA * pa, count);
+        G9_TRY(launched("repack_f16"));
+        a = scr; la = pa; xa = rowsA * pa;
+    }
+    if (bytesB) {
+        __half *dstB = (__half *)((char *)scr + bytesA);
+        repack_f16<<<d->sm_count * 8, 256, 0, st>>>((const __half *)B, ldb, sB, (int)rowsB, (int)colsB, dstB, pb,
+                                                   rowsB * pb, count);
+        G9_TRY(launched("repack_f16"));
+        b = dstB; lb = pb; xb = rowsB * pb;
     }
     if (count == 1) {   // a batch stride is still required by the 3-D map; any legal value works
         xa = (rowsA * la + 7) / 8 * 8;
         xb = (rowsB * lb + 7) / 8 * 8;
     }
-    CUtensorMap mA, mB;
-    // K-major operands: box 64 (K) × rows; MN-major operands: box 64 (M or N) × 64 (K).
-    if (!tA) G9_TRY(encode_map(&mA, a, K, M, la, count, xa, TC_BK, TC_BM));
-    else G9_TRY(encode_map(&mA, a, M, K, la, count, xa, 64, TC_BK));
-    if (tB) G9_TRY(encode_map(&mB, b, K, N, lb, count, xb, TC_BK, TC_BN));
-    else G9_TRY(encode_map(&mB, b, N, K, lb, count, xb, 64, TC_BK));
-
     TcParams p;
     p.M = M; p.N = N; p.K = K; p.count = count;
-    p.tiles_m = (M + TC_BM - 1) / TC_BM;
-    p.tiles_n = (N + TC_BN - 1) / TC_BN;
-    p.total_tiles = p.tiles_m * p.tiles_n * count;
     p.a_mn = tA ? 1 : 0;
     p.b_mn = tB ? 0 : 1;
     p.alpha = (float)alpha;
@@ -382,6 +722,42 @@ int launch_hgemm_tc(int type, int tA, int tB, int M, int N, int K, double alpha,
     p.sC = sC;
     p.c_vec = ((uintptr_t)C & 15) == 0 && (ldc % 8) == 0 && (count == 1 || (sC % 8) == 0);
     p.err = d->err_dev;
+    p.dp_tiles = p.split = p.units = 0;
+    p.partial = nullptr;
+    p.flags = nullptr;
+    p.epoch = 0;
+    CUtensorMap mA, mB;
+    // K-major operands: box 64 (K) × rows; MN-major operands: box 64 (M or N) × 64 (K).
+    if (!tA) G9_TRY(encode_map(&mA, a, K, M, la, count, xa, TC_BK, pair ? 128 : TC_BM));
+    else G9_TRY(encode_map(&mA, a, M, K, la, count, xa, 64, TC_BK));
+    if (tB) G9_TRY(encode_map(&mB, b, K, N, lb, count, xb, TC_BK, pair ? bn / 2 : TC_BN));
+    else G9_TRY(encode_map(&mB, b, N, K, lb, count, xb, 64, TC_BK));
+
+    if (pair) {
+        p.tiles_m = (M + T2_BM - 1) / T2_BM;
+        p.tiles_n = (N + bn - 1) / bn;
+        p.total_tiles = (int)tiles;
+        p.dp_tiles = (int)dp;
+        p.split = split;
+        p.units = (int)units;
+        if (split > 1) {
+            if (!d->gemm_flags) {
+                G9_CU(cudaMalloc((void **)&d->gemm_flags, 4096 * sizeof(unsigned)));
+                G9_CU(cudaMemsetAsync(d->gemm_flags, 0, 4096 * sizeof(unsigned), st));
+            }
+            if (++d->gemm_epoch == 0) d->gemm_epoch = 1;
+            p.partial = (float *)((char *)scr + bytesA + bytesB);
+            p.flags = d->gemm_flags;
+            p.epoch = d->gemm_epoch;
+        }
+        const int grid2 = 2 * (int)(units < pairs ? units : pairs);
+        if (type == GEN9BLAS_H) return bn == 256 ? launch_pair<true, 256>(mA, mB, p, grid2, st)
+                                                 : launch_pair<true, 128>(mA, mB, p, grid2, st);
+        return bn == 256 ? launch_pair<false, 256>(mA, mB, p, grid2, st) : launch_pair<false, 128>(mA, mB, p, grid2, st);
+    }
+    p.tiles_m = (M + TC_BM - 1) / TC_BM;
+    p.tiles_n = (N + TC_BN - 1) / TC_BN;
+    p.total_tiles = p.tiles_m * p.tiles_n * count;
     const int grid = p.total_tiles < d->sm_count ? p.total_tiles : d->sm_count;
     if (type == GEN9BLAS_H) {
         static bool attr = false;

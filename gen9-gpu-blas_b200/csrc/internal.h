@@ -33,6 +33,8 @@ struct DevState {
     unsigned *err_host = nullptr;                              // mapped pinned word: device-side error code
     unsigned *err_dev = nullptr;                               // its device address
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    unsigned *gemm_flags = nullptr;                            // split-K handoff flags of the HGEMM pair kernel (zeroed)
+    unsigned gemm_epoch = 0;                                   // launch counter written into those flags
 };
 
 // Process-wide call state (the caller serialises calls, as for the reference).

@@ -166,3 +166,25 @@ def test_large_sampled_rows(g9, name, dt, accurate, tol_avg, tol_max):
     avg, mx = gemm_error(C[rows], a64 @ b64, np.abs(a64) @ np.abs(b64))
     lim_max = 1e-3 if dt == np.float16 else tol_max
     assert mx <= lim_max and avg <= (1e-4 if accurate else tol_avg), (name, avg, mx)
+
+
+@pytest.mark.parametrize("t", [abi.H, abi.HS])
+def test_hgemm_split_k_tail(gpu_lib, t):
+    """Shapes whose last wave of 256×256 tiles is split along K over idle CTA pairs (2, 3 or 4 parts, uneven K
+    ranges, edge columns, alpha/beta): the finishing part adds the other parts' FP32 partial sums."""
+    rng = np.random.default_rng(21)
+    for (M, N, K, al, be) in ((3072, 1792, 1024, 1.0, 0.0), (2304, 2304, 520, 1.5, -0.5), (1000, 5000, 300, 1.0, 1.0),
+                              (4096, 4096, 4096, 0.5, 0.25)):
+        A = (rng.standard_normal((M, K)) / np.sqrt(K)).astype(np.float16)
+        B = (rng.standard_normal((K, N)) / np.sqrt(K)).astype(np.float16)
+        C0 = rng.uniform(-1, 1, (M, N)).astype(np.float16)
+        C = C0.copy()
+        for _ in range(2):   # twice: the handoff flags carry a per-launch epoch
+            C[...] = C0
+            assert gpu_lib.gemm(t, 0, 0, M, N, K, al, A.ctypes.data, K, B.ctypes.data, N, be, C.ctypes.data, N) == 0
+            rows = np.concatenate([np.arange(0, M, max(1, M // 97)), [M - 1]])
+            a64, b64 = A[rows].astype(np.float64), B.astype(np.float64)
+            ref = al * a64 @ b64 + be * C0[rows].astype(np.float64)
+            scale = abs(al) * np.abs(a64) @ np.abs(b64) + abs(be) * np.abs(C0[rows].astype(np.float64))
+            avg, mx = gemm_error(C[rows], ref, scale)
+            assert mx <= 1e-3, (t, M, N, K, mx)
