@@ -111,13 +111,30 @@ __global__ void __launch_bounds__(kThreads) reduce_partial(long long n, const T 
         constexpr int W = V16<T>::W;
         using R = typename Compute<T>::R;
         const long long nv = n / W;
-        for (long long v = tid; v < nv; v += stride) {
+        double s2 = 0;   // second chain: two independent 16-byte loads (per operand) in flight per trip
+        long long v = tid;
+        for (; v + stride < nv; v += 2 * stride) {
+            R xv[W], yv[W], xw[W], yw[W];
+            load16<T>(x + v * W, xv);
+            load16<T>(x + (v + stride) * W, xw);
+            if (MODE == 0) {
+                load16<T>(y + v * W, yv);
+                load16<T>(y + (v + stride) * W, yw);
+            }
+#pragma unroll
+            for (int k = 0; k < W; k++) {
+                s += red_term<MODE>((double)xv[k], MODE == 0 ? (double)yv[k] : 0.0);
+                s2 += red_term<MODE>((double)xw[k], MODE == 0 ? (double)yw[k] : 0.0);
+            }
+        }
+        if (v < nv) {
             R xv[W], yv[W];
             load16<T>(x + v * W, xv);
             if (MODE == 0) load16<T>(y + v * W, yv);
 #pragma unroll
             for (int k = 0; k < W; k++) s += red_term<MODE>((double)xv[k], MODE == 0 ? (double)yv[k] : 0.0);
         }
+        s += s2;
         for (long long i = nv * W + tid; i < n; i += stride)
             s += red_term<MODE>((double)to_r(x[i]), MODE == 0 ? (double)to_r(y[i]) : 0.0);
     } else {
@@ -143,7 +160,7 @@ static int reduce_t(int mode, int n, const void *xv, long long ox, long long ix,
     const T *x = (const T *)xv + ox;
     const T *y = yv ? (const T *)yv + oy : x;
     const bool vec = ix == 1 && (mode != 0 || iy == 1) && (((uintptr_t)x | (uintptr_t)(mode == 0 ? y : x)) & 15) == 0;
-    const int g = vec ? grid_for(n / V16<T>::W + 1, 4) : grid_for(n, 4);
+    const int g = vec ? grid_for(n / V16<T>::W + 1, 8) : grid_for(n, 8);
     double *part = result_dev + 8;   // the scratch holds [result, pad..., partials]
 #define G9_RED(M)                                                                                          \
     if (vec) reduce_partial<T, M, true><<<g, kThreads, 0, st>>>(n, x, ix, y, iy, part);                   \
@@ -199,7 +216,23 @@ __global__ void __launch_bounds__(kThreads) iamax_partial(long long n, const T *
     if (VEC) {
         constexpr int W = V16<T>::W;
         const long long nv = n / W;
-        for (long long v = tid; v < nv; v += stride) {
+        long long v = tid;
+        for (; v + stride < nv; v += 2 * stride) {   // two loads in flight; scanned in index order
+            R xv[W], xw[W];
+            load16<T>(x + v * W, xv);
+            load16<T>(x + (v + stride) * W, xw);
+#pragma unroll
+            for (int k = 0; k < W; k++) {
+                const R a = fabs(xv[k]);
+                if (a > bv) { bv = a; bi = v * W + k; }
+            }
+#pragma unroll
+            for (int k = 0; k < W; k++) {
+                const R a = fabs(xw[k]);
+                if (a > bv) { bv = a; bi = (v + stride) * W + k; }
+            }
+        }
+        if (v < nv) {
             R xv[W];
             load16<T>(x + v * W, xv);
 #pragma unroll
@@ -238,7 +271,7 @@ static int iamax_t(int n, const void *xv, long long ox, long long ix, long long 
     using R = typename Compute<T>::R;
     const T *x = (const T *)xv + ox;
     const bool vec = ix == 1 && ((uintptr_t)x & 15) == 0;
-    const int g = vec ? grid_for(n / V16<T>::W + 1, 4) : grid_for(n, 4);
+    const int g = vec ? grid_for(n / V16<T>::W + 1, 8) : grid_for(n, 8);
     long long *pi = result_dev + 8;
     R *pv = reinterpret_cast<R *>(pi + g);
     if (vec) iamax_partial<T, true><<<g, kThreads, 0, st>>>(n, x, ix, pv, pi);
@@ -257,7 +290,8 @@ int launch_iamax(int type, int n, const void *x, long long ox, long long ix, lon
 // ------------------------------------------------------------------------------------------------ gemv N
 // One warp computes kRowsN rows; each lane reads 16-byte vectors of the rows and of x (x comes from L1: every warp
 // of the block walks the same columns). Sum order: per-lane partials, then a fixed shuffle tree.
-constexpr int kRowsN = 4;
+constexpr int kRowsN = 2;
+constexpr int kTripsN = 4;   // trips of 16-byte loads issued before their FMAs
 
 template <typename T>
 __device__ __forceinline__ void gemv_store(T *y, long long k, typename Compute<T>::R alpha, typename Compute<T>::R beta,
@@ -282,7 +316,24 @@ __global__ void __launch_bounds__(kThreads) gemv_n_kernel(int M, int N, typename
     if (VEC) {
         constexpr int W = V16<T>::W;
         const int nv = N / W;
-        for (int v = lane; v < nv; v += 32) {
+        int v = lane;
+        for (; v + 32 * (kTripsN - 1) < nv; v += 32 * kTripsN) {
+            R xv[kTripsN][W], av[kTripsN][kRowsN][W];
+#pragma unroll
+            for (int u = 0; u < kTripsN; u++) {
+                load16<T>(x + (long long)(v + 32 * u) * W, xv[u]);
+#pragma unroll
+                for (int r = 0; r < kRowsN; r++)
+                    load16<T>(a0 + (r < nr ? r : 0) * lda + (long long)(v + 32 * u) * W, av[u][r]);
+            }
+#pragma unroll
+            for (int u = 0; u < kTripsN; u++)
+#pragma unroll
+                for (int r = 0; r < kRowsN; r++)
+#pragma unroll
+                    for (int k = 0; k < W; k++) s[r] = fma_r(av[u][r][k], xv[u][k], s[r]);
+        }
+        for (; v < nv; v += 32) {
             R xv[W];
             load16<T>(x + (long long)v * W, xv);
 #pragma unroll

@@ -56,7 +56,6 @@ __device__ __forceinline__ void skinny_store(const SkinnyArgs &p, int m, int n, 
 
 // ------------------------------------------------------------------------------------------------ FP16, K-contiguous
 constexpr int WK_WARPS = 8;
-constexpr int WK_UNROLL = 4;   // 32-wide K steps per batch of loads
 
 __device__ __forceinline__ void mma_16816(float *d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                           uint32_t b1) {
@@ -81,8 +80,10 @@ __device__ __forceinline__ uint32_t word(const uint4 &v, int i) {
 
 // Requirements (checked on the host): K % 8 == 0, weight rows and token rows contiguous along K with 16-byte aligned
 // starts. grid = (ceil(Nc / 16), ceil(Mc / 16)).
-template <bool TWO_NTILES>
-__global__ void __launch_bounds__(WK_WARPS * 32) wk_f16_mma(const SkinnyArgs p) {
+// UNROLL 32-wide K steps are loaded before any is used: 8 with one token tile (M <= 8), 4 with two, which keeps 16
+// (or 8) independent 16-byte weight loads in flight per lane -- at decode shapes HBM needs ~100 KiB in flight per SM.
+template <bool TWO_NTILES, int UNROLL>
+__global__ void __launch_bounds__(WK_WARPS * 32, 2) wk_f16_mma(const SkinnyArgs p) {
     __shared__ float red[WK_WARPS][16][17];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
@@ -101,10 +102,10 @@ __global__ void __launch_bounds__(WK_WARPS * 32) wk_f16_mma(const SkinnyArgs p) 
     const int per_warp = (steps + WK_WARPS - 1) / WK_WARPS;
     const int s_beg = warp * per_warp, s_end = min(steps, s_beg + per_warp);
     float d0[4] = {0, 0, 0, 0}, d1[4] = {0, 0, 0, 0};
-    for (int s = s_beg; s < s_end; s += WK_UNROLL) {
-        uint4 wv0[WK_UNROLL], wv1[WK_UNROLL], av0[WK_UNROLL], av1[WK_UNROLL];
+    for (int s = s_beg; s < s_end; s += UNROLL) {
+        uint4 wv0[UNROLL], wv1[UNROLL], av0[UNROLL], av1[UNROLL];
 #pragma unroll
-        for (int u = 0; u < WK_UNROLL; u++) {
+        for (int u = 0; u < UNROLL; u++) {
             const int k = (s + u) * 32 + 8 * t;
             const bool in = s + u < s_end && k < p.K;
             wv0[u] = in ? ldg_nc16(w0 + k) : make_uint4(0, 0, 0, 0);
@@ -113,7 +114,7 @@ __global__ void __launch_bounds__(WK_WARPS * 32) wk_f16_mma(const SkinnyArgs p) 
             if (TWO_NTILES) av1[u] = in ? __ldg(reinterpret_cast<const uint4 *>(a1 + k)) : make_uint4(0, 0, 0, 0);
         }
 #pragma unroll
-        for (int u = 0; u < WK_UNROLL; u++) {
+        for (int u = 0; u < UNROLL; u++) {
 #pragma unroll
             for (int j = 0; j < 2; j++) {
                 const uint32_t A0 = word(wv0[u], 2 * j), A1 = word(wv1[u], 2 * j);
@@ -336,8 +337,8 @@ static int skinny_t(SkinnyArgs p, cudaStream_t st) {
             }
             if (sizeof(T) == 2) {
                 dim3 grid((p.Nc + 15) / 16, (p.Mc + 15) / 16);
-                if (p.Mc > 8) wk_f16_mma<true><<<grid, WK_WARPS * 32, 0, st>>>(p);
-                else wk_f16_mma<false><<<grid, WK_WARPS * 32, 0, st>>>(p);
+                if (p.Mc > 8) wk_f16_mma<true, 4><<<grid, WK_WARPS * 32, 0, st>>>(p);
+                else wk_f16_mma<false, 8><<<grid, WK_WARPS * 32, 0, st>>>(p);
                 return launched("skinny_wk_f16_mma");
             }
             const int mt = p.Mc <= 1 ? 1 : p.Mc <= 4 ? 4 : p.Mc <= 8 ? 8 : 16;
