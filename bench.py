@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--workload", default="auto", choices=["auto", "hgemm4096", "scaleout"])
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample (profiling runs)")
+    ap.add_argument("--gather", default="fused", choices=["fused", "nccl"],
+                    help="scale-out exchange: fused GEMM + NVLink stores (default) or NCCL all-gather")
     return ap.parse_args()
 
 
@@ -192,7 +194,7 @@ def run_reference(args):
             "cpu_baseline": {"value": round(v, 4), "unit": "TFLOP/s", "cores": threads, "kind": kind,
                              "sample": sample},
             "e2e": {"value": round(v, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -334,7 +336,7 @@ def run_ours(args):
     else:
         line = run_scaleout(args, L, torch, stream, barrier, rank, world, local)
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
@@ -342,80 +344,123 @@ def run_ours(args):
 
 
 def run_scaleout(args, L, torch, stream, barrier, rank, world, local):
-    """HGEMM n = 32768, B/C column-sharded, A replicated, C all-gathered (NCCL) and re-laid out."""
+    """HGEMM n = 32768, B/C column-sharded, A replicated, C all-gathered (NCCL) and re-laid out; plus the
+    tensor-parallel skinny GEMM (M = 8, W 32768 × 8192 FP16 row-sharded)."""
+    sys.path.insert(0, PKG)
+    import g9dist
     n = 32768
     steps = args.steps or 5
     warm = max(args.warmup or 3, 3)
     nb = n // world
     chunks = 4 if world > 1 else 1
-    cw = nb // chunks
     g = torch.Generator(device="cuda")
     g.manual_seed(7)   # same A on every rank
     A = torch.randn(n, n, device="cuda", generator=g, dtype=torch.float16).div_(n ** 0.5)
     g.manual_seed(100 + rank)
     Bs = torch.randn(n, nb, device="cuda", generator=g, dtype=torch.float16).div_(n ** 0.5)   # this rank's columns
     C = torch.empty(n, n, device="cuda", dtype=torch.float16)
-    # local result, chunk-major (N = 1 writes straight into C)
-    Cs = torch.empty(chunks, n, cw, device="cuda", dtype=torch.float16) if world > 1 else None
-    Cg = torch.empty(chunks, world, n, cw, device="cuda", dtype=torch.float16) if world > 1 else None
     comm = torch.cuda.Stream()
     flops = 2.0 * n * n * n
 
+    def local_gemm(Ap, Bp, Cp):
+        g9dist.gemm_local(L.dll, Ap, Bp, Cp)
+
+    fused = args.gather == "fused" and world > 1
+    peers = g9dist.PeerView(L.dll, C, rank, world) if fused else None
+
     def step():
         with torch.cuda.stream(stream):
-            for c in range(chunks):
-                dst, ldc = (Cs[c].data_ptr(), cw) if world > 1 else (C.data_ptr(), n)
-                r = L.gemm(H, 0, 0, n, cw, n, 1.0, A.data_ptr(), n, Bs[:, c * cw:].data_ptr(), nb, 0.0, dst, ldc)
-                if r:
-                    raise RuntimeError(L.error().decode())
-                if world > 1:
-                    ev = torch.cuda.Event()
-                    ev.record(stream)
-                    comm.wait_event(ev)
-                    with torch.cuda.stream(comm):
-                        torch.distributed.all_gather_into_tensor(Cg[c], Cs[c])
+            if fused:
+                g9dist.fused_column_sharded_gemm(L.dll, A, Bs, C, peers, rank, world)
+            else:
+                g9dist.column_sharded_gemm(A, Bs, C, rank, world, local_gemm, chunks=chunks, comm_stream=comm)
+
+    def timed(fn, k):
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        l0 = L.kernel_launches()
+        e0.record(stream)
+        for _ in range(k):
+            fn()
+        e1.record(stream)
+        e1.synchronize()
+        launches = L.kernel_launches() - l0
+        ms = torch.tensor([e0.elapsed_time(e1)], device="cuda")
         if world > 1:
-            stream.wait_stream(comm)
-            with torch.cuda.stream(stream):
-                # column block (rank q, chunk c) -> C[:, q*nb + c*cw : ... + cw]
-                C.view(n, world, chunks, cw).copy_(Cg.permute(2, 1, 0, 3))
+            torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+        barrier()
+        return float(ms.item()), launches
 
     for _ in range(warm):
         step()
-    barrier()
     clocks = ClockSampler(local)
     clocks.start()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    l0 = L.kernel_launches()
-    e0.record(stream)
-    for _ in range(steps):
-        step()
-    e1.record(stream)
-    e1.synchronize()
-    launches = L.kernel_launches() - l0
+    ms_total, launches = timed(step, steps)
     clk = clocks.stop()
-    ms = torch.tensor([e0.elapsed_time(e1)], device="cuda")
-    if world > 1:
-        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
-    barrier()
-    ms_total = float(ms.item())
     value = flops * steps / (ms_total * 1e-3) / 1e12
-    peak_t, _, peak_kind = measured_peaks()
+
+    # tensor-parallel skinny GEMM (decode): C (8 × 32768) = A · Wᵀ, W rows split over the ranks
+    Nw, Kw, Mw = 32768, 8192, 8
+    nr = Nw // world
+    Wsh = torch.randn(nr, Kw, device="cuda", generator=g, dtype=torch.float16).mul_(0.02)
+    Aw = torch.randn(Mw, Kw, device="cuda", generator=g, dtype=torch.float16)
+    Cw = torch.empty(Mw, Nw, device="cuda", dtype=torch.float16)
+
+    def local_skinny(Ap, Wp, Cp):
+        r = L.gemm(H, 0, 1, Ap.shape[0], Wp.shape[0], Ap.shape[1], 1.0, Ap.data_ptr(), Ap.stride(0), Wp.data_ptr(),
+                   Wp.stride(0), 0.0, Cp.data_ptr(), Cp.stride(0))
+        if r:
+            raise RuntimeError(L.error().decode())
+
+    def tp_step():
+        with torch.cuda.stream(stream):
+            g9dist.row_sharded_skinny(Aw, Wsh, Cw, rank, world, local_skinny)
+
+    for _ in range(5):
+        tp_step()
+    tp_ms, _ = timed(tp_step, 50)
+    tp_us = tp_ms * 1e3 / 50
+    if peers is not None:
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        peers.close()
+    peak_t, peak_hbm, peak_kind = measured_peaks()
     return {"metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": steps,
             "warmup": warm, "ms_per_step": round(ms_total / steps, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {"workload": "scaleout: BASELINE configs[4], HGEMM FP16 n=32768, A replicated, B/C column-"
-                                   f"sharded over {world} GPU(s), C all-gathered with NCCL in {chunks} chunk(s) "
-                                   "overlapped with the GEMM of the next chunk, then re-laid out row-major",
+                                   f"sharded over {world} GPU(s); " + (
+                                       "fused GEMM + all-gather: the epilogue stores every C tile into all ranks' C "
+                                       "over NVLink (CUDA IPC), one stream-ordered all-reduce per step" if fused else
+                                       f"C all-gathered with NCCL in {chunks} chunk(s) overlapped with the GEMM of the "
+                                       "next chunk, then re-laid out row-major"),
                        "n": n, "l2": "inputs larger than L2 (A alone 2 GiB)"},
             "roofline": {"bound": "tensor", "achieved": round(value / world, 2), "peak": peak_t, "unit": "TFLOP/s",
                          "frac": round(value / world / peak_t, 4), "traffic": None,
-                         "peak_kind": f"{peak_kind} bf16 dense per GPU; achieved = whole step per GPU incl. gather"},
+                         "peak_kind": f"{peak_kind} cuBLAS bf16 dense sustained, per GPU; achieved = whole step per "
+                                      "GPU including the gather"},
+            "skinny_tp": {"shape": "C(8x32768) = A(8x8192) * W^T, W 32768x8192 FP16 row-sharded", "us_per_step":
+                          round(tp_us, 2), "weight_GBps_per_gpu": round(nr * Kw * 2 / (tp_us * 1e-6) / 1e9, 1),
+                          "includes": "local skinny GEMM + NCCL all-gather of the outputs + re-layout"},
             "cpu_baseline": None, "e2e": None, "gpu_launches": launches, "clocks": clk}
 
 
+_OUT_FD = None
+
+
+def emit(line):
+    """Prints the result line on the original stdout (libraries such as NCCL print banners on fd 1 during the run,
+    which is redirected to stderr so that rank 0's stdout carries exactly one JSON line)."""
+    os.write(_OUT_FD if _OUT_FD is not None else 1, (json.dumps(line) + "\n").encode())
+
+
 def main():
+    global _OUT_FD
     args = parse()
+    sys.stdout.flush()
+    _OUT_FD = os.dup(1)
+    os.dup2(2, 1)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

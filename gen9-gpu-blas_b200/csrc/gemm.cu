@@ -11,7 +11,7 @@ namespace g9 {
 
 int launch_hgemm_tc(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, long long sA,
                     const void *B, int ldb, long long sB, double beta, void *C, int ldc, long long sC, int count,
-                    cudaStream_t st);
+                    cudaStream_t st, void *const *peers = nullptr, int npeers = 0, long long col_off = 0);
 int launch_gemm_simt(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, long long sA,
                      const void *B, int ldb, long long sB, double beta, void *C, int ldc, long long sC, int count,
                      cudaStream_t st);
@@ -59,6 +59,32 @@ GEN9BLAS_API int gen9blas_gemm_batched(int type, int tA, int tB, int M, int N, i
     G9_TRY(launch_gemm(type, tA, tB, M, N, K, alpha, op[0].dptr, lda, sA, op[1].dptr, ldb, sB, beta, op[2].dptr, ldc, sC,
                        count, stream()));
     int r = finish_op(op, 3);
+    timer_stop();
+    return r;
+}
+
+// Fused GEMM + all-gather for column-sharded multi-GPU GEMM: this rank computes its column block
+// C[:, col_offset : col_offset + N] = alpha·op(A)·op(B) (beta = 0) and its epilogue stores every finished tile into all
+// ranks' C (peer device pointers from gen9blas_ipc_open) over NVLink, overlapping the exchange with the next tiles.
+GEN9BLAS_API int gen9blas_gemm_allgather(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A,
+                                         int lda, const void *B, int ldb, void *const *rank_C, int nranks, int ldc,
+                                         int64_t col_offset) {
+    if (int e = begin_op()) return e;
+    if (type != GEN9BLAS_H && type != GEN9BLAS_HS)
+        return fail(GEN9BLAS_ERR_UNSUPPORTED, "gen9blas_gemm_allgather supports FP16 (GEN9BLAS_H / GEN9BLAS_HS)");
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    if (!rank_C || nranks < 1 || nranks > 8) return fail(GEN9BLAS_ERR_INVALID_ARG, "1..8 destination buffers required");
+    if (col_offset < 0 || ldc < col_offset + N) return fail(GEN9BLAS_ERR_INVALID_ARG, "ldc < col_offset + N");
+    timer_start();
+    Operand op[2];
+    const size_t es = 2;
+    G9_TRY(map_operand(op[0], A, ((tA ? (size_t)(K - 1) * lda + M : (size_t)(M - 1) * lda + K)) * es, 0, true, false));
+    G9_TRY(map_operand(op[1], B, ((tB ? (size_t)(N - 1) * ldb + K : (size_t)(K - 1) * ldb + N)) * es, 1, true, false));
+    if (!op[0].zc || !op[1].zc) return fail(GEN9BLAS_ERR_INVALID_ARG, "gen9blas_gemm_allgather takes device operands");
+    timer_kernel();
+    G9_TRY(launch_hgemm_tc(type, tA ? 1 : 0, tB ? 1 : 0, M, N, K, alpha, op[0].dptr, lda, 0, op[1].dptr, ldb, 0, 0.0,
+                           rank_C[0], ldc, 0, 1, stream(), rank_C, nranks, col_offset));
+    int r = finish_op(op, 2);
     timer_stop();
     return r;
 }

@@ -54,6 +54,11 @@ struct TcParams {
     float *partial;
     unsigned *flags;
     unsigned epoch;
+    // destinations of the pair kernel's epilogue: the tile is written to every dst[q] (row-major, pitch ldc) at column
+    // col_off + n. One destination (C itself) for an ordinary GEMM; every rank's C for the fused GEMM + all-gather.
+    __half *dst[8];
+    int ndst;
+    long long col_off;
 };
 
 __device__ __forceinline__ void tile_coords(const TcParams &p, int tile, int &b, int &mb, int &nb) {
@@ -550,7 +555,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
             } else {
                 const int row = mb * T2_BM + row_in_tile;
                 const bool row_ok = row < p.M;
-                __half *crow = p.C + (long long)b * p.sC + (long long)(row_ok ? row : 0) * p.ldc;
+                const long long roff = (long long)b * p.sC + (long long)(row_ok ? row : 0) * p.ldc + p.col_off;
                 bool have = true;
                 if (w.part == 0) {
                     // finisher: wait (bounded) until every other part of this tile has left its partial sums
@@ -574,7 +579,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
                     tmem_ld_wait();
                     if (!have || col0 >= p.N || !row_ok) continue;
                     if (w.part < 0) {
-                        store_chunk<F16ACC>(p, r, crow, col0, row_ok);
+                        for (int q = 0; q < p.ndst; q++) store_chunk<F16ACC>(p, r, p.dst[q] + roff, col0, row_ok);
                     } else {
                         float v[32];
                         acc_to_f32<F16ACC>(r, v);
@@ -588,9 +593,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
                                 v[4 * e] += t.x; v[4 * e + 1] += t.y; v[4 * e + 2] += t.z; v[4 * e + 3] += t.w;
                             }
                         }
-                        store_vals(p, v, crow, col0);
+                        for (int q = 0; q < p.ndst; q++) store_vals(p, v, p.dst[q] + roff, col0);
                     }
                 }
+                if (p.ndst > 1) __threadfence_system();   // peer stores ordered before the ranks' next barrier
             }
             tc_fence_before();
             __syncwarp();
@@ -652,16 +658,17 @@ static bool tma_ok(const void *p, long long ld, long long s, int count) {
 
 int launch_hgemm_tc(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, long long sA,
                     const void *B, int ldb, long long sB, double beta, void *C, int ldc, long long sC, int count,
-                    cudaStream_t st) {
+                    cudaStream_t st, void *const *peers, int npeers, long long col_off) {
     DevState *d = dev_state();
     if (!d) return G.status;
+    if (npeers > 8) return fail(GEN9BLAS_ERR_INVALID_ARG, "at most 8 ranks for the fused GEMM + all-gather");
     // GEN9BLAS_HGEMM_PAIR: 0 keeps the one-CTA kernel, 128 / 256 force the pair tile width (comparisons).
     static int pair_env = -1;
     if (pair_env < 0) {
         const char *e = getenv("GEN9BLAS_HGEMM_PAIR");
         pair_env = e ? atoi(e) : 1;
     }
-    const bool pair = pair_env && M > 128;
+    const bool pair = (pair_env && M > 128) || npeers > 0;
     const int bn = pair_env == 128 ? 128 : 256;
     const int pairs = d->sm_count / 2;
     const int nk = (K + TC_BK - 1) / TC_BK;
@@ -726,6 +733,17 @@ int launch_hgemm_tc(int type, int tA, int tB, int M, int N, int K, double alpha,
     p.partial = nullptr;
     p.flags = nullptr;
     p.epoch = 0;
+    p.dst[0] = (__half *)C;
+    p.ndst = 1;
+    p.col_off = 0;
+    if (peers && npeers > 0) {   // fused GEMM + all-gather: write the tile into every rank's C
+        for (int q = 0; q < npeers; q++) p.dst[q] = (__half *)peers[q];
+        p.ndst = npeers;
+        p.col_off = col_off;
+        bool al = (col_off % 8) == 0;
+        for (int q = 0; q < npeers; q++) al = al && ((uintptr_t)peers[q] & 15) == 0;
+        p.c_vec = p.c_vec && al;
+    }
     CUtensorMap mA, mB;
     // K-major operands: box 64 (K) × rows; MN-major operands: box 64 (M or N) × 64 (K).
     if (!tA) G9_TRY(encode_map(&mA, a, K, M, la, count, xa, TC_BK, pair ? 128 : TC_BM));

@@ -376,6 +376,69 @@ GEN9BLAS_API int gen9blas_set_stream(void *s) {
 
 GEN9BLAS_API void gen9blas_set_nowait(int on) { G.nowait = on != 0; }
 
+// ---- device buffers shared between the ranks' processes (CUDA IPC over NVLink / NVSwitch) ----
+GEN9BLAS_API void *gen9blas_dev_alloc(size_t bytes) {
+    if (begin_op()) return nullptr;
+    void *p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes ? bytes : 1);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        fail(GEN9BLAS_ERR_OUT_OF_MEMORY, "cudaMalloc(%zu) = %s", bytes, cudaGetErrorName(e));
+        return nullptr;
+    }
+    return p;
+}
+
+GEN9BLAS_API void gen9blas_dev_free(void *p) {
+    if (!p || gen9blas_init()) return;
+    cudaDeviceSynchronize();
+    if (cudaFree(p) != cudaSuccess) cudaGetLastError();
+}
+
+GEN9BLAS_API int gen9blas_ipc_handle(const void *dev_ptr, void *handle, int64_t *offset) {
+    if (int e = begin_op()) return e;
+    if (!dev_ptr || !handle || !offset) return fail(GEN9BLAS_ERR_INVALID_ARG, "NULL argument");
+    // The handle names the whole cudaMalloc allocation; the pointer's offset inside it travels alongside.
+    static PFN_cuMemGetAddressRange_v3020 range = nullptr;
+    if (!range) {
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", (void **)&range, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            return fail(GEN9BLAS_ERR, "cuMemGetAddressRange is not available from the driver");
+        }
+    }
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (range(&base, &size, (CUdeviceptr)dev_ptr) != CUDA_SUCCESS)
+        return fail(GEN9BLAS_ERR_INVALID_ARG, "not device memory of this process");
+    cudaIpcMemHandle_t h;
+    G9_CU(cudaIpcGetMemHandle(&h, (void *)base));
+    memcpy(handle, &h, sizeof h);
+    *offset = (int64_t)((CUdeviceptr)dev_ptr - base);
+    return 0;
+}
+
+GEN9BLAS_API void *gen9blas_ipc_open(const void *handle) {
+    if (begin_op()) return nullptr;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof h);
+    void *p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        fail(GEN9BLAS_ERR, "cudaIpcOpenMemHandle = %s", cudaGetErrorName(e));
+        return nullptr;
+    }
+    return p;
+}
+
+GEN9BLAS_API int gen9blas_ipc_close(void *peer_ptr) {
+    if (int e = begin_op()) return e;
+    G9_CU(cudaIpcCloseMemHandle(peer_ptr));
+    return 0;
+}
+
 GEN9BLAS_API int gen9blas_flush(void) {
     if (begin_op()) return G.status;
     G9_CU(cudaStreamSynchronize(stream()));

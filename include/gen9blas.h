@@ -167,6 +167,24 @@ GEN9BLAS_API int gen9blas_set_stream(void *cuda_stream);
  * (or any synchronisation of the stream). Calls with host operands still wait. */
 GEN9BLAS_API void gen9blas_set_nowait(int on);
 GEN9BLAS_API int gen9blas_flush(void);
+/* Multi-GPU, one process per GPU (no counterpart in the reference, which drives one device).
+ * Device buffers that other ranks write into: any cudaMalloc memory (gen9blas_dev_alloc, torch tensors). For a
+ * pointer into such memory gen9blas_ipc_handle fills a 64-byte CUDA IPC handle of its allocation and the pointer's
+ * byte offset in it (send both to the other ranks); gen9blas_ipc_open maps a peer's handle into this process and
+ * returns the allocation's base, usable by this rank's kernels over NVLink (add the offset). */
+GEN9BLAS_API void *gen9blas_dev_alloc(size_t bytes);
+GEN9BLAS_API void gen9blas_dev_free(void *p);
+GEN9BLAS_API int gen9blas_ipc_handle(const void *dev_ptr, void *handle64, int64_t *offset);
+GEN9BLAS_API void *gen9blas_ipc_open(const void *handle64);
+GEN9BLAS_API int gen9blas_ipc_close(void *peer_ptr);
+/* Fused GEMM + all-gather of a column-sharded FP16 GEMM (type GEN9BLAS_H or _HS): this rank computes its column block
+ * C[:, col_offset : col_offset + N] = alpha·op(A)·op(B) (M × N, beta = 0) and the tensor-core kernel's epilogue stores
+ * every finished tile into the C of all nranks ranks (rank_C: their device pointers, own C included, row pitch ldc)
+ * with plain NVLink stores, overlapping the exchange with the remaining tiles. A and B must be device memory. The
+ * caller synchronises the ranks (e.g. a barrier) before reading C. At most 8 ranks. */
+GEN9BLAS_API int gen9blas_gemm_allgather(int type, int transA, int transB, int M, int N, int K, double alpha,
+                                         const void *A, int lda, const void *B, int ldb, void *const *rank_C,
+                                         int nranks, int ldc, int64_t col_offset);
 /* Number of kernels this library launched since the process started (launch accounting for benchmarks). */
 GEN9BLAS_API long long gen9blas_kernel_launches(void);
 /* Diagnostic of the bounded device-side waits: runs a kernel whose mbarrier wait can never complete; the wait gives

@@ -188,3 +188,30 @@ def test_hgemm_split_k_tail(gpu_lib, t):
             scale = abs(al) * np.abs(a64) @ np.abs(b64) + abs(be) * np.abs(C0[rows].astype(np.float64))
             avg, mx = gemm_error(C[rows], ref, scale)
             assert mx <= 1e-3, (t, M, N, K, mx)
+
+
+def test_gemm_allgather_writes_every_destination(gpu_lib):
+    """The fused GEMM + all-gather epilogue on one GPU: two local buffers stand in for two ranks' C; each receives
+    this rank's column block at col_offset and nothing else changes."""
+    torch = pytest.importorskip("torch")
+    M, K, N, nb = 512, 384, 1024, 256
+    g = torch.Generator(device="cuda").manual_seed(3)
+    A = torch.randn(M, K, device="cuda", generator=g, dtype=torch.float16)
+    B = torch.randn(K, nb, device="cuda", generator=g, dtype=torch.float16)
+    C1 = torch.full((M, N), 7.0, device="cuda", dtype=torch.float16)
+    C2 = torch.full((M, N), 7.0, device="cuda", dtype=torch.float16)
+    torch.cuda.synchronize()
+    arr = (ctypes.c_void_p * 2)(C1.data_ptr(), C2.data_ptr())
+    f = gpu_lib.dll.gen9blas_gemm_allgather
+    f.argtypes = [ctypes.c_int] * 6 + [ctypes.c_double, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                                       ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int64]
+    for t in (abi.H, abi.HS):
+        assert f(t, 0, 0, M, nb, K, 1.0, A.data_ptr(), K, B.data_ptr(), nb, arr, 2, N, 512) == 0, gpu_lib.error()
+        torch.cuda.synchronize()
+        ref = A.double() @ B.double()
+        scale = A.double().abs() @ B.double().abs()
+        for C in (C1, C2):
+            blk = C[:, 512:768].double()
+            assert float(((blk - ref).abs() / scale).max()) <= 1e-3
+            rest = torch.cat([C[:, :512], C[:, 768:]], 1)
+            assert bool((rest == 7.0).all())

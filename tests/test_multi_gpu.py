@@ -1,0 +1,75 @@
+"""Multi-GPU paths on real GPUs (skipped with fewer than 2): the fused GEMM + all-gather kernel writing into the
+other rank's C over NVLink through CUDA IPC, and the NCCL column-sharded GEMM, both against the full product."""
+import os
+import socket
+import subprocess
+import sys
+
+import pytest
+
+from conftest import ROOT
+
+pytestmark = pytest.mark.gpu
+
+CHILD = r'''
+import ctypes, os, sys
+import torch, torch.distributed as dist
+sys.path.insert(0, os.path.join(sys.argv[1], "gen9-gpu-blas_b200"))
+import g9dist
+rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+torch.cuda.set_device(rank)
+import datetime
+dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+lib = ctypes.CDLL(os.path.join(sys.argv[1], "gen9-gpu-blas_b200", "libgen9blas.so"))
+lib.gen9blas_error.restype = ctypes.c_char_p
+assert lib.gen9blas_set_device(rank) == 0
+M, K, N = 1024, 512, 2048
+g = torch.Generator(device="cuda").manual_seed(11)
+A = torch.randn(M, K, device="cuda", generator=g, dtype=torch.float16)
+B = torch.randn(K, N, device="cuda", generator=g, dtype=torch.float16)
+nb = N // world
+Bs = B[:, rank * nb:(rank + 1) * nb].contiguous()
+C = torch.zeros(M, N, device="cuda", dtype=torch.float16)
+peers = g9dist.PeerView(lib, C, rank, world)
+torch.cuda.synchronize()
+g9dist.fused_column_sharded_gemm(lib, A, Bs, C, peers, rank, world)
+torch.cuda.synchronize()
+ref = A.double() @ B.double()
+scale = A.double().abs() @ B.double().abs()
+e1 = float(((C.double() - ref).abs() / scale).max())
+C2 = torch.zeros(M, N, device="cuda", dtype=torch.float16)
+g9dist.column_sharded_gemm(A, Bs, C2, rank, world, lambda a, b, c: g9dist.gemm_local(lib, a, b, c), chunks=4,
+                           comm_stream=torch.cuda.Stream())
+torch.cuda.synchronize()
+e2 = float(((C2.double() - ref).abs() / scale).max())
+dist.barrier()
+peers.close()
+dist.destroy_process_group()
+print("ERR", rank, e1, e2)
+'''
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def test_fused_and_nccl_allgather_two_ranks():
+    torch = pytest.importorskip("torch")
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    port = _port()
+    procs = []
+    for r in range(2):
+        env = dict(os.environ, RANK=str(r), WORLD_SIZE="2", MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port),
+                   LOCAL_RANK=str(r), NCCL_NVLS_ENABLE="0")
+        procs.append(subprocess.Popen([sys.executable, "-c", CHILD, ROOT], env=env, stdout=subprocess.PIPE,
+                                      stderr=subprocess.PIPE, text=True))
+    outs = [p.communicate(timeout=300) for p in procs]
+    for p, (o, e) in zip(procs, outs):
+        assert p.returncode == 0, e[-2000:]
+        line = [ln for ln in o.splitlines() if ln.startswith("ERR")][0].split()
+        assert float(line[2]) <= 1e-3 and float(line[3]) <= 1e-3, line
