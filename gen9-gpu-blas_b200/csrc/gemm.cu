@@ -12,9 +12,11 @@ namespace g9 {
 int launch_hgemm_tc(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, long long sA,
                     const void *B, int ldb, long long sB, double beta, void *C, int ldc, long long sC, int count,
                     cudaStream_t st, void *const *peers = nullptr, int npeers = 0, long long col_off = 0);
-int launch_gemm_simt(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, long long sA,
-                     const void *B, int ldb, long long sB, double beta, void *C, int ldc, long long sC, int count,
-                     cudaStream_t st);
+int launch_sgemm(int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, long long sA, const void *B,
+                 int ldb, long long sB, double beta, void *C, int ldc, long long sC, int count, cudaStream_t st);
+int launch_dgemm_dmma(int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, long long sA,
+                      const void *B, int ldb, long long sB, double beta, void *C, int ldc, long long sC, int count,
+                      cudaStream_t st);
 
 static int elem_size(int type) { return type == GEN9BLAS_S ? 4 : type == GEN9BLAS_D ? 8 : 2; }
 
@@ -25,7 +27,9 @@ int launch_gemm(int type, int tA, int tB, int M, int N, int K, double alpha, con
         return launch_skinny(type, tA, tB, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, st);
     if (type == GEN9BLAS_H || type == GEN9BLAS_HS)
         return launch_hgemm_tc(type, tA, tB, M, N, K, alpha, A, lda, sA, B, ldb, sB, beta, C, ldc, sC, count, st);
-    return launch_gemm_simt(type, tA, tB, M, N, K, alpha, A, lda, sA, B, ldb, sB, beta, C, ldc, sC, count, st);
+    if (type == GEN9BLAS_D)
+        return launch_dgemm_dmma(tA, tB, M, N, K, alpha, A, lda, sA, B, ldb, sB, beta, C, ldc, sC, count, st);
+    return launch_sgemm(tA, tB, M, N, K, alpha, A, lda, sA, B, ldb, sB, beta, C, ldc, sC, count, st);
 }
 
 }  // namespace g9
