@@ -6,6 +6,10 @@ Workloads:
 - hgemm4096 (default at N = 1, configs[1]): HGEMM FP16 n = 4096, row-major, A, B iid N(0,1)/sqrt(n), C = A·B with
   FP16 accumulation (GEN9BLAS_H); one step = one gen9blas_gemm call. The FP32-accumulate mode (GEN9BLAS_HS) is timed
   the same way and reported under "modes".
+- rows (N = 1, on request): every BASELINE config row measured on its own (SGEMM n = 1024/4096/8192, HGEMM
+  n = 1024..8192 fast and accurate, DGEMM n = 3000/4096 column-major all transposes, skinny GEMM for the four weight
+  shapes × M = 1..16, level-1 n = 2^28 and level-2 32768² in FP32 and FP64), one JSON line per case with its
+  roofline fraction, the cuBLAS time for GEMM shapes, and the reference's CPU path on a bounded sample per family.
 - scaleout (default at N > 1, configs[4]): HGEMM n = 32768 with B and C column-sharded over the N ranks, A
   replicated, C all-gathered over NVLink (NCCL); one step = local GEMM of the rank's column block + all-gather +
   re-layout into the row-major C. Strong scaling (total work fixed).
@@ -43,7 +47,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=0)
     ap.add_argument("--warmup", type=int, default=0)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="auto", choices=["auto", "hgemm4096", "scaleout"])
+    ap.add_argument("--workload", default="auto", choices=["auto", "hgemm4096", "scaleout", "rows"],
+                    help="rows: one JSON line per BASELINE config row (GEMM, skinny, level 1/2), N = 1 only")
+    ap.add_argument("--rows", default="C0,C1,C2,C3a,C3b,C3c", help="rows workload: which config rows to measure")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample (profiling runs)")
     ap.add_argument("--gather", default="fused", choices=["fused", "nccl"],
@@ -234,6 +240,10 @@ def run_ours(args):
     import torch
     rank, world, local = dist_env()
     workload = args.workload if args.workload != "auto" else ("hgemm4096" if world == 1 else "scaleout")
+    if workload == "rows":
+        if world != 1:
+            raise SystemExit("--workload rows runs on one GPU")
+        return run_rows(args, torch)
     torch.cuda.set_device(local)
     if world > 1:
         import datetime
@@ -444,6 +454,265 @@ def run_scaleout(args, L, torch, stream, barrier, rank, world, local):
                           round(tp_us, 2), "weight_GBps_per_gpu": round(nr * Kw * 2 / (tp_us * 1e-6) / 1e9, 1),
                           "includes": "local skinny GEMM + NCCL all-gather of the outputs + re-layout"},
             "cpu_baseline": None, "e2e": None, "gpu_launches": launches, "clocks": clk}
+
+
+# --------------------------------------------------------------------------------------------- per-row measurements
+CBLAS_ROW, CBLAS_COL, CBLAS_N, CBLAS_T = 101, 102, 111, 112
+
+
+def cpu_row_samples():
+    """The reference's CPU path (oracle/_ref: lib/src/cblas.c in CPU mode over OpenBLAS, all host threads) on bounded
+    samples, one per row family: {family: {"value", "unit", "sample"}}. Empty if the reference layer is absent."""
+    L, kind = load_reference_cblas()
+    if L is None:
+        return {}, kind
+    f, d, i, vp = ctypes.c_float, ctypes.c_double, ctypes.c_int, ctypes.c_void_p
+    L.cblas_dgemm.argtypes = [i] * 6 + [d, vp, i, vp, i, d, vp, i]
+    L.cblas_saxpy.argtypes = [i, f, vp, i, vp, i]
+    L.cblas_sdot.argtypes = [i, vp, i, vp, i]
+    L.cblas_sdot.restype = f
+    L.cblas_snrm2.argtypes = [i, vp, i]
+    L.cblas_snrm2.restype = f
+    L.cblas_isamax.argtypes = [i, vp, i]
+    L.cblas_isamax.restype = ctypes.c_size_t
+    L.cblas_sgemv.argtypes = [i, i, i, i, f, vp, i, vp, i, f, vp, i]
+    L.cblas_sger.argtypes = [i, i, i, f, vp, i, vp, i, vp, i]
+    rng = np.random.default_rng(0)
+
+    def best(fn, reps=3):
+        fn()
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return min(ts)
+
+    out = {}
+    n = 1024
+    A, B, C = (rng.uniform(-1, 1, (n, n)).astype(np.float32) for _ in range(3))
+    t = best(lambda: L.cblas_sgemm(CBLAS_ROW, CBLAS_N, CBLAS_N, n, n, n, 1.0, A.ctypes.data, n, B.ctypes.data, n, 0.0,
+                                   C.ctypes.data, n), 5)
+    out["sgemm"] = {"value": round(2 * n ** 3 / t / 1e12, 4), "unit": "TFLOP/s", "sample": "cblas_sgemm n=1024, best of 5"}
+    n = 3000
+    A, B, C = (rng.uniform(-1, 1, (n, n)) for _ in range(3))
+    t = best(lambda: L.cblas_dgemm(CBLAS_COL, CBLAS_N, CBLAS_N, n, n, n, 1.5, A.ctypes.data, n, B.ctypes.data, n, 0.5,
+                                   C.ctypes.data, n), 2)
+    out["dgemm"] = {"value": round(2 * n ** 3 / t / 1e12, 4), "unit": "TFLOP/s",
+                    "sample": "cblas_dgemm ColMajor NN n=3000 alpha=1.5 beta=0.5, best of 2"}
+    N, K, M = 4096, 4096, 8
+    W = rng.normal(0, 0.02, (N, K)).astype(np.float32)
+    X = rng.normal(0, 1, (M, K)).astype(np.float32)
+    Y = np.empty((M, N), np.float32)
+    t = best(lambda: L.cblas_sgemm(CBLAS_ROW, CBLAS_N, CBLAS_T, M, N, K, 1.0, X.ctypes.data, K, W.ctypes.data, K, 0.0,
+                                   Y.ctypes.data, N), 5)
+    out["skinny"] = {"value": round(t * 1e6, 1), "unit": "us", "gbps": round(N * K * 4 / t / 1e9, 1),
+                     "sample": "cblas_sgemm RowMajor N,T M=8 N=K=4096 (FP32 stand-in for the FP16 weights), best of 5"}
+    n = 1 << 26
+    x = rng.uniform(-1, 1, n).astype(np.float32)
+    y = rng.uniform(-1, 1, n).astype(np.float32)
+    for name, fn, nbytes in (("axpy", lambda: L.cblas_saxpy(n, 0.5, x.ctypes.data, 1, y.ctypes.data, 1), 12 * n),
+                             ("dot", lambda: L.cblas_sdot(n, x.ctypes.data, 1, y.ctypes.data, 1), 8 * n),
+                             ("nrm2", lambda: L.cblas_snrm2(n, x.ctypes.data, 1), 4 * n),
+                             ("iamax", lambda: L.cblas_isamax(n, x.ctypes.data, 1), 4 * n)):
+        t = best(fn)
+        out[name] = {"value": round(nbytes / t / 1e9, 1), "unit": "GB/s", "sample": f"cblas_s{name} n=2^26 FP32, best of 3"}
+    m = 16384
+    Am = rng.uniform(-1, 1, (m, m)).astype(np.float32)
+    xv = rng.uniform(-1, 1, m).astype(np.float32)
+    yv = np.zeros(m, np.float32)
+    t = best(lambda: L.cblas_sgemv(CBLAS_ROW, CBLAS_N, m, m, 1.0, Am.ctypes.data, m, xv.ctypes.data, 1, 0.0,
+                                   yv.ctypes.data, 1))
+    out["gemv"] = {"value": round(m * m * 4 / t / 1e9, 1), "unit": "GB/s", "sample": "cblas_sgemv N 16384^2 FP32, best of 3"}
+    t = best(lambda: L.cblas_sger(CBLAS_ROW, m, m, 0.5, xv.ctypes.data, 1, yv.ctypes.data, 1, Am.ctypes.data, m))
+    out["ger"] = {"value": round(2 * m * m * 4 / t / 1e9, 1), "unit": "GB/s", "sample": "cblas_sger 16384^2 FP32, best of 3"}
+    return out, kind
+
+
+def run_rows(args, torch):
+    """One JSON line per BASELINE config row on one GPU (see the module docstring)."""
+    os.environ["GEN9BLAS_PROFILE"] = "1"        # gen9blas_last_time_ms = device time of the last call
+    L = load_lib()
+    stream = torch.cuda.Stream()
+    assert L.set_stream(ctypes.c_void_p(stream.cuda_stream)) == 0
+    peak_t, peak_hbm, peak_kind = measured_peaks()
+    mhz_max = 1965.0
+    peak_ffma = 148 * 128 * 2 * mhz_max * 1e6 / 1e12
+    peak_dmma = 148 * 64 * 2 * mhz_max * 1e6 / 1e12
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1)
+    cpu, cpu_kind = ({}, None) if args.no_cpu else cpu_row_samples()
+    rows = []
+    want = set(args.rows.split(","))
+
+    def queued_ms(call, reps, warm=3):
+        """Device time per call of `reps` calls enqueued back to back behind a sleep kernel (so that host-side call
+        overhead does not leave gaps between kernels); CUDA events on the library's stream."""
+        L.set_nowait(1)
+        with torch.cuda.stream(stream):
+            for i in range(warm):
+                call(i)
+            torch.cuda.synchronize()
+            torch.cuda._sleep(int(2e6 + reps * 30e3))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for i in range(reps):
+                call(i)
+            e1.record(stream)
+            e1.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    def synced_ms(call, reps):
+        """Median device time of calls that return a host result (reductions): gen9blas_last_time_ms."""
+        L.set_nowait(0)
+        call(0)
+        ts = []
+        for i in range(reps):
+            call(i)
+            ts.append(L.last_time_ms())
+        return statistics.median(ts)
+
+    def chk(r):
+        if r:
+            raise RuntimeError(L.error().decode())
+
+    def emit_row(row, case, value, unit, ms, bound, achieved, peak, peak_unit, peak_note, extra=None, cpu_key=None):
+        line = {"row": row, "case": case, "value": round(value, 3), "unit": unit, "us": round(ms * 1e3, 2),
+                "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": round(peak, 1), "unit": peak_unit,
+                             "frac": round(achieved / peak, 4), "peak_kind": peak_note}}
+        if extra:
+            line.update(extra)
+        if cpu_key and cpu_key in cpu:
+            line["cpu_baseline"] = dict(cpu[cpu_key], kind=cpu_kind, cores=os.cpu_count())
+        rows.append(line)
+        emit(line)
+
+    def gemm_rows(row, kind, dt, n, ta=0, tb=0, colmajor=False, alpha=1.0, beta=0.0, sets=None, label="", cpu_key=None):
+        es = torch.tensor([], dtype=dt).element_size()
+        sets = sets or (4 if 12 * n * n * es < 2e9 else 2)
+        mk = (lambda: torch.randn(n, n, device="cuda", generator=g, dtype=torch.float32).div_(n ** 0.5).to(dt)) \
+            if dt == torch.float16 else (lambda: torch.rand(n, n, device="cuda", generator=g, dtype=dt).mul_(2).sub_(1))
+        A = [mk() for _ in range(sets)]
+        B = [mk() for _ in range(sets)]
+        C = [mk() for _ in range(sets)]
+
+        def call(i):
+            j = i % sets
+            if colmajor:   # column-major C = op(A)·op(B) is row-major Cᵀ = op(B)ᵀ·op(A)ᵀ (the CBLAS swap identity)
+                chk(L.gemm(kind, tb, ta, n, n, n, alpha, B[j].data_ptr(), n, A[j].data_ptr(), n, beta, C[j].data_ptr(), n))
+            else:
+                chk(L.gemm(kind, ta, tb, n, n, n, alpha, A[j].data_ptr(), n, B[j].data_ptr(), n, beta, C[j].data_ptr(), n))
+
+        reps = max(4, min(200, int(0.25 / (2 * n ** 3 / 50e12))))
+        ms = queued_ms(call, reps)
+        # cuBLAS on the same operands (torch.matmul / addmm), TF32 off
+        torch.backends.cuda.matmul.allow_tf32 = False
+        with torch.cuda.stream(stream):
+            opA = (lambda j: A[j].t()) if ta else (lambda j: A[j])
+            opB = (lambda j: B[j].t()) if tb else (lambda j: B[j])
+            for j in range(2):
+                torch.matmul(opA(j % sets), opB(j % sets), out=C[j % sets])
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for i in range(reps):
+                torch.matmul(opA(i % sets), opB(i % sets), out=C[i % sets])
+            e1.record(stream)
+            e1.synchronize()
+        ms_cublas = e0.elapsed_time(e1) / reps
+        tf = 2 * n ** 3 / (ms * 1e-3) / 1e12
+        peak, note = {torch.float16: (peak_t, f"{peak_kind} cuBLAS bf16 dense sustained, MEASURED_PEAKS.json"),
+                      torch.float32: (peak_ffma, "FP32 FFMA nominal: 148 SMs x 128 lanes x 2 x 1965 MHz"),
+                      torch.float64: (peak_dmma, "FP64 DMMA nominal: 148 SMs x 64 FMA/clk x 2 x 1965 MHz")}[dt]
+        emit_row(row, label, tf, "TFLOP/s", ms, "tensor" if dt != torch.float32 else "ffma", tf, peak, "TFLOP/s", note,
+                 {"cublas_tflops": round(2 * n ** 3 / (ms_cublas * 1e-3) / 1e12, 2)}, cpu_key)
+        del A, B, C
+        torch.cuda.empty_cache()
+
+    for n in (1024, 4096, 8192) if "C0" in want else ():
+        gemm_rows("C0", S, torch.float32, n, label=f"sgemm n={n} RM NN", cpu_key="sgemm" if n == 1024 else None)
+    for n in (1024, 2048, 3000, 4096, 8192) if "C1" in want else ():
+        for kind, nm in ((H, "fast (FP16 accumulate)"), (HS, "accurate (FP32 accumulate)")):
+            gemm_rows("C1", kind, torch.float16, n, label=f"hgemm n={n} RM NN {nm}")
+    for n in (3000, 4096) if "C3a" in want else ():
+        for ta, tb in ((0, 0), (1, 0), (0, 1), (1, 1)):
+            gemm_rows("C3a", D, torch.float64, n, ta, tb, colmajor=True, alpha=1.5, beta=0.5,
+                      label=f"dgemm n={n} col-major {'NT'[ta]}{'NT'[tb]} alpha=1.5 beta=0.5",
+                      cpu_key="dgemm" if (n, ta, tb) == (3000, 0, 0) else None)
+
+    # skinny: C (M × N) = A (M × K) · Wᵀ, W resident in HBM, rotated over copies that exceed L2
+    for N, K in ((4096, 4096), (12288, 4096), (11008, 4096), (4096, 11008)) if "C2" in want else ():
+        copies = max(2, int(512e6 // (N * K * 2)) + 1)
+        Ws = [torch.randn(N, K, device="cuda", generator=g, dtype=torch.float32).mul_(0.02).half() for _ in range(copies)]
+        for M in (1, 2, 4, 8, 16):
+            X = torch.randn(M, K, device="cuda", generator=g, dtype=torch.float32).half()
+            Y = torch.empty(M, N, device="cuda", dtype=torch.float16)
+
+            def call(i, M=M, X=X, Y=Y):
+                chk(L.gemm(H, 0, 1, M, N, K, 1.0, X.data_ptr(), K, Ws[i % copies].data_ptr(), K, 0.0, Y.data_ptr(), N))
+
+            ms = queued_ms(call, 200)
+            with torch.cuda.stream(stream):
+                for i in range(3):
+                    torch.matmul(X, Ws[i % copies].t(), out=Y)
+                torch.cuda._sleep(int(2e6 + 200 * 30e3))
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for i in range(200):
+                    torch.matmul(X, Ws[i % copies].t(), out=Y)
+                e1.record(stream)
+                e1.synchronize()
+            ms_cublas = e0.elapsed_time(e1) / 200
+            nbytes = N * K * 2 + M * K * 2 + M * N * 2
+            gbps = nbytes / (ms * 1e-3) / 1e9
+            emit_row("C2", f"skinny M={M} W={N}x{K}", ms * 1e3, "us", ms, "hbm", gbps, peak_hbm, "GB/s",
+                     f"{peak_kind} HBM copy, MEASURED_PEAKS.json",
+                     {"gbps": round(gbps, 1), "cublas_us": round(ms_cublas * 1e3, 2),
+                      },
+                     "skinny" if (N, K, M) == (4096, 4096, 8) else None)
+        del Ws
+        torch.cuda.empty_cache()
+
+    # level 1 (n = 2^28) and level 2 (32768²), FP32 and FP64
+    n1 = 1 << 28
+    for kind, dt, tag in ((S, torch.float32, "s"), (D, torch.float64, "d")) if want & {"C3b", "C3c"} else ():
+        es = 4 if kind == S else 8
+        x = torch.rand(n1, device="cuda", generator=g, dtype=dt).mul_(2).sub_(1)
+        y = torch.rand(n1, device="cuda", generator=g, dtype=dt).mul_(2).sub_(1)
+        res = ctypes.c_double()
+        ires = ctypes.c_int64()
+        ms = queued_ms(lambda i: chk(L.axpy(kind, n1, 0.5, x.data_ptr(), 1, y.data_ptr(), 1)), 10)
+        emit_row("C3b", f"{tag}axpy n=2^28", 3 * n1 * es / (ms * 1e-3) / 1e9, "GB/s", ms, "hbm",
+                 3 * n1 * es / (ms * 1e-3) / 1e9, peak_hbm, "GB/s", f"{peak_kind} HBM copy", None,
+                 "axpy" if kind == S else None)
+        for nm, fn, nb in (("dot", lambda i: chk(L.dot(kind, n1, x.data_ptr(), 1, y.data_ptr(), 1, ctypes.byref(res))), 2),
+                           ("nrm2", lambda i: chk(L.nrm2(kind, n1, x.data_ptr(), 1, ctypes.byref(res))), 1),
+                           ("asum", lambda i: chk(L.asum(kind, n1, x.data_ptr(), 1, ctypes.byref(res))), 1),
+                           ("iamax", lambda i: chk(L.iamax(kind, n1, x.data_ptr(), 1, ctypes.byref(ires))), 1)):
+            ms = synced_ms(fn, 10)
+            gbps = nb * n1 * es / (ms * 1e-3) / 1e9
+            emit_row("C3b", f"{tag}{nm} n=2^28", gbps, "GB/s", ms, "hbm", gbps, peak_hbm, "GB/s",
+                     f"{peak_kind} HBM copy; time = gen9blas_last_time_ms (includes the 8-byte result copy)", None,
+                     nm if kind == S and nm in ("dot", "nrm2", "iamax") else None)
+        del x, y
+        torch.cuda.empty_cache()
+        m = 32768
+        A = torch.rand(m, m, device="cuda", generator=g, dtype=dt).mul_(2).sub_(1)
+        xv = torch.rand(m, device="cuda", generator=g, dtype=dt)
+        yv = torch.rand(m, device="cuda", generator=g, dtype=dt)
+        for trans in (0, 1):
+            ms = queued_ms(lambda i: chk(L.gemv(kind, trans, m, m, 1.0, A.data_ptr(), m, xv.data_ptr(), 1, 0.0,
+                                                yv.data_ptr(), 1)), 10)
+            gbps = (m * m + 2 * m) * es / (ms * 1e-3) / 1e9
+            emit_row("C3c", f"{tag}gemv {'NT'[trans]} 32768^2", gbps, "GB/s", ms, "hbm", gbps, peak_hbm, "GB/s",
+                     f"{peak_kind} HBM copy", None, "gemv" if kind == S and trans == 0 else None)
+        ms = queued_ms(lambda i: chk(L.ger(kind, m, m, 1e-3, xv.data_ptr(), 1, yv.data_ptr(), 1, A.data_ptr(), m)), 10)
+        gbps = 2 * m * m * es / (ms * 1e-3) / 1e9
+        emit_row("C3c", f"{tag}ger 32768^2", gbps, "GB/s", ms, "hbm", gbps, peak_hbm, "GB/s", f"{peak_kind} HBM copy",
+                 None, "ger" if kind == S else None)
+        del A, xv, yv
+        torch.cuda.empty_cache()
+    return 0
 
 
 _OUT_FD = None

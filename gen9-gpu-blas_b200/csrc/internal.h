@@ -35,6 +35,8 @@ struct DevState {
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     unsigned *gemm_flags = nullptr;                            // split-K handoff flags of the HGEMM pair kernel (zeroed)
     unsigned gemm_epoch = 0;                                   // launch counter written into those flags
+    int *sk_count = nullptr;                                   // arrival counters of the stream-K skinny kernel (zeroed;
+    size_t sk_count_n = 0;                                     // every launch leaves them at zero)
 };
 
 // Process-wide call state (the caller serialises calls, as for the reference).
@@ -90,6 +92,8 @@ int map_operand(Operand &op, const void *p, size_t bytes, int slot, bool copy_in
 int finish_op(Operand *ops, int n);
 // Scratch buffer of at least `bytes` on the current device (grow-only). Waits for queued work before growing.
 int scratch(size_t bytes, void **p);
+// Arrival counters (n ints, all zero between launches) of the stream-K skinny kernel; grows (and zeroes) on demand.
+int skinny_counters(size_t n, int **p);
 // Call timing: timer_start at entry (wall clock), timer_kernel right before the main kernels (GEN9BLAS_PROFILE=1:
 // CUDA event), timer_stop at the end: last_time_ms is the kernel time with profiling, else the whole call.
 void timer_start();

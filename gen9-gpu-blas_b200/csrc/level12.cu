@@ -109,32 +109,37 @@ __global__ void __launch_bounds__(kThreads) reduce_partial(long long n, const T 
     double s = 0;
     if (VEC) {
         constexpr int W = V16<T>::W;
+        // 16-byte loads (per operand) in flight per trip, one accumulation chain each: 4 for single-operand FP32 / FP16
+        // sums (4-8 terms per load: longer chains would bound them below HBM speed), 2 otherwise.
+        constexpr int U = (sizeof(T) == 8 || MODE == 0) ? 2 : 4;
         using R = typename Compute<T>::R;
         const long long nv = n / W;
-        double s2 = 0;   // second chain: two independent 16-byte loads (per operand) in flight per trip
+        double acc[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) acc[u] = 0;
         long long v = tid;
-        for (; v + stride < nv; v += 2 * stride) {
-            R xv[W], yv[W], xw[W], yw[W];
-            load16<T>(x + v * W, xv);
-            load16<T>(x + (v + stride) * W, xw);
-            if (MODE == 0) {
-                load16<T>(y + v * W, yv);
-                load16<T>(y + (v + stride) * W, yw);
+        for (; v + (U - 1) * stride < nv; v += U * stride) {
+            R xv[U][W], yv[U][W];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                load16<T>(x + (v + u * stride) * W, xv[u]);
+                if (MODE == 0) load16<T>(y + (v + u * stride) * W, yv[u]);
             }
 #pragma unroll
-            for (int k = 0; k < W; k++) {
-                s += red_term<MODE>((double)xv[k], MODE == 0 ? (double)yv[k] : 0.0);
-                s2 += red_term<MODE>((double)xw[k], MODE == 0 ? (double)yw[k] : 0.0);
-            }
+            for (int u = 0; u < U; u++)
+#pragma unroll
+                for (int k = 0; k < W; k++)
+                    acc[u] += red_term<MODE>((double)xv[u][k], MODE == 0 ? (double)yv[u][k] : 0.0);
         }
-        if (v < nv) {
+        for (; v < nv; v += stride) {
             R xv[W], yv[W];
             load16<T>(x + v * W, xv);
             if (MODE == 0) load16<T>(y + v * W, yv);
 #pragma unroll
-            for (int k = 0; k < W; k++) s += red_term<MODE>((double)xv[k], MODE == 0 ? (double)yv[k] : 0.0);
+            for (int k = 0; k < W; k++) acc[0] += red_term<MODE>((double)xv[k], MODE == 0 ? (double)yv[k] : 0.0);
         }
-        s += s2;
+#pragma unroll
+        for (int u = 0; u < U; u++) s += acc[u];
         for (long long i = nv * W + tid; i < n; i += stride)
             s += red_term<MODE>((double)to_r(x[i]), MODE == 0 ? (double)to_r(y[i]) : 0.0);
     } else {
@@ -215,32 +220,38 @@ __global__ void __launch_bounds__(kThreads) iamax_partial(long long n, const T *
     long long bi = kNoIndex;
     if (VEC) {
         constexpr int W = V16<T>::W;
+        constexpr int U = sizeof(T) == 8 ? 2 : 4;   // loads in flight per trip; chain u scans the elements of load u
         const long long nv = n / W;
+        R cv[U];
+        long long ci[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) { cv[u] = (R)-1; ci[u] = kNoIndex; }
         long long v = tid;
-        for (; v + stride < nv; v += 2 * stride) {   // two loads in flight; scanned in index order
-            R xv[W], xw[W];
-            load16<T>(x + v * W, xv);
-            load16<T>(x + (v + stride) * W, xw);
+        for (; v + (U - 1) * stride < nv; v += U * stride) {
+            R xv[U][W];
 #pragma unroll
-            for (int k = 0; k < W; k++) {
-                const R a = fabs(xv[k]);
-                if (a > bv) { bv = a; bi = v * W + k; }
-            }
+            for (int u = 0; u < U; u++) load16<T>(x + (v + u * stride) * W, xv[u]);
 #pragma unroll
-            for (int k = 0; k < W; k++) {
-                const R a = fabs(xw[k]);
-                if (a > bv) { bv = a; bi = (v + stride) * W + k; }
-            }
+            for (int u = 0; u < U; u++)
+#pragma unroll
+                for (int k = 0; k < W; k++) {
+                    const R a = fabs(xv[u][k]);
+                    if (a > cv[u]) { cv[u] = a; ci[u] = (v + u * stride) * W + k; }
+                }
         }
-        if (v < nv) {
+        for (; v < nv; v += stride) {
             R xv[W];
             load16<T>(x + v * W, xv);
 #pragma unroll
             for (int k = 0; k < W; k++) {
                 const R a = fabs(xv[k]);
-                if (a > bv) { bv = a; bi = v * W + k; }
+                if (a > cv[0]) { cv[0] = a; ci[0] = v * W + k; }
             }
         }
+        // Each chain holds the first index of its largest value; the (value, index) combination keeps the smaller
+        // index on ties, so the thread's result is the first index of its largest value.
+#pragma unroll
+        for (int u = 0; u < U; u++) better(bv, bi, cv[u], ci[u]);
         for (long long i = nv * W + tid; i < n; i += stride) {
             const R a = fabs(to_r(x[i]));
             if (a > bv) { bv = a; bi = i; }

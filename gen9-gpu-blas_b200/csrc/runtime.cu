@@ -176,6 +176,21 @@ int scratch(size_t bytes, void **p) {
     return 0;
 }
 
+int skinny_counters(size_t n, int **p) {
+    DevState *d = dev_state();
+    if (!d) return G.status;
+    if (d->sk_count_n < n) {
+        void *buf = d->sk_count;
+        size_t bytes = d->sk_count_n * sizeof(int);
+        G9_TRY(ensure_dev_buf(&buf, &bytes, n * sizeof(int)));
+        G9_CU(cudaMemsetAsync(buf, 0, bytes, stream()));
+        d->sk_count = (int *)buf;
+        d->sk_count_n = bytes / sizeof(int);
+    }
+    *p = d->sk_count;
+    return 0;
+}
+
 int map_operand(Operand &op, const void *p, size_t bytes, int slot, bool copy_in, bool written) {
     op.user = p;
     op.bytes = bytes;
@@ -244,7 +259,7 @@ int finish_op(Operand *ops, int n) {
 static double g_t0;
 void timer_start() { g_t0 = now_s(); }
 void timer_kernel() {
-    if (G.profile) {
+    if (G.profile && !G.nowait) {   // read back by timer_stop only for synchronous calls
         DevState *d = dev_state();
         if (d) cudaEventRecord(d->ev0, stream());
     }

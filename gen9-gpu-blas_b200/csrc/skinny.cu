@@ -8,11 +8,11 @@
 // this path, gemm.c:191-199).
 //
 // B200 kernels:
-// - wk_f16_mma: weights FP16, contiguous along K. A CTA owns 16 weight rows; its 8 warps split K. Each lane streams
-//   16-byte loads of two weight rows (ld.global.nc, deep unroll) and feeds them to mma.sync m16n8k16 (FP16 in, FP32
-//   accumulate) with the weight rows as the MMA's M side and up to 16 tokens as N. The K order inside a 32-wide step
-//   is permuted identically for weights and tokens (a dot product does not depend on it), so every lane's 16-byte
-//   load is directly an MMA fragment. Warp partial sums are combined in shared memory in a fixed order.
+// - wk_f16_sk: weights FP16, contiguous along K. The (16-row block, K chunk) iterations are split evenly over every
+//   warp of a one-wave grid (stream-K), so all SMs stream the same number of weight bytes whatever the shape; each
+//   lane streams 16-byte loads of two weight rows (ld.global.nc, deep unroll) into mma.sync m16n8k16 (FP16 in, FP32
+//   accumulate). Row blocks shared by several warps are finished by the last warp to arrive, which sums the others'
+//   FP32 partial tiles in K order (deterministic, no waiting).
 // - wk_f32: weights FP32, contiguous along K, FFMA: a CTA owns 4 rows, 8 warps split K, lanes read float4, warp
 //   shuffle reduction, fixed-order combination across warps.
 // - wn_partial + wn_final: weights contiguous along N: split-K partial sums P[part][m][n] in FP32, then a fixed-order
@@ -74,80 +74,126 @@ __device__ __forceinline__ uint4 ldg_nc16(const void *p) {
     return v;
 }
 
+// Weight stream: read-only, no L1 allocation, and a 256-byte L2 prefetch hint (each lane's 16 bytes sit in a 64-byte
+// run of its row, and the warp walks the row in consecutive 64-byte runs).
+__device__ __forceinline__ uint4 ldg_w16(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
 __device__ __forceinline__ uint32_t word(const uint4 &v, int i) {
     return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }
 
 // Requirements (checked on the host): K % 8 == 0, weight rows and token rows contiguous along K with 16-byte aligned
-// starts. grid = (ceil(Nc / 16), ceil(Mc / 16)).
-// UNROLL 32-wide K steps are loaded before any is used: 8 with one token tile (M <= 8), 4 with two, which keeps 16
-// (or 8) independent 16-byte weight loads in flight per lane -- at decode shapes HBM needs ~100 KiB in flight per SM.
+// starts. grid = (CTAs, ceil(Mc / 16)).
+// Each warp computes 16 weight rows × 16 tokens with mma.sync.m16n8k16: the weight rows are the MMA's M side and the
+// tokens its N side (one or two 8-token tiles). UNROLL 32-wide K steps are loaded before any is used: 8 with one token
+// tile (M <= 8), 4 with two, which keeps 16 (or 8) independent 16-byte weight loads in flight per lane -- at decode
+// shapes HBM needs ~100 KiB in flight per SM. The K order inside a 32-wide step is permuted identically for weights
+// and tokens (a dot product does not depend on it), so every lane's 16-byte load is directly an MMA fragment.
+//
+// Work is spread stream-K style over the whole GPU in one wave. The iteration space is (rb, kc): rb = block of 16
+// weight rows, kc = chunk of UNROLL·32 K elements; T = RB·KC iterations are split evenly over all warps of the grid
+// (warp w owns [T·w/W, T·(w+1)/W)), so every SM streams the same number of weight bytes whatever the shape. A warp that
+// covers a whole row block stores C directly. Otherwise each contributor of the block writes its FP32 partial tile to
+// its slot (slots ordered by K), and the last contributor to arrive (counter per block) sums the slots in slot order
+// and stores C -- deterministic, no spinning: nobody waits for anybody.
 template <bool TWO_NTILES, int UNROLL>
-__global__ void __launch_bounds__(WK_WARPS * 32, 2) wk_f16_mma(const SkinnyArgs p) {
-    __shared__ float red[WK_WARPS][16][17];
+__global__ void __launch_bounds__(WK_WARPS * 32, 2)
+wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *__restrict__ count) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
-    const int r0 = blockIdx.x * 16, t0 = blockIdx.y * 16;
-    const __half *W = (const __half *)p.w;
+    const int t0 = blockIdx.y * 16;
+    const int RB = (p.Nc + 15) / 16;
+    const long long T = (long long)RB * KC;
+    const int W = gridDim.x * WK_WARPS;
+    const int wg = blockIdx.x * WK_WARPS + warp;
+    long long it = T * wg / W;
+    const long long it_end = T * (wg + 1) / W;
+    const __half *Wt = (const __half *)p.w;
     const __half *A = (const __half *)p.a;
-    // Rows beyond the edges are clamped (valid addresses); their results are never stored.
-    const int wr0 = min(r0 + g, p.Nc - 1), wr1 = min(r0 + g + 8, p.Nc - 1);
     const int ta0 = min(t0 + g, p.Mc - 1), ta1 = min(t0 + g + 8, p.Mc - 1);
-    const __half *w0 = W + (long long)wr0 * p.swn;
-    const __half *w1 = W + (long long)wr1 * p.swn;
     const __half *a0 = A + (long long)ta0 * p.sam;
     const __half *a1 = A + (long long)ta1 * p.sam;
-
-    const int steps = (p.K + 31) / 32;
-    const int per_warp = (steps + WK_WARPS - 1) / WK_WARPS;
-    const int s_beg = warp * per_warp, s_end = min(steps, s_beg + per_warp);
-    float d0[4] = {0, 0, 0, 0}, d1[4] = {0, 0, 0, 0};
-    for (int s = s_beg; s < s_end; s += UNROLL) {
-        uint4 wv0[UNROLL], wv1[UNROLL], av0[UNROLL], av1[UNROLL];
+    while (it < it_end) {
+        const int rb = (int)(it / KC), kc0 = (int)(it % KC);
+        const int kc1 = (int)min((long long)KC, kc0 + (it_end - it));
+        const int r0 = rb * 16;
+        // Rows beyond the edge are clamped (valid addresses); their results are never stored.
+        const __half *w0 = Wt + (long long)min(r0 + g, p.Nc - 1) * p.swn;
+        const __half *w1 = Wt + (long long)min(r0 + g + 8, p.Nc - 1) * p.swn;
+        float d0[4] = {0, 0, 0, 0}, d1[4] = {0, 0, 0, 0};
+        for (int kc = kc0; kc < kc1; kc++) {
+            uint4 wv0[UNROLL], wv1[UNROLL], av0[UNROLL], av1[UNROLL];
 #pragma unroll
-        for (int u = 0; u < UNROLL; u++) {
-            const int k = (s + u) * 32 + 8 * t;
-            const bool in = s + u < s_end && k < p.K;
-            wv0[u] = in ? ldg_nc16(w0 + k) : make_uint4(0, 0, 0, 0);
-            wv1[u] = in ? ldg_nc16(w1 + k) : make_uint4(0, 0, 0, 0);
-            av0[u] = in ? __ldg(reinterpret_cast<const uint4 *>(a0 + k)) : make_uint4(0, 0, 0, 0);
-            if (TWO_NTILES) av1[u] = in ? __ldg(reinterpret_cast<const uint4 *>(a1 + k)) : make_uint4(0, 0, 0, 0);
-        }
+            for (int u = 0; u < UNROLL; u++) {
+                const int k = (kc * UNROLL + u) * 32 + 8 * t;
+                const bool in = k < p.K;
+                wv0[u] = in ? ldg_w16(w0 + k) : make_uint4(0, 0, 0, 0);
+                wv1[u] = in ? ldg_w16(w1 + k) : make_uint4(0, 0, 0, 0);
+                av0[u] = in ? __ldg(reinterpret_cast<const uint4 *>(a0 + k)) : make_uint4(0, 0, 0, 0);
+                if (TWO_NTILES) av1[u] = in ? __ldg(reinterpret_cast<const uint4 *>(a1 + k)) : make_uint4(0, 0, 0, 0);
+            }
 #pragma unroll
-        for (int u = 0; u < UNROLL; u++) {
+            for (int u = 0; u < UNROLL; u++) {
 #pragma unroll
-            for (int j = 0; j < 2; j++) {
-                const uint32_t A0 = word(wv0[u], 2 * j), A1 = word(wv1[u], 2 * j);
-                const uint32_t A2 = word(wv0[u], 2 * j + 1), A3 = word(wv1[u], 2 * j + 1);
-                mma_16816(d0, A0, A1, A2, A3, word(av0[u], 2 * j), word(av0[u], 2 * j + 1));
-                if (TWO_NTILES) mma_16816(d1, A0, A1, A2, A3, word(av1[u], 2 * j), word(av1[u], 2 * j + 1));
+                for (int j = 0; j < 2; j++) {
+                    const uint32_t A0 = word(wv0[u], 2 * j), A1 = word(wv1[u], 2 * j);
+                    const uint32_t A2 = word(wv0[u], 2 * j + 1), A3 = word(wv1[u], 2 * j + 1);
+                    mma_16816(d0, A0, A1, A2, A3, word(av0[u], 2 * j), word(av0[u], 2 * j + 1));
+                    if (TWO_NTILES) mma_16816(d1, A0, A1, A2, A3, word(av1[u], 2 * j), word(av1[u], 2 * j + 1));
+                }
             }
         }
-    }
-    // D fragment: d[0..1] = (row g, tokens 2t, 2t+1), d[2..3] = (row g+8, tokens 2t, 2t+1).
-    red[warp][g][2 * t] = d0[0];
-    red[warp][g][2 * t + 1] = d0[1];
-    red[warp][g + 8][2 * t] = d0[2];
-    red[warp][g + 8][2 * t + 1] = d0[3];
-    if (TWO_NTILES) {
-        red[warp][g][8 + 2 * t] = d1[0];
-        red[warp][g][8 + 2 * t + 1] = d1[1];
-        red[warp][g + 8][8 + 2 * t] = d1[2];
-        red[warp][g + 8][8 + 2 * t + 1] = d1[3];
-    } else {
-        red[warp][g][8 + 2 * t] = 0;
-        red[warp][g][8 + 2 * t + 1] = 0;
-        red[warp][g + 8][8 + 2 * t] = 0;
-        red[warp][g + 8][8 + 2 * t + 1] = 0;
-    }
-    __syncthreads();
-    const int row = threadIdx.x >> 4, tok = threadIdx.x & 15;
-    const int n = r0 + row, m = t0 + tok;
-    if (n < p.Nc && m < p.Mc) {
-        float s = 0;
+        // D fragment: d[0..1] = (row g, tokens 2t, 2t+1), d[2..3] = (row g+8, tokens 2t, 2t+1); d1: tokens + 8.
+        if (kc0 == 0 && kc1 == KC) {
 #pragma unroll
-        for (int w = 0; w < WK_WARPS; w++) s += red[w][row][tok];
-        skinny_store<__half>(p, m, n, s);
+            for (int e = 0; e < 8; e++) {
+                if (!TWO_NTILES && e >= 4) break;
+                const float v = e < 4 ? d0[e] : d1[e - 4];
+                const int n = r0 + g + ((e & 2) ? 8 : 0), m = t0 + 2 * t + (e & 1) + (e >= 4 ? 8 : 0);
+                if (n < p.Nc && m < p.Mc) skinny_store<__half>(p, m, n, v);
+            }
+        } else {
+            const long long x0 = (long long)rb * KC, x1 = x0 + KC - 1;
+            const int wf = (int)(((x0 + 1) * W - 1) / T), wl = (int)(((x1 + 1) * W - 1) / T);
+            const int nc = wl - wf + 1;
+            const long long blk = (long long)blockIdx.y * RB + rb;
+            float *sp = part + (blk * maxc + (wg - wf)) * 256;
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                if (!TWO_NTILES && e >= 4) break;
+                const int row = g + ((e & 2) ? 8 : 0), tok = 2 * t + (e & 1) + (e >= 4 ? 8 : 0);
+                sp[row * 16 + tok] = e < 4 ? d0[e] : d1[e - 4];
+            }
+            __syncwarp();
+            __threadfence();
+            int prev = 0;
+            if (lane == 0) prev = atomicAdd(count + blk, 1);
+            prev = __shfl_sync(0xffffffffu, prev, 0);
+            if (prev == nc - 1) {
+                __threadfence();
+                const int row = lane >> 1, tb = (lane & 1) * 8;
+                if (t0 + tb < p.Mc && r0 + row < p.Nc) {
+                    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                    for (int q = 0; q < nc; q++) {
+                        const float4 *src = reinterpret_cast<const float4 *>(part + (blk * maxc + q) * 256 + row * 16 + tb);
+                        const float4 u0 = __ldcg(src), u1 = __ldcg(src + 1);
+                        acc[0] += u0.x; acc[1] += u0.y; acc[2] += u0.z; acc[3] += u0.w;
+                        acc[4] += u1.x; acc[5] += u1.y; acc[6] += u1.z; acc[7] += u1.w;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; j++)
+                        if (t0 + tb + j < p.Mc) skinny_store<__half>(p, t0 + tb + j, r0 + row, acc[j]);
+                }
+                if (lane == 0) count[blk] = 0;   // ready for the next launch
+            }
+        }
+        it += kc1 - kc0;
     }
 }
 
@@ -326,9 +372,21 @@ static int skinny_t(SkinnyArgs p, cudaStream_t st) {
         const bool w_ok = ((uintptr_t)p.w & 15) == 0 && (p.swn * es) % 16 == 0 && p.K % kq == 0;
         if (w_ok) {
             const bool a_ok = p.sak == 1 && ((uintptr_t)p.a & 15) == 0 && (p.sam * es) % 16 == 0;
+            // Scratch layout: [repacked small operand (when needed) | stream-K partial tiles (FP32)].
+            const size_t a_bytes = a_ok ? 0 : ((size_t)p.Mc * p.K * es + 255) / 256 * 256;
+            const int unroll = p.Mc > 8 ? 4 : 8;
+            const int KC = (p.K + unroll * 32 - 1) / (unroll * 32);
+            const int RB = (p.Nc + 15) / 16, mtiles = (p.Mc + 15) / 16;
+            const long long iters = (long long)RB * KC;
+            long long ctas = (iters + 2 * WK_WARPS - 1) / (2 * WK_WARPS);   // at least ~2 iterations per warp
+            if (ctas > 2 * d->sm_count) ctas = 2 * d->sm_count;
+            if (ctas < 1) ctas = 1;
+            const long long q = iters / (ctas * WK_WARPS);
+            const int maxc = (int)(q == 0 ? KC : (KC / q + 2 < KC ? KC / q + 2 : KC));
+            const size_t part_bytes = sizeof(T) == 2 ? (size_t)mtiles * RB * maxc * 256 * sizeof(float) : 0;
+            void *scr = nullptr;
+            if (a_bytes + part_bytes) G9_TRY(scratch(a_bytes + part_bytes, &scr));
             if (!a_ok) {
-                void *scr = nullptr;
-                G9_TRY(scratch((size_t)p.Mc * p.K * es + 256, &scr));
                 repack_small<T><<<d->sm_count * 4, 256, 0, st>>>((const T *)p.a, p.sam, p.sak, p.Mc, p.K, p.K, (T *)scr);
                 G9_TRY(launched("repack_small"));
                 p.a = scr;
@@ -336,10 +394,13 @@ static int skinny_t(SkinnyArgs p, cudaStream_t st) {
                 p.sak = 1;
             }
             if (sizeof(T) == 2) {
-                dim3 grid((p.Nc + 15) / 16, (p.Mc + 15) / 16);
-                if (p.Mc > 8) wk_f16_mma<true, 4><<<grid, WK_WARPS * 32, 0, st>>>(p);
-                else wk_f16_mma<false, 8><<<grid, WK_WARPS * 32, 0, st>>>(p);
-                return launched("skinny_wk_f16_mma");
+                int *count = nullptr;
+                G9_TRY(skinny_counters((size_t)mtiles * RB, &count));
+                float *part = (float *)((char *)scr + a_bytes);
+                dim3 grid((unsigned)ctas, mtiles);
+                if (p.Mc > 8) wk_f16_sk<true, 4><<<grid, WK_WARPS * 32, 0, st>>>(p, KC, maxc, part, count);
+                else wk_f16_sk<false, 8><<<grid, WK_WARPS * 32, 0, st>>>(p, KC, maxc, part, count);
+                return launched("skinny_wk_f16_sk");
             }
             const int mt = p.Mc <= 1 ? 1 : p.Mc <= 4 ? 4 : p.Mc <= 8 ? 8 : 16;
             dim3 grid((p.Nc + WKF_ROWS - 1) / WKF_ROWS, (p.Mc + mt - 1) / mt);
