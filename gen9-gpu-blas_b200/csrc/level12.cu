@@ -121,14 +121,15 @@ __global__ void __launch_bounds__(kThreads) reduce_partial(long long n, const T 
         for (; v + (U - 1) * stride < nv; v += U * stride) {
             R xv[U][W], yv[U][W];
 #pragma unroll
-            for (int u = 0; u < U; u++) {
-                load16<T>(x + (v + u * stride) * W, xv[u]);
-                if (MODE == 0) load16<T>(y + (v + u * stride) * W, yv[u]);
+            for (int u = 0; u < U; u++) load16<T>(x + (v + u * stride) * W, xv[u]);
+            if (MODE == 0) {
+#pragma unroll
+                for (int u = 0; u < U; u++) load16<T>(y + (v + u * stride) * W, yv[u]);
             }
 #pragma unroll
-            for (int u = 0; u < U; u++)
+            for (int k = 0; k < W; k++)
 #pragma unroll
-                for (int k = 0; k < W; k++)
+                for (int u = 0; u < U; u++)
                     acc[u] += red_term<MODE>((double)xv[u][k], MODE == 0 ? (double)yv[u][k] : 0.0);
         }
         for (; v < nv; v += stride) {
@@ -397,7 +398,21 @@ __global__ void __launch_bounds__(kThreads) gemv_t_partial(int M, int N, int rpp
     for (int k = 0; k < W; k++) s[k] = 0;
     const bool full = c + W <= N;
     if (VEC && full) {
-        for (int i = i0; i < i1; i++) {
+        constexpr int U = 4;   // rows whose 16-byte loads are in flight together (row order of the sums kept)
+        int i = i0;
+        for (; i + U <= i1; i += U) {
+            R av[U][W], xv[U];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                load16<T>(A + (long long)(i + u) * lda + c, av[u]);
+                xv[u] = to_r(x[(long long)(i + u) * ix]);
+            }
+#pragma unroll
+            for (int u = 0; u < U; u++)
+#pragma unroll
+                for (int k = 0; k < W; k++) s[k] = fma_r(av[u][k], xv[u], s[k]);
+        }
+        for (; i < i1; i++) {
             const R xv = to_r(x[i * ix]);
             R av[W];
             load16<T>(A + i * lda + c, av);
@@ -430,6 +445,17 @@ __global__ void __launch_bounds__(kThreads) gemv_t_final(int N, int parts, const
     gemv_store<T>(y, j * iy, alpha, beta, t);
 }
 
+// Row parts of the transposed product: as many as fill exactly one wave of resident blocks together with the column
+// blocks (a second, nearly empty wave would double the time).
+template <typename T> static int gemv_t_wave_parts(bool vec, int col_blocks, int sm_count) {
+    int per_sm = 0;
+    if (vec) cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_t_partial<T, true>, kThreads, 0);
+    else cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_t_partial<T, false>, kThreads, 0);
+    if (per_sm < 1) per_sm = 1;
+    const int parts = sm_count * per_sm / col_blocks;
+    return parts < 1 ? 1 : parts;
+}
+
 template <typename T>
 static int gemv_t(int trans, int M, int N, double alpha, const void *Av, int lda, const void *xv, long long ox,
                   long long ix, double beta, void *yv, long long oy, long long iy, cudaStream_t st) {
@@ -450,8 +476,7 @@ static int gemv_t(int trans, int M, int N, double alpha, const void *Av, int lda
     const int w = vec ? W : 1;
     const int col_blocks = (int)(((long long)N + (long long)kThreads * w - 1) / ((long long)kThreads * w));
     DevState *d = dev_state();
-    const int want = (d ? d->sm_count : 148) * 8;
-    int parts = (want + col_blocks - 1) / col_blocks;
+    int parts = gemv_t_wave_parts<T>(vec, col_blocks, d ? d->sm_count : 148);
     if (parts > M) parts = M;
     if (parts > 65535) parts = 65535;
     if (parts < 1) parts = 1;
@@ -728,7 +753,7 @@ static int gemv_noalloc_t(int trans, int M, int N, double alpha, const T *A, int
     const bool vec = (((uintptr_t)A) & 15) == 0 && ((long long)lda * sizeof(T)) % 16 == 0;
     const int w = vec ? V16<T>::W : 1;
     const int col_blocks = (int)(((long long)N + (long long)kThreads * w - 1) / ((long long)kThreads * w));
-    int parts = (sm_count * 8 + col_blocks - 1) / col_blocks;   // the split of gen9blas_gemv ...
+    int parts = gemv_t_wave_parts<T>(vec, col_blocks, sm_count);   // the split of gen9blas_gemv ...
     const long long fit = (long long)(kNoAllocScratchBytes / row_bytes);
     if (parts > fit) parts = (int)fit;                          // ... capped by the fixed scratch
     if (parts > M) parts = M;

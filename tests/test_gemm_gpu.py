@@ -170,11 +170,13 @@ def test_large_sampled_rows(g9, name, dt, accurate, tol_avg, tol_max):
 
 @pytest.mark.parametrize("t", [abi.H, abi.HS])
 def test_hgemm_split_k_tail(gpu_lib, t):
-    """Shapes whose last wave of 256×256 tiles is split along K over idle CTA pairs (2, 3 or 4 parts, uneven K
-    ranges, edge columns, alpha/beta): the finishing part adds the other parts' FP32 partial sums."""
+    """Shapes whose last wave of 256×256 tiles -- or only wave, for problems with fewer tiles than CTA pairs -- is
+    split along K over idle CTA pairs (2, 3 or 4 parts, uneven K ranges, edge columns, alpha/beta): the finishing part
+    adds the other parts' FP32 partial sums."""
     rng = np.random.default_rng(21)
     for (M, N, K, al, be) in ((3072, 1792, 1024, 1.0, 0.0), (2304, 2304, 520, 1.5, -0.5), (1000, 5000, 300, 1.0, 1.0),
-                              (4096, 4096, 4096, 0.5, 0.25)):
+                              (4096, 4096, 4096, 0.5, 0.25), (1024, 1024, 1024, 1.0, 0.0), (768, 1280, 2048, 1.5, 0.5),
+                              (1536, 1536, 640, 1.0, -1.0)):
         A = (rng.standard_normal((M, K)) / np.sqrt(K)).astype(np.float16)
         B = (rng.standard_normal((K, N)) / np.sqrt(K)).astype(np.float16)
         C0 = rng.uniform(-1, 1, (M, N)).astype(np.float16)
