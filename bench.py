@@ -377,11 +377,12 @@ def run_scaleout(args, L, torch, stream, barrier, rank, world, local):
 
     fused = args.gather == "fused" and world > 1
     peers = g9dist.PeerView(L.dll, C, rank, world) if fused else None
+    bar = g9dist.PeerBarrier(L.dll, rank, world) if fused else None
 
     def step():
         with torch.cuda.stream(stream):
             if fused:
-                g9dist.fused_column_sharded_gemm(L.dll, A, Bs, C, peers, rank, world)
+                g9dist.fused_column_sharded_gemm(L.dll, A, Bs, C, peers, rank, world, barrier=bar)
             else:
                 g9dist.column_sharded_gemm(A, Bs, C, rank, world, local_gemm, chunks=chunks, comm_stream=comm)
 
@@ -422,19 +423,46 @@ def run_scaleout(args, L, torch, stream, barrier, rank, world, local):
         if r:
             raise RuntimeError(L.error().decode())
 
+    pw = g9dist.PeerView(L.dll, Cw, rank, world) if fused else None
+
     def tp_step():
         with torch.cuda.stream(stream):
-            g9dist.row_sharded_skinny(Aw, Wsh, Cw, rank, world, local_skinny)
+            if fused:
+                g9dist.fused_row_sharded_skinny(L.dll, Aw, Wsh, Cw, pw, rank, world, barrier=bar)
+            else:
+                g9dist.row_sharded_skinny(Aw, Wsh, Cw, rank, world, local_skinny)
 
     for _ in range(5):
         tp_step()
-    tp_ms, _ = timed(tp_step, 50)
+    tp_run = tp_step
+    graph = None
+    if fused:
+        # Decode steps are launch-bound: the fused step (skinny kernel + NVLink barrier, both stream-ordered and free of
+        # host synchronisation) is captured once in a CUDA graph and replayed. The barrier's epoch lives on the device.
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream()
+        with torch.cuda.graph(graph, stream=cap, capture_error_mode="relaxed"):
+            L.set_stream(ctypes.c_void_p(cap.cuda_stream))
+            g9dist.fused_row_sharded_skinny(L.dll, Aw, Wsh, Cw, pw, rank, world, barrier=bar)
+        L.set_stream(ctypes.c_void_p(stream.cuda_stream))
+
+        def tp_run():
+            with torch.cuda.stream(stream):
+                graph.replay()
+
+        for _ in range(5):
+            tp_run()
+    tp_ms, tp_launches = timed(tp_run, 50)
     tp_us = tp_ms * 1e3 / 50
     if peers is not None:
         torch.cuda.synchronize()
         if world > 1:
             torch.distributed.barrier()
+        graph = None
         peers.close()
+        pw.close()
+        bar.close()
     peak_t, peak_hbm, peak_kind = measured_peaks()
     return {"metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": steps,
             "warmup": warm, "ms_per_step": round(ms_total / steps, 4), "higher_is_better": True, "scaling": "strong",
@@ -442,7 +470,7 @@ def run_scaleout(args, L, torch, stream, barrier, rank, world, local):
             "config": {"workload": "scaleout: BASELINE configs[4], HGEMM FP16 n=32768, A replicated, B/C column-"
                                    f"sharded over {world} GPU(s); " + (
                                        "fused GEMM + all-gather: the epilogue stores every C tile into all ranks' C "
-                                       "over NVLink (CUDA IPC), one stream-ordered all-reduce per step" if fused else
+                                       "over NVLink (CUDA IPC), then an NVLink flag barrier per step" if fused else
                                        f"C all-gathered with NCCL in {chunks} chunk(s) overlapped with the GEMM of the "
                                        "next chunk, then re-laid out row-major"),
                        "n": n, "l2": "inputs larger than L2 (A alone 2 GiB)"},
@@ -452,7 +480,9 @@ def run_scaleout(args, L, torch, stream, barrier, rank, world, local):
                                       "GPU including the gather"},
             "skinny_tp": {"shape": "C(8x32768) = A(8x8192) * W^T, W 32768x8192 FP16 row-sharded", "us_per_step":
                           round(tp_us, 2), "weight_GBps_per_gpu": round(nr * Kw * 2 / (tp_us * 1e-6) / 1e9, 1),
-                          "includes": "local skinny GEMM + NCCL all-gather of the outputs + re-layout"},
+                          "includes": ("fused: skinny kernel storing its outputs into every rank's C over NVLink + "
+                                       "NVLink flag barrier, replayed as one CUDA graph per step" if fused else
+                                       "local skinny GEMM + NCCL all-gather of the outputs + re-layout")},
             "cpu_baseline": None, "e2e": None, "gpu_launches": launches, "clocks": clk}
 
 

@@ -70,6 +70,8 @@ GEN9BLAS_API int gen9blas_gemm_batched(int type, int tA, int tB, int M, int N, i
 // Fused GEMM + all-gather for column-sharded multi-GPU GEMM: this rank computes its column block
 // C[:, col_offset : col_offset + N] = alpha·op(A)·op(B) (beta = 0) and its epilogue stores every finished tile into all
 // ranks' C (peer device pointers from gen9blas_ipc_open) over NVLink, overlapping the exchange with the next tiles.
+// With M at most the skinny threshold (decode: C = X·W_shardᵀ with the weight rows split over the ranks) the skinny
+// kernel computes the block and stores its outputs the same way.
 GEN9BLAS_API int gen9blas_gemm_allgather(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A,
                                          int lda, const void *B, int ldb, void *const *rank_C, int nranks, int ldc,
                                          int64_t col_offset) {
@@ -86,8 +88,12 @@ GEN9BLAS_API int gen9blas_gemm_allgather(int type, int tA, int tB, int M, int N,
     G9_TRY(map_operand(op[1], B, ((tB ? (size_t)(N - 1) * ldb + K : (size_t)(K - 1) * ldb + N)) * es, 1, true, false));
     if (!op[0].zc || !op[1].zc) return fail(GEN9BLAS_ERR_INVALID_ARG, "gen9blas_gemm_allgather takes device operands");
     timer_kernel();
-    G9_TRY(launch_hgemm_tc(type, tA ? 1 : 0, tB ? 1 : 0, M, N, K, alpha, op[0].dptr, lda, 0, op[1].dptr, ldb, 0, 0.0,
-                           rank_C[0], ldc, 0, 1, stream(), rank_C, nranks, col_offset));
+    if (M <= skinny_threshold(type))   // tensor-parallel decode: skinny kernel, outputs stored into every rank's C
+        G9_TRY(launch_skinny(type, tA ? 1 : 0, tB ? 1 : 0, M, N, K, alpha, op[0].dptr, lda, op[1].dptr, ldb, 0.0,
+                             rank_C[0], ldc, stream(), rank_C, nranks, col_offset));
+    else
+        G9_TRY(launch_hgemm_tc(type, tA ? 1 : 0, tB ? 1 : 0, M, N, K, alpha, op[0].dptr, lda, 0, op[1].dptr, ldb, 0,
+                               0.0, rank_C[0], ldc, 0, 1, stream(), rank_C, nranks, col_offset));
     int r = finish_op(op, 2);
     timer_stop();
     return r;

@@ -124,7 +124,8 @@ int launch_gemm(int type, int tA, int tB, int M, int N, int K, double alpha, con
                 cudaStream_t st);
 // Skinny GEMM (min(M, N) small) on device pointers.
 int launch_skinny(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, const void *B,
-                  int ldb, double beta, void *C, int ldc, cudaStream_t st);
+                  int ldb, double beta, void *C, int ldc, cudaStream_t st, void *const *peers = nullptr, int npeers = 0,
+                  long long col_off = 0);
 int skinny_threshold(int type);
 
 }  // namespace g9

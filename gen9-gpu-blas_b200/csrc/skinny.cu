@@ -44,14 +44,31 @@ struct SkinnyArgs {
     long long swn, swk;
     void *C;         // C[m*scm + n*scn]
     long long scm, scn;
+    // Fused all-gather (tensor-parallel decode): the result is also stored into the C of the other ranks (peer
+    // pointers over NVLink, dst[0] == C), at element offset off = m·scm + n·scn + coff. ndst == 1: C only.
+    void *dst[8];
+    int ndst;
+    long long coff;
 };
 
 template <typename T>
 __device__ __forceinline__ void skinny_store(const SkinnyArgs &p, int m, int n, float s) {
-    T *c = (T *)p.C + (long long)m * p.scm + (long long)n * p.scn;
+    const long long off = (long long)m * p.scm + (long long)n * p.scn + p.coff;
+    T *c = (T *)p.C + off;
     float v = p.alpha * s;
     if (p.beta != 0.0f) v = __fmaf_rn(p.beta, to_r(*c), v);
-    *c = from_r<T>(v);
+    const T o = from_r<T>(v);
+    if (p.ndst == 1) {
+        *c = o;
+        return;
+    }
+    for (int q = 0; q < p.ndst; q++) ((T *)p.dst[q])[off] = o;
+}
+
+// End of every skinny kernel: with peer destinations, the thread's stores are made visible system-wide before the
+// kernel ends, so that a rank barrier enqueued after it orders them before its flag (early returns store nothing).
+__device__ __forceinline__ void skinny_peer_fence(const SkinnyArgs &p) {
+    if (p.ndst > 1) __threadfence_system();
 }
 
 // ------------------------------------------------------------------------------------------------ FP16, K-contiguous
@@ -195,6 +212,7 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *_
         }
         it += kc1 - kc0;
     }
+    skinny_peer_fence(p);
 }
 
 // ------------------------------------------------------------------------------------------------ FP32, K-contiguous
@@ -261,6 +279,7 @@ __global__ void __launch_bounds__(WK_WARPS * 32) wk_f32(const SkinnyArgs p) {
             skinny_store<float>(p, mm, n, s);
         }
     }
+    skinny_peer_fence(p);
 }
 
 // ------------------------------------------------------------------------------------------------ N-contiguous
@@ -322,6 +341,7 @@ __global__ void __launch_bounds__(256) wn_final(const SkinnyArgs p, int parts, c
     float s = 0;
     for (int q = 0; q < parts; q++) s += P[((long long)q * p.Mc + m) * p.Nc + n];
     skinny_store<T>(p, m, n, s);
+    skinny_peer_fence(p);
 }
 
 // ------------------------------------------------------------------------------------------------ generic
@@ -349,6 +369,7 @@ __global__ void __launch_bounds__(256) skinny_generic(const SkinnyArgs p) {
             if (lane == 0 && m0 + j < p.Mc) skinny_store<T>(p, m0 + j, (int)n, s);
         }
     }
+    skinny_peer_fence(p);
 }
 
 // Dense K-contiguous copy of the small operand (Mc × K, row pitch Kp = K rounded up to 8) for the fast kernels.
@@ -435,12 +456,23 @@ static int skinny_t(SkinnyArgs p, cudaStream_t st) {
 }
 
 int launch_skinny(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, const void *B,
-                  int ldb, double beta, void *C, int ldc, cudaStream_t st) {
+                  int ldb, double beta, void *C, int ldc, cudaStream_t st, void *const *peers, int npeers,
+                  long long col_off) {
     SkinnyArgs p;
     p.K = K;
     p.alpha = (float)alpha;
     p.beta = (float)beta;
     p.C = C;
+    p.ndst = 1;
+    p.dst[0] = C;
+    p.coff = 0;
+    if (peers && npeers > 0) {
+        if (npeers > 8) return fail(GEN9BLAS_ERR_INVALID_ARG, "at most 8 ranks for the fused skinny GEMM + all-gather");
+        for (int q = 0; q < npeers; q++) p.dst[q] = peers[q];
+        p.ndst = npeers;
+        p.C = peers[0];
+        p.coff = col_off;   // C is row-major with pitch ldc: a column offset is an element offset
+    }
     // Role choice of the reference (gemm.c:213-221): the smaller of M and N is the token side.
     if (M <= N) {
         p.Mc = M; p.Nc = N; p.a = A; p.w = B; p.scm = ldc; p.scn = 1;

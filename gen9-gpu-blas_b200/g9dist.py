@@ -148,22 +148,71 @@ class PeerView:
         self.opened = []
 
 
-def fused_column_sharded_gemm(lib, A, B_shard, C, peers, rank, world, accurate=False, group=None):
+class PeerBarrier:
+    """Rank barrier over NVLink peer memory (gen9blas_peer_barrier): every rank owns a zeroed array of world + 1
+    32-bit words (one flag per rank and the device-side epoch counter) mapped into the other ranks. wait() is enqueued
+    on the library's stream and can be captured in a CUDA graph; all ranks must call it the same number of times.
+    Collective construction."""
+
+    def __init__(self, lib, rank, world, device=None, timeout_ms=5000.0, group=None):
+        import torch
+        self.lib, self.rank, self.world, self.timeout_ms = lib, rank, world, timeout_ms
+        self.flags = torch.zeros(world + 1, dtype=torch.int32, device=device or torch.cuda.current_device())
+        torch.cuda.synchronize()
+        self.view = PeerView(lib, self.flags, rank, world, group=group)
+        self.arr = (ctypes.c_void_p * world)(*self.view.ptrs)
+        lib.gen9blas_peer_barrier.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_double]
+
+    def wait(self):
+        r = self.lib.gen9blas_peer_barrier(self.arr, self.world, self.rank, self.timeout_ms)
+        if r != 0:
+            raise RuntimeError(self.lib.gen9blas_error().decode())
+
+    def close(self):
+        self.view.close()
+
+
+def fused_column_sharded_gemm(lib, A, B_shard, C, peers, rank, world, accurate=False, group=None, barrier=None):
     """C (M × N on every rank) = A · B with B column-sharded, in one kernel per rank: the HGEMM epilogue writes each
-    finished tile of this rank's block into every rank's C (peers: PeerView of C) over NVLink, then a stream-ordered
-    all-reduce of one element orders the ranks before C is used. FP16 only."""
+    finished tile of this rank's block into every rank's C (peers: PeerView of C) over NVLink; then the ranks meet in
+    a barrier (barrier: PeerBarrier, else a stream-ordered NCCL all-reduce of one element) before C is used. FP16."""
     M, K = A.shape
     nb = B_shard.shape[1]
+    _allgather(lib, A, B_shard, 0, C, peers, rank * nb, accurate)
+    _meet(C, world, group, barrier)
+    return C
+
+
+def fused_row_sharded_skinny(lib, A, W_shard, C, peers, rank, world, accurate=False, group=None, barrier=None):
+    """Tensor-parallel decode: C (M × N on every rank, M <= 16) = A · Wᵀ with the weight rows split over the ranks
+    (W_shard = W[rows_rank], N/world × K). The skinny kernel stores this rank's M × N/world block into every rank's C
+    over NVLink; then the ranks meet as in fused_column_sharded_gemm. FP16."""
+    _allgather(lib, A, W_shard, 1, C, peers, rank * W_shard.shape[0], accurate)
+    _meet(C, world, group, barrier)
+    return C
+
+
+def _allgather(lib, A, B, transB, C, peers, col_off, accurate):
+    M, K = A.shape
+    nb = B.shape[0] if transB else B.shape[1]
+    world = len(peers.ptrs)
     arr = (ctypes.c_void_p * world)(*peers.ptrs)
     lib.gen9blas_gemm_allgather.argtypes = [ctypes.c_int] * 6 + [ctypes.c_double, ctypes.c_void_p, ctypes.c_int,
                                                                   ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
                                                                   ctypes.c_int, ctypes.c_int, ctypes.c_int64]
-    r = lib.gen9blas_gemm_allgather(GEN9BLAS_HS if accurate else GEN9BLAS_H, 0, 0, M, nb, K, 1.0,
-                                    A.data_ptr(), A.stride(0), B_shard.data_ptr(), B_shard.stride(0), arr, world,
-                                    C.stride(0), rank * nb)
+    r = lib.gen9blas_gemm_allgather(GEN9BLAS_HS if accurate else GEN9BLAS_H, 0, transB, M, nb, K, 1.0,
+                                    A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), arr, world,
+                                    C.stride(0), col_off)
     if r != 0:
         raise RuntimeError(lib.gen9blas_error().decode())
-    if world > 1:
+
+
+def _meet(C, world, group, barrier):
+    import torch
+    if world == 1:
+        return
+    if barrier is not None:
+        barrier.wait()
+    else:
         flag = torch.ones(1, device=C.device)
         torch.distributed.all_reduce(flag, group=group)
-    return C

@@ -180,11 +180,23 @@ GEN9BLAS_API int gen9blas_ipc_close(void *peer_ptr);
 /* Fused GEMM + all-gather of a column-sharded FP16 GEMM (type GEN9BLAS_H or _HS): this rank computes its column block
  * C[:, col_offset : col_offset + N] = alpha·op(A)·op(B) (M × N, beta = 0) and the tensor-core kernel's epilogue stores
  * every finished tile into the C of all nranks ranks (rank_C: their device pointers, own C included, row pitch ldc)
- * with plain NVLink stores, overlapping the exchange with the remaining tiles. A and B must be device memory. The
- * caller synchronises the ranks (e.g. a barrier) before reading C. At most 8 ranks. */
+ * with plain NVLink stores, overlapping the exchange with the remaining tiles. With M at most 16 (decode: C = X·Wᵀ
+ * with the weight rows split over the ranks, transB = 1) the skinny kernel computes the block and stores its outputs
+ * the same way. A and B must be device memory. The caller synchronises the ranks (gen9blas_peer_barrier) before
+ * reading C. At most 8 ranks. */
 GEN9BLAS_API int gen9blas_gemm_allgather(int type, int transA, int transB, int M, int N, int K, double alpha,
                                          const void *A, int lda, const void *B, int ldb, void *const *rank_C,
                                          int nranks, int ldc, int64_t col_offset);
+/* Barrier of the ranks over NVLink peer memory, enqueued on the library's stream (no counterpart in the reference).
+ * rank_flags[q]: device pointer (own or peer-mapped with gen9blas_ipc_open) to rank q's array of nranks + 1 32-bit
+ * words, all zero before the first barrier. The kernel raises this rank's flag in every array (after the stores of
+ * the preceding work on this stream) and waits until every rank's flag in this rank's array is raised, so that work
+ * enqueued after it sees every rank's stores (e.g. a gen9blas_gemm_allgather result). The epoch of each barrier is
+ * counted in the array's last word on the device, so the call can be captured in a CUDA graph and replayed; every
+ * rank must run the same sequence of barriers on the same arrays. The wait gives up after timeout_ms (0.1 .. 60000):
+ * the call (or, with no-wait, the next synchronising call) returns GEN9BLAS_ERR and the device stays usable. At most
+ * 8 ranks. */
+GEN9BLAS_API int gen9blas_peer_barrier(void *const *rank_flags, int nranks, int rank, double timeout_ms);
 /* Number of kernels this library launched since the process started (launch accounting for benchmarks). */
 GEN9BLAS_API long long gen9blas_kernel_launches(void);
 /* Diagnostic of the bounded device-side waits: runs a kernel whose mbarrier wait can never complete; the wait gives

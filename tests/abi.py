@@ -22,6 +22,7 @@ SIGNATURES = {
     "flush": ([], _i), "kernel_launches": ([], ctypes.c_longlong),
     "selftest_wait": ([_d], _i),
     "gemv_noalloc": ([_i, _i, _i, _i, _d, _p, _i, _p, _i, _d, _p, _i], _i),
+    "peer_barrier": ([_p, _i, _i, _d], _i),
 }
 
 

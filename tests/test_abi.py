@@ -31,7 +31,7 @@ def test_header_declares_reference_surface():
                  "gen9blas_dot", "gen9blas_nrm2", "gen9blas_asum", "gen9blas_iamax", "gen9blas_gemv", "gen9blas_ger",
                  "gen9blas_init", "gen9blas_error", "gen9blas_alloc", "gen9blas_spr2", "gen9blas_set_device"):
         assert must in names
-    assert len(names) == 65
+    assert len(names) == 66
 
 
 def test_library_exports_every_declared_function():

@@ -1,5 +1,7 @@
 """Multi-GPU paths on real GPUs (skipped with fewer than 2): the fused GEMM + all-gather kernel writing into the
-other rank's C over NVLink through CUDA IPC, and the NCCL column-sharded GEMM, both against the full product."""
+other rank's C over NVLink through CUDA IPC (ranks met by an NCCL all-reduce, then by the NVLink flag barrier), the
+NCCL column-sharded GEMM, and the tensor-parallel skinny GEMM whose outputs go straight into every rank's C, all
+against the full product."""
 import os
 import socket
 import subprocess
@@ -42,10 +44,37 @@ g9dist.column_sharded_gemm(A, Bs, C2, rank, world, lambda a, b, c: g9dist.gemm_l
                            comm_stream=torch.cuda.Stream())
 torch.cuda.synchronize()
 e2 = float(((C2.double() - ref).abs() / scale).max())
+# the same fused GEMM with the NVLink rank barrier instead of the NCCL all-reduce
+bar = g9dist.PeerBarrier(lib, rank, world)
+C.zero_()
+torch.cuda.synchronize()
+dist.barrier()   # every rank's C is zeroed before any rank stores into it
+g9dist.fused_column_sharded_gemm(lib, A, Bs, C, peers, rank, world, barrier=bar)
+torch.cuda.synchronize()
+e3 = float(((C.double() - ref).abs() / scale).max())
+# tensor-parallel decode: weight rows split over the ranks, outputs stored into every rank's C, barrier; three rounds
+Mw, Kw, Nw = 8, 1024, 4096
+W = (torch.randn(Nw, Kw, device="cuda", generator=g) * 0.02).half()
+nr = Nw // world
+Ws = W[rank * nr:(rank + 1) * nr].contiguous()
+Cs = torch.zeros(Mw, Nw, device="cuda", dtype=torch.float16)
+pv = g9dist.PeerView(lib, Cs, rank, world)
+e4 = 0.0
+for it in range(3):
+    X = torch.randn(Mw, Kw, device="cuda", generator=g, dtype=torch.float16)
+    torch.cuda.synchronize()
+    g9dist.fused_row_sharded_skinny(lib, X, Ws, Cs, pv, rank, world, barrier=bar)
+    torch.cuda.synchronize()
+    r4 = X.double() @ W.double().t()
+    s4 = X.double().abs() @ W.double().abs().t()
+    e4 = max(e4, float(((Cs.double() - r4).abs() / s4).max()))
+    dist.barrier()   # nobody overwrites Cs for the next round before every rank has checked this one
 dist.barrier()
+pv.close()
+bar.close()
 peers.close()
 dist.destroy_process_group()
-print("ERR", rank, e1, e2)
+print("ERR", rank, e1, e2, e3, e4)
 '''
 
 
@@ -72,4 +101,4 @@ def test_fused_and_nccl_allgather_two_ranks():
     for p, (o, e) in zip(procs, outs):
         assert p.returncode == 0, e[-2000:]
         line = [ln for ln in o.splitlines() if ln.startswith("ERR")][0].split()
-        assert float(line[2]) <= 1e-3 and float(line[3]) <= 1e-3, line
+        assert all(float(v) <= 1e-3 for v in line[2:6]), line
