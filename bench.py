@@ -325,9 +325,9 @@ def run_ours(args):
                    "h2d_bytes_per_step": 2 * n * n * 2, "d2h_bytes_per_step": n * n * 2,
                    "steps": e2e_steps, "path": "gen9blas_gemm(GEN9BLAS_H) on pinned host pointers"}
         peak_t, _, peak_kind = measured_peaks()
-        traffic = profile_traffic("hgemm_tc_n4096")
+        traffic = profile_traffic("hgemm_tc2_n4096")
         roof = {"bound": "tensor", "achieved": round(value, 2), "peak": peak_t, "unit": "TFLOP/s",
-                "frac": round(value / peak_t, 4), "traffic": traffic, "kernel": "hgemm_tc_kernel<true>",
+                "frac": round(value / peak_t, 4), "traffic": traffic, "kernel": "hgemm_tc2_kernel<true, 256> (CTA pair, 256x256 tiles)",
                 "algorithmic": f"2*n^3 = {flops:.4g} FLOP per launch, one launch per step",
                 "peak_kind": f"{peak_kind} cuBLAS bf16 dense, sustained (the timed loop runs ~0.5 s under the 1 kW "
                              "power cap), MEASURED_PEAKS.json"}
@@ -402,15 +402,9 @@ def run_scaleout(args, L, torch, stream, barrier, rank, world, local):
         barrier()
         return float(ms.item()), launches
 
-    for _ in range(warm):
-        step()
-    clocks = ClockSampler(local)
-    clocks.start()
-    ms_total, launches = timed(step, steps)
-    clk = clocks.stop()
-    value = flops * steps / (ms_total * 1e-3) / 1e12
 
-    # tensor-parallel skinny GEMM (decode): C (8 × 32768) = A · Wᵀ, W rows split over the ranks
+    # tensor-parallel skinny GEMM (decode): C (8 × 32768) = A · Wᵀ, W rows split over the ranks. Measured before the
+    # long dense GEMM, whose power draw leaves the GPUs at capped clocks for a while.
     Nw, Kw, Mw = 32768, 8192, 8
     nr = Nw // world
     Wsh = torch.randn(nr, Kw, device="cuda", generator=g, dtype=torch.float16).mul_(0.02)
@@ -453,8 +447,53 @@ def run_scaleout(args, L, torch, stream, barrier, rank, world, local):
 
         for _ in range(5):
             tp_run()
-    tp_ms, tp_launches = timed(tp_run, 50)
-    tp_us = tp_ms * 1e3 / 50
+    tp_ms, tp_launches = timed(tp_run, 200)
+    tp_us = tp_ms * 1e3 / 200
+
+    for _ in range(warm):
+        step()
+    clocks = ClockSampler(local)
+    clocks.start()
+    ms_total, launches = timed(step, steps)
+    clk = clocks.stop()
+    value = flops * steps / (ms_total * 1e-3) / 1e12
+
+    # e2e through the public path with this rank's inputs in pinned host memory: every step copies A and the rank's
+    # B block to the device, runs the sharded GEMM + gather, and reads the rank's block of C back (together the ranks
+    # read all of C). Wall clock between barriers, max over ranks.
+    e2e = None
+    if not args.no_e2e:
+        hA = torch.empty((n, n), dtype=torch.float16, pin_memory=True)
+        hB = torch.empty((n, nb), dtype=torch.float16, pin_memory=True)
+        hC = torch.empty((n, nb), dtype=torch.float16, pin_memory=True)
+        hA.copy_(A)
+        hB.copy_(Bs)
+        e2e_steps = 3
+
+        def e2e_step():
+            with torch.cuda.stream(stream):
+                A.copy_(hA, non_blocking=True)
+                Bs.copy_(hB, non_blocking=True)
+            step()
+            with torch.cuda.stream(stream):
+                hC.copy_(C[:, rank * nb:(rank + 1) * nb], non_blocking=True)
+            stream.synchronize()
+
+        e2e_step()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            e2e_step()
+        dt = torch.tensor([time.perf_counter() - t0], device="cuda", dtype=torch.float64)
+        if world > 1:
+            torch.distributed.all_reduce(dt, op=torch.distributed.ReduceOp.MAX)
+        barrier()
+        e2e = {"value": round(flops * e2e_steps / float(dt.item()) / 1e12, 3), "unit": "TFLOP/s",
+               "h2d_bytes_per_step": world * (n * n * 2 + n * nb * 2), "d2h_bytes_per_step": n * n * 2,
+               "steps": e2e_steps,
+               "path": "per rank: A and B block pinned host -> device, sharded GEMM + gather, C block -> host; "
+                       "bytes summed over the ranks"}
+        del hA, hB, hC
     if peers is not None:
         torch.cuda.synchronize()
         if world > 1:
@@ -483,7 +522,7 @@ def run_scaleout(args, L, torch, stream, barrier, rank, world, local):
                           "includes": ("fused: skinny kernel storing its outputs into every rank's C over NVLink + "
                                        "NVLink flag barrier, replayed as one CUDA graph per step" if fused else
                                        "local skinny GEMM + NCCL all-gather of the outputs + re-layout")},
-            "cpu_baseline": None, "e2e": None, "gpu_launches": launches, "clocks": clk}
+            "cpu_baseline": None, "e2e": e2e, "gpu_launches": launches, "clocks": clk}
 
 
 # --------------------------------------------------------------------------------------------- per-row measurements

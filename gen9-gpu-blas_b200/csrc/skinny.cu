@@ -187,19 +187,35 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *_
                 const int row = g + ((e & 2) ? 8 : 0), tok = 2 * t + (e & 1) + (e >= 4 ? 8 : 0);
                 sp[row * 16 + tok] = e < 4 ? d0[e] : d1[e - 4];
             }
+            // The warp's partial stores are ordered before the counter update by the warp barrier and the release of
+            // the atomic (cumulative at GPU scope); the last arriver's acquire makes every slot visible to its lanes.
             __syncwarp();
-            __threadfence();
             int prev = 0;
-            if (lane == 0) prev = atomicAdd(count + blk, 1);
+            if (lane == 0)
+                asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(prev) : "l"(count + blk) : "memory");
             prev = __shfl_sync(0xffffffffu, prev, 0);
             if (prev == nc - 1) {
-                __threadfence();
+                __syncwarp();   // the lanes' slot reads are ordered after lane 0's acquire
                 const int row = lane >> 1, tb = (lane & 1) * 8;
                 if (t0 + tb < p.Mc && r0 + row < p.Nc) {
                     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                    for (int q = 0; q < nc; q++) {
-                        const float4 *src = reinterpret_cast<const float4 *>(part + (blk * maxc + q) * 256 + row * 16 + tb);
-                        const float4 u0 = __ldcg(src), u1 = __ldcg(src + 1);
+                    const float4 *src0 = reinterpret_cast<const float4 *>(part + blk * maxc * 256 + row * 16 + tb);
+                    int q = 0;
+                    for (; q + 4 <= nc; q += 4) {   // four slots' loads in flight, summed in slot order
+                        float4 u[4][2];
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            u[j][0] = __ldcg(src0 + (q + j) * 64);
+                            u[j][1] = __ldcg(src0 + (q + j) * 64 + 1);
+                        }
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            acc[0] += u[j][0].x; acc[1] += u[j][0].y; acc[2] += u[j][0].z; acc[3] += u[j][0].w;
+                            acc[4] += u[j][1].x; acc[5] += u[j][1].y; acc[6] += u[j][1].z; acc[7] += u[j][1].w;
+                        }
+                    }
+                    for (; q < nc; q++) {
+                        const float4 u0 = __ldcg(src0 + q * 64), u1 = __ldcg(src0 + q * 64 + 1);
                         acc[0] += u0.x; acc[1] += u0.y; acc[2] += u0.z; acc[3] += u0.w;
                         acc[4] += u1.x; acc[5] += u1.y; acc[6] += u1.z; acc[7] += u1.w;
                     }
