@@ -35,6 +35,8 @@ struct DevState {
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     unsigned *gemm_flags = nullptr;                            // split-K handoff flags of the HGEMM pair kernel (zeroed)
     unsigned gemm_epoch = 0;                                   // launch counter written into those flags
+    void *l3 = nullptr;                                        // level-3 work matrices (grow-only)
+    size_t l3_n = 0;
     int *sk_count = nullptr;                                   // arrival counters of the stream-K skinny kernel (zeroed;
     size_t sk_count_n = 0;                                     // every launch leaves them at zero)
 };

@@ -23,21 +23,6 @@ GEN9BLAS_API int gen9blas_gemm_pb(int, int, double, const void *, int, const gen
     G9_UNSUPPORTED("gen9blas_gemm_pb");
 }
 GEN9BLAS_API void gen9blas_packed_b_free(gen9blas_packed_b *) {}
-GEN9BLAS_API int gen9blas_symm(int, int, int, int, int, double, const void *, int, const void *, int, double, void *, int) {
-    G9_UNSUPPORTED("gen9blas_symm");
-}
-GEN9BLAS_API int gen9blas_syrk(int, int, int, int, int, double, const void *, int, double, void *, int) {
-    G9_UNSUPPORTED("gen9blas_syrk");
-}
-GEN9BLAS_API int gen9blas_syr2k(int, int, int, int, int, double, const void *, int, const void *, int, double, void *, int) {
-    G9_UNSUPPORTED("gen9blas_syr2k");
-}
-GEN9BLAS_API int gen9blas_trmm(int, int, int, int, int, int, int, double, const void *, int, void *, int) {
-    G9_UNSUPPORTED("gen9blas_trmm");
-}
-GEN9BLAS_API int gen9blas_trsm(int, int, int, int, int, int, int, double, const void *, int, void *, int) {
-    G9_UNSUPPORTED("gen9blas_trsm");
-}
 GEN9BLAS_API int gen9blas_scal(int, int, double, void *, int) { G9_UNSUPPORTED("gen9blas_scal"); }
 GEN9BLAS_API int gen9blas_copy(int, int, const void *, int, void *, int) { G9_UNSUPPORTED("gen9blas_copy"); }
 GEN9BLAS_API int gen9blas_swap(int, int, void *, int, void *, int) { G9_UNSUPPORTED("gen9blas_swap"); }

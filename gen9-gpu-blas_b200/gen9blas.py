@@ -7,9 +7,11 @@
     X = gen9blas.empty((n, n), np.float16)        # managed memory: used in place by the GPU, writable by the CPU
     gen9blas.axpy(0.5, x, y); d = gen9blas.dot(x, y); i = gen9blas.iamax(x)
     y = gen9blas.gemv(A, x); gen9blas.ger(1.0, x, y, A)
+    C = gen9blas.symm(S, B); C = gen9blas.syrk(A, "L"); X = gen9blas.trsm(T, B, "L", "U")   # level 3 on GEMM
 
 Same function names, argument meaning and error behaviour as the reference module lib/gen9blas.py of
-kprzybys/gen9-gpu-blas (gemm/hgemm/sgemm/gemm_batched 168-204, empty/free_pool 60-115, axpy..ger 335-419): the type
+kprzybys/gen9-gpu-blas (gemm/hgemm/sgemm/gemm_batched 168-204, symm..trsm 207-272, empty/free_pool 60-115,
+axpy..ger 335-419): the type
 follows the dtype, views map to leading dimensions and transpose flags (lib/gen9blas.py:316-328), errors raise
 RuntimeError with gen9blas_error(). Plain NumPy arrays are staged through device buffers by the library; arrays from
 gen9blas.empty() live in CUDA managed memory and are used in place.
@@ -45,6 +47,11 @@ _lib.gen9blas_nrm2.argtypes = [_i, _i, _p, _i, ctypes.POINTER(_d)]
 _lib.gen9blas_iamax.argtypes = [_i, _i, _p, _i, ctypes.POINTER(_l)]
 _lib.gen9blas_gemv.argtypes = [_i, _i, _i, _i, _d, _p, _i, _p, _i, _d, _p, _i]
 _lib.gen9blas_ger.argtypes = [_i, _i, _i, _d, _p, _i, _p, _i, _p, _i]
+_lib.gen9blas_symm.argtypes = [_i, _i, _i, _i, _i, _d, _p, _i, _p, _i, _d, _p, _i]
+_lib.gen9blas_syrk.argtypes = [_i, _i, _i, _i, _i, _d, _p, _i, _d, _p, _i]
+_lib.gen9blas_syr2k.argtypes = [_i, _i, _i, _i, _i, _d, _p, _i, _p, _i, _d, _p, _i]
+_lib.gen9blas_trmm.argtypes = [_i, _i, _i, _i, _i, _i, _i, _d, _p, _i, _p, _i]
+_lib.gen9blas_trsm.argtypes = [_i, _i, _i, _i, _i, _i, _i, _d, _p, _i, _p, _i]
 _lib.gen9blas_set_device.argtypes = [_i]
 _lib.gen9blas_set_stream.argtypes = [_p]
 _lib.gen9blas_set_nowait.argtypes = [_i]
@@ -217,6 +224,95 @@ def gemm_batched(A, B, alpha=1.0, beta=0.0, C=None, accurate=False):
     _check(_lib.gen9blas_gemm_batched(_kind(dt, accurate), 0, 0, M, N, K, alpha, a.ctypes.data, K, M * K,
                                       b.ctypes.data, N, K * N, beta if given else 0.0, C.ctypes.data, N, M * N, cnt))
     return C
+
+
+# ---------------- level 3 on GEMM (lib/gen9blas.py:207-272 of the reference) ----------------
+_SIDE = {"L": 0, "R": 1}
+_TRI = {"L": 0, "U": 1}
+
+
+def _square(A, dt, uplo):
+    """(array, pointer, n, ld, trans, uplo) of a square operand; a transposed view is the same memory read with the
+    triangle swapped (and, for triangular operands, transA flipped)."""
+    if A.ndim != 2 or A.shape[0] != A.shape[1]:
+        raise ValueError("expected a square matrix")
+    a, pa, lda, ta = _m3(A, dt)
+    if ta:
+        uplo = "U" if uplo == "L" else "L"
+    return a, pa, A.shape[0], lda, ta, uplo
+
+
+def symm(A, B, side="L", uplo="L", alpha=1.0, beta=0.0, C=None, accurate=False):
+    """C = alpha·A·B + beta·C (side="L") or alpha·B·A + beta·C (side="R"); A symmetric, its uplo triangle is read."""
+    _init()
+    dt = B.dtype if B.dtype in (np.float16, np.float32, np.float64) else np.float32
+    a, pa, n, lda, _, uplo = _square(A, dt, uplo)
+    b, pb, ldb, tb = _m3(B, dt)
+    if tb:
+        b, pb, ldb, tb = _m3(_c(B, dt), dt)
+    M, N = b.shape
+    if n != (M if side == "L" else N):
+        raise ValueError(f"incompatible dimensions: {A.shape} and {B.shape} (side {side})")
+    C, given, ldc = _output(C, (M, N), dt)
+    _check(_lib.gen9blas_symm(_kind(dt, accurate), _SIDE[side], _TRI[uplo], M, N, alpha, pa, lda, pb, ldb,
+                              beta if given else 0.0, C.ctypes.data, ldc))
+    return C
+
+
+def syrk(A, uplo="L", trans=False, alpha=1.0, beta=0.0, C=None, accurate=False):
+    """C = alpha·op(A)·op(A)ᵀ + beta·C on the uplo triangle (the other triangle of C is not modified)."""
+    _init()
+    dt = A.dtype if A.dtype in (np.float16, np.float32, np.float64) else np.float32
+    N, K = (A.shape[1], A.shape[0]) if trans else A.shape
+    a, pa, lda, ta = _m3(A, dt)   # a transposed view flips trans
+    C, given, ldc = _output(C, (N, N), dt)
+    if not given:
+        C[...] = 0
+    _check(_lib.gen9blas_syrk(_kind(dt, accurate), _TRI[uplo], int(trans) ^ ta, N, K, alpha, pa, lda,
+                              beta if given else 0.0, C.ctypes.data, ldc))
+    return C
+
+
+def syr2k(A, B, uplo="L", trans=False, alpha=1.0, beta=0.0, C=None, accurate=False):
+    """C = alpha·(op(A)·op(B)ᵀ + op(B)·op(A)ᵀ) + beta·C on the uplo triangle."""
+    _init()
+    dt = A.dtype if A.dtype in (np.float16, np.float32, np.float64) else np.float32
+    N, K = (A.shape[1], A.shape[0]) if trans else A.shape
+    a, pa, lda, ta = _m3(A, dt)
+    b, pb, ldb, tb = _m3(B, dt)
+    if ta != tb:   # one trans flag for both operands: B is copied to A's layout
+        b, pb, ldb, tb = _m3(np.ascontiguousarray(B.T, dtype=dt).T if ta else _c(B, dt), dt)
+    C, given, ldc = _output(C, (N, N), dt)
+    if not given:
+        C[...] = 0
+    _check(_lib.gen9blas_syr2k(_kind(dt, accurate), _TRI[uplo], int(trans) ^ ta, N, K, alpha, pa, lda, pb, ldb,
+                               beta if given else 0.0, C.ctypes.data, ldc))
+    return C
+
+
+def trmm(A, B, side="L", uplo="L", transA=False, diag=False, alpha=1.0, accurate=False):
+    """Returns alpha·op(A)·B (side="L") or alpha·B·op(A) (side="R"); A triangular. B is not modified."""
+    _init()
+    dt = B.dtype if B.dtype in (np.float16, np.float32, np.float64) else np.float32
+    a, pa, _, lda, ta, uplo = _square(A, dt, uplo)
+    b = np.array(B, dtype=dt, order="C", copy=True)
+    M, N = b.shape
+    _check(_lib.gen9blas_trmm(_kind(dt, accurate), _SIDE[side], _TRI[uplo], int(transA) ^ ta, int(diag), M, N,
+                              alpha, pa, lda, b.ctypes.data, N))
+    return b
+
+
+def trsm(A, B, side="L", uplo="L", transA=False, diag=False, alpha=1.0, accurate=False):
+    """Returns X with op(A)·X = alpha·B (side="L") or X·op(A) = alpha·B (side="R"); A triangular. B is not modified.
+    Diagonal-block inverses in FP64 on the GPU; the block updates in the element type's GEMM."""
+    _init()
+    dt = B.dtype if B.dtype in (np.float16, np.float32, np.float64) else np.float32
+    a, pa, _, lda, ta, uplo = _square(A, dt, uplo)
+    b = np.array(B, dtype=dt, order="C", copy=True)
+    M, N = b.shape
+    _check(_lib.gen9blas_trsm(_kind(dt, accurate), _SIDE[side], _TRI[uplo], int(transA) ^ ta, int(diag), M, N,
+                              alpha, pa, lda, b.ctypes.data, N))
+    return b
 
 
 def last_time_ms():

@@ -7,7 +7,9 @@
    order (element-wise FMA results and iamax indices), with the call recipe of tools/golden/blas_golden.py:16-66.
 2. ref_cblas_outputs.npz: outputs of the reference's CBLAS layer itself (oracle/_ref/libgen9blas_blas_ref.so, built
    from lib/src/cblas.c by oracle/Makefile, running on OpenBLAS) for small seeded calls: row- and column-major SGEMM /
-   DGEMM with all transposes, alpha/beta, non-tile-multiple sizes, gemv N/T, ger, axpy, dot, nrm2, asum, iamax.
+   DGEMM with all transposes, alpha/beta, non-tile-multiple sizes, gemv N/T, ger, axpy, dot, nrm2, asum, iamax, and
+   the level-3 set on GEMM (row- and column-major SYMM, SYRK, SYR2K, TRMM, TRSM over every side / triangle /
+   transpose / diagonal option; inputs from l3_inputs).
 The GPU box never reads the reference: the tests only read these files.
 """
 import ctypes
@@ -63,6 +65,105 @@ def hash_seed(*parts):
     for ch in repr(parts):
         s = (s * 131 + ord(ch)) % (1 << 61)
     return s
+
+
+Upper, Lower, NonUnit, Unit, Left, Right = 121, 122, 131, 132, 141, 142
+L3_SYMM = (23, 17, 1.5, -0.5)          # M, N, alpha, beta
+L3_SYRK = (19, 27, 0.7, 0.3)           # N, K, alpha, beta
+L3_TRXM = (21, 13, 1.25)               # M, N, alpha
+
+
+def l3_inputs(tag, op, *key):
+    """Seeded logical inputs of one level-3 case: SYMM (A n×n, B, C0), SYRK/SYR2K (A, B as op-shapes N×K before the
+    trans flag, C0), TRMM/TRSM (A n×n with a dominant diagonal so that the triangular solves are well conditioned,
+    B)."""
+    dt = np.float32 if tag == "s" else np.float64
+    rng = np.random.default_rng(hash_seed(tag, op, key))
+    if op == "symm":
+        side = key[1]
+        M, N = L3_SYMM[:2]
+        n = M if side == Left else N
+        return (rng.uniform(-1, 1, (n, n)).astype(dt), rng.uniform(-1, 1, (M, N)).astype(dt),
+                rng.uniform(-1, 1, (M, N)).astype(dt))
+    if op in ("syrk", "syr2k"):
+        trans = key[2]
+        N, K = L3_SYRK[:2]
+        shape = (K, N) if trans == Trans else (N, K)
+        return (rng.uniform(-1, 1, shape).astype(dt), rng.uniform(-1, 1, shape).astype(dt),
+                rng.uniform(-1, 1, (N, N)).astype(dt))
+    side = key[1]
+    M, N = L3_TRXM[:2]
+    n = M if side == Left else N
+    A = rng.uniform(-1, 1, (n, n))
+    A[np.diag_indices(n)] = n + rng.uniform(0, 1, n)
+    return A.astype(dt), rng.uniform(-1, 1, (M, N)).astype(dt)
+
+
+def store(X, order):
+    """(storage array, leading dimension) of a logical matrix in the given CBLAS order."""
+    if order == RowMajor:
+        return np.ascontiguousarray(X), X.shape[1]
+    return np.asfortranarray(X), X.shape[0]
+
+
+def l3_cases():
+    """Every (op, order, options) combination of the level-3 fixtures."""
+    for order in (RowMajor, ColMajor):
+        for side in (Left, Right):
+            for uplo in (Upper, Lower):
+                yield ("symm", order, side, uplo)
+        for uplo in (Upper, Lower):
+            for trans in (NoTrans, Trans):
+                yield ("syrk", order, uplo, trans)
+                yield ("syr2k", order, uplo, trans)
+        for side in (Left, Right):
+            for uplo in (Upper, Lower):
+                for trans in (NoTrans, Trans):
+                    for diag in (NonUnit, Unit):
+                        yield ("trmm", order, side, uplo, trans, diag)
+                        yield ("trsm", order, side, uplo, trans, diag)
+
+
+def l3_key(tag, case):
+    return tag + case[0] + "_" + "_".join(str(v) for v in case[1:])
+
+
+def run_l3(L, tag, case):
+    """Runs one level-3 case through CBLAS library L; returns the logical (row-major) result matrix."""
+    F = ctypes.c_float if tag == "s" else ctypes.c_double
+    I, P = ctypes.c_int, ctypes.c_void_p
+    op, order = case[0], case[1]
+    if op == "symm":
+        side, uplo = case[2], case[3]
+        M, N, al, be = L3_SYMM
+        A, B, C0 = l3_inputs(tag, op, *case[1:])
+        (As, lda), (Bs, ldb), (Cs, ldc) = store(A, order), store(B, order), store(C0.copy(), order)
+        f = getattr(L, f"cblas_{tag}symm")
+        f.argtypes = [I, I, I, I, I, F, P, I, P, I, F, P, I]
+        f(order, side, uplo, M, N, al, As.ctypes.data, lda, Bs.ctypes.data, ldb, be, Cs.ctypes.data, ldc)
+        return np.ascontiguousarray(Cs)
+    if op in ("syrk", "syr2k"):
+        uplo, trans = case[2], case[3]
+        N, K, al, be = L3_SYRK
+        A, B, C0 = l3_inputs(tag, op, *case[1:])
+        (As, lda), (Bs, ldb), (Cs, ldc) = store(A, order), store(B, order), store(C0.copy(), order)
+        if op == "syrk":
+            f = getattr(L, f"cblas_{tag}syrk")
+            f.argtypes = [I, I, I, I, I, F, P, I, F, P, I]
+            f(order, uplo, trans, N, K, al, As.ctypes.data, lda, be, Cs.ctypes.data, ldc)
+        else:
+            f = getattr(L, f"cblas_{tag}syr2k")
+            f.argtypes = [I, I, I, I, I, F, P, I, P, I, F, P, I]
+            f(order, uplo, trans, N, K, al, As.ctypes.data, lda, Bs.ctypes.data, ldb, be, Cs.ctypes.data, ldc)
+        return np.ascontiguousarray(Cs)
+    side, uplo, trans, diag = case[2:]
+    M, N, al = L3_TRXM
+    A, B = l3_inputs(tag, op, *case[1:])
+    (As, lda), (Bs, ldb) = store(A, order), store(B.copy(), order)
+    f = getattr(L, f"cblas_{tag}{op}")
+    f.argtypes = [I, I, I, I, I, I, I, F, P, I, P, I]
+    f(order, side, uplo, trans, diag, M, N, al, As.ctypes.data, lda, Bs.ctypes.data, ldb)
+    return np.ascontiguousarray(Bs)
 
 
 def vec_inputs(tag, what, *shape):
@@ -135,6 +236,8 @@ def ref_outputs():
         iam.argtypes = [I, P, I]
         iam.restype = ctypes.c_size_t
         res[f"i{tag}amax"] = np.array(iam(n, x.ctypes.data, 1), np.int64)
+        for case in l3_cases():
+            res[l3_key(tag, case)] = run_l3(L, tag, case)
     return res
 
 

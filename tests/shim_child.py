@@ -14,7 +14,8 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 sys.path.insert(0, os.path.join(HERE, "golden"))
-from make_golden import GEMM_CASES, ColMajor, NoTrans, RowMajor, Trans, gemm_inputs, vec_inputs  # noqa: E402
+from make_golden import (GEMM_CASES, L3_SYMM, L3_SYRK, L3_TRXM, ColMajor, Left, NoTrans, RowMajor, Trans,  # noqa: E402
+                         Unit, Upper, gemm_inputs, l3_cases, l3_inputs, l3_key, run_l3, vec_inputs)
 
 OPENBLAS_DIR = "/opt/prime-rl/.venv/lib/python3.12/site-packages/opencv_python_headless.libs"
 for dep in ("libquadmath-2284e583.so.0.0.0", "libgfortran-83c28eba.so.5.0.0"):
@@ -54,6 +55,57 @@ def group_cblas_gemm():
                         want = REF[f"{tag}gemm_o{order}_t{ta}{tb}_{M}x{N}x{K}"]
                         worst = max(worst, rel(np.ascontiguousarray(Cs), want, scale))
         out[f"{tag}gemm_vs_ref_cblas"] = worst
+    return out
+
+
+def l3_scale(tag, case):
+    """Denominator of the elementwise metric of lib/test_level3.py for one level-3 case (logical matrices)."""
+    op = case[0]
+    f64 = lambda x: x.astype(np.float64)
+    if op == "symm":
+        side, uplo = case[2], case[3]
+        M, N, al, be = L3_SYMM
+        A, B, C0 = l3_inputs(tag, op, *case[1:])
+        S = np.abs(f64(A))
+        return abs(al) * (S @ np.abs(f64(B)) if side == Left else np.abs(f64(B)) @ S) + abs(be) * np.abs(f64(C0))
+    if op in ("syrk", "syr2k"):
+        trans = case[3]
+        N, K, al, be = L3_SYRK
+        A, B, C0 = l3_inputs(tag, op, *case[1:])
+        oA, oB = (f64(A).T, f64(B).T) if trans == Trans else (f64(A), f64(B))
+        P = np.abs(oA) @ np.abs(oA).T if op == "syrk" else np.abs(oA) @ np.abs(oB).T + np.abs(oB) @ np.abs(oA).T
+        return abs(al) * P + abs(be) * np.abs(f64(C0))
+    side = case[2]
+    M, N, al = L3_TRXM
+    A, B = l3_inputs(tag, op, *case[1:])
+    return abs(al) * (np.abs(f64(A)) @ np.abs(f64(B)) if side == Left else np.abs(f64(B)) @ np.abs(f64(A)))
+
+
+def group_level3():
+    """SYMM / SYRK / SYR2K / TRMM / TRSM, row- and column-major, every option: compared with the reference CBLAS
+    layer's own outputs. Metric of lib/test_level3.py: elementwise for the products (the untouched triangle of
+    SYRK / SYR2K must match exactly), max|X - X_ref| / max|X_ref| for TRSM."""
+    out = {}
+    for tag in ("s", "d"):
+        worst = {"symm": 0.0, "syrk": 0.0, "syr2k": 0.0, "trmm": 0.0, "trsm": 0.0}
+        other_exact = True
+        for case in l3_cases():
+            got = run_l3(L, tag, case)
+            want = REF[l3_key(tag, case)]
+            op = case[0]
+            if op == "trsm":
+                e = float(np.abs(got.astype(np.float64) - want).max() / np.abs(want).max())
+            else:
+                e = rel(got, want, np.maximum(l3_scale(tag, case), 1e-30))
+            worst[op] = max(worst[op], e)
+            if op in ("syrk", "syr2k"):   # the triangle that is not uplo stays as C0
+                order, uplo = case[1], case[2]
+                lower_logical = (uplo != Upper)
+                mask = np.triu(np.ones(got.shape, bool), 1) if lower_logical else np.tril(np.ones(got.shape, bool), -1)
+                other_exact &= bool(np.array_equal(got[mask], want[mask]))
+        for op, v in worst.items():
+            out[f"{tag}{op}"] = v
+        out[f"{tag}_other_triangle_exact"] = other_exact
     return out
 
 
@@ -151,5 +203,6 @@ def group_forwarded():
 
 
 if __name__ == "__main__":
-    groups = {"cblas_gemm": group_cblas_gemm, "fortran_l12": group_fortran_and_l12, "forwarded": group_forwarded}
+    groups = {"cblas_gemm": group_cblas_gemm, "fortran_l12": group_fortran_and_l12, "forwarded": group_forwarded,
+              "level3": group_level3}
     print(json.dumps(groups[sys.argv[1]]()))

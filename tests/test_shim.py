@@ -38,6 +38,30 @@ def test_cpu_mode_routes_everything_to_the_cpu_blas():
     assert "-> GPU" not in err and "sgemm -> CPU" in err
 
 
+def test_cpu_mode_level3_is_the_reference_cblas():
+    """GEN9BLAS_BLAS=cpu: the level-3 symbols go to the CPU BLAS and reproduce the reference layer's outputs."""
+    res, err = child("level3", GEN9BLAS_BLAS="cpu", GEN9BLAS_BLAS_INFO="1")
+    for tag in ("s", "d"):
+        for op in ("symm", "syrk", "syr2k", "trmm", "trsm"):
+            assert res[tag + op] <= (1e-6 if tag == "s" else 1e-13), (tag + op, res[tag + op])
+        assert res[tag + "_other_triangle_exact"]
+    assert "-> GPU" not in err and "strsm -> CPU" in err
+
+
+@pytest.mark.gpu
+def test_gpu_level3_matches_reference_cblas():
+    """SYMM, SYRK, SYR2K, TRMM, TRSM (S and D, row- and column-major, every side / triangle / transpose / diagonal)
+    on the GPU against the reference CBLAS layer's outputs, with lib/test_level3.py's limits."""
+    res, err = child("level3", GEN9BLAS_BLAS="gpu", GEN9BLAS_BLAS_INFO="1")
+    for op in ("symm", "syrk", "syr2k", "trmm"):
+        assert res["s" + op] <= 1e-5 and res["d" + op] <= 1e-13, (op, res)
+    assert res["strsm"] <= 1e-4 and res["dtrsm"] <= 1e-12, res
+    assert res["s_other_triangle_exact"] and res["d_other_triangle_exact"]
+    for f in ("ssymm", "dsyrk", "ssyr2k", "dtrmm", "strsm", "dtrsm"):
+        assert f"{f} -> GPU" in err, f
+    assert "-> CPU" not in err
+
+
 @pytest.mark.gpu
 def test_gpu_gemm_matches_reference_cblas():
     res, err = child("cblas_gemm", GEN9BLAS_BLAS="gpu", GEN9BLAS_BLAS_INFO="1")
