@@ -49,7 +49,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="auto", choices=["auto", "hgemm4096", "scaleout", "rows"],
                     help="rows: one JSON line per BASELINE config row (GEMM, skinny, level 1/2), N = 1 only")
-    ap.add_argument("--rows", default="C0,C1,C2,C3a,C3b,C3c", help="rows workload: which config rows to measure")
+    ap.add_argument("--rows", default="C0,C1,C2,C3a,C3b,C3c,L3",
+                    help="rows workload: which config rows to measure (L3: level 3 on GEMM)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample (profiling runs)")
     ap.add_argument("--gather", default="fused", choices=["fused", "nccl"],
@@ -780,6 +781,55 @@ def run_rows(args, torch):
         emit_row("C3c", f"{tag}ger 32768^2", gbps, "GB/s", ms, "hbm", gbps, peak_hbm, "GB/s", f"{peak_kind} HBM copy",
                  None, "ger" if kind == S else None)
         del A, xv, yv
+        torch.cuda.empty_cache()
+
+    # level 3 on GEMM (the scope table's next row): n = 4096, FP32 and FP64, left / lower / no transpose
+    f = ctypes.c_int, ctypes.c_double, ctypes.c_void_p
+    for fn, args_t in (("symm", [f[0]] * 5 + [f[1], f[2], f[0], f[2], f[0], f[1], f[2], f[0]]),
+                       ("syrk", [f[0]] * 5 + [f[1], f[2], f[0], f[1], f[2], f[0]]),
+                       ("syr2k", [f[0]] * 5 + [f[1], f[2], f[0], f[2], f[0], f[1], f[2], f[0]]),
+                       ("trmm", [f[0]] * 7 + [f[1], f[2], f[0], f[2], f[0]]),
+                       ("trsm", [f[0]] * 7 + [f[1], f[2], f[0], f[2], f[0]])):
+        getattr(L.dll, "gen9blas_" + fn).argtypes = args_t
+    n3 = 4096
+    for kind, dt, tag in ((S, torch.float32, "s"), (D, torch.float64, "d")) if "L3" in want else ():
+        A = torch.rand(n3, n3, device="cuda", generator=g, dtype=dt).mul_(2).sub_(1)
+        A.diagonal().add_(float(n3))    # well-conditioned triangle for TRSM
+        Bm = torch.rand(n3, n3, device="cuda", generator=g, dtype=dt).mul_(2).sub_(1)
+        Cm = torch.zeros(n3, n3, device="cuda", dtype=dt)
+        peak, note = ((peak_ffma, "FP32 FFMA nominal: 148 SMs x 128 lanes x 2 x 1965 MHz") if kind == S else
+                      (peak_dmma, "FP64 DMMA nominal: 148 SMs x 64 FMA/clk x 2 x 1965 MHz"))
+        cases = (("symm", 2.0 * n3 ** 3, lambda i: chk(L.dll.gen9blas_symm(kind, 0, 0, n3, n3, 1.0, A.data_ptr(), n3,
+                                                                          Bm.data_ptr(), n3, 0.0, Cm.data_ptr(), n3))),
+                 ("syrk", 1.0 * n3 ** 3, lambda i: chk(L.dll.gen9blas_syrk(kind, 0, 0, n3, n3, 1.0, A.data_ptr(), n3, 0.0,
+                                                                          Cm.data_ptr(), n3))),
+                 ("syr2k", 2.0 * n3 ** 3, lambda i: chk(L.dll.gen9blas_syr2k(kind, 0, 0, n3, n3, 1.0, A.data_ptr(), n3,
+                                                                            Bm.data_ptr(), n3, 0.0, Cm.data_ptr(), n3))),
+                 ("trmm", 1.0 * n3 ** 3, lambda i: chk(L.dll.gen9blas_trmm(kind, 0, 0, 0, 0, n3, n3, 1.0, A.data_ptr(),
+                                                                          n3, Cm.data_ptr(), n3))),
+                 ("trsm", 1.0 * n3 ** 3, lambda i: chk(L.dll.gen9blas_trsm(kind, 0, 0, 0, 0, n3, n3, 1.0, A.data_ptr(),
+                                                                          n3, Cm.data_ptr(), n3))))
+        for nm, fl, call in cases:
+            Cm.copy_(Bm)
+            ms = queued_ms(call, 5, warm=1)
+            tf = fl / (ms * 1e-3) / 1e12
+            extra = None
+            if nm == "trsm":   # cuBLAS trsm through torch on the same triangle
+                Lt = torch.tril(A)
+                with torch.cuda.stream(stream):
+                    torch.linalg.solve_triangular(Lt, Bm, upper=False)
+                    torch.cuda.synchronize()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    for _ in range(5):
+                        torch.linalg.solve_triangular(Lt, Bm, upper=False)
+                    e1.record(stream)
+                    e1.synchronize()
+                extra = {"cublas_tflops": round(fl / (e0.elapsed_time(e1) / 5 * 1e-3) / 1e12, 2)}
+                del Lt
+            emit_row("L3", f"{tag}{nm} n=4096 left lower", tf, "TFLOP/s", ms, "tensor" if kind == D else "ffma", tf,
+                     peak, "TFLOP/s", note + "; FLOP = the operation's own count (SYRK and TRMM/TRSM n^3)", extra)
+        del A, Bm, Cm
         torch.cuda.empty_cache()
     return 0
 
