@@ -37,6 +37,8 @@ struct DevState {
     unsigned gemm_epoch = 0;                                   // launch counter written into those flags
     void *l3 = nullptr;                                        // level-3 work matrices (grow-only)
     size_t l3_n = 0;
+    void *l2x = nullptr;                                       // level-2 work vectors / unpacked triangles (grow-only)
+    size_t l2x_n = 0;
     int *sk_count = nullptr;                                   // arrival counters of the stream-K skinny kernel (zeroed;
     size_t sk_count_n = 0;                                     // every launch leaves them at zero)
 };
@@ -94,6 +96,10 @@ int map_operand(Operand &op, const void *p, size_t bytes, int slot, bool copy_in
 int finish_op(Operand *ops, int n);
 // Scratch buffer of at least `bytes` on the current device (grow-only). Waits for queued work before growing.
 int scratch(size_t bytes, void **p);
+// Triangular solve op(A)·X = alpha·B (left) or X·op(A) = alpha·B (right) on device pointers (level-3 TRSM; B is
+// overwritten). Uses the level-3 work buffer and the GEMM scratch.
+int launch_trsm_dev(int type, int left, int upper, int tA, int unit, int M, int N, double alpha, const void *A, int lda,
+                    void *B, int ldb, cudaStream_t st);
 // Arrival counters (n ints, all zero between launches) of the stream-K skinny kernel; grows (and zeroes) on demand.
 int skinny_counters(size_t n, int **p);
 // Call timing: timer_start at entry (wall clock), timer_kernel right before the main kernels (GEN9BLAS_PROFILE=1:

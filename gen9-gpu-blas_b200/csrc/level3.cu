@@ -276,6 +276,15 @@ static int trsm_t(int type, int left, int upper, int tA, int unit, int M, int N,
     return launched("trsm_write");
 }
 
+int launch_trsm_dev(int type, int left, int upper, int tA, int unit, int M, int N, double alpha, const void *A, int lda,
+                    void *B, int ldb, cudaStream_t st) {
+    if (type == GEN9BLAS_S)
+        return trsm_t<float>(type, left, upper, tA, unit, M, N, alpha, (const float *)A, lda, (float *)B, ldb, st);
+    if (type == GEN9BLAS_D)
+        return trsm_t<double>(type, left, upper, tA, unit, M, N, alpha, (const double *)A, lda, (double *)B, ldb, st);
+    return trsm_t<__half>(type, left, upper, tA, unit, M, N, alpha, (const __half *)A, lda, (__half *)B, ldb, st);
+}
+
 }  // namespace g9
 
 using namespace g9;

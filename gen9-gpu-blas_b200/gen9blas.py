@@ -431,3 +431,298 @@ def ger(alpha, x, y, A):
         raise ValueError("lengths of x, y do not match A")
     _check(_lib.gen9blas_ger(_kind_basic(t), M, N, alpha, px, ix, py, iy, pa, lda))
     return A
+
+
+# ---------------- rest of levels 1-2 (lib/gen9blas.py:343-373, 420-610 of the reference) ----------------
+_lib.gen9blas_scal.argtypes = [_i, _i, _d, _p, _i]
+_lib.gen9blas_copy.argtypes = [_i, _i, _p, _i, _p, _i]
+_lib.gen9blas_swap.argtypes = [_i, _i, _p, _i, _p, _i]
+_lib.gen9blas_rot.argtypes = [_i, _i, _p, _i, _p, _i, _d, _d]
+_lib.gen9blas_rotm.argtypes = [_i, _i, _p, _i, _p, _i, ctypes.POINTER(_d)]
+_fp = ctypes.POINTER(ctypes.c_float)
+_lib.gen9blas_rotg.argtypes = [_fp, _fp, _fp, _fp]
+_lib.gen9blas_rotg.restype = None
+_lib.gen9blas_rotmg.argtypes = [_fp, _fp, _fp, ctypes.c_float, _fp]
+_lib.gen9blas_rotmg.restype = None
+_lib.gen9blas_symv.argtypes = [_i, _i, _i, _d, _p, _i, _p, _i, _d, _p, _i]
+_lib.gen9blas_trmv.argtypes = [_i, _i, _i, _i, _i, _p, _i, _p, _i]
+_lib.gen9blas_trsv.argtypes = [_i, _i, _i, _i, _i, _p, _i, _p, _i]
+_lib.gen9blas_syr.argtypes = [_i, _i, _i, _d, _p, _i, _p, _i]
+_lib.gen9blas_syr2.argtypes = [_i, _i, _i, _d, _p, _i, _p, _i, _p, _i]
+_lib.gen9blas_gbmv.argtypes = [_i] * 6 + [_d, _p, _i, _p, _i, _d, _p, _i]
+_lib.gen9blas_sbmv.argtypes = [_i] * 4 + [_d, _p, _i, _p, _i, _d, _p, _i]
+_lib.gen9blas_tbmv.argtypes = [_i] * 6 + [_p, _i, _p, _i]
+_lib.gen9blas_tbsv.argtypes = [_i] * 6 + [_p, _i, _p, _i]
+_lib.gen9blas_spmv.argtypes = [_i] * 3 + [_d, _p, _p, _i, _d, _p, _i]
+_lib.gen9blas_tpmv.argtypes = [_i] * 5 + [_p, _p, _i]
+_lib.gen9blas_tpsv.argtypes = [_i] * 5 + [_p, _p, _i]
+_lib.gen9blas_spr.argtypes = [_i] * 3 + [_d, _p, _i, _p]
+_lib.gen9blas_spr2.argtypes = [_i] * 3 + [_d, _p, _i, _p, _i, _p]
+
+
+def _pair(x, y, write_y=True):
+    t = _dtype_of(x)
+    x, px, n, ix = _vec(x, t, True)
+    y, py, ny, iy = _vec(y, t, write_y)
+    if ny != n:
+        raise ValueError("lengths differ")
+    return t, x, px, n, ix, y, py, iy
+
+
+def scal(a, x):
+    """x = a·x (in place); returns x."""
+    _init()
+    t = _dtype_of(x)
+    x, px, n, ix = _vec(x, t, True)
+    _check(_lib.gen9blas_scal(_kind_basic(t), n, a, px, ix))
+    return x
+
+
+def copy(x, y=None):
+    """y = x; without y: a new array (gen9blas.empty) of the type of x."""
+    _init()
+    t = _dtype_of(y if y is not None else x)
+    if y is None:
+        y = empty(x.shape, t)
+    y, py, n, iy = _vec(y, t, True)
+    x, px, nx, ix = _vec(x, t)
+    if nx != n:
+        raise ValueError("lengths differ")
+    _check(_lib.gen9blas_copy(_kind_basic(t), n, px, ix, py, iy))
+    return y
+
+
+def swap(x, y):
+    _init()
+    t, x, px, n, ix, y, py, iy = _pair(x, y)
+    _check(_lib.gen9blas_swap(_kind_basic(t), n, px, ix, py, iy))
+    return x, y
+
+
+def rot(x, y, c, s):
+    """x, y = c·x + s·y, c·y − s·x (in place)."""
+    _init()
+    t, x, px, n, ix, y, py, iy = _pair(x, y)
+    _check(_lib.gen9blas_rot(_kind_basic(t), n, px, ix, py, iy, c, s))
+    return x, y
+
+
+def rotm(x, y, param):
+    """x, y = h11·x + h12·y, h21·x + h22·y (in place); param: (flag, h11, h21, h12, h22) as in BLAS."""
+    _init()
+    t, x, px, n, ix, y, py, iy = _pair(x, y)
+    pr = (_d * 5)(*[float(v) for v in param])
+    _check(_lib.gen9blas_rotm(_kind_basic(t), n, px, ix, py, iy, pr))
+    return x, y
+
+
+def rotg(a, b):
+    """(r, z, c, s): the Givens rotation that zeroes b (computed on the CPU)."""
+    w = [ctypes.c_float(a), ctypes.c_float(b), ctypes.c_float(), ctypes.c_float()]
+    _lib.gen9blas_rotg(*[ctypes.byref(v) for v in w])
+    return tuple(v.value for v in w)
+
+
+def rotmg(d1, d2, x1, y1):
+    """(d1, d2, x1, param): modified Givens rotation (CPU); param as in BLAS (5 numbers)."""
+    w = [ctypes.c_float(d1), ctypes.c_float(d2), ctypes.c_float(x1)]
+    pr = (ctypes.c_float * 5)()
+    _lib.gen9blas_rotmg(*[ctypes.byref(v) for v in w], ctypes.c_float(y1), pr)
+    return w[0].value, w[1].value, w[2].value, np.array(pr[:], np.float32)
+
+
+_FLIP = {"L": "U", "U": "L"}
+
+
+def _sq(A, t, uplo):
+    """(pointer, n, ld, transposed, uplo in memory): an A.T view is read in place with the triangle swapped."""
+    A, pa, M, N, lda, tr = _mat(A, t)
+    if M != N:
+        raise ValueError("expected a square matrix")
+    return A, pa, N, lda, tr, _FLIP[uplo] if tr else uplo
+
+
+def _out_vec(y, n, t, beta):
+    if y is None:
+        return empty((n,), t), 0.0
+    return y, beta
+
+
+def symv(A, x, uplo="L", alpha=1.0, beta=0.0, y=None):
+    """y = alpha·A·x + beta·y, A symmetric (its uplo triangle is read); without y: a new array."""
+    _init()
+    t = _dtype_of(A)
+    A, pa, n, lda, _, u = _sq(A, t, uplo)
+    x, px, nx, ix = _vec(x, t)
+    y, beta = _out_vec(y, n, t, beta)
+    y, py, ny, iy = _vec(y, t, True)
+    if nx != n or ny != n:
+        raise ValueError("lengths of x, y do not match A")
+    _check(_lib.gen9blas_symv(_kind_basic(t), _TRI[u], n, alpha, pa, lda, px, ix, beta, py, iy))
+    return y
+
+
+def trmv(A, x, uplo="L", trans=False, diag=False):
+    """x = op(A)·x (in place), A triangular; diag=True: unit diagonal. Returns x."""
+    _init()
+    t = _dtype_of(x)
+    A, pa, n, lda, tr, u = _sq(A, t, uplo)
+    x, px, nx, ix = _vec(x, t, True)
+    if nx != n:
+        raise ValueError("length of x does not match A")
+    _check(_lib.gen9blas_trmv(_kind_basic(t), _TRI[u], int(trans) ^ tr, int(diag), n, pa, lda, px, ix))
+    return x
+
+
+def trsv(A, x, uplo="L", trans=False, diag=False):
+    """Solves op(A)·z = x and stores z in x (in place); A triangular. Returns x."""
+    _init()
+    t = _dtype_of(x)
+    A, pa, n, lda, tr, u = _sq(A, t, uplo)
+    x, px, nx, ix = _vec(x, t, True)
+    if nx != n:
+        raise ValueError("length of x does not match A")
+    _check(_lib.gen9blas_trsv(_kind_basic(t), _TRI[u], int(trans) ^ tr, int(diag), n, pa, lda, px, ix))
+    return x
+
+
+def syr(alpha, x, A, uplo="L"):
+    """A = alpha·x·xᵀ + A on the uplo triangle (in place); returns A."""
+    _init()
+    t = _dtype_of(A)
+    A, pa, M, N, lda, _ = _mat(A, t, True)
+    x, px, n, ix = _vec(x, t)
+    if not M == N == n:
+        raise ValueError("dimensions do not match")
+    _check(_lib.gen9blas_syr(_kind_basic(t), _TRI[uplo], n, alpha, px, ix, pa, lda))
+    return A
+
+
+def syr2(alpha, x, y, A, uplo="L"):
+    """A = alpha·(x·yᵀ + y·xᵀ) + A on the uplo triangle (in place); returns A."""
+    _init()
+    t = _dtype_of(A)
+    A, pa, M, N, lda, _ = _mat(A, t, True)
+    x, px, n, ix = _vec(x, t)
+    y, py, ny, iy = _vec(y, t)
+    if not M == N == n == ny:
+        raise ValueError("dimensions do not match")
+    _check(_lib.gen9blas_syr2(_kind_basic(t), _TRI[uplo], n, alpha, px, ix, py, iy, pa, lda))
+    return A
+
+
+def _band(A, t, width, write=False):
+    A, pa, M, W, lda, tr = _mat(A, t, write)
+    if tr or W != width:
+        raise ValueError(f"band: expected a row-major array with {width} columns")
+    return A, pa, M, lda
+
+
+def _packed(Ap, t, n, write=False):
+    Ap, pp, m, inc = _vec(Ap, t, write)
+    if inc != 1 or m != n * (n + 1) // 2:
+        raise ValueError(f"packed: expected a contiguous vector of length {n * (n + 1) // 2}")
+    return Ap, pp
+
+
+def gbmv(A, x, M, N, KL, KU, alpha=1.0, beta=0.0, y=None, trans=False):
+    """y = alpha·op(A)·x + beta·y, A: M×N banded (array (M, KL + KU + 1), A[i, KL + j − i] = A(i, j))."""
+    _init()
+    t = _dtype_of(A)
+    A, pa, m, lda = _band(A, t, KL + KU + 1)
+    if m != M:
+        raise ValueError("number of band rows != M")
+    x, px, nx, ix = _vec(x, t)
+    y, beta = _out_vec(y, N if trans else M, t, beta)
+    y, py, ny, iy = _vec(y, t, True)
+    if nx != (M if trans else N) or ny != (N if trans else M):
+        raise ValueError("lengths of x, y")
+    _check(_lib.gen9blas_gbmv(_kind_basic(t), int(trans), M, N, KL, KU, alpha, pa, lda, px, ix, beta, py, iy))
+    return y
+
+
+def sbmv(A, x, K, uplo="L", alpha=1.0, beta=0.0, y=None):
+    """y = alpha·A·x + beta·y, A symmetric banded (array (n, K + 1), the uplo triangle)."""
+    _init()
+    t = _dtype_of(A)
+    A, pa, n, lda = _band(A, t, K + 1)
+    x, px, nx, ix = _vec(x, t)
+    y, beta = _out_vec(y, n, t, beta)
+    y, py, ny, iy = _vec(y, t, True)
+    if nx != n or ny != n:
+        raise ValueError("lengths of x, y")
+    _check(_lib.gen9blas_sbmv(_kind_basic(t), _TRI[uplo], n, K, alpha, pa, lda, px, ix, beta, py, iy))
+    return y
+
+
+def tbmv(A, x, K, uplo="L", trans=False, diag=False):
+    """x = op(A)·x (in place), A triangular banded (array (n, K + 1))."""
+    _init()
+    t = _dtype_of(x)
+    A, pa, n, lda = _band(A, t, K + 1)
+    x, px, nx, ix = _vec(x, t, True)
+    _check(_lib.gen9blas_tbmv(_kind_basic(t), _TRI[uplo], int(trans), int(diag), n, K, pa, lda, px, ix))
+    return x
+
+
+def tbsv(A, x, K, uplo="L", trans=False, diag=False):
+    """Solves op(A)·z = x (in place), A triangular banded (array (n, K + 1))."""
+    _init()
+    t = _dtype_of(x)
+    A, pa, n, lda = _band(A, t, K + 1)
+    x, px, nx, ix = _vec(x, t, True)
+    _check(_lib.gen9blas_tbsv(_kind_basic(t), _TRI[uplo], int(trans), int(diag), n, K, pa, lda, px, ix))
+    return x
+
+
+def spmv(Ap, x, uplo="L", alpha=1.0, beta=0.0, y=None):
+    """y = alpha·A·x + beta·y, A symmetric packed (vector of n(n+1)/2)."""
+    _init()
+    t = _dtype_of(Ap)
+    x, px, n, ix = _vec(x, t)
+    Ap, pp = _packed(Ap, t, n)
+    y, beta = _out_vec(y, n, t, beta)
+    y, py, ny, iy = _vec(y, t, True)
+    _check(_lib.gen9blas_spmv(_kind_basic(t), _TRI[uplo], n, alpha, pp, px, ix, beta, py, iy))
+    return y
+
+
+def tpmv(Ap, x, uplo="L", trans=False, diag=False):
+    """x = op(A)·x (in place), A triangular packed."""
+    _init()
+    t = _dtype_of(x)
+    x, px, n, ix = _vec(x, t, True)
+    Ap, pp = _packed(Ap, t, n)
+    _check(_lib.gen9blas_tpmv(_kind_basic(t), _TRI[uplo], int(trans), int(diag), n, pp, px, ix))
+    return x
+
+
+def tpsv(Ap, x, uplo="L", trans=False, diag=False):
+    """Solves op(A)·z = x (in place), A triangular packed."""
+    _init()
+    t = _dtype_of(x)
+    x, px, n, ix = _vec(x, t, True)
+    Ap, pp = _packed(Ap, t, n)
+    _check(_lib.gen9blas_tpsv(_kind_basic(t), _TRI[uplo], int(trans), int(diag), n, pp, px, ix))
+    return x
+
+
+def spr(alpha, x, Ap, uplo="L"):
+    """A = alpha·x·xᵀ + A (packed, in place)."""
+    _init()
+    t = _dtype_of(Ap)
+    x, px, n, ix = _vec(x, t)
+    Ap, pp = _packed(Ap, t, n, True)
+    _check(_lib.gen9blas_spr(_kind_basic(t), _TRI[uplo], n, alpha, px, ix, pp))
+    return Ap
+
+
+def spr2(alpha, x, y, Ap, uplo="L"):
+    """A = alpha·(x·yᵀ + y·xᵀ) + A (packed, in place)."""
+    _init()
+    t = _dtype_of(Ap)
+    x, px, n, ix = _vec(x, t)
+    y, py, ny, iy = _vec(y, t)
+    Ap, pp = _packed(Ap, t, n, True)
+    _check(_lib.gen9blas_spr2(_kind_basic(t), _TRI[uplo], n, alpha, px, ix, py, iy, pp))
+    return Ap

@@ -202,7 +202,144 @@ def group_forwarded():
     return {"zgemm_forwarded": float(np.abs(C - A @ B).max())}
 
 
+def group_l2x():
+    """The rest of levels 1-2 through the library (GPU) and straight through OpenBLAS (the CPU BLAS the reference's
+    CBLAS layer forwards to) on the same data: RowMajor, ColMajor and Fortran calls, random data in the whole band
+    array / packed vector (as the reference's lib/test_blas_banded.py). Reports max |diff| / scale per function."""
+    ob = ctypes.CDLL(os.environ["GEN9BLAS_BLAS_CPU"])
+    rng = np.random.default_rng(9)
+    out = {}
+    n, K, M, N, KL, KU = 37, 4, 29, 41, 3, 5
+    UP, LO, NT, TR, NU, UN = 121, 122, 111, 112, 131, 132
+    for tag, F, dt in (("s", ctypes.c_float, np.float32), ("d", ctypes.c_double, np.float64)):
+        def ref(p):
+            return np.ascontiguousarray(p).copy()
+
+        def call(name, args_fn):
+            """args_fn(lib) -> (output arrays); returns max relative difference (GPU vs OpenBLAS)."""
+            a = args_fn(L)
+            b = args_fn(ob)
+            worst = 0.0
+            for x, y in zip(a, b):
+                scale = max(1.0, float(np.abs(y.astype(np.float64)).max()))
+                worst = max(worst, float(np.abs(x.astype(np.float64) - y.astype(np.float64)).max()) / scale)
+            out[tag + name] = max(out.get(tag + name, 0.0), worst)
+
+        A = rng.uniform(-1, 1, (n, n)).astype(dt)
+        Ad = A.copy()
+        Ad[np.diag_indices(n)] = n
+        Ab = rng.uniform(-1, 1, (n, K + 1)).astype(dt)
+        Abd = Ab.copy()
+        Ap = rng.uniform(-1, 1, n * (n + 1) // 2).astype(dt)
+        G = rng.uniform(-1, 1, (max(M, N), KL + KU + 1)).astype(dt)
+        x0 = rng.uniform(-1, 1, max(M, N) * 2).astype(dt)
+        y0 = rng.uniform(-1, 1, max(M, N) * 2).astype(dt)
+        P = ctypes.c_void_p
+        for o in (101, 102):
+            for u in (UP, LO):
+                Abd[:, 0 if (u == UP) == (o == 101) else K] = 4 + K   # dominant band diagonal in either storage order
+                # packed with a dominant diagonal: rebuild from a dense matrix in this order's packing
+                for fn in ("symv",):
+                    def f(lib, fn=fn):
+                        y = y0[:n].copy()
+                        g = getattr(lib, f"cblas_{tag}symv")
+                        g.argtypes = [ctypes.c_int] * 3 + [F, P, ctypes.c_int, P, ctypes.c_int, F, P, ctypes.c_int]
+                        g(o, u, n, 1.5, A.ctypes.data, n, x0.ctypes.data, 1, -0.5, y.ctypes.data, 1)
+                        return (y,)
+                    call("symv", f)
+                for t in (NT, TR):
+                    for d in (NU, UN):
+                        for nm, mat, extra in (("trmv", A, None), ("trsv", Ad, None), ("tbmv", Ab, K), ("tbsv", Abd, K),
+                                               ("tpmv", Ap, -1), ("tpsv", None, -1)):
+                            if nm == "tpsv":   # packed triangle of Ad in this (order, uplo)
+                                lower_rm = (u == LO) == (o == 101)
+                                mat = np.array([Ad[i, j] for i in range(n) for j in
+                                                (range(0, i + 1) if lower_rm else range(i, n))], dt)
+                            def f(lib, nm=nm, mat=mat, extra=extra):
+                                x = x0[:n].copy()
+                                g = getattr(lib, f"cblas_{tag}{nm}")
+                                if extra is None:
+                                    g.argtypes = [ctypes.c_int] * 5 + [P, ctypes.c_int, P, ctypes.c_int]
+                                    g(o, u, t, d, n, mat.ctypes.data, n, x.ctypes.data, 1)
+                                elif extra == -1:
+                                    g.argtypes = [ctypes.c_int] * 5 + [P, P, ctypes.c_int]
+                                    g(o, u, t, d, n, mat.ctypes.data, x.ctypes.data, 1)
+                                else:
+                                    g.argtypes = [ctypes.c_int] * 6 + [P, ctypes.c_int, P, ctypes.c_int]
+                                    g(o, u, t, d, n, extra, mat.ctypes.data, K + 1, x.ctypes.data, 1)
+                                return (x,)
+                            call(nm, f)
+
+                def f(lib):
+                    y = y0[:n].copy()
+                    g = getattr(lib, f"cblas_{tag}sbmv")
+                    g.argtypes = [ctypes.c_int] * 4 + [F, P, ctypes.c_int, P, ctypes.c_int, F, P, ctypes.c_int]
+                    g(o, u, n, K, 0.75, Ab.ctypes.data, K + 1, x0.ctypes.data, 1, 0.25, y.ctypes.data, 1)
+                    return (y,)
+                call("sbmv", f)
+
+                def f(lib):
+                    y = y0[:n].copy()
+                    g = getattr(lib, f"cblas_{tag}spmv")
+                    g.argtypes = [ctypes.c_int] * 3 + [F, P, P, ctypes.c_int, F, P, ctypes.c_int]
+                    g(o, u, n, 0.75, Ap.ctypes.data, x0.ctypes.data, 1, 0.25, y.ctypes.data, 1)
+                    return (y,)
+                call("spmv", f)
+                for nm in ("syr", "syr2", "spr", "spr2"):
+                    def f(lib, nm=nm):
+                        Aout = (A.copy() if nm.startswith("sy") else Ap.copy())
+                        g = getattr(lib, f"cblas_{tag}{nm}")
+                        two = nm.endswith("2")
+                        packed = nm.startswith("sp")
+                        if two and packed:
+                            g.argtypes = [ctypes.c_int] * 3 + [F, P, ctypes.c_int, P, ctypes.c_int, P]
+                            g(o, u, n, 0.5, x0.ctypes.data, 1, y0.ctypes.data, 1, Aout.ctypes.data)
+                        elif packed:
+                            g.argtypes = [ctypes.c_int] * 3 + [F, P, ctypes.c_int, P]
+                            g(o, u, n, 0.5, x0.ctypes.data, 1, Aout.ctypes.data)
+                        elif two:
+                            g.argtypes = [ctypes.c_int] * 3 + [F, P, ctypes.c_int, P, ctypes.c_int, P, ctypes.c_int]
+                            g(o, u, n, 0.5, x0.ctypes.data, 1, y0.ctypes.data, 1, Aout.ctypes.data, n)
+                        else:
+                            g.argtypes = [ctypes.c_int] * 3 + [F, P, ctypes.c_int, P, ctypes.c_int]
+                            g(o, u, n, 0.5, x0.ctypes.data, 1, Aout.ctypes.data, n)
+                        return (Aout,)
+                    call(nm, f)
+            for t in (NT, TR):
+                def f(lib, t=t):
+                    rows = M if o == 101 else N     # band rows of the stored array
+                    g = getattr(lib, f"cblas_{tag}gbmv")
+                    g.argtypes = [ctypes.c_int] * 6 + [F, P, ctypes.c_int, P, ctypes.c_int, F, P, ctypes.c_int]
+                    ny = (N if t == TR else M)
+                    y = y0[:ny].copy()
+                    Gm = np.ascontiguousarray(G[:rows])
+                    g(o, t, M, N, KL, KU, 1.25, Gm.ctypes.data, KL + KU + 1, x0.ctypes.data, 1, -0.75, y.ctypes.data, 1)
+                    return (y,)
+                call("gbmv", f)
+        # level 1 (no storage order)
+        for nm in ("scal", "copy", "swap", "rot", "rotm"):
+            def f(lib, nm=nm):
+                x, y = x0[:N].copy(), y0[:N].copy()
+                g = getattr(lib, f"cblas_{tag}{nm}")
+                if nm == "scal":
+                    g.argtypes = [ctypes.c_int, F, P, ctypes.c_int]
+                    g(N, 0.7, x.ctypes.data, 1)
+                elif nm == "rot":
+                    g.argtypes = [ctypes.c_int, P, ctypes.c_int, P, ctypes.c_int, F, F]
+                    g(N, x.ctypes.data, 1, y.ctypes.data, 1, 0.6, 0.8)
+                elif nm == "rotm":
+                    prm = np.array([-1.0, 0.5, -0.25, 0.75, 1.5], dt)
+                    g.argtypes = [ctypes.c_int, P, ctypes.c_int, P, ctypes.c_int, P]
+                    g(N, x.ctypes.data, 1, y.ctypes.data, 1, prm.ctypes.data)
+                else:
+                    g.argtypes = [ctypes.c_int, P, ctypes.c_int, P, ctypes.c_int]
+                    g(N, x.ctypes.data, 1, y.ctypes.data, 1)
+                return (x, y)
+            call(nm, f)
+    return out
+
+
 if __name__ == "__main__":
     groups = {"cblas_gemm": group_cblas_gemm, "fortran_l12": group_fortran_and_l12, "forwarded": group_forwarded,
-              "level3": group_level3}
+              "level3": group_level3, "l2x": group_l2x}
     print(json.dumps(groups[sys.argv[1]]()))

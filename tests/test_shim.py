@@ -62,6 +62,31 @@ def test_gpu_level3_matches_reference_cblas():
     assert "-> CPU" not in err
 
 
+L2X = ("symv", "trmv", "trsv", "tbmv", "tbsv", "tpmv", "tpsv", "sbmv", "spmv", "syr", "syr2", "spr", "spr2", "gbmv",
+       "scal", "copy", "swap", "rot", "rotm")
+
+
+def test_cpu_mode_level12_extras_are_the_cpu_blas():
+    res, err = child("l2x", GEN9BLAS_BLAS="cpu", GEN9BLAS_BLAS_INFO="1")
+    for tag in ("s", "d"):
+        for f in L2X:
+            assert res[tag + f] <= 1e-12, (tag + f, res[tag + f])
+    assert "-> GPU" not in err
+
+
+@pytest.mark.gpu
+def test_gpu_level12_extras_match_openblas():
+    """lib/test_blas_banded.py's differential check (RowMajor and ColMajor, every triangle / transpose / diagonal)
+    for the rest of levels 1-2 on the GPU: max |diff| / scale <= 1e-5 (FP32; solves 1e-4), 1e-12 (FP64)."""
+    res, err = child("l2x", GEN9BLAS_BLAS="gpu", GEN9BLAS_BLAS_INFO="1")
+    for f in L2X:
+        tol = 1e-4 if f in ("trsv", "tbsv", "tpsv") else 1e-5
+        assert res["s" + f] <= tol and res["d" + f] <= 1e-12, (f, res["s" + f], res["d" + f])
+    for f in ("ssymv", "dtrsv", "stbsv", "dtpsv", "sgbmv", "dspr2", "sscal", "drotm"):
+        assert f"{f} -> GPU" in err, f
+    assert "-> CPU" not in err
+
+
 @pytest.mark.gpu
 def test_gpu_gemm_matches_reference_cblas():
     res, err = child("cblas_gemm", GEN9BLAS_BLAS="gpu", GEN9BLAS_BLAS_INFO="1")
