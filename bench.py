@@ -8,7 +8,8 @@ Workloads:
   the same way and reported under "modes".
 - rows (N = 1, on request): every BASELINE config row measured on its own (SGEMM n = 1024/4096/8192, HGEMM
   n = 1024..8192 fast and accurate, DGEMM n = 3000/4096 column-major all transposes, skinny GEMM for the four weight
-  shapes × M = 1..16, level-1 n = 2^28 and level-2 32768² in FP32 and FP64), one JSON line per case with its
+  shapes × M = 1..16, level-1 n = 2^28 and level-2 32768² in FP32 and FP64; level 3 on GEMM at n = 4096; packed
+  weights: gemm_pb_skinny on the weight shapes, gemm_pb against gemm), one JSON line per case with its
   roofline fraction, the cuBLAS time for GEMM shapes, and the reference's CPU path on a bounded sample per family.
 - scaleout (default at N > 1, configs[4]): HGEMM n = 32768 with B and C column-sharded over the N ranks, A
   replicated, C all-gathered over NVLink (NCCL); one step = local GEMM of the rank's column block + all-gather +
@@ -49,8 +50,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="auto", choices=["auto", "hgemm4096", "scaleout", "rows"],
                     help="rows: one JSON line per BASELINE config row (GEMM, skinny, level 1/2), N = 1 only")
-    ap.add_argument("--rows", default="C0,C1,C2,C3a,C3b,C3c,L3",
-                    help="rows workload: which config rows to measure (L3: level 3 on GEMM)")
+    ap.add_argument("--rows", default="C0,C1,C2,C3a,C3b,C3c,L3,PB",
+                    help="rows workload: which config rows to measure (L3: level 3 on GEMM, PB: packed weights)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample (profiling runs)")
     ap.add_argument("--gather", default="fused", choices=["fused", "nccl"],
@@ -781,6 +782,61 @@ def run_rows(args, torch):
         emit_row("C3c", f"{tag}ger 32768^2", gbps, "GB/s", ms, "hbm", gbps, peak_hbm, "GB/s", f"{peak_kind} HBM copy",
                  None, "ger" if kind == S else None)
         del A, xv, yv
+        torch.cuda.empty_cache()
+
+    # constant weights (packed once): gemm_pb_skinny (F32 activations x FP16 weights) on the decoder shapes, and
+    # gemm_pb against gemm on the same operands for large M
+    if "PB" in want:
+        pb_sigs = {"pack_b": ([ctypes.c_int] * 4 + [ctypes.c_void_p, ctypes.c_int], ctypes.c_void_p),
+                   "packed_b_free": ([ctypes.c_void_p], None),
+                   "gemm_pb": ([ctypes.c_int, ctypes.c_int, ctypes.c_double, ctypes.c_void_p, ctypes.c_int,
+                                ctypes.c_void_p, ctypes.c_double, ctypes.c_void_p, ctypes.c_int], ctypes.c_int),
+                   "gemm_pb_skinny": ([ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                                       ctypes.c_int, ctypes.c_void_p], ctypes.c_int)}
+        for nm, (a_t, r_t) in pb_sigs.items():
+            getattr(L.dll, "gen9blas_" + nm).argtypes, getattr(L.dll, "gen9blas_" + nm).restype = a_t, r_t
+        for N, K in ((4096, 4096), (12288, 4096), (11008, 4096), (4096, 11008)):
+            copies = max(2, int(512e6 // (N * K * 2)) + 1)
+            Ps = []
+            for _ in range(copies):
+                W = torch.randn(N, K, device="cuda", generator=g, dtype=torch.float32).mul_(0.02).half()
+                Ps.append(L.dll.gen9blas_pack_b(HS, 1, K, N, W.data_ptr(), K))
+                assert Ps[-1], L.error().decode()
+                del W
+            for M in (1, 4, 8, 16):
+                X = torch.randn(M, K, device="cuda", generator=g, dtype=torch.float32)
+                Y = torch.empty(M, N, device="cuda", dtype=torch.float32)
+
+                def call(i, M=M, X=X, Y=Y):
+                    chk(L.dll.gen9blas_gemm_pb_skinny(M, X.data_ptr(), K, Ps[i % copies], Y.data_ptr(), N, None))
+
+                ms = queued_ms(call, 200)
+                nbytes = N * K * 2 + M * K * 4 + M * N * 4
+                gbps = nbytes / (ms * 1e-3) / 1e9
+                emit_row("PB", f"gemm_pb_skinny M={M} W={N}x{K} (F32 x FP16)", ms * 1e3, "us", ms, "hbm", gbps,
+                         peak_hbm, "GB/s", f"{peak_kind} HBM copy, MEASURED_PEAKS.json", {"gbps": round(gbps, 1)})
+            for P in Ps:
+                L.dll.gen9blas_packed_b_free(P)
+        for kind, dt, M, N, K in ((HS, torch.float16, 4096, 4096, 4096), (H, torch.float16, 4096, 4096, 4096),
+                                  (S, torch.float32, 512, 8960, 1536)):
+            A = torch.rand(M, K, device="cuda", generator=g, dtype=torch.float32).sub_(0.5).to(dt)
+            Wt = torch.rand(N, K, device="cuda", generator=g, dtype=torch.float32).sub_(0.5).to(dt)
+            Cm = torch.empty(M, N, device="cuda", dtype=dt)
+            P = L.dll.gen9blas_pack_b(kind, 1, K, N, Wt.data_ptr(), K)
+            assert P, L.error().decode()
+            reps = max(4, min(200, int(0.25 / (2 * M * N * K / 50e12))))
+            ms = queued_ms(lambda i: chk(L.dll.gen9blas_gemm_pb(0, M, 1.0, A.data_ptr(), K, P, 0.0, Cm.data_ptr(), N)),
+                           reps)
+            ms_g = queued_ms(lambda i: chk(L.gemm(kind, 0, 1, M, N, K, 1.0, A.data_ptr(), K, Wt.data_ptr(), K, 0.0,
+                                                  Cm.data_ptr(), N)), reps)
+            tf = 2 * M * N * K / (ms * 1e-3) / 1e12
+            peak, note = ((peak_t, f"{peak_kind} cuBLAS bf16 dense sustained, MEASURED_PEAKS.json") if dt == torch.float16
+                          else (peak_ffma, "FP32 FFMA nominal: 148 SMs x 128 lanes x 2 x 1965 MHz"))
+            tag = {H: "h", HS: "hs", S: "s"}[kind]
+            emit_row("PB", f"gemm_pb {tag} {M}x{N}x{K}", tf, "TFLOP/s", ms, "tensor" if dt == torch.float16 else "ffma",
+                     tf, peak, "TFLOP/s", note, {"gemm_same_operands_tflops": round(2 * M * N * K / (ms_g * 1e-3) / 1e12, 2)})
+            L.dll.gen9blas_packed_b_free(P)
+            del A, Wt, Cm
         torch.cuda.empty_cache()
 
     # level 3 on GEMM (the scope table's next row): n = 4096, FP32 and FP64, left / lower / no transpose

@@ -48,7 +48,7 @@ def build_core(force=False, ptxas_verbose=False):
     os.makedirs(OBJ, exist_ok=True)
     sources = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
     headers = glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh")) + \
-        [os.path.join(ROOT, "include", "gen9blas.h")]
+        glob.glob(os.path.join(ROOT, "include", "*.h"))
     jobs, objs, logs = [], [], []
     for src in sources:
         obj = os.path.join(OBJ, os.path.basename(src)[:-3] + ".o")

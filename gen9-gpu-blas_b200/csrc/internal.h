@@ -30,8 +30,8 @@ struct DevState {
     void *scratch = nullptr;                                   // partial sums, packed operands
     size_t scratch_n = 0;
     double *result_host = nullptr;                             // pinned: scalar results of reductions
-    unsigned *err_host = nullptr;                              // mapped pinned word: device-side error code
-    unsigned *err_dev = nullptr;                               // its device address
+    unsigned *err_host = nullptr;                              // mapped pinned words: [0] device-side error code,
+    unsigned *err_dev = nullptr;                               // [1] non-finite flag of gemm_pb_skinny; device address
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     unsigned *gemm_flags = nullptr;                            // split-K handoff flags of the HGEMM pair kernel (zeroed)
     unsigned gemm_epoch = 0;                                   // launch counter written into those flags
@@ -135,6 +135,11 @@ int launch_skinny(int type, int tA, int tB, int M, int N, int K, double alpha, c
                   int ldb, double beta, void *C, int ldc, cudaStream_t st, void *const *peers = nullptr, int npeers = 0,
                   long long col_off = 0);
 int skinny_threshold(int type);
+// Skinny GEMM with FP32 activations and FP16 weights (gemm_pb_skinny): C (M × N, FP32) = A (M × K, FP32) · Wᵀ with W
+// N rows of ldw FP16 elements (ldw >= K rounded up to 8, zero past K, rows 16-byte aligned). A non-finite result sets
+// *nf (device-visible word).
+int launch_skinny_f32a(int M, int N, int K, const float *A, int lda, const void *W, int ldw, float *C, int ldc,
+                       unsigned *nf, cudaStream_t st);
 
 }  // namespace g9
 #pragma GCC visibility pop

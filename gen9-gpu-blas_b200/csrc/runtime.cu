@@ -271,9 +271,11 @@ void timer_stop() {
             cudaEventRecord(d->ev1, stream());
             cudaEventSynchronize(d->ev1);
             float ms = 0;
-            cudaEventElapsedTime(&ms, d->ev0, d->ev1);
-            G.last_ms = ms;
-            return;
+            if (cudaEventElapsedTime(&ms, d->ev0, d->ev1) == cudaSuccess) {
+                G.last_ms = ms;
+                return;
+            }
+            cudaGetLastError();   // the start event was not recorded by this call: wall clock below
         }
     }
     G.last_ms = (now_s() - g_t0) * 1e3;
@@ -319,7 +321,8 @@ GEN9BLAS_API int gen9blas_has(int f) {
     switch (f) {
     case GEN9BLAS_FEAT_FP16:
     case GEN9BLAS_FEAT_FP32:
-    case GEN9BLAS_FEAT_FP64: return 1;
+    case GEN9BLAS_FEAT_FP64:
+    case GEN9BLAS_FEAT_SKINNY_PB: return 1;   // gen9blas_gemm_pb_skinny
     default: return 0;
     }
 }

@@ -49,6 +49,11 @@ struct SkinnyArgs {
     void *dst[8];
     int ndst;
     long long coff;
+    // F32 activations (gemm_pb_skinny): a is the FP16 "hi" part of the scaled activations and a + alo the "lo" part
+    // (same pitch); a result is multiplied by tscale[m] (2^-s of its row), C is FP32, and a non-finite result sets *nf.
+    long long alo;
+    const float *tscale;
+    unsigned *nf;
 };
 
 template <typename T>
@@ -63,6 +68,21 @@ __device__ __forceinline__ void skinny_store(const SkinnyArgs &p, int m, int n, 
         return;
     }
     for (int q = 0; q < p.ndst; q++) ((T *)p.dst[q])[off] = o;
+}
+
+// Store of the F32-activation variant: undo the row's power-of-two scale, FP32 C, flag non-finite results.
+__device__ __forceinline__ void skinny_store_f32a(const SkinnyArgs &p, int m, int n, float s) {
+    float *c = (float *)p.C + (long long)m * p.scm + (long long)n * p.scn;
+    float v = p.alpha * (s * p.tscale[m]);
+    if (p.beta != 0.0f) v = __fmaf_rn(p.beta, *c, v);
+    if (!isfinite(v)) *(volatile unsigned *)p.nf = 1u;
+    *c = v;
+}
+
+template <bool F32A>
+__device__ __forceinline__ void skinny_out(const SkinnyArgs &p, int m, int n, float s) {
+    if constexpr (F32A) skinny_store_f32a(p, m, n, s);
+    else skinny_store<__half>(p, m, n, s);
 }
 
 // End of every skinny kernel: with peer destinations, the thread's stores are made visible system-wide before the
@@ -108,10 +128,12 @@ __device__ __forceinline__ uint32_t word(const uint4 &v, int i) {
 // Requirements (checked on the host): K % 8 == 0, weight rows and token rows contiguous along K with 16-byte aligned
 // starts. grid = (CTAs, ceil(Mc / 16)).
 // Each warp computes 16 weight rows × 16 tokens with mma.sync.m16n8k16: the weight rows are the MMA's M side and the
-// tokens its N side (one or two 8-token tiles). UNROLL 32-wide K steps are loaded before any is used: 8 with one token
-// tile (M <= 8), 4 with two, which keeps 16 (or 8) independent 16-byte weight loads in flight per lane -- at decode
-// shapes HBM needs ~100 KiB in flight per SM. The K order inside a 32-wide step is permuted identically for weights
-// and tokens (a dot product does not depend on it), so every lane's 16-byte load is directly an MMA fragment.
+// tokens its N side (one or two 8-token tiles). The weights of UNROLL = 8 32-wide K steps are loaded before any is
+// used, which keeps 16 independent 16-byte weight loads in flight per lane -- at decode shapes HBM needs ~100 KiB in
+// flight per SM. The token fragments (L1 hits) are loaded right before their MMAs (LAZY), which leaves that register
+// budget to the weights also with two token tiles (measured on B200: M = 16, W 4096 × 4096, 13.1 µs against 14.3 with
+// the tokens prefetched at UNROLL 4). The K order inside a 32-wide step is permuted identically for weights and tokens
+// (a dot product does not depend on it), so every lane's 16-byte load is directly an MMA fragment.
 //
 // Work is spread stream-K style over the whole GPU in one wave. The iteration space is (rb, kc): rb = block of 16
 // weight rows, kc = chunk of UNROLL·32 K elements; T = RB·KC iterations are split evenly over all warps of the grid
@@ -119,9 +141,26 @@ __device__ __forceinline__ uint32_t word(const uint4 &v, int i) {
 // covers a whole row block stores C directly. Otherwise each contributor of the block writes its FP32 partial tile to
 // its slot (slots ordered by K), and the last contributor to arrive (counter per block) sums the slots in slot order
 // and stores C -- deterministic, no spinning: nobody waits for anybody.
-template <bool TWO_NTILES, int UNROLL>
+//
+// Activation modes (the F32 ones serve gemm_pb_skinny, whose activations arrive split into two FP16 parts, a =
+// (hi + lo)·2^-s per row, written by split_f32_rows; both parts go through the MMA into FP32 accumulators, FP16
+// products being exact in FP32, so the result carries the activations to ~22 bits):
+// - ACT_F16: FP16 activations, Mc tokens.
+// - ACT_PAIRED (Mc <= 8 real tokens): hi and lo interleaved as 2·Mc virtual token rows (2m: hi, 2m+1: lo). The loads
+//   and MMAs are those of ACT_F16 on the virtual rows, and since lane (g, t) holds virtual tokens 2t and 2t+1 of its
+//   D fragment, the hi and lo sums of real token t meet in the same lane: the epilogue adds them. With one tile
+//   (Mc <= 4) the token fragments are prefetched with the weights (measured faster there than LAZY).
+// - ACT_SPLIT (9..16 real tokens): hi and lo as two matrices (lo at a + alo), both MMA'd into the same accumulator,
+//   their fragments loaded right before use.
+// In both F32 modes the kernel is launched as the programmatic dependent of split_f32_rows: it issues its first weight
+// loads, then waits for the split (griddepcontrol.wait) before the first activation access.
+enum { ACT_F16 = 0, ACT_PAIRED = 1, ACT_SPLIT = 2 };
+
+template <bool TWO_NTILES, int UNROLL, int MODE = ACT_F16, bool LAZY = false>
 __global__ void __launch_bounds__(WK_WARPS * 32, 2)
 wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *__restrict__ count) {
+    constexpr bool F32A = MODE != ACT_F16;
+    constexpr bool late = LAZY || MODE == ACT_SPLIT;   // activation fragments loaded right before their MMAs
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
     const int t0 = blockIdx.y * 16;
@@ -136,6 +175,9 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *_
     const int ta0 = min(t0 + g, p.Mc - 1), ta1 = min(t0 + g + 8, p.Mc - 1);
     const __half *a0 = A + (long long)ta0 * p.sam;
     const __half *a1 = A + (long long)ta1 * p.sam;
+    const __half *l0 = a0 + p.alo, *l1 = a1 + p.alo;   // ACT_SPLIT: lo parts
+    const int Mout = MODE == ACT_PAIRED ? p.Mc / 2 : p.Mc;   // tokens stored
+    bool waited = false;
     while (it < it_end) {
         const int rb = (int)(it / KC), kc0 = (int)(it % KC);
         const int kc1 = (int)min((long long)KC, kc0 + (it_end - it));
@@ -146,34 +188,90 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *_
         float d0[4] = {0, 0, 0, 0}, d1[4] = {0, 0, 0, 0};
         for (int kc = kc0; kc < kc1; kc++) {
             uint4 wv0[UNROLL], wv1[UNROLL], av0[UNROLL], av1[UNROLL];
+            const uint4 z = make_uint4(0, 0, 0, 0);
+            if constexpr (MODE == ACT_F16 && !late) {
 #pragma unroll
-            for (int u = 0; u < UNROLL; u++) {
-                const int k = (kc * UNROLL + u) * 32 + 8 * t;
-                const bool in = k < p.K;
-                wv0[u] = in ? ldg_w16(w0 + k) : make_uint4(0, 0, 0, 0);
-                wv1[u] = in ? ldg_w16(w1 + k) : make_uint4(0, 0, 0, 0);
-                av0[u] = in ? __ldg(reinterpret_cast<const uint4 *>(a0 + k)) : make_uint4(0, 0, 0, 0);
-                if (TWO_NTILES) av1[u] = in ? __ldg(reinterpret_cast<const uint4 *>(a1 + k)) : make_uint4(0, 0, 0, 0);
+                for (int u = 0; u < UNROLL; u++) {
+                    const int k = (kc * UNROLL + u) * 32 + 8 * t;
+                    const bool in = k < p.K;
+                    wv0[u] = in ? ldg_w16(w0 + k) : z;
+                    wv1[u] = in ? ldg_w16(w1 + k) : z;
+                    av0[u] = in ? __ldg(reinterpret_cast<const uint4 *>(a0 + k)) : z;
+                    if (TWO_NTILES) av1[u] = in ? __ldg(reinterpret_cast<const uint4 *>(a1 + k)) : z;
+                }
+            } else {
+#pragma unroll
+                for (int u = 0; u < UNROLL; u++) {
+                    const int k = (kc * UNROLL + u) * 32 + 8 * t;
+                    const bool in = k < p.K;
+                    wv0[u] = in ? ldg_w16(w0 + k) : z;
+                    wv1[u] = in ? ldg_w16(w1 + k) : z;
+                }
+                if (F32A && !waited) {   // activations, scales: written by the preceding split kernel
+                    asm volatile("griddepcontrol.wait;" ::: "memory");
+                    waited = true;
+                }
+                if constexpr (MODE == ACT_PAIRED && !late) {
+#pragma unroll
+                    for (int u = 0; u < UNROLL; u++) {
+                        const int k = (kc * UNROLL + u) * 32 + 8 * t;
+                        const bool in = k < p.K;
+                        av0[u] = in ? __ldg(reinterpret_cast<const uint4 *>(a0 + k)) : z;
+                        if (TWO_NTILES) av1[u] = in ? __ldg(reinterpret_cast<const uint4 *>(a1 + k)) : z;
+                    }
+                }
             }
 #pragma unroll
             for (int u = 0; u < UNROLL; u++) {
+                uint4 lo0 = z, lo1 = z;
+                if constexpr (late) {
+                    const int k = (kc * UNROLL + u) * 32 + 8 * t;
+                    const bool in = k < p.K;
+                    av0[u] = in ? __ldg(reinterpret_cast<const uint4 *>(a0 + k)) : z;
+                    if (TWO_NTILES) av1[u] = in ? __ldg(reinterpret_cast<const uint4 *>(a1 + k)) : z;
+                    if (MODE == ACT_SPLIT) {
+                        lo0 = in ? __ldg(reinterpret_cast<const uint4 *>(l0 + k)) : z;
+                        if (TWO_NTILES) lo1 = in ? __ldg(reinterpret_cast<const uint4 *>(l1 + k)) : z;
+                    }
+                }
 #pragma unroll
                 for (int j = 0; j < 2; j++) {
                     const uint32_t A0 = word(wv0[u], 2 * j), A1 = word(wv1[u], 2 * j);
                     const uint32_t A2 = word(wv0[u], 2 * j + 1), A3 = word(wv1[u], 2 * j + 1);
                     mma_16816(d0, A0, A1, A2, A3, word(av0[u], 2 * j), word(av0[u], 2 * j + 1));
                     if (TWO_NTILES) mma_16816(d1, A0, A1, A2, A3, word(av1[u], 2 * j), word(av1[u], 2 * j + 1));
+                    if constexpr (MODE == ACT_SPLIT) {
+                        mma_16816(d0, A0, A1, A2, A3, word(lo0, 2 * j), word(lo0, 2 * j + 1));
+                        if (TWO_NTILES) mma_16816(d1, A0, A1, A2, A3, word(lo1, 2 * j), word(lo1, 2 * j + 1));
+                    }
                 }
             }
         }
         // D fragment: d[0..1] = (row g, tokens 2t, 2t+1), d[2..3] = (row g+8, tokens 2t, 2t+1); d1: tokens + 8.
+        // ACT_PAIRED: tokens 2t, 2t+1 are the hi and lo parts of real token t (d1: 4 + t); their sum is its value.
+        float v[8];
+        int vm[8], vr[8], nv;
+        if constexpr (MODE == ACT_PAIRED) {
+            v[0] = d0[0] + d0[1]; vr[0] = g;     vm[0] = t;
+            v[1] = d0[2] + d0[3]; vr[1] = g + 8; vm[1] = t;
+            v[2] = d1[0] + d1[1]; vr[2] = g;     vm[2] = 4 + t;
+            v[3] = d1[2] + d1[3]; vr[3] = g + 8; vm[3] = 4 + t;
+            nv = TWO_NTILES ? 4 : 2;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                v[e] = e < 4 ? d0[e] : d1[e - 4];
+                vr[e] = g + ((e & 2) ? 8 : 0);
+                vm[e] = 2 * t + (e & 1) + (e >= 4 ? 8 : 0);
+            }
+            nv = TWO_NTILES ? 8 : 4;
+        }
         if (kc0 == 0 && kc1 == KC) {
 #pragma unroll
             for (int e = 0; e < 8; e++) {
-                if (!TWO_NTILES && e >= 4) break;
-                const float v = e < 4 ? d0[e] : d1[e - 4];
-                const int n = r0 + g + ((e & 2) ? 8 : 0), m = t0 + 2 * t + (e & 1) + (e >= 4 ? 8 : 0);
-                if (n < p.Nc && m < p.Mc) skinny_store<__half>(p, m, n, v);
+                if (e >= nv) break;
+                const int n = r0 + vr[e], m = t0 + vm[e];
+                if (n < p.Nc && m < Mout) skinny_out<F32A>(p, m, n, v[e]);
             }
         } else {
             const long long x0 = (long long)rb * KC, x1 = x0 + KC - 1;
@@ -183,9 +281,8 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *_
             float *sp = part + (blk * maxc + (wg - wf)) * 256;
 #pragma unroll
             for (int e = 0; e < 8; e++) {
-                if (!TWO_NTILES && e >= 4) break;
-                const int row = g + ((e & 2) ? 8 : 0), tok = 2 * t + (e & 1) + (e >= 4 ? 8 : 0);
-                sp[row * 16 + tok] = e < 4 ? d0[e] : d1[e - 4];
+                if (e >= nv) break;
+                sp[vr[e] * 16 + vm[e]] = v[e];
             }
             // The warp's partial stores are ordered before the counter update by the warp barrier and the release of
             // the atomic (cumulative at GPU scope); the last arriver's acquire makes every slot visible to its lanes.
@@ -197,7 +294,7 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *_
             if (prev == nc - 1) {
                 __syncwarp();   // the lanes' slot reads are ordered after lane 0's acquire
                 const int row = lane >> 1, tb = (lane & 1) * 8;
-                if (t0 + tb < p.Mc && r0 + row < p.Nc) {
+                if (t0 + tb < Mout && r0 + row < p.Nc) {
                     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
                     const float4 *src0 = reinterpret_cast<const float4 *>(part + blk * maxc * 256 + row * 16 + tb);
                     int q = 0;
@@ -221,7 +318,7 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *_
                     }
 #pragma unroll
                     for (int j = 0; j < 8; j++)
-                        if (t0 + tb + j < p.Mc) skinny_store<__half>(p, t0 + tb + j, r0 + row, acc[j]);
+                        if (t0 + tb + j < Mout) skinny_out<F32A>(p, t0 + tb + j, r0 + row, acc[j]);
                 }
                 if (lane == 0) count[blk] = 0;   // ready for the next launch
             }
@@ -398,6 +495,30 @@ __global__ void repack_small(const T *__restrict__ a, long long sam, long long s
     }
 }
 
+// Stream-K plan of wk_f16_sk: a one-wave grid of CTAs, K chunks of unroll·32 elements, and the partial-tile slots
+// per 16-row block (the most warps that can share one block).
+struct SkPlan {
+    int KC, RB, mtiles, maxc;
+    long long ctas;
+    size_t part_bytes;
+};
+
+static SkPlan sk_plan(int Mc, int Nc, int K, int unroll, int sm_count) {
+    SkPlan q;
+    q.KC = (K + unroll * 32 - 1) / (unroll * 32);
+    q.RB = (Nc + 15) / 16;
+    q.mtiles = (Mc + 15) / 16;
+    const long long iters = (long long)q.RB * q.KC;
+    long long ctas = (iters + 2 * WK_WARPS - 1) / (2 * WK_WARPS);   // at least ~2 iterations per warp
+    if (ctas > 2 * sm_count) ctas = 2 * sm_count;
+    if (ctas < 1) ctas = 1;
+    const long long per = iters / (ctas * WK_WARPS);
+    q.maxc = (int)(per == 0 ? q.KC : (q.KC / per + 2 < q.KC ? q.KC / per + 2 : q.KC));
+    q.ctas = ctas;
+    q.part_bytes = (size_t)q.mtiles * q.RB * q.maxc * 256 * sizeof(float);
+    return q;
+}
+
 template <typename T>
 static int skinny_t(SkinnyArgs p, cudaStream_t st) {
     DevState *d = dev_state();
@@ -411,16 +532,8 @@ static int skinny_t(SkinnyArgs p, cudaStream_t st) {
             const bool a_ok = p.sak == 1 && ((uintptr_t)p.a & 15) == 0 && (p.sam * es) % 16 == 0;
             // Scratch layout: [repacked small operand (when needed) | stream-K partial tiles (FP32)].
             const size_t a_bytes = a_ok ? 0 : ((size_t)p.Mc * p.K * es + 255) / 256 * 256;
-            const int unroll = p.Mc > 8 ? 4 : 8;
-            const int KC = (p.K + unroll * 32 - 1) / (unroll * 32);
-            const int RB = (p.Nc + 15) / 16, mtiles = (p.Mc + 15) / 16;
-            const long long iters = (long long)RB * KC;
-            long long ctas = (iters + 2 * WK_WARPS - 1) / (2 * WK_WARPS);   // at least ~2 iterations per warp
-            if (ctas > 2 * d->sm_count) ctas = 2 * d->sm_count;
-            if (ctas < 1) ctas = 1;
-            const long long q = iters / (ctas * WK_WARPS);
-            const int maxc = (int)(q == 0 ? KC : (KC / q + 2 < KC ? KC / q + 2 : KC));
-            const size_t part_bytes = sizeof(T) == 2 ? (size_t)mtiles * RB * maxc * 256 * sizeof(float) : 0;
+            const SkPlan q = sk_plan(p.Mc, p.Nc, p.K, 8, d->sm_count);
+            const size_t part_bytes = sizeof(T) == 2 ? q.part_bytes : 0;
             void *scr = nullptr;
             if (a_bytes + part_bytes) G9_TRY(scratch(a_bytes + part_bytes, &scr));
             if (!a_ok) {
@@ -432,11 +545,11 @@ static int skinny_t(SkinnyArgs p, cudaStream_t st) {
             }
             if (sizeof(T) == 2) {
                 int *count = nullptr;
-                G9_TRY(skinny_counters((size_t)mtiles * RB, &count));
+                G9_TRY(skinny_counters((size_t)q.mtiles * q.RB, &count));
                 float *part = (float *)((char *)scr + a_bytes);
-                dim3 grid((unsigned)ctas, mtiles);
-                if (p.Mc > 8) wk_f16_sk<true, 4><<<grid, WK_WARPS * 32, 0, st>>>(p, KC, maxc, part, count);
-                else wk_f16_sk<false, 8><<<grid, WK_WARPS * 32, 0, st>>>(p, KC, maxc, part, count);
+                dim3 grid((unsigned)q.ctas, q.mtiles);
+                if (p.Mc > 8) wk_f16_sk<true, 8, ACT_F16, true><<<grid, WK_WARPS * 32, 0, st>>>(p, q.KC, q.maxc, part, count);
+                else wk_f16_sk<false, 8, ACT_F16, true><<<grid, WK_WARPS * 32, 0, st>>>(p, q.KC, q.maxc, part, count);
                 return launched("skinny_wk_f16_sk");
             }
             const int mt = p.Mc <= 1 ? 1 : p.Mc <= 4 ? 4 : p.Mc <= 8 ? 8 : 16;
@@ -471,6 +584,131 @@ static int skinny_t(SkinnyArgs p, cudaStream_t st) {
     return launched("skinny_wn_final");
 }
 
+// ------------------------------------------------------------------------------------------------ F32 activations
+constexpr int SPLIT_THREADS = 512;
+
+// Input of the F32-activation kernel: row m of a, scaled by 2^s (s puts the row's largest magnitude in [2^14, 2^15),
+// clamped to |s| <= 126), split into FP16 hi = rn(x) and lo = rn(x - hi) (rows of Kp elements, zero past K);
+// tscale[m] = 2^-s. x - hi is exact in FP32, so hi + lo carries x to 2^-22 relative plus 2^-25 absolute (FP16
+// subnormals), i.e. 2^-39 of the row's largest value. A row holding inf or NaN is not scaled (s = 0); its results come
+// out non-finite and are flagged. One CTA per row, 16-byte loads when the rows allow them (vec4); the second pass
+// re-reads the row from L1.
+// The kernel lets its dependent grid (the weight-streaming kernel, launched with programmatic stream serialization)
+// start right away: that grid issues its first weight loads and then waits (griddepcontrol.wait) for this one.
+// Row m of the parts starts at hi + m·rs and lo + m·rs (ACT_PAIRED: rs = 2·Kp, lo = hi + Kp; ACT_SPLIT: rs = Kp, lo
+// = hi + M·Kp).
+__global__ void __launch_bounds__(SPLIT_THREADS) split_f32_rows(const float *__restrict__ a, long long lda, int K,
+                                                               int Kp, bool vec4, __half *__restrict__ hi,
+                                                               __half *__restrict__ lo, long long rs,
+                                                               float *__restrict__ tscale) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    __shared__ float red[SPLIT_THREADS / 32];
+    __shared__ float sc;
+    const int m = blockIdx.x;
+    const float *row = a + (long long)m * lda;
+    const int K4 = vec4 ? K / 4 : 0;
+    float mx = 0.0f;
+    for (int i = threadIdx.x; i < K4; i += SPLIT_THREADS) {
+        const float4 v = reinterpret_cast<const float4 *>(row)[i];
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+    for (int k = 4 * K4 + threadIdx.x; k < K; k += SPLIT_THREADS) mx = fmaxf(mx, fabsf(row[k]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < SPLIT_THREADS / 32; w++) mx = fmaxf(mx, red[w]);
+        const int e = (int)((__float_as_uint(mx) >> 23) & 255u);   // biased exponent; 0 for zero / subnormal
+        int s = 0;
+        if (mx > 0.0f && e != 255) {
+            s = 14 - ((e == 0 ? 1 : e) - 127);
+            s = s > 126 ? 126 : s < -126 ? -126 : s;
+        }
+        sc = __uint_as_float((unsigned)(s + 127) << 23);
+        tscale[m] = __uint_as_float((unsigned)(127 - s) << 23);
+    }
+    __syncthreads();
+    const float f = sc;
+    __half *h = hi + (long long)m * rs, *l = lo + (long long)m * rs;
+    for (int i = threadIdx.x; i < Kp / 4; i += SPLIT_THREADS) {   // Kp is a multiple of 8: 8-byte stores
+        const int k = 4 * i;
+        float x[4];
+        if (i < K4) {
+            const float4 v = reinterpret_cast<const float4 *>(row)[i];
+            x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; j++) x[j] = k + j < K ? row[k + j] : 0.0f;
+        }
+        __half2 hv[2], lv[2];
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            const float x0 = x[2 * j] * f, x1 = x[2 * j + 1] * f;
+            hv[j] = __floats2half2_rn(x0, x1);
+            const float2 hf = __half22float2(hv[j]);
+            lv[j] = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
+        }
+        *reinterpret_cast<uint2 *>(h + k) = make_uint2(*reinterpret_cast<uint32_t *>(&hv[0]), *reinterpret_cast<uint32_t *>(&hv[1]));
+        *reinterpret_cast<uint2 *>(l + k) = make_uint2(*reinterpret_cast<uint32_t *>(&lv[0]), *reinterpret_cast<uint32_t *>(&lv[1]));
+    }
+}
+
+template <bool TWO_NTILES, int UNROLL, int MODE, bool LAZY = false>
+static int launch_f32a_main(const SkinnyArgs &p, const SkPlan &q, float *part, int *count, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)q.ctas, q.mtiles);
+    cfg.blockDim = dim3(WK_WARPS * 32);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, wk_f16_sk<TWO_NTILES, UNROLL, MODE, LAZY>, p, q.KC, q.maxc, part, count);
+    return launched("skinny_wk_f16_sk_f32a");
+}
+
+int launch_skinny_f32a(int M, int N, int K, const float *A, int lda, const void *W, int ldw, float *C, int ldc,
+                       unsigned *nf, cudaStream_t st) {
+    DevState *d = dev_state();
+    if (!d) return G.status;
+    const int Kp = (K + 7) / 8 * 8;
+    if (ldw < Kp || ldw % 8 != 0 || ((uintptr_t)W & 15) != 0)
+        return fail(GEN9BLAS_ERR_INVALID_ARG, "F32-activation skinny GEMM: weight rows must be padded, 16-byte aligned");
+    SkinnyArgs p;
+    const bool paired = M <= 8;
+    p.Mc = paired ? 2 * M : M;   // ACT_PAIRED: virtual token rows (hi, lo interleaved)
+    p.Nc = N; p.K = Kp;
+    p.alpha = 1.0f; p.beta = 0.0f;
+    p.w = W; p.swn = ldw; p.swk = 1;
+    p.C = C; p.scm = ldc; p.scn = 1;
+    p.dst[0] = C; p.ndst = 1; p.coff = 0;
+    p.sam = Kp; p.sak = 1;
+    p.alo = paired ? 0 : (long long)M * Kp;
+    p.nf = nf;
+    const SkPlan q = sk_plan(p.Mc, N, Kp, 8, d->sm_count);
+    // Scratch layout: [hi, lo (2·M rows of Kp FP16) | row scales | stream-K partial tiles (FP32)].
+    const size_t a_bytes = ((size_t)2 * M * Kp * sizeof(__half) + 255) / 256 * 256, s_bytes = 256;
+    void *scr = nullptr;
+    G9_TRY(scratch(a_bytes + s_bytes + q.part_bytes, &scr));
+    int *count = nullptr;
+    G9_TRY(skinny_counters((size_t)q.mtiles * q.RB, &count));
+    __half *hi = (__half *)scr;
+    float *ts = (float *)((char *)scr + a_bytes);
+    p.a = hi;
+    p.tscale = ts;
+    const bool vec4 = ((uintptr_t)A & 15) == 0 && lda % 4 == 0;
+    if (paired) split_f32_rows<<<M, SPLIT_THREADS, 0, st>>>(A, lda, K, Kp, vec4, hi, hi + Kp, 2LL * Kp, ts);
+    else split_f32_rows<<<M, SPLIT_THREADS, 0, st>>>(A, lda, K, Kp, vec4, hi, hi + (size_t)M * Kp, Kp, ts);
+    G9_TRY(launched("skinny_split_f32"));
+    float *part = (float *)((char *)scr + a_bytes + s_bytes);
+    if (!paired) return launch_f32a_main<true, 8, ACT_SPLIT>(p, q, part, count, st);
+    if (p.Mc > 8) return launch_f32a_main<true, 8, ACT_PAIRED, true>(p, q, part, count, st);
+    return launch_f32a_main<false, 8, ACT_PAIRED>(p, q, part, count, st);
+}
+
 int launch_skinny(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, const void *B,
                   int ldb, double beta, void *C, int ldc, cudaStream_t st, void *const *peers, int npeers,
                   long long col_off) {
@@ -482,6 +720,9 @@ int launch_skinny(int type, int tA, int tB, int M, int N, int K, double alpha, c
     p.ndst = 1;
     p.dst[0] = C;
     p.coff = 0;
+    p.alo = 0;
+    p.tscale = nullptr;
+    p.nf = nullptr;
     if (peers && npeers > 0) {
         if (npeers > 8) return fail(GEN9BLAS_ERR_INVALID_ARG, "at most 8 ranks for the fused skinny GEMM + all-gather");
         for (int q = 0; q < npeers; q++) p.dst[q] = peers[q];

@@ -726,3 +726,73 @@ def spr2(alpha, x, y, Ap, uplo="L"):
     Ap, pp = _packed(Ap, t, n, True)
     _check(_lib.gen9blas_spr2(_kind_basic(t), _TRI[uplo], n, alpha, px, ix, py, iy, pp))
     return Ap
+
+
+# ---------------- constant weights kept on the GPU (lib/gen9blas.h:89-97, lib/gen9blas_ml.h:25-28) ----------------
+_lib.gen9blas_pack_b.argtypes = [_i, _i, _i, _i, _p, _i]
+_lib.gen9blas_pack_b.restype = _p
+_lib.gen9blas_gemm_pb.argtypes = [_i, _i, _d, _p, _i, _p, _d, _p, _i]
+_lib.gen9blas_packed_b_free.argtypes = [_p]
+_lib.gen9blas_packed_b_free.restype = None
+_lib.gen9blas_gemm_pb_skinny.argtypes = [_i, _p, _i, _p, _p, _i, ctypes.POINTER(_i)]
+
+
+class PackedB:
+    """op(B) packed once into GPU memory (gen9blas_pack_b), multiplied many times. B: a (K, N) matrix, or with
+    transB=True the (N, K) weight matrix (W[N][K] as ggml and most checkpoints store it); a transposed view is read in
+    place. B may be changed or freed afterwards. The device memory is released by free() (or when the object is
+    collected)."""
+
+    def __init__(self, B, transB=False, accurate=False):
+        _init()
+        dt = B.dtype if B.dtype in (np.float16, np.float32, np.float64) else np.float32
+        B, pb, R, Cn, ldb, tr = _mat(B, dt)
+        tB = int(transB) ^ tr                 # stored R × Cn: op(B) is R × Cn (tB = 0) or Cn × R (tB = 1)
+        self.K, self.N = (Cn, R) if tB else (R, Cn)
+        self.dtype, self.type = np.dtype(dt), _kind(dt, accurate)
+        p = _lib.gen9blas_pack_b(self.type, tB, self.K, self.N, pb, ldb)
+        if not p:
+            raise RuntimeError(_lib.gen9blas_error().decode())
+        self._p = p
+
+    def free(self):
+        if getattr(self, "_p", None):
+            _lib.gen9blas_packed_b_free(self._p)
+            self._p = None
+
+    def __del__(self):
+        self.free()
+
+    def gemm(self, A, alpha=1.0, beta=0.0, C=None):
+        """C = alpha·A·op(B) + beta·C (A: M × K of the packed type; an A.T view is read in place)."""
+        if not self._p:
+            raise ValueError("packed B was freed")
+        a, pa, M, K, lda, ta = _mat(A, self.dtype)
+        if ta:
+            M, K = K, M
+        if K != self.K:
+            raise ValueError(f"A has {K} columns, the packed B {self.K} rows")
+        C, given, ldc = _output(C, (M, self.N), self.dtype)
+        _check(_lib.gen9blas_gemm_pb(ta, M, alpha, pa, lda, self._p, beta if given else 0.0, C.ctypes.data, ldc))
+        return C
+
+    def skinny(self, A):
+        """(C, nonfinite): C = A·op(B) in FP32 for FP32 activations A (1 to 16 rows) and FP16 weights packed with
+        accurate=True (gen9blas_gemm_pb_skinny)."""
+        if not self._p:
+            raise ValueError("packed B was freed")
+        A = np.ascontiguousarray(A, dtype=np.float32)
+        M, K = A.shape
+        if K != self.K:
+            raise ValueError(f"A has {K} columns, the packed B {self.K} rows")
+        C = np.empty((M, self.N), np.float32)
+        nf = _i(0)
+        r = _lib.gen9blas_gemm_pb_skinny(M, A.ctypes.data, K, self._p, C.ctypes.data, self.N, ctypes.byref(nf))
+        if r == 1:
+            raise ValueError("gemm_pb_skinny takes 1 to 16 rows")
+        _check(r)
+        return C, bool(nf.value)
+
+
+def pack_b(B, transB=False, accurate=False):
+    return PackedB(B, transB, accurate)

@@ -70,7 +70,7 @@ enum {
     GEN9BLAS_FEAT_CPY,
     GEN9BLAS_FEAT_SET_ROWS,
 };                                                        /* ref: lib/gen9blas.h:56-66 */
-GEN9BLAS_API int gen9blas_has(int feature);              /* ref: lib/gen9blas.h:68; 1 for FP16/FP32/FP64, else 0 */
+GEN9BLAS_API int gen9blas_has(int feature);              /* ref: lib/gen9blas.h:68; 1: FP16/FP32/FP64, SKINNY_PB */
 GEN9BLAS_API const char *gen9blas_error(void);           /* ref: lib/gen9blas.h:69 */
 GEN9BLAS_API int gen9blas_last_status(void);             /* ref: lib/gen9blas.h:70 */
 GEN9BLAS_API double gen9blas_last_time_ms(void);         /* ref: lib/gen9blas.h:71; GEN9BLAS_PROFILE=1: kernel time */
@@ -90,13 +90,17 @@ GEN9BLAS_API int gen9blas_gemm(int type, int transA, int transB, int M, int N, i
 GEN9BLAS_API int gen9blas_gemm_batched(int type, int transA, int transB, int M, int N, int K, double alpha,
                                        const void *A, int lda, int64_t sA, const void *B, int ldb, int64_t sB,
                                        double beta, void *C, int ldc, int64_t sC, int count);
-/* Constant packed weights (ref: lib/gen9blas.h:94-98): not built in this tier, return UNSUPPORTED / NULL. */
+/* Constant weights kept on the GPU (ref: lib/gen9blas.h:89-97): pack op(B) (K×N; transB: B stored N×K, host or device
+ * memory) once into HBM of the current device, multiply many times. gemm_pb: C = alpha·op(A)·Bp + beta·C with op(A)
+ * M×K of the type Bp was packed with (GEN9BLAS_H, _S, _HS, _D). pack_b: NULL on error (gen9blas_error()); B may be
+ * overwritten or freed once it returns. packed_b_free waits for queued work first. */
 typedef struct gen9blas_packed_b gen9blas_packed_b;
 GEN9BLAS_API gen9blas_packed_b *gen9blas_pack_b(int type, int transB, int K, int N, const void *B, int ldb);
 GEN9BLAS_API int gen9blas_gemm_pb(int transA, int M, double alpha, const void *A, int lda, const gen9blas_packed_b *Bp,
                                   double beta, void *C, int ldc);
 GEN9BLAS_API void gen9blas_packed_b_free(gen9blas_packed_b *Bp);
-/* Level-3 derived operations (ref: lib/gen9blas.h:100-113): not built in this tier, return UNSUPPORTED. */
+/* Level-3 operations on top of GEMM (ref: lib/gen9blas.h:98-113): SYMM, SYRK, SYR2K, TRMM (all four types) and TRSM
+ * (FP32, FP64, FP16 H / HS); only the uplo triangle of A is read, SYRK / SYR2K modify only the uplo triangle of C. */
 GEN9BLAS_API int gen9blas_symm(int type, int side, int uplo, int M, int N, double alpha, const void *A, int lda,
                                const void *B, int ldb, double beta, void *C, int ldc);
 GEN9BLAS_API int gen9blas_syrk(int type, int uplo, int trans, int N, int K, double alpha, const void *A, int lda,
@@ -140,7 +144,7 @@ GEN9BLAS_API int gen9blas_syr2(int type, int uplo, int n, double alpha, const vo
 /* A = alpha·x·yᵀ + A, A M×N. ref: lib/gen9blas.h:147-148 */
 GEN9BLAS_API int gen9blas_ger(int type, int M, int N, double alpha, const void *x, int incx, const void *y, int incy,
                               void *A, int lda);
-/* Banded and packed level 2 (ref: lib/gen9blas.h:150-168): not built in this tier, return UNSUPPORTED. */
+/* Banded and packed level 2 (ref: lib/gen9blas.h:150-168), CBLAS RowMajor storage. */
 GEN9BLAS_API int gen9blas_gbmv(int type, int trans, int M, int N, int KL, int KU, double alpha, const void *A, int lda,
                                const void *x, int incx, double beta, void *y, int incy);
 GEN9BLAS_API int gen9blas_sbmv(int type, int uplo, int N, int K, double alpha, const void *A, int lda, const void *x, int incx,

@@ -23,6 +23,10 @@ SIGNATURES = {
     "selftest_wait": ([_d], _i),
     "gemv_noalloc": ([_i, _i, _i, _i, _d, _p, _i, _p, _i, _d, _p, _i], _i),
     "peer_barrier": ([_p, _i, _i, _d], _i),
+    "pack_b": ([_i, _i, _i, _i, _p, _i], _p),
+    "gemm_pb": ([_i, _i, _d, _p, _i, _p, _d, _p, _i], _i),
+    "packed_b_free": ([_p], None),
+    "gemm_pb_skinny": ([_i, _p, _i, _p, _p, _i, ctypes.POINTER(_i)], _i),
 }
 
 

@@ -10,12 +10,12 @@ import pytest
 
 from conftest import PKG, ROOT
 
-HEADER = os.path.join(ROOT, "include", "gen9blas.h")
+HEADERS = [os.path.join(ROOT, "include", h) for h in ("gen9blas.h", "gen9blas_ml.h")]
 LIB = os.path.join(PKG, "libgen9blas.so")
 
 
 def declared_functions():
-    text = open(HEADER).read()
+    text = "".join(open(h).read() for h in HEADERS)
     return sorted(set(re.findall(r"GEN9BLAS_API\s+[^;(]*?\b(gen9blas_\w+)\s*\(", text)))
 
 
@@ -29,9 +29,10 @@ def test_header_declares_reference_surface():
     # the 51 entry points of the reference's lib/gen9blas.h plus the additions of this build
     for must in ("gen9blas_gemm", "gen9blas_gemm_batched", "gen9blas_hgemm", "gen9blas_sgemm", "gen9blas_axpy",
                  "gen9blas_dot", "gen9blas_nrm2", "gen9blas_asum", "gen9blas_iamax", "gen9blas_gemv", "gen9blas_ger",
-                 "gen9blas_init", "gen9blas_error", "gen9blas_alloc", "gen9blas_spr2", "gen9blas_set_device"):
+                 "gen9blas_init", "gen9blas_error", "gen9blas_alloc", "gen9blas_spr2", "gen9blas_set_device",
+                 "gen9blas_pack_b", "gen9blas_gemm_pb", "gen9blas_packed_b_free", "gen9blas_gemm_pb_skinny"):
         assert must in names
-    assert len(names) == 66
+    assert len(names) == 67
 
 
 def test_library_exports_every_declared_function():

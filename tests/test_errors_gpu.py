@@ -30,9 +30,22 @@ def test_status_codes(gpu_lib):
     assert L.gemv(abi.S, 0, 8, 8, 1.0, a.ctypes.data, 4, x.ctypes.data, 1, 0.0, y.ctypes.data, 1) == INVALID
     assert L.axpy(abi.S, 8, 1.0, x.ctypes.data, 0, y.ctypes.data, 1) == INVALID
     assert L.gemm(abi.S, 0, 0, 0, 8, 8, 1.0, a.ctypes.data, 8, b.ctypes.data, 8, 0.0, c.ctypes.data, 8) == OK  # empty
-    L.dll.gen9blas_pack_b.restype = ctypes.c_void_p
-    assert L.dll.gen9blas_pack_b(abi.S, 0, 8, 8, ctypes.c_void_p(b.ctypes.data), 8) is None
-    assert L.last_status() == UNSUPPORTED
+    # packed weights: lib/test_errors.py:47-59
+    assert L.gemm_pb(0, 8, 1.0, a.ctypes.data, 8, None, 0.0, c.ctypes.data, 8) == INVALID
+    assert L.pack_b(7, 0, 8, 8, b.ctypes.data, 8) is None and L.last_status() == UNSUPPORTED
+    assert L.pack_b(abi.S, 0, 0, 8, b.ctypes.data, 8) is None and L.last_status() == INVALID
+    w = np.ones((64, 64), np.float16)
+    P = L.pack_b(abi.HS, 1, 64, 64, w.ctypes.data, 64)
+    assert P
+    A, C64, nf = np.ones((17, 64), np.float32), np.zeros((17, 64), np.float32), ctypes.c_int(0)
+    assert L.gemm_pb_skinny(17, A.ctypes.data, 64, P, C64.ctypes.data, 64, ctypes.byref(nf)) == 1   # DECLINED
+    assert not C64.any()
+    Sp = L.pack_b(abi.S, 1, 64, 64, np.ones((64, 64), np.float32).ctypes.data, 64)
+    assert L.gemm_pb_skinny(4, A.ctypes.data, 64, Sp, C64.ctypes.data, 64, ctypes.byref(nf)) == INVALID
+    assert L.gemm_pb_skinny(4, A.ctypes.data, 64, P, C64.ctypes.data, 64, ctypes.byref(nf)) == OK
+    assert (C64[:4] == 64).all() and nf.value == 0
+    L.packed_b_free(P)
+    L.packed_b_free(Sp)
     assert L.alloc(1 << 50) is None and L.last_status() == OOM
     p = L.alloc(4096)
     assert p and L.is_usm(p, 4096) == 1 and L.is_usm(p, 8192 * 1024 * 1024) == 0
