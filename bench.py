@@ -50,8 +50,9 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="auto", choices=["auto", "hgemm4096", "scaleout", "rows"],
                     help="rows: one JSON line per BASELINE config row (GEMM, skinny, level 1/2), N = 1 only")
-    ap.add_argument("--rows", default="C0,C1,C2,C3a,C3b,C3c,L3,PB",
-                    help="rows workload: which config rows to measure (L3: level 3 on GEMM, PB: packed weights)")
+    ap.add_argument("--rows", default="C0,C1,C2,C3a,C3b,C3c,L3,L2X,PB",
+                    help="rows workload: which config rows to measure (L3: level 3 on GEMM, L2X: rest of levels 1-2, "
+                         "PB: packed weights)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample (profiling runs)")
     ap.add_argument("--gather", default="fused", choices=["fused", "nccl"],
@@ -838,6 +839,79 @@ def run_rows(args, torch):
             L.dll.gen9blas_packed_b_free(P)
             del A, Wt, Cm
         torch.cuda.empty_cache()
+
+    # rest of levels 1-2 (the scope table's next row): level 1 at n = 2^28, level 2 at n = 16384 (dense, band K = 64,
+    # packed), FP32 and FP64; each against its algorithmic HBM bytes (the stored elements read and written once)
+    if "L2X" in want:
+        ci, cd, cp = ctypes.c_int, ctypes.c_double, ctypes.c_void_p
+        sigs = {"scal": [ci, ci, cd, cp, ci], "copy": [ci, ci, cp, ci, cp, ci], "swap": [ci, ci, cp, ci, cp, ci],
+                "rot": [ci, ci, cp, ci, cp, ci, cd, cd], "symv": [ci, ci, ci, cd, cp, ci, cp, ci, cd, cp, ci],
+                "trmv": [ci] * 5 + [cp, ci, cp, ci], "trsv": [ci] * 5 + [cp, ci, cp, ci],
+                "syr": [ci, ci, ci, cd, cp, ci, cp, ci], "syr2": [ci, ci, ci, cd, cp, ci, cp, ci, cp, ci],
+                "gbmv": [ci] * 6 + [cd, cp, ci, cp, ci, cd, cp, ci], "sbmv": [ci] * 4 + [cd, cp, ci, cp, ci, cd, cp, ci],
+                "tbmv": [ci] * 6 + [cp, ci, cp, ci], "tbsv": [ci] * 6 + [cp, ci, cp, ci],
+                "spmv": [ci] * 3 + [cd, cp, cp, ci, cd, cp, ci], "tpmv": [ci] * 5 + [cp, cp, ci],
+                "tpsv": [ci] * 5 + [cp, cp, ci], "spr": [ci] * 3 + [cd, cp, ci, cp],
+                "spr2": [ci] * 3 + [cd, cp, ci, cp, ci, cp]}
+        fn = {}
+        for nm, a_t in sigs.items():
+            f = getattr(L.dll, "gen9blas_" + nm)
+            f.argtypes, f.restype = a_t, ctypes.c_int
+            fn[nm] = f
+        n1 = 1 << 28
+        m, kb = 16384, 64
+        for kind, dt, tag in ((S, torch.float32, "s"), (D, torch.float64, "d")):
+            es = 4 if kind == S else 8
+            x = torch.rand(n1, device="cuda", generator=g, dtype=dt)
+            y = torch.rand(n1, device="cuda", generator=g, dtype=dt)
+            px, py = x.data_ptr(), y.data_ptr()
+            for nm, call, nbytes in (
+                    ("scal", lambda i: chk(fn["scal"](kind, n1, 0.999, px, 1)), 2 * n1 * es),
+                    ("copy", lambda i: chk(fn["copy"](kind, n1, px, 1, py, 1)), 2 * n1 * es),
+                    ("swap", lambda i: chk(fn["swap"](kind, n1, px, 1, py, 1)), 4 * n1 * es),
+                    ("rot", lambda i: chk(fn["rot"](kind, n1, px, 1, py, 1, 0.6, 0.8)), 4 * n1 * es)):
+                ms = queued_ms(call, 10)
+                gbps = nbytes / (ms * 1e-3) / 1e9
+                emit_row("L2X", f"{tag}{nm} n=2^28", gbps, "GB/s", ms, "hbm", gbps, peak_hbm, "GB/s", f"{peak_kind} HBM copy")
+            del x, y
+            A = torch.rand(m, m, device="cuda", generator=g, dtype=dt).div_(m)
+            A.diagonal().fill_(1.0)
+            xv = torch.rand(m, device="cuda", generator=g, dtype=dt)
+            yv = torch.rand(m, device="cuda", generator=g, dtype=dt)
+            Bd = torch.rand(m, 2 * kb + 1, device="cuda", generator=g, dtype=dt).div_(kb)
+            Bd[:, kb] = 1.0    # diagonal of the band (general: column KL; lower symmetric / triangular: column K)
+            Bs = Bd[:, kb:].contiguous()   # K + 1 columns, diagonal in column 0 (upper storage)
+            npk = m * (m + 1) // 2
+            Ap = torch.rand(npk, device="cuda", generator=g, dtype=dt).div_(m)
+            pA, pX, pY, pB, pS, pP = A.data_ptr(), xv.data_ptr(), yv.data_ptr(), Bd.data_ptr(), Bs.data_ptr(), Ap.data_ptr()
+            tri = m * (m + 1) // 2 * es
+            band = m * (2 * kb + 1) * es
+            sband = m * (kb + 1) * es
+            vec = m * es
+            cases = (
+                ("symv", lambda i: chk(fn["symv"](kind, 0, m, 1.0, pA, m, pX, 1, 0.0, pY, 1)), tri + 2 * vec),
+                ("trmv", lambda i: chk(fn["trmv"](kind, 0, 0, 0, m, pA, m, pX, 1)), tri + 2 * vec),
+                ("trsv", lambda i: chk(fn["trsv"](kind, 0, 0, 0, m, pA, m, pX, 1)), tri + 2 * vec),
+                ("syr", lambda i: chk(fn["syr"](kind, 0, m, 1e-9, pX, 1, pA, m)), 2 * tri + vec),
+                ("syr2", lambda i: chk(fn["syr2"](kind, 0, m, 1e-9, pX, 1, pY, 1, pA, m)), 2 * tri + 2 * vec),
+                ("gbmv", lambda i: chk(fn["gbmv"](kind, 0, m, m, kb, kb, 1.0, pB, 2 * kb + 1, pX, 1, 0.0, pY, 1)),
+                 band + 2 * vec),
+                ("sbmv", lambda i: chk(fn["sbmv"](kind, 1, m, kb, 1.0, pS, kb + 1, pX, 1, 0.0, pY, 1)), sband + 2 * vec),
+                ("tbmv", lambda i: chk(fn["tbmv"](kind, 1, 0, 0, m, kb, pS, kb + 1, pX, 1)), sband + 2 * vec),
+                ("tbsv", lambda i: chk(fn["tbsv"](kind, 1, 0, 0, m, kb, pS, kb + 1, pX, 1)), sband + 2 * vec),
+                ("spmv", lambda i: chk(fn["spmv"](kind, 0, m, 1.0, pP, pX, 1, 0.0, pY, 1)), tri + 2 * vec),
+                ("tpmv", lambda i: chk(fn["tpmv"](kind, 0, 0, 0, m, pP, pX, 1)), tri + 2 * vec),
+                ("tpsv", lambda i: chk(fn["tpsv"](kind, 0, 0, 0, m, pP, pX, 1)), tri + 2 * vec),
+                ("spr", lambda i: chk(fn["spr"](kind, 0, m, 1e-9, pX, 1, pP)), 2 * tri + vec),
+                ("spr2", lambda i: chk(fn["spr2"](kind, 0, m, 1e-9, pX, 1, pY, 1, pP)), 2 * tri + 2 * vec))
+            for nm, call, nbytes in cases:
+                ms = queued_ms(call, 5, warm=1)
+                gbps = nbytes / (ms * 1e-3) / 1e9
+                shape = f"n={m}" + (f" K={kb}" if nm[1] == "b" else "")
+                emit_row("L2X", f"{tag}{nm} {shape}", gbps, "GB/s", ms, "hbm", gbps, peak_hbm, "GB/s",
+                         f"{peak_kind} HBM copy; bytes = stored elements read (+ written) once")
+            del A, xv, yv, Bd, Bs, Ap
+            torch.cuda.empty_cache()
 
     # level 3 on GEMM (the scope table's next row): n = 4096, FP32 and FP64, left / lower / no transpose
     f = ctypes.c_int, ctypes.c_double, ctypes.c_void_p

@@ -39,6 +39,9 @@ struct DevState {
     size_t l3_n = 0;
     void *l2x = nullptr;                                       // level-2 work vectors / unpacked triangles (grow-only)
     size_t l2x_n = 0;
+    unsigned *sv_flags = nullptr;                              // per-block completion flags of the look-back
+    size_t sv_flags_n = 0;                                     // triangular solve (epoch-stamped, zeroed on growth)
+    unsigned sv_epoch = 0;
     int *sk_count = nullptr;                                   // arrival counters of the stream-K skinny kernel (zeroed;
     size_t sk_count_n = 0;                                     // every launch leaves them at zero)
 };

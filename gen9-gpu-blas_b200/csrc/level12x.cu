@@ -6,15 +6,17 @@
 // an invalid argument, n <= 0 a no-op, beta = 0 never reads y, FP16 computed in FP32 and FP64 in FP64, the row-major
 // band layout A(i, j) = A[i·lda + KL + j − i] (symmetric / triangular: upper KL = 0, KU = K; lower KL = K, KU = 0) and
 // the packed layouts (upper row i starts at i·n − i(i−1)/2, lower row i at i(i+1)/2). B200 design:
-// - level 1: one grid-stride kernel per operation on the strided vectors;
-// - matrix-vector products of every layout: one kernel template, one warp per output row, each lane summing a strided
-//   share of the row's nonzero range through a layout accessor (symmetric layouts read the mirrored element where the
-//   row leaves the stored triangle), a fixed shuffle tree, then alpha·sum + beta·y. In-place products (trmv, tbmv,
+// - level 1: one grid-stride kernel per operation (16-byte vectors when both vectors are contiguous and aligned);
+// - matrix-vector products of dense and packed symmetric / triangular matrices: strips of 64 rows × 2048 columns of
+//   the stored triangle, each read once along its rows, giving row partial sums (the product) and column partial sums
+//   (the mirrored half, or the transposed product), added per output in a fixed order by a second kernel;
+// - banded products: one kernel template, one warp per output row, each lane summing a strided share of the row's
+//   band through a layout accessor, a fixed shuffle tree, then alpha·sum + beta·y. In-place products (trmv, tbmv,
 //   tpmv) write a work vector that is copied back;
-// - rank updates (syr, syr2, spr, spr2): one block per row of the stored triangle;
-// - solves: trsv and tpsv run the blocked TRSM of the level-3 code with one right-hand side (tpsv after expanding the
-//   packed triangle); tbsv, whose band keeps the dense form out of reach for large n, runs one CTA that walks the rows
-//   in dependency order, the threads sharing each row's band dot product.
+// - rank updates (syr, syr2, spr, spr2): one block per row of the stored triangle, four elements per thread in
+//   flight;
+// - solves (trsv, tpsv, tbsv): one cooperative look-back kernel over 64-row blocks in dependency order, FP64 inverses
+//   of the diagonal blocks, per-block flags with bounded waits.
 #include "common.cuh"
 #include "internal.h"
 #include <cmath>
@@ -119,6 +121,134 @@ __global__ void __launch_bounds__(256) l2x_mv(const L2Mat m, typename Compute<T>
     }
 }
 
+// Stored-triangle products (dense or packed; symmetric, or triangular with op = A or Aᵀ), the stored triangle read
+// once in strips: CTA (p, rb) takes the 64 rows of block rb and the columns of piece p (2048 wide) that lie in the
+// stored triangle. Warp w owns rows 8w .. 8w + 7 and walks the strip in 128-column chunks, lane l reading columns
+// l + 32e (e < 4) of its 8 rows (32 loads in flight, 8 KB contiguous per row and CTA). Row part (symmetric;
+// triangular op = A): each lane keeps its 8 rows' sums, reduced over the warp at the end into Prow[p][i]. Column
+// part (symmetric: off-diagonal elements, the mirrored half; triangular op = Aᵀ: every stored element): per chunk the
+// 8 warps' column sums are combined in warp order through shared memory into Pcol[rb][j]. A unit diagonal is read
+// as 1. l2x_tri_final adds the partials of each output in a fixed order.
+constexpr int kTriRows = 64, kTriPiece = 2048;
+
+template <typename T>
+__global__ void __launch_bounds__(256) l2x_tri_strip(const L2Mat m, int use_row, int use_col, const T *__restrict__ x,
+                                                     long long ox, long long ix, typename Compute<T>::R *Prow,
+                                                     typename Compute<T>::R *Pcol) {
+    using R = typename Compute<T>::R;
+    __shared__ R csum[8][128];
+    const int n = m.n, rb = blockIdx.y, pc = blockIdx.x;
+    const int r0 = rb * kTriRows, r1 = min(n, r0 + kTriRows);
+    // stored columns of this row block: lower [0, r1), upper [r0, n); this piece's share of them
+    const int c_lo = max(m.upper ? r0 : 0, pc * kTriPiece), c_hi = min(m.upper ? n : r1, (pc + 1) * kTriPiece);
+    if (c_lo >= c_hi) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool tri = m.kind == l2x::kTriangular;
+    const T *A = (const T *)m.A;
+    const T *rowp[8];
+    R xi[8], racc[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+        const int i = min(r0 + warp * 8 + u, n - 1);
+        long long base;
+        if (m.layout == l2x::kDense) base = (long long)i * m.lda;
+        else base = m.upper ? (long long)i * n - (long long)i * (i - 1) / 2 - i : (long long)i * (i + 1) / 2;
+        rowp[u] = A + base;   // stored element (i, j) at rowp[j]
+        xi[u] = to_r(x[ox + (long long)i * ix]);
+        racc[u] = 0;
+    }
+    for (int c0 = c_lo; c0 < c_hi; c0 += 128) {
+        R cacc[4] = {0, 0, 0, 0}, xc[4];
+        R a[8][4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int j = c0 + lane + 32 * e;
+            xc[e] = j < c_hi ? to_r(x[ox + (long long)j * ix]) : R(0);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int i = r0 + warp * 8 + u;
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int j = c0 + lane + 32 * e;
+                const bool st = i < r1 && j < c_hi && (m.upper ? j >= i : j <= i);
+                R v = st ? to_r(rowp[u][j]) : R(0);
+                if (tri && m.unit && i == j) v = R(1);
+                a[u][e] = v;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int i = r0 + warp * 8 + u;
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                racc[u] = fma_r(a[u][e], xc[e], racc[u]);
+                const int j = c0 + lane + 32 * e;
+                cacc[e] = fma_r((!tri && j == i) ? R(0) : a[u][e], xi[u], cacc[e]);
+            }
+        }
+        if (use_col) {
+#pragma unroll
+            for (int e = 0; e < 4; e++) csum[warp][lane + 32 * e] = cacc[e];
+            __syncthreads();
+            if (threadIdx.x < 128) {
+                const int j = c0 + threadIdx.x;
+                R sum = csum[0][threadIdx.x];
+#pragma unroll
+                for (int w = 1; w < 8; w++) sum += csum[w][threadIdx.x];
+                if (j < c_hi) Pcol[(long long)rb * n + j] = sum;
+            }
+            __syncthreads();
+        }
+    }
+    if (!use_row) return;
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+        R sum = racc[u];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        const int i = r0 + warp * 8 + u;
+        if (lane == 0 && i < r1) Prow[(long long)pc * n + i] = sum;
+    }
+}
+
+// y_k = alpha·(row partials of k + column partials of k) + beta·y_k (beta = 0: y not read). Row partials: the pieces
+// of k's row block that hold stored columns; column partials: the row blocks whose stored rows reach column k. A
+// block takes 32 consecutive outputs (lane = output, coalesced reads); warp w sums every 8th partial of its range and
+// the 8 warp sums are added in warp order (fixed order, deterministic).
+template <typename T>
+__global__ void __launch_bounds__(256) l2x_tri_final(const L2Mat m, int use_row, int use_col,
+                                                     const typename Compute<T>::R *__restrict__ Prow,
+                                                     const typename Compute<T>::R *__restrict__ Pcol,
+                                                     typename Compute<T>::R alpha, typename Compute<T>::R beta, T *y,
+                                                     long long oy, long long iy) {
+    using R = typename Compute<T>::R;
+    __shared__ R part[8][32];
+    const int n = m.n, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int k = blockIdx.x * 32 + lane;
+    const int kk = k < n ? k : n - 1;
+    const int rb = kk / kTriRows, nrb = (n + kTriRows - 1) / kTriRows;
+    const int r0 = rb * kTriRows, r1 = min(n, r0 + kTriRows);
+    R sum = 0;
+    if (use_row) {   // pieces p with [p·2048, (p+1)·2048) meeting this row block's stored columns
+        const int p_lo = m.upper ? r0 / kTriPiece : 0, p_hi = m.upper ? (n - 1) / kTriPiece : (r1 - 1) / kTriPiece;
+        for (int p = p_lo + warp; p <= p_hi; p += 8) sum += Prow[(long long)p * n + kk];
+    }
+    if (use_col) {   // row blocks whose stored rows include column kk: lower rows >= kk, upper rows <= kk
+        const int b_lo = m.upper ? 0 : rb, b_hi = m.upper ? rb : nrb - 1;
+        for (int b = b_lo + warp; b <= b_hi; b += 8) sum += Pcol[(long long)b * n + kk];
+    }
+    part[warp][lane] = sum;
+    __syncthreads();
+    if (warp == 0 && k < n) {
+        R tot = part[0][lane];
+#pragma unroll
+        for (int w = 1; w < 8; w++) tot += part[w][lane];
+        T &yk = y[oy + (long long)k * iy];
+        yk = from_r<T>(beta == R(0) ? alpha * tot : fma_r(beta, to_r(yk), alpha * tot));
+    }
+}
+
 // Stored triangle update: A(i, j) += alpha·(x_i·y_j + y_i·x_j) (two = 1) or alpha·x_i·x_j, one block per row.
 template <typename T>
 __global__ void l2x_rank(const L2Mat m, typename Compute<T>::R alpha, const T *__restrict__ x, long long ox,
@@ -129,54 +259,183 @@ __global__ void l2x_rank(const L2Mat m, typename Compute<T>::R alpha, const T *_
     const R xi = to_r(x[ox + (long long)i * ix]);
     const R yi = two ? to_r(y[oy + (long long)i * iy]) : R(0);
     const int j0 = m.upper ? i : 0, j1 = m.upper ? m.n : i + 1;
-    for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) {
-        const R xj = to_r(x[ox + (long long)j * ix]);
-        R d = xi * xj;
-        if (two) d = fma_r(xi, to_r(y[oy + (long long)j * iy]), yi * xj);
-        T *a = m.layout == l2x::kDense ? A + (long long)i * m.lda + j : A + packed_index(m, i, j);
-        *a = from_r<T>(fma_r(alpha, d, to_r(*a)));
+    // the stored row is contiguous in both layouts; four elements per thread in flight
+    T *row = m.layout == l2x::kDense ? A + (long long)i * m.lda : A + packed_index(m, i, j0) - j0;
+    const int step = blockDim.x;
+    for (int jb = j0 + threadIdx.x; jb < j1; jb += 4 * step) {
+        R av[4], d[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int j = jb + u * step;
+            av[u] = j < j1 ? to_r(row[j]) : R(0);
+            const R xj = j < j1 ? to_r(x[ox + (long long)j * ix]) : R(0);
+            d[u] = xi * xj;
+            if (two) d[u] = fma_r(xi, j < j1 ? to_r(y[oy + (long long)j * iy]) : R(0), yi * xj);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int j = jb + u * step;
+            if (j < j1) row[j] = from_r<T>(fma_r(alpha, d[u], av[u]));
+        }
     }
 }
 
-// Banded triangular solve op(A)·z = b in place (x holds b), rows in dependency order, one CTA.
+// ---------------------------------------------------------------- triangular solves (trsv, tpsv, tbsv)
+// One cooperative kernel over blocks of 64 rows of op(A) in dependency order (op(A) upper: the rows are taken in
+// reversed order, which makes it lower). Every CTA owns blocks b = blockIdx.x, + gridDim.x, ...; for a block it
+// (1) inverts the diagonal block in FP64 in shared memory (independent of x, so it overlaps the earlier blocks),
+// (2) accumulates op(A)[block b][block c]·x_c over the earlier blocks c in order (band: only the blocks the band
+// reaches), streaming the next tile into registers while it waits for block c's flag and multiplies the current one,
+// (3) writes x_b = inv·(b_b − acc) in place and publishes its flag (release). The flags carry a per-launch epoch, so
+// they are never reset. All CTAs are co-resident (cooperative launch sized by the occupancy), and every wait is
+// bounded: a wait that gives up sets the device error word and the CTA returns; the others then give up as well.
+constexpr int kSvNb = 64;
+
+__device__ __forceinline__ unsigned sv_ld_acquire(const unsigned *a) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ void sv_st_release(unsigned *a, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long sv_timer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+struct SvArgs {
+    L2Mat m;            // triangular, dense / band / packed
+    int rev;            // op(A) upper: reversed index order
+    void *x;
+    long long ox, ix;
+    unsigned *flags;
+    unsigned epoch;
+    unsigned *err;
+    int nb, back;       // blocks; band: earlier blocks a block depends on (0: all)
+    unsigned long long limit_ns;
+};
+
 template <typename T>
-__global__ void __launch_bounds__(256) l2x_tbsv(const L2Mat m, T *x, long long ox, long long ix) {
+__device__ __forceinline__ typename Compute<T>::R sv_at(const SvArgs &a, int fr, int fc) {   // op(A), forward indices
+    const int n = a.m.n;
+    return elem<T>(a.m, a.rev ? n - 1 - fr : fr, a.rev ? n - 1 - fc : fc);
+}
+
+// Dynamic shared memory: inverse (FP64) | tile | x block | right-hand side | flag word.
+template <typename T> constexpr size_t sv_smem_bytes() {
+    return sizeof(double) * kSvNb * (kSvNb + 1) + sizeof(typename Compute<T>::R) * (kSvNb * (kSvNb + 1) + kSvNb) +
+           sizeof(double) * kSvNb + 16;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) l2x_trsv_lb(const SvArgs a) {
     using R = typename Compute<T>::R;
-    __shared__ R part[8];
-    const bool forward = !(m.upper != (m.trans != 0));   // op(A) lower: rows 0, 1, ...
-    const int n = m.rows, k = m.KL + m.KU;
-    for (int s = 0; s < n; s++) {
-        const int i = forward ? s : n - 1 - s;
-        const int j0 = forward ? max(0, i - k) : i + 1, j1 = forward ? i : min(n, i + k + 1);
-        R acc = 0;
-        for (int j = j0 + (int)threadIdx.x; j < j1; j += blockDim.x)
-            acc = fma_r(elem<T>(m, i, j), to_r(x[ox + (long long)j * ix]), acc);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+    extern __shared__ __align__(16) unsigned char sv_smem[];
+    auto inv = reinterpret_cast<double (*)[kSvNb + 1]>(sv_smem);
+    auto tile = reinterpret_cast<R (*)[kSvNb + 1]>(sv_smem + sizeof(double) * kSvNb * (kSvNb + 1));
+    R *xs = &tile[kSvNb][0];
+    double *rhs = reinterpret_cast<double *>(xs + kSvNb + (sizeof(R) == 4 && kSvNb % 2 ? 1 : 0));
+    int &go = *reinterpret_cast<int *>(rhs + kSvNb);
+    T *x = (T *)a.x;
+    const int n = a.m.n, tid = threadIdx.x, r = tid >> 2, q = tid & 3;
+    const bool tr = a.m.trans != 0;   // op(A)(i, j) = A(j, i): A's rows run along the tile's column index
+    auto xi = [&](int f) { return a.ox + (long long)(a.rev ? n - 1 - f : f) * a.ix; };
+    // element e of a 64 × 64 tile for this thread: consecutive threads follow A's contiguous direction
+    auto tij = [&](int e, int &i, int &j) {
+        if (tr) { j = e / kSvNb; i = e % kSvNb; } else { i = e / kSvNb; j = e % kSvNb; }
+    };
+    for (int b = blockIdx.x; b < a.nb; b += gridDim.x) {
+        const int f0 = b * kSvNb, rows = min(kSvNb, n - f0);
         __syncthreads();
-        if (threadIdx.x == 0) {
-            R t = 0;
-            for (int q = 0; q < (int)(blockDim.x >> 5); q++) t += part[q];
-            T &xi = x[ox + (long long)i * ix];
-            const R v = to_r(xi) - t;
-            xi = from_r<T>(m.unit ? v : v / elem<T>(m, i, i));
+        // (1) diagonal block (identity past the last row), inverse column c by the 4 lanes of row-group c
+        for (int e = tid; e < kSvNb * kSvNb; e += 256) {
+            int i, j;
+            tij(e, i, j);
+            R v = i == j ? R(1) : R(0);
+            if (i < rows && j < rows && j <= i) v = sv_at<T>(a, f0 + i, f0 + j);
+            tile[i][j] = v;
+        }
+        if (tid < kSvNb) rhs[tid] = tid < rows ? (double)to_r(x[xi(f0 + tid)]) : 0.0;
+        __syncthreads();
+        {
+            const int c = r;
+            for (int i = 0; i < kSvNb; i++) {
+                double s = 0.0;
+                for (int k = c + q; k < i; k += 4) s += (double)tile[i][k] * inv[k][c];
+                s += __shfl_xor_sync(0xffffffffu, s, 1);
+                s += __shfl_xor_sync(0xffffffffu, s, 2);
+                if (q == 0) inv[i][c] = i < c ? 0.0 : ((i == c ? 1.0 : 0.0) - s) / (double)tile[i][i];
+                __syncwarp();
+            }
+        }
+        // (2) earlier blocks
+        R acc = 0;
+        const int c_lo = a.back ? max(0, b - a.back) : 0;
+        R pre[kSvNb * kSvNb / 256];
+        auto fetch = [&](int c) {
+#pragma unroll
+            for (int u = 0; u < kSvNb * kSvNb / 256; u++) {
+                int i, j;
+                tij(tid + 256 * u, i, j);
+                pre[u] = i < rows ? sv_at<T>(a, f0 + i, c * kSvNb + j) : R(0);
+            }
+        };
+        if (c_lo < b) fetch(c_lo);
+        for (int c = c_lo; c < b; c++) {
+            __syncthreads();   // the previous tile and x block are consumed (and the inverse is complete)
+#pragma unroll
+            for (int u = 0; u < kSvNb * kSvNb / 256; u++) {
+                int i, j;
+                tij(tid + 256 * u, i, j);
+                tile[i][j] = pre[u];
+            }
+            if (c + 1 < b) fetch(c + 1);
+            if (tid == 0) {
+                const unsigned *f = a.flags + c;
+                int ok = 1;
+                if (sv_ld_acquire(f) != a.epoch) {
+                    const unsigned long long t0 = sv_timer();
+                    for (unsigned it = 0; sv_ld_acquire(f) != a.epoch; ++it)
+                        if ((it & 63) == 63 && sv_timer() - t0 > a.limit_ns) {
+                            ok = 0;
+                            break;
+                        }
+                }
+                go = ok;
+            }
+            __syncthreads();
+            if (!go) {
+                if (tid == 0) *(volatile unsigned *)a.err = kDevErrWaitTimeout;
+                return;
+            }
+            if (tid < kSvNb) xs[tid] = to_r(__ldcg(x + xi(c * kSvNb + tid)));
+            __syncthreads();
+            R s = 0;
+#pragma unroll
+            for (int j = q; j < kSvNb; j += 4) s = fma_r(tile[r][j], xs[j], s);
+            acc += s;
+        }
+        // (3) x_b = inv·(b_b − acc), FP64, 4 lanes per row; then the flag
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+        __syncthreads();
+        if (q == 0) rhs[r] -= (double)acc;
+        __syncthreads();
+        double v = 0.0;
+        for (int k = q; k <= r; k += 4) v += inv[r][k] * rhs[k];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        if (q == 0 && r < rows) {
+            x[xi(f0 + r)] = from_r<T>((R)v);
+            __threadfence();
         }
         __syncthreads();
-    }
-}
-
-// Dense n×n matrix (pitch n) of a packed triangle, zeros outside it.
-template <typename T>
-__global__ void l2x_unpack(const T *__restrict__ Ap, int n, int upper, T *D) {
-    const long long total = (long long)n * n;
-    L2Mat m{};
-    m.n = n;
-    m.upper = upper;
-    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total; e += (long long)gridDim.x * blockDim.x) {
-        const int i = (int)(e / n), j = (int)(e % n);
-        const bool in = upper ? j >= i : j <= i;
-        D[e] = in ? Ap[packed_index(m, i, j)] : from_r<T>(0);
+        if (tid == 0) {
+            __threadfence();
+            sv_st_release(a.flags + b, a.epoch);
+        }
     }
 }
 
@@ -206,6 +465,53 @@ __global__ void l1x(int mode, int n, T *x, long long ox, long long ix, T *y, lon
     }
 }
 
+// The same on contiguous vectors (increments both 1 or both -1: element pairs share their memory index, so the raw
+// regions [x, x + n) and [y, y + n) are processed), 16-byte aligned: 16-byte loads and stores.
+template <typename T>
+__global__ void __launch_bounds__(256) l1x_vec(int mode, long long n, T *x, T *y, double a,
+                                               double h11, double h12, double h21, double h22) {
+    using R = typename Compute<T>::R;
+    constexpr int W = V16<T>::W;
+    const long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x, stride = (long long)gridDim.x * blockDim.x;
+    const long long nv = n / W;
+    for (long long v = tid; v < nv; v += stride) {
+        T *px = x + v * W, *py = y + v * W;
+        if (mode == 0) {
+            *reinterpret_cast<uint4 *>(py) = *reinterpret_cast<const uint4 *>(px);
+        } else if (mode == 2) {
+            const uint4 tx = *reinterpret_cast<const uint4 *>(px), ty = *reinterpret_cast<const uint4 *>(py);
+            *reinterpret_cast<uint4 *>(px) = ty;
+            *reinterpret_cast<uint4 *>(py) = tx;
+        } else if (mode == 1) {
+            R xv[W];
+            load16_rw<T>(px, xv);
+#pragma unroll
+            for (int k = 0; k < W; k++) xv[k] = (R)a * xv[k];
+            store16<T>(px, xv);
+        } else {
+            R xv[W], yv[W], ox[W];
+            load16_rw<T>(px, xv);
+            load16_rw<T>(py, yv);
+#pragma unroll
+            for (int k = 0; k < W; k++) {
+                ox[k] = fma_r((R)h11, xv[k], (R)h12 * yv[k]);
+                yv[k] = fma_r((R)h21, xv[k], (R)h22 * yv[k]);
+            }
+            store16<T>(px, ox);
+            store16<T>(py, yv);
+        }
+    }
+    for (long long e = nv * W + tid; e < n; e += stride) {   // tail
+        T *px = x + e, *py = y + e;
+        if (mode == 1) { *px = from_r<T>((R)a * to_r(*px)); continue; }
+        if (mode == 0) { *py = *px; continue; }
+        if (mode == 2) { const T t = *px; *px = *py; *py = t; continue; }
+        const R vx = to_r(*px), vy = to_r(*py);
+        *px = from_r<T>(fma_r((R)h11, vx, (R)h12 * vy));
+        *py = from_r<T>(fma_r((R)h21, vx, (R)h22 * vy));
+    }
+}
+
 static int l2x_grid(long long n) {
     DevState *d = dev_state();
     long long g = (n + 255) / 256, cap = (long long)(d ? d->sm_count : 148) * 16;
@@ -232,9 +538,27 @@ static int l2x_buffer(size_t bytes, void **p) {
 }
 
 template <typename T>
+static int tri_mv_t(const L2Mat &m, double alpha, const void *x, long long ox, long long ix, double beta, void *y,
+                    long long oy, long long iy, cudaStream_t st) {
+    using R = typename Compute<T>::R;
+    const int nrb = (m.n + kTriRows - 1) / kTriRows, np = (m.n + kTriPiece - 1) / kTriPiece;
+    const int use_row = m.kind == l2x::kSymmetric || !m.trans, use_col = m.kind == l2x::kSymmetric || m.trans;
+    void *p = nullptr;
+    G9_TRY(scratch((size_t)(np + nrb) * m.n * sizeof(R), &p));
+    R *Prow = (R *)p, *Pcol = Prow + (size_t)np * m.n;
+    l2x_tri_strip<T><<<dim3(np, nrb), 256, 0, st>>>(m, use_row, use_col, (const T *)x, ox, ix, Prow, Pcol);
+    G9_TRY(launched("l2x_tri_strip"));
+    l2x_tri_final<T><<<(m.n + 31) / 32, 256, 0, st>>>(m, use_row, use_col, Prow, Pcol, (R)alpha, (R)beta, (T *)y, oy,
+                                                      iy);
+    return launched("l2x_tri_final");
+}
+
+template <typename T>
 static int mv_t(const L2Mat &m, double alpha, const void *x, long long ox, long long ix, double beta, void *y,
                 long long oy, long long iy, cudaStream_t st) {
     using R = typename Compute<T>::R;
+    if (m.layout != l2x::kBand && m.kind != l2x::kGeneral && m.n <= 65535 * kTriRows)
+        return tri_mv_t<T>(m, alpha, x, ox, ix, beta, y, oy, iy, st);
     const long long threads = (long long)m.rows * 32;
     l2x_mv<T><<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(m, (R)alpha, (const T *)x, ox, ix, (R)beta, (T *)y, oy, iy);
     return launched("l2x_mv");
@@ -250,16 +574,48 @@ static int mv_inplace_t(const L2Mat &m, void *x, long long ox, long long ix, cud
     return launched("l1x_copy");
 }
 
-// Dense triangular solve with one right-hand side through the level-3 TRSM (contiguous copy of x in and out).
+// op(A)·z = x in place through the look-back kernel (any layout; band: back = the blocks the band reaches).
 template <typename T>
-static int trsv_dense_t(int type, int upper, int trans, int unit, int n, const void *A, int lda, void *x, long long ox,
-                        long long ix, void *work, cudaStream_t st) {
-    T *b = (T *)work;
-    l1x<T><<<l2x_grid(n), 256, 0, st>>>(0, n, (T *)x, ox, ix, b, 0, 1, 0, 0, 0, 0, 0);
-    G9_TRY(launched("l1x_copy"));
-    G9_TRY(launch_trsm_dev(type, 1, upper, trans, unit, n, 1, 1.0, A, lda, b, 1, st));
-    l1x<T><<<l2x_grid(n), 256, 0, st>>>(0, n, b, 0, 1, (T *)x, ox, ix, 0, 0, 0, 0, 0);
-    return launched("l1x_copy");
+static int trsv_lb_t(const L2Mat &m, void *x, long long ox, long long ix, cudaStream_t st) {
+    DevState *d = dev_state();
+    if (!d) return G.status;
+    SvArgs a;
+    a.m = m;
+    a.rev = (m.upper != 0) != (m.trans != 0);   // op(A) upper
+    a.x = x;
+    a.ox = ox;
+    a.ix = ix;
+    a.nb = (m.n + kSvNb - 1) / kSvNb;
+    a.back = m.layout == l2x::kBand ? (m.KL + m.KU + kSvNb - 1) / kSvNb : 0;
+    a.err = d->err_dev;
+    a.limit_ns = 1000000000ull;
+    if (d->sv_flags_n < (size_t)a.nb) {
+        if (d->sv_flags) {
+            G9_CU(cudaStreamSynchronize(st));
+            G9_CU(cudaFree(d->sv_flags));
+            d->sv_flags = nullptr;
+        }
+        const size_t want = ((size_t)a.nb + 1023) & ~(size_t)1023;
+        G9_CU(cudaMalloc((void **)&d->sv_flags, want * sizeof(unsigned)));
+        G9_CU(cudaMemsetAsync(d->sv_flags, 0, want * sizeof(unsigned), st));
+        d->sv_flags_n = want;
+    }
+    if (++d->sv_epoch == 0) d->sv_epoch = 1;
+    a.flags = d->sv_flags;
+    a.epoch = d->sv_epoch;
+    static int per_sm[3] = {0, 0, 0};
+    const int slot = sizeof(T) == 8 ? 2 : sizeof(T) == 4 ? 1 : 0;
+    constexpr size_t smem = sv_smem_bytes<T>();
+    if (!per_sm[slot]) {
+        G9_CU(cudaFuncSetAttribute(l2x_trsv_lb<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        G9_CU(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm[slot], l2x_trsv_lb<T>, 256, smem));
+    }
+    int grid = per_sm[slot] * d->sm_count;
+    if (grid > a.nb) grid = a.nb;
+    if (grid < 1) return fail(GEN9BLAS_ERR, "triangular solve kernel does not fit on an SM");
+    void *args[] = {&a};
+    G9_CU(cudaLaunchCooperativeKernel((const void *)l2x_trsv_lb<T>, dim3(grid), dim3(256), args, smem, st));
+    return launched("l2x_trsv_lb");
 }
 
 }  // namespace g9
@@ -309,12 +665,18 @@ int l1x_call(int mode, int type, int n, void *x, int incx, void *y, int incy, do
     timer_kernel();
     const long long ox = vec_off(n, incx), oy = two ? vec_off(n, incy) : 0;
     cudaStream_t st = stream();
-#define G9_L1X(TT)                                                                                                  \
-    l1x<TT><<<l2x_grid(n), 256, 0, st>>>(mode, n, (TT *)op[0].dptr, ox, incx, two ? (TT *)op[1].dptr : nullptr, oy, \
-                                         incy, a, h11, h12, h21, h22)
-    if (type == GEN9BLAS_S) G9_L1X(float);
-    else if (type == GEN9BLAS_D) G9_L1X(double);
-    else G9_L1X(__half);
+    const bool contiguous = (incx == 1 || incx == -1) && (!two || incy == incx) &&
+                            (((uintptr_t)op[0].dptr | (two ? (uintptr_t)op[1].dptr : 0)) & 15) == 0;
+#define G9_L1X(TT)                                                                                                   \
+    if (contiguous)                                                                                                  \
+        l1x_vec<TT><<<l2x_grid((n + V16<TT>::W - 1) / V16<TT>::W), 256, 0, st>>>(                                    \
+            mode, n, (TT *)op[0].dptr, two ? (TT *)op[1].dptr : (TT *)op[0].dptr, a, h11, h12, h21, h22);             \
+    else                                                                                                             \
+        l1x<TT><<<l2x_grid(n), 256, 0, st>>>(mode, n, (TT *)op[0].dptr, ox, incx, two ? (TT *)op[1].dptr : nullptr,  \
+                                             oy, incy, a, h11, h12, h21, h22)
+    if (type == GEN9BLAS_S) { G9_L1X(float); }
+    else if (type == GEN9BLAS_D) { G9_L1X(double); }
+    else { G9_L1X(__half); }
 #undef G9_L1X
     G9_TRY(launched("l1x"));
     G.last_zc = op[0].zc | (two ? op[1].zc << 1 : 0);
@@ -350,6 +712,21 @@ int mv_inplace_call(int type, int es, L2Mat m, size_t abytes, void *x, int incx)
     timer_kernel();
     m.A = op[0].dptr;
     G9_TRY(L2X_DISPATCH(mv_inplace_t, m, op[1].dptr, vec_off(m.rows, incx), incx, stream()));
+    G.last_zc = op[0].zc | op[1].zc << 1;
+    int r = finish_op(op, 2);
+    timer_stop();
+    return r;
+}
+
+// op(A)·z = x in place (trsv, tpsv, tbsv).
+int solve_call(int type, int es, L2Mat m, size_t abytes, void *x, int incx) {
+    timer_start();
+    Operand op[2];
+    G9_TRY(map_operand(op[0], m.A, abytes, 0, true, false));
+    G9_TRY(map_operand(op[1], x, vec_span(m.n, incx) * es, 1, true, true));
+    timer_kernel();
+    m.A = op[0].dptr;
+    G9_TRY(L2X_DISPATCH(trsv_lb_t, m, op[1].dptr, vec_off(m.n, incx), incx, stream()));
     G.last_zc = op[0].zc | op[1].zc << 1;
     int r = finish_op(op, 2);
     timer_stop();
@@ -540,19 +917,9 @@ GEN9BLAS_API int gen9blas_trmv(int type, int uplo, int trans, int diag, int n, c
 GEN9BLAS_API int gen9blas_trsv(int type, int uplo, int trans, int diag, int n, const void *A, int lda, void *x, int incx) {
     L2X_BEGIN(n, !incx);
     if (lda < n) return fail(GEN9BLAS_ERR_INVALID_ARG, "lda < n");
-    timer_start();
-    Operand op[2];
-    G9_TRY(map_operand(op[0], A, dense_bytes(n, n, lda, es), 0, true, false));
-    G9_TRY(map_operand(op[1], x, vec_span(n, incx) * es, 1, true, true));
-    void *work = nullptr;
-    G9_TRY(l2x_buffer((size_t)n * es, &work));
-    timer_kernel();
-    G9_TRY(L2X_DISPATCH(trsv_dense_t, type, uplo == GEN9BLAS_UPPER, trans ? 1 : 0, diag == GEN9BLAS_UNIT, n, op[0].dptr,
-                        lda, op[1].dptr, vec_off(n, incx), incx, work, stream()));
-    G.last_zc = op[0].zc | op[1].zc << 1;
-    int r = finish_op(op, 2);
-    timer_stop();
-    return r;
+    const L2Mat m = mat(A, lda, l2x::kDense, l2x::kTriangular, n, n, uplo == GEN9BLAS_UPPER, trans ? 1 : 0,
+                        diag == GEN9BLAS_UNIT, 0, 0, n);
+    return solve_call(type, es, m, dense_bytes(n, n, lda, es), x, incx);
 }
 
 GEN9BLAS_API int gen9blas_syr(int type, int uplo, int n, double alpha, const void *x, int incx, void *A, int lda) {
@@ -604,24 +971,9 @@ GEN9BLAS_API int gen9blas_tbsv(int type, int uplo, int trans, int diag, int N, i
     L2X_BEGIN(N, !incx);
     if (K < 0 || lda < K + 1) return fail(GEN9BLAS_ERR_INVALID_ARG, "tbsv: K or lda");
     const int up = uplo == GEN9BLAS_UPPER;
-    L2Mat m = mat(A, lda, l2x::kBand, l2x::kTriangular, N, N, up, trans ? 1 : 0, diag == GEN9BLAS_UNIT, up ? 0 : K,
-                  up ? K : 0, N);
-    timer_start();
-    Operand op[2];
-    G9_TRY(map_operand(op[0], A, dense_bytes(N, K + 1, lda, es), 0, true, false));
-    G9_TRY(map_operand(op[1], x, vec_span(N, incx) * es, 1, true, true));
-    timer_kernel();
-    m.A = op[0].dptr;
-    const long long ox = vec_off(N, incx);
-    cudaStream_t st = stream();
-    if (type == GEN9BLAS_S) l2x_tbsv<float><<<1, 256, 0, st>>>(m, (float *)op[1].dptr, ox, incx);
-    else if (type == GEN9BLAS_D) l2x_tbsv<double><<<1, 256, 0, st>>>(m, (double *)op[1].dptr, ox, incx);
-    else l2x_tbsv<__half><<<1, 256, 0, st>>>(m, (__half *)op[1].dptr, ox, incx);
-    G9_TRY(launched("l2x_tbsv"));
-    G.last_zc = op[0].zc | op[1].zc << 1;
-    int r = finish_op(op, 2);
-    timer_stop();
-    return r;
+    const L2Mat m = mat(A, lda, l2x::kBand, l2x::kTriangular, N, N, up, trans ? 1 : 0, diag == GEN9BLAS_UNIT,
+                        up ? 0 : K, up ? K : 0, N);
+    return solve_call(type, es, m, dense_bytes(N, K + 1, lda, es), x, incx);
 }
 
 // ---------------------------------------------------------------- packed
@@ -641,32 +993,9 @@ GEN9BLAS_API int gen9blas_tpmv(int type, int uplo, int trans, int diag, int N, c
 
 GEN9BLAS_API int gen9blas_tpsv(int type, int uplo, int trans, int diag, int N, const void *Ap, void *x, int incx) {
     L2X_BEGIN(N, !incx);
-    timer_start();
-    Operand op[2];
-    G9_TRY(map_operand(op[0], Ap, packed_bytes(N, es), 0, true, false));
-    G9_TRY(map_operand(op[1], x, vec_span(N, incx) * es, 1, true, true));
-    void *work = nullptr;   // [dense triangle N×N | contiguous right-hand side]
-    const size_t dbytes = ((size_t)N * N * es + 255) / 256 * 256;
-    G9_TRY(l2x_buffer(dbytes + (size_t)N * es, &work));
-    timer_kernel();
-    cudaStream_t st = stream();
-    const int up = uplo == GEN9BLAS_UPPER;
-    void *rhs = (char *)work + dbytes;
-#define G9_TPSV(TT)                                                                                                   \
-    do {                                                                                                              \
-        l2x_unpack<TT><<<l2x_grid((long long)N * N), 256, 0, st>>>((const TT *)op[0].dptr, N, up, (TT *)work);        \
-        G9_TRY(launched("l2x_unpack"));                                                                                \
-        G9_TRY(trsv_dense_t<TT>(type, up, trans ? 1 : 0, diag == GEN9BLAS_UNIT, N, work, N, op[1].dptr,               \
-                                vec_off(N, incx), incx, rhs, st));                                                    \
-    } while (0)
-    if (type == GEN9BLAS_S) G9_TPSV(float);
-    else if (type == GEN9BLAS_D) G9_TPSV(double);
-    else G9_TPSV(__half);
-#undef G9_TPSV
-    G.last_zc = op[0].zc | op[1].zc << 1;
-    int r = finish_op(op, 2);
-    timer_stop();
-    return r;
+    const L2Mat m = mat(Ap, 0, l2x::kPacked, l2x::kTriangular, N, N, uplo == GEN9BLAS_UPPER, trans ? 1 : 0,
+                        diag == GEN9BLAS_UNIT, 0, 0, N);
+    return solve_call(type, es, m, packed_bytes(N, es), x, incx);
 }
 
 GEN9BLAS_API int gen9blas_spr(int type, int uplo, int N, double alpha, const void *x, int incx, void *Ap) {

@@ -215,3 +215,64 @@ def test_packed(g9, dt, tol, n):
         ref = D + 0.5 * (o + o.T)
         got = packed_dense(f64(W), n, up)
         assert emax(got[m], ref[m], (np.abs(D) + 0.5 * (np.abs(o) + np.abs(o.T)))[m], dt) <= tol
+
+
+@pytest.mark.parametrize("dt", [np.float32, np.float64])
+def test_solves_and_products_large_strided(g9, dt):
+    """Sizes spanning many 64-row blocks of the look-back solve and many 128×128 tiles of the triangle products, with
+    strided and negative-stride vectors: trsv (n = 2000), tpsv (n = 1500), tbsv (n = 3000, K = 150: three blocks
+    back), symv / trmv / spmv on the same triangles."""
+    rng = np.random.default_rng(9)
+    tol = SOLVE_TOL[dt]
+    for n, step in ((2000, 2), (1300, -3)):
+        buf = rnd(rng, n * abs(step), dt)
+        for uplo in "LU":
+            up = uplo == "U"
+            A = rnd(rng, (n, n), dt)
+            A[np.diag_indices(n)] = 2.0 * np.sqrt(n)
+            for trans in (False, True):
+                for diag in (False, True):
+                    Ad = (f64(A) / (n if diag else 1)).astype(dt) if diag else A
+                    T = tri(f64(Ad), up, diag)
+                    T = T.T if trans else T
+                    x = buf.copy()[::step]
+                    z = np.linalg.solve(T, f64(x))
+                    W = g9.trsv(Ad, x, uplo, trans, diag)
+                    assert np.abs(f64(W) - z).max() / np.abs(z).max() <= tol, (n, uplo, trans, diag)
+                    x = buf.copy()[::step]
+                    W = g9.trmv(Ad, x, uplo, trans, diag)
+                    assert emax(W, T @ f64(buf[::step]), np.abs(T) @ np.abs(f64(buf[::step]))) <= 1e-5
+            S = sym_of(f64(A), up)
+            y = buf.copy()[::step]
+            W = g9.symv(A, buf[::step], uplo, 0.5, 2.0, y)
+            assert emax(W, 0.5 * S @ f64(buf[::step]) + 2.0 * f64(buf[::step]),
+                        0.5 * np.abs(S) @ np.abs(f64(buf[::step])) + 2.0 * np.abs(f64(buf[::step]))) <= 1e-5
+    n = 1500
+    for uplo in "LU":
+        up = uplo == "U"
+        D = tri(rnd(rng, (n, n), np.float64), up, False)
+        np.fill_diagonal(D, 2.0 * np.sqrt(n))
+        Ap = np.array([D[i, j] for i in range(n) for j in (range(i, n) if up else range(0, i + 1))]).astype(dt)
+        Dq = packed_dense(f64(Ap), n, up)
+        for trans in (False, True):
+            T = Dq.T if trans else Dq
+            x = rnd(rng, 2 * n, dt)[::-2]   # a negative-stride view, solved in place
+            z = np.linalg.solve(T, f64(x))
+            W = g9.tpsv(Ap, x, uplo, trans, False)
+            assert np.abs(f64(W) - z).max() / np.abs(z).max() <= tol, ("tpsv", uplo, trans)
+        S = Dq + Dq.T - np.diag(np.diag(Dq))
+        x = rnd(rng, n, dt)
+        W = g9.spmv(Ap, x, uplo)
+        assert emax(W, S @ f64(x), np.abs(S) @ np.abs(f64(x))) <= 1e-5
+    n, K = 3000, 150
+    for uplo in "LU":
+        up = uplo == "U"
+        Ab = rnd(rng, (n, K + 1), dt)
+        Ab[:, 0 if up else K] = 4.0 * np.sqrt(K)
+        Td0 = band_dense(f64(Ab), n, n, 0 if up else K, K if up else 0)
+        for trans in (False, True):
+            T = Td0.T if trans else Td0
+            x = rnd(rng, 3 * n, dt)[::3]
+            z = np.linalg.solve(T, f64(x))
+            W = g9.tbsv(Ab, x, K, uplo, trans, False)
+            assert np.abs(f64(W) - z).max() / np.abs(z).max() <= tol, ("tbsv", uplo, trans)
