@@ -131,7 +131,29 @@ __global__ void __launch_bounds__(256) l2x_mv(const L2Mat m, typename Compute<T>
 // as 1. l2x_tri_final adds the partials of each output in a fixed order.
 constexpr int kTriRows = 64, kTriPiece = 2048;
 
-template <typename T>
+// Four consecutive elements p[0..3] (VEC: one 16-byte load for FP32, two for FP64, one 8-byte load for FP16; the
+// caller guarantees the alignment).
+template <typename T, bool VEC>
+__device__ __forceinline__ void load4(const T *p, typename Compute<T>::R *v) {
+    if constexpr (VEC && sizeof(T) == 4) {
+        const float4 q = *reinterpret_cast<const float4 *>(p);
+        v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+    } else if constexpr (VEC && sizeof(T) == 8) {
+        const double2 q0 = reinterpret_cast<const double2 *>(p)[0], q1 = reinterpret_cast<const double2 *>(p)[1];
+        v[0] = q0.x; v[1] = q0.y; v[2] = q1.x; v[3] = q1.y;
+    } else if constexpr (VEC && sizeof(T) == 2) {
+        const uint2 q = *reinterpret_cast<const uint2 *>(p);
+        const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&q.x));
+        const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&q.y));
+        v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
+    } else {
+#pragma unroll
+        for (int k = 0; k < 4; k++) v[k] = to_r(p[k]);
+    }
+}
+
+// VEC: dense rows whose element (i, 4k) is 16-byte aligned (8-byte for FP16).
+template <typename T, bool VEC>
 __global__ void __launch_bounds__(256) l2x_tri_strip(const L2Mat m, int use_row, int use_col, const T *__restrict__ x,
                                                      long long ox, long long ix, typename Compute<T>::R *Prow,
                                                      typename Compute<T>::R *Pcol) {
@@ -158,38 +180,58 @@ __global__ void __launch_bounds__(256) l2x_tri_strip(const L2Mat m, int use_row,
         racc[u] = 0;
     }
     for (int c0 = c_lo; c0 < c_hi; c0 += 128) {
-        R cacc[4] = {0, 0, 0, 0}, xc[4];
+        // lane l: columns c0 + 4l .. c0 + 4l + 3
+        const int j0 = c0 + 4 * lane;
+        // interior chunk: every (row of the block, column of the chunk) strictly inside the stored triangle
+        const bool interior = c0 + 128 <= c_hi && (m.upper ? c0 >= r1 : c0 + 128 <= r0);
+        R xc[4], cacc[4] = {0, 0, 0, 0};
         R a[8][4];
+        if (interior) {
+            if (ix == 1) load4<T, false>(x + ox + j0, xc);
+            else {
 #pragma unroll
-        for (int e = 0; e < 4; e++) {
-            const int j = c0 + lane + 32 * e;
-            xc[e] = j < c_hi ? to_r(x[ox + (long long)j * ix]) : R(0);
-        }
-#pragma unroll
-        for (int u = 0; u < 8; u++) {
-            const int i = r0 + warp * 8 + u;
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const int j = c0 + lane + 32 * e;
-                const bool st = i < r1 && j < c_hi && (m.upper ? j >= i : j <= i);
-                R v = st ? to_r(rowp[u][j]) : R(0);
-                if (tri && m.unit && i == j) v = R(1);
-                a[u][e] = v;
+                for (int k = 0; k < 4; k++) xc[k] = to_r(x[ox + (long long)(j0 + k) * ix]);
             }
-        }
 #pragma unroll
-        for (int u = 0; u < 8; u++) {
-            const int i = r0 + warp * 8 + u;
+            for (int u = 0; u < 8; u++) {
+                if (r0 + warp * 8 + u < r1) load4<T, VEC>(rowp[u] + j0, a[u]);
+                else a[u][0] = a[u][1] = a[u][2] = a[u][3] = R(0);
+            }
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
-                racc[u] = fma_r(a[u][e], xc[e], racc[u]);
-                const int j = c0 + lane + 32 * e;
-                cacc[e] = fma_r((!tri && j == i) ? R(0) : a[u][e], xi[u], cacc[e]);
+            for (int u = 0; u < 8; u++)
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    racc[u] = fma_r(a[u][k], xc[k], racc[u]);
+                    cacc[k] = fma_r(a[u][k], xi[u], cacc[k]);
+                }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 4; k++) xc[k] = j0 + k < c_hi ? to_r(x[ox + (long long)(j0 + k) * ix]) : R(0);
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int i = r0 + warp * 8 + u;
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const int j = j0 + k;
+                    const bool st = i < r1 && j < c_hi && (m.upper ? j >= i : j <= i);
+                    R v = st ? to_r(rowp[u][j]) : R(0);
+                    if (tri && m.unit && i == j) v = R(1);
+                    a[u][k] = v;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int i = r0 + warp * 8 + u;
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    racc[u] = fma_r(a[u][k], xc[k], racc[u]);
+                    cacc[k] = fma_r((!tri && j0 + k == i) ? R(0) : a[u][k], xi[u], cacc[k]);
+                }
             }
         }
         if (use_col) {
 #pragma unroll
-            for (int e = 0; e < 4; e++) csum[warp][lane + 32 * e] = cacc[e];
+            for (int k = 0; k < 4; k++) csum[warp][4 * lane + k] = cacc[k];
             __syncthreads();
             if (threadIdx.x < 128) {
                 const int j = c0 + threadIdx.x;
@@ -546,7 +588,10 @@ static int tri_mv_t(const L2Mat &m, double alpha, const void *x, long long ox, l
     void *p = nullptr;
     G9_TRY(scratch((size_t)(np + nrb) * m.n * sizeof(R), &p));
     R *Prow = (R *)p, *Pcol = Prow + (size_t)np * m.n;
-    l2x_tri_strip<T><<<dim3(np, nrb), 256, 0, st>>>(m, use_row, use_col, (const T *)x, ox, ix, Prow, Pcol);
+    const size_t va = sizeof(T) == 2 ? 8 : 16;
+    const bool vec = m.layout == l2x::kDense && ((uintptr_t)m.A % va) == 0 && ((size_t)m.lda * sizeof(T)) % va == 0;
+    if (vec) l2x_tri_strip<T, true><<<dim3(np, nrb), 256, 0, st>>>(m, use_row, use_col, (const T *)x, ox, ix, Prow, Pcol);
+    else l2x_tri_strip<T, false><<<dim3(np, nrb), 256, 0, st>>>(m, use_row, use_col, (const T *)x, ox, ix, Prow, Pcol);
     G9_TRY(launched("l2x_tri_strip"));
     l2x_tri_final<T><<<(m.n + 31) / 32, 256, 0, st>>>(m, use_row, use_col, Prow, Pcol, (R)alpha, (R)beta, (T *)y, oy,
                                                       iy);
