@@ -39,8 +39,8 @@ struct DevState {
     size_t l3_n = 0;
     void *l2x = nullptr;                                       // level-2 work vectors / unpacked triangles (grow-only)
     size_t l2x_n = 0;
-    unsigned *sv_flags = nullptr;                              // per-block completion flags of the look-back
-    size_t sv_flags_n = 0;                                     // triangular solve (epoch-stamped, zeroed on growth)
+    unsigned long long *sv_msg = nullptr;                      // value messages of the look-back triangular solve
+    size_t sv_msg_n = 0;                                       // (epoch-stamped 64-bit words, zeroed on growth)
     unsigned sv_epoch = 0;
     int *sk_count = nullptr;                                   // arrival counters of the stream-K skinny kernel (zeroed;
     size_t sk_count_n = 0;                                     // every launch leaves them at zero)

@@ -327,20 +327,25 @@ __global__ void l2x_rank(const L2Mat m, typename Compute<T>::R alpha, const T *_
 // reversed order, which makes it lower). Every CTA owns blocks b = blockIdx.x, + gridDim.x, ...; for a block it
 // (1) inverts the diagonal block in FP64 in shared memory (independent of x, so it overlaps the earlier blocks),
 // (2) accumulates op(A)[block b][block c]·x_c over the earlier blocks c in order (band: only the blocks the band
-// reaches), streaming the next tile into registers while it waits for block c's flag and multiplies the current one,
-// (3) writes x_b = inv·(b_b − acc) in place and publishes its flag (release). The flags carry a per-launch epoch, so
-// they are never reset. All CTAs are co-resident (cooperative launch sized by the occupancy), and every wait is
-// bounded: a wait that gives up sets the device error word and the CTA returns; the others then give up as well.
+// reaches), streaming the next tile into registers while it waits for x_c and multiplies the current one,
+// (3) writes x_b = inv·(b_b − acc) in place and publishes it. Publication is a message per value: a 64-bit word holding
+// the value's bits (FP32: the whole value; FP64: one half per word) and the launch's epoch, stored with one relaxed
+// 64-bit access, so a reader that sees the epoch sees the value -- one L2 round trip per dependency, no flag and no
+// fence. The epochs make the message buffer reusable without resets. All CTAs are co-resident (cooperative launch
+// sized by the occupancy), and every wait is bounded: a wait that gives up sets the device error word and the CTA
+// returns; the CTAs that wait for it then give up as well.
 constexpr int kSvNb = 64;
 
-__device__ __forceinline__ unsigned sv_ld_acquire(const unsigned *a) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+__device__ __forceinline__ unsigned long long sv_ld_msg(const unsigned long long *a) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
     return v;
 }
-__device__ __forceinline__ void sv_st_release(unsigned *a, unsigned v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+__device__ __forceinline__ void sv_st_msg(unsigned long long *a, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
 }
+// Words per value in the message buffer.
+template <typename R> __host__ __device__ constexpr int sv_words() { return sizeof(R) == 8 ? 2 : 1; }
 __device__ __forceinline__ unsigned long long sv_timer() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -352,7 +357,7 @@ struct SvArgs {
     int rev;            // op(A) upper: reversed index order
     void *x;
     long long ox, ix;
-    unsigned *flags;
+    unsigned long long *msg;   // [block][row][sv_words] messages
     unsigned epoch;
     unsigned *err;
     int nb, back;       // blocks; band: earlier blocks a block depends on (0: all)
@@ -388,6 +393,7 @@ __global__ void __launch_bounds__(256) l2x_trsv_lb(const SvArgs a) {
     auto tij = [&](int e, int &i, int &j) {
         if (tr) { j = e / kSvNb; i = e % kSvNb; } else { i = e / kSvNb; j = e % kSvNb; }
     };
+    if (tid == 0) go = 1;
     for (int b = blockIdx.x; b < a.nb; b += gridDim.x) {
         const int f0 = b * kSvNb, rows = min(kSvNb, n - f0);
         __syncthreads();
@@ -434,26 +440,33 @@ __global__ void __launch_bounds__(256) l2x_trsv_lb(const SvArgs a) {
                 tile[i][j] = pre[u];
             }
             if (c + 1 < b) fetch(c + 1);
-            if (tid == 0) {
-                const unsigned *f = a.flags + c;
-                int ok = 1;
-                if (sv_ld_acquire(f) != a.epoch) {
+            if (tid < kSvNb) {   // x_c[tid]: poll its message word(s) until they carry this launch's epoch
+                const unsigned long long *w = a.msg + ((long long)c * kSvNb + tid) * sv_words<R>();
+                unsigned long long v0 = sv_ld_msg(w), v1 = sv_words<R>() == 2 ? sv_ld_msg(w + 1) : 0ull;
+                auto ready = [&]() {
+                    return (unsigned)(v0 >> 32) == a.epoch && (sv_words<R>() == 1 || (unsigned)(v1 >> 32) == a.epoch);
+                };
+                if (!ready()) {
                     const unsigned long long t0 = sv_timer();
-                    for (unsigned it = 0; sv_ld_acquire(f) != a.epoch; ++it)
+                    for (unsigned it = 0; !ready(); ++it) {
+                        v0 = sv_ld_msg(w);
+                        if (sv_words<R>() == 2) v1 = sv_ld_msg(w + 1);
                         if ((it & 63) == 63 && sv_timer() - t0 > a.limit_ns) {
-                            ok = 0;
+                            go = 0;
                             break;
                         }
+                    }
                 }
-                go = ok;
+                if constexpr (sizeof(R) == 8)
+                    xs[tid] = __longlong_as_double((long long)((v1 << 32) | (v0 & 0xffffffffull)));
+                else
+                    xs[tid] = __uint_as_float((unsigned)v0);
             }
             __syncthreads();
             if (!go) {
                 if (tid == 0) *(volatile unsigned *)a.err = kDevErrWaitTimeout;
                 return;
             }
-            if (tid < kSvNb) xs[tid] = to_r(__ldcg(x + xi(c * kSvNb + tid)));
-            __syncthreads();
             R s = 0;
 #pragma unroll
             for (int j = q; j < kSvNb; j += 4) s = fma_r(tile[r][j], xs[j], s);
@@ -470,13 +483,18 @@ __global__ void __launch_bounds__(256) l2x_trsv_lb(const SvArgs a) {
         v += __shfl_xor_sync(0xffffffffu, v, 1);
         v += __shfl_xor_sync(0xffffffffu, v, 2);
         if (q == 0 && r < rows) {
-            x[xi(f0 + r)] = from_r<T>((R)v);
-            __threadfence();
-        }
-        __syncthreads();
-        if (tid == 0) {
-            __threadfence();
-            sv_st_release(a.flags + b, a.epoch);
+            const T xv = from_r<T>((R)v);
+            x[xi(f0 + r)] = xv;
+            const R pv = to_r(xv);   // the rounded value, as the later blocks would read it from x
+            unsigned long long *w = a.msg + ((long long)b * kSvNb + r) * sv_words<R>();
+            const unsigned long long tag = (unsigned long long)a.epoch << 32;
+            if constexpr (sizeof(R) == 8) {
+                const unsigned long long bits = (unsigned long long)__double_as_longlong(pv);
+                sv_st_msg(w, tag | (bits & 0xffffffffull));
+                sv_st_msg(w + 1, tag | (bits >> 32));
+            } else {
+                sv_st_msg(w, tag | __float_as_uint(pv));
+            }
         }
     }
 }
@@ -634,19 +652,20 @@ static int trsv_lb_t(const L2Mat &m, void *x, long long ox, long long ix, cudaSt
     a.back = m.layout == l2x::kBand ? (m.KL + m.KU + kSvNb - 1) / kSvNb : 0;
     a.err = d->err_dev;
     a.limit_ns = 1000000000ull;
-    if (d->sv_flags_n < (size_t)a.nb) {
-        if (d->sv_flags) {
+    const size_t words = (size_t)a.nb * kSvNb * 2;   // enough for FP64 (two words per value)
+    if (d->sv_msg_n < words) {
+        if (d->sv_msg) {
             G9_CU(cudaStreamSynchronize(st));
-            G9_CU(cudaFree(d->sv_flags));
-            d->sv_flags = nullptr;
+            G9_CU(cudaFree(d->sv_msg));
+            d->sv_msg = nullptr;
         }
-        const size_t want = ((size_t)a.nb + 1023) & ~(size_t)1023;
-        G9_CU(cudaMalloc((void **)&d->sv_flags, want * sizeof(unsigned)));
-        G9_CU(cudaMemsetAsync(d->sv_flags, 0, want * sizeof(unsigned), st));
-        d->sv_flags_n = want;
+        const size_t want = (words + 65535) & ~(size_t)65535;
+        G9_CU(cudaMalloc((void **)&d->sv_msg, want * sizeof(unsigned long long)));
+        G9_CU(cudaMemsetAsync(d->sv_msg, 0, want * sizeof(unsigned long long), st));
+        d->sv_msg_n = want;
     }
     if (++d->sv_epoch == 0) d->sv_epoch = 1;
-    a.flags = d->sv_flags;
+    a.msg = d->sv_msg;
     a.epoch = d->sv_epoch;
     static int per_sm[3] = {0, 0, 0};
     const int slot = sizeof(T) == 8 ? 2 : sizeof(T) == 4 ? 1 : 0;
