@@ -66,7 +66,13 @@ def dist_env():
 
 # --------------------------------------------------------------------------------------------- clocks during the run
 class ClockSampler:
-    """nvidia-smi samples (every 100 ms) of one GPU while the timed region runs."""
+    """Clock samples of one GPU while the timed region runs: NVML queries every millisecond from a thread (read-only:
+    SM clock, its maximum, the active clock-event reasons), so that short timed regions are sampled too; nvidia-smi
+    (100 ms) where NVML is unavailable."""
+
+    # NVML clock-event reason bits (nvml.h: nvmlClocksEventReason*)
+    REASON_BITS = (("sw_power_cap", 0x4), ("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20),
+                   ("hw_thermal_slowdown", 0x40))
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -76,8 +82,46 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.lines = []
+        self.nvml = None
+        self.samples = []
+        self.running = False
+
+    def _nvml_loop(self):
+        nv, h = self.nvml
+        while self.running:
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                     nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                                     if hasattr(nv, "nvmlDeviceGetCurrentClocksEventReasons")
+                                     else nv.nvmlDeviceGetCurrentClocksThrottleReasons(h)))
+            except Exception:
+                pass
+            time.sleep(0.001)
 
     def start(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = None
+            try:   # the CUDA device's PCI address: NVML indices need not follow CUDA_VISIBLE_DEVICES
+                import torch
+                pr = torch.cuda.get_device_properties(self.gpu)
+                bus = "%08X:%02X:%02X.0" % (pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
+                h = nv.nvmlDeviceGetHandleByPciBusId(bus.encode())
+            except Exception:
+                h = None
+            if h is None:
+                vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
+                idx = int(vis[self.gpu]) if self.gpu < len(vis) and vis[self.gpu].strip().isdigit() else self.gpu
+                h = nv.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            self.nvml = (nv, h)
+            self.running = True
+            self.thread = threading.Thread(target=self._nvml_loop, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS,
                                           "--format=csv,noheader,nounits", "-lms", "100"],
@@ -92,6 +136,20 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def stop(self):
+        if self.nvml:
+            self.running = False
+            self.thread.join(timeout=2)
+            nv = self.nvml[0]
+            try:
+                nv.nvmlShutdown()
+            except Exception:
+                pass
+            mx = self.max_mhz
+            sm = [float(c) for c, _ in self.samples]
+            reasons = sorted({nm for _, bits in self.samples for nm, b in self.REASON_BITS if bits & b})
+            loaded = [v for v in sm if v > 0.3 * mx] or sm
+            return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": mx, "reasons": reasons,
+                    "samples": len(sm), "source": "nvml"}
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
