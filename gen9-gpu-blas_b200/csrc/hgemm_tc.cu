@@ -59,6 +59,9 @@ struct TcParams {
     __half *dst[8];
     int ndst;
     long long col_off;
+    // pair kernel, alpha = 1, beta = 0, one destination with a TMA-legal C: the epilogue stages each warp's 32 × 32
+    // FP16 block in shared memory and writes it with one TMA store (tmC)
+    int tma_c;
 };
 
 __device__ __forceinline__ void tile_coords(const TcParams &p, int tile, int &b, int &mb, int &nb) {
@@ -336,7 +339,8 @@ template <int BN> struct PairCfg {
     static constexpr int STAGE_BYTES = T2_A_BYTES + B_BYTES;
     static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;   // 6 (BN 256) or 8 (BN 128)
     static constexpr int NBUF = 512 / BN;                       // TMEM accumulators
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 512;
+    static constexpr int STAGING = 4 * 2 * 2048;                // epilogue: 4 warps × 2 buffers of 32 × 32 FP16
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 512 + STAGING;
 };
 
 __device__ __forceinline__ void tile_coords_pair(const TcParams &p, int tile, int &b, int &mb, int &nb) {
@@ -385,7 +389,8 @@ __device__ __forceinline__ void epilogue_bar() { asm volatile("bar.sync 1, 128;"
 
 template <bool F16ACC, int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
-    hgemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const TcParams p) {
+    hgemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, const TcParams p) {
     using Cfg = PairCfg<BN>;
     constexpr int STAGES = Cfg::STAGES, NBUF = Cfg::NBUF;
     extern __shared__ uint8_t smem_raw[];
@@ -401,6 +406,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     uint64_t *drain = bars + 2 * STAGES + 2 * NBUF;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    uint8_t *staging = smem + STAGES * Cfg::STAGE_BYTES + 512;   // 128-byte aligned
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
@@ -419,6 +425,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
         fence_barrier_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
+        if (p.tma_c) tma_prefetch_desc(&tmC);
     }
     if (warp == 1) {
         tmem_alloc_pair(tmem_slot, TC_TMEM_COLS);
@@ -547,6 +554,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < 8; j++) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
                 }
+                __threadfence();   // each thread's partial stores, at GPU scope, before the flag
                 epilogue_bar();
                 if (threadIdx.x == 64) {
                     __threadfence();
@@ -577,6 +585,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
                     if (F16ACC) tmem_ld_32x32_pack16(t_row + c * 32, r);
                     else tmem_ld_32x32(t_row + c * 32, r);
                     tmem_ld_wait();
+                    if (w.part < 0 && p.tma_c) {
+                        // FP16 block of this warp (32 rows × 32 columns) into its staging buffer, then one TMA store;
+                        // rows and columns past M and N are clipped by the store. The buffer used two chunks ago
+                        // must have been read by its store first.
+                        uint32_t h[16];
+                        if (F16ACC) {
+#pragma unroll
+                            for (int k = 0; k < 16; k++) h[k] = r[k];
+                        } else {
+#pragma unroll
+                            for (int k = 0; k < 16; k++) {
+                                const __half2 v2 = __floats2half2_rn(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
+                                h[k] = *reinterpret_cast<const uint32_t *>(&v2);
+                            }
+                        }
+                        uint8_t *stg = staging + ((q * 2) + (c & 1)) * 2048;
+                        if (lane == 0) bulk_wait_read<1>();
+                        __syncwarp();
+                        uint4 *d4 = reinterpret_cast<uint4 *>(stg + lane * 64);
+#pragma unroll
+                        for (int k = 0; k < 4; k++) d4[k] = make_uint4(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
+                        fence_proxy_async();
+                        __syncwarp();
+                        const int row_w = mb * T2_BM + 128 * rank + q * 32;
+                        if (lane == 0 && row_w < p.M && col0 < p.N) {
+                            tma_store_3d(&tmC, stg, col0, row_w, b);
+                            bulk_commit();
+                        }
+                        continue;
+                    }
                     if (!have || col0 >= p.N || !row_ok) continue;
                     if (w.part < 0) {
                         for (int q = 0; q < p.ndst; q++) store_chunk<F16ACC>(p, r, p.dst[q] + roff, col0, row_ok);
@@ -602,6 +640,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[buf]), 0));
         }
+        if (p.tma_c && lane == 0) bulk_wait<0>();   // this warp's C stores are complete before the CTA ends
     }
     __syncthreads();
     cluster_sync();   // the pair's MMAs (drained by the leader) no longer read either CTA's shared memory
@@ -612,14 +651,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
 }
 
 template <bool F16ACC, int BN>
-static int launch_pair(const CUtensorMap &mA, const CUtensorMap &mB, const TcParams &p, int grid, cudaStream_t st) {
+static int launch_pair(const CUtensorMap &mA, const CUtensorMap &mB, const CUtensorMap &mC, const TcParams &p, int grid,
+                       cudaStream_t st) {
     static bool attr = false;
     if (!attr) {
         G9_CU(cudaFuncSetAttribute(hgemm_tc2_kernel<F16ACC, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    PairCfg<BN>::SMEM));
         attr = true;
     }
-    hgemm_tc2_kernel<F16ACC, BN><<<grid, TC_THREADS, PairCfg<BN>::SMEM, st>>>(mA, mB, p);
+    hgemm_tc2_kernel<F16ACC, BN><<<grid, TC_THREADS, PairCfg<BN>::SMEM, st>>>(mA, mB, mC, p);
     return launched("hgemm_tc2");
 }
 
@@ -649,6 +689,23 @@ static int encode_map(CUtensorMap *m, const void *base, long long inner, long lo
     if (r != CUDA_SUCCESS)
         return fail(GEN9BLAS_ERR, "cuTensorMapEncodeTiled failed (%d): inner %lld outer %lld ld %lld count %lld", (int)r,
                     inner, outer, ld, count);
+    return 0;
+}
+
+// C as a TMA store target: FP16, {N, M, count} with row pitch ldc and batch stride sC (elements), 32 × 32 boxes, no
+// swizzle (the epilogue stages plain 64-byte rows).
+static int encode_c_map(CUtensorMap *m, void *base, long long N, long long M, long long ldc, long long count,
+                        long long sC) {
+    auto enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(tensor_map_encoder());
+    if (!enc) return fail(GEN9BLAS_ERR, "cuTensorMapEncodeTiled is not available from the driver");
+    cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)count};
+    cuuint64_t strides[2] = {(cuuint64_t)ldc * 2, (cuuint64_t)sC * 2};
+    cuuint32_t box[3] = {32, 32, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(GEN9BLAS_ERR, "cuTensorMapEncodeTiled (C) failed (%d): N %lld M %lld ldc %lld", (int)r, N, M, ldc);
     return 0;
 }
 
@@ -757,6 +814,12 @@ int launch_hgemm_tc(int type, int tA, int tB, int M, int N, int K, double alpha,
     if (tB) G9_TRY(encode_map(&mB, b, K, N, lb, count, xb, TC_BK, pair ? bn / 2 : TC_BN));
     else G9_TRY(encode_map(&mB, b, N, K, lb, count, xb, 64, TC_BK));
 
+    CUtensorMap mC = mB;   // unused unless p.tma_c
+    p.tma_c = 0;
+    if (pair && p.plain && !(peers && npeers > 0) && p.c_vec && (count == 1 || (sC * 2) % 16 == 0)) {
+        G9_TRY(encode_c_map(&mC, C, N, M, ldc, count, count == 1 ? ((long long)M * ldc + 7) / 8 * 8 : sC));
+        p.tma_c = 1;
+    }
     if (pair) {
         p.tiles_m = (M + T2_BM - 1) / T2_BM;
         p.tiles_n = (N + bn - 1) / bn;
@@ -775,9 +838,10 @@ int launch_hgemm_tc(int type, int tA, int tB, int M, int N, int K, double alpha,
             p.epoch = d->gemm_epoch;
         }
         const int grid2 = 2 * (int)(units < pairs ? units : pairs);
-        if (type == GEN9BLAS_H) return bn == 256 ? launch_pair<true, 256>(mA, mB, p, grid2, st)
-                                                 : launch_pair<true, 128>(mA, mB, p, grid2, st);
-        return bn == 256 ? launch_pair<false, 256>(mA, mB, p, grid2, st) : launch_pair<false, 128>(mA, mB, p, grid2, st);
+        if (type == GEN9BLAS_H) return bn == 256 ? launch_pair<true, 256>(mA, mB, mC, p, grid2, st)
+                                                 : launch_pair<true, 128>(mA, mB, mC, p, grid2, st);
+        return bn == 256 ? launch_pair<false, 256>(mA, mB, mC, p, grid2, st)
+                         : launch_pair<false, 128>(mA, mB, mC, p, grid2, st);
     }
     p.tiles_m = (M + TC_BM - 1) / TC_BM;
     p.tiles_n = (N + TC_BN - 1) / TC_BN;

@@ -284,15 +284,17 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *_
                 if (e >= nv) break;
                 sp[vr[e] * 16 + vm[e]] = v[e];
             }
-            // The warp's partial stores are ordered before the counter update by the warp barrier and the release of
-            // the atomic (cumulative at GPU scope); the last arriver's acquire makes every slot visible to its lanes.
+            // Every lane fences its own partial stores at GPU scope before lane 0 counts the warp's arrival (release);
+            // the last arriver's lanes fence again after lane 0's acquire, before they read the other warps' slots.
+            __threadfence();
             __syncwarp();
             int prev = 0;
             if (lane == 0)
                 asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(prev) : "l"(count + blk) : "memory");
             prev = __shfl_sync(0xffffffffu, prev, 0);
             if (prev == nc - 1) {
-                __syncwarp();   // the lanes' slot reads are ordered after lane 0's acquire
+                __syncwarp();
+                __threadfence();
                 const int row = lane >> 1, tb = (lane & 1) * 8;
                 if (t0 + tb < Mout && r0 + row < p.Nc) {
                     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
