@@ -284,9 +284,10 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *_
                 if (e >= nv) break;
                 sp[vr[e] * 16 + vm[e]] = v[e];
             }
-            // Every lane fences its own partial stores at GPU scope before lane 0 counts the warp's arrival (release);
-            // the last arriver's lanes fence again after lane 0's acquire, before they read the other warps' slots.
-            __threadfence();
+            // Every lane orders its own partial stores at GPU scope (acq_rel fence) before lane 0 counts the warp's
+            // arrival (release); the last arriver's lanes fence again after lane 0's acquire, before they read the
+            // other warps' slots.
+            asm volatile("fence.acq_rel.gpu;" ::: "memory");
             __syncwarp();
             int prev = 0;
             if (lane == 0)
@@ -294,7 +295,7 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *_
             prev = __shfl_sync(0xffffffffu, prev, 0);
             if (prev == nc - 1) {
                 __syncwarp();
-                __threadfence();
+                asm volatile("fence.acq_rel.gpu;" ::: "memory");
                 const int row = lane >> 1, tb = (lane & 1) * 8;
                 if (t0 + tb < Mout && r0 + row < p.Nc) {
                     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
