@@ -302,13 +302,14 @@ static int sg_cfg(int tA, int tB, int M, int N, int K, float al, const float *a,
     const int tiles_n = (N + BN - 1) / BN, tiles_m = (M + BM - 1) / BM;
     if (tiles_m > 65535 || count > 65535)
         return fail(GEN9BLAS_ERR_INVALID_ARG, "SGEMM grid too large (M %d, count %d)", M, count);
-    // Split K when one matrix fills less than 60 % of one wave (two CTAs per SM): 4 parts (2 for K < 512). Measured
-    // on B200 at n = 1024 (64 tiles): 20 TF/s unsplit, 34 TF/s with 4 parts. Fuller waves keep whole K: the partial
-    // tiles cost a round trip through HBM (M = 512, N = 8960, K = 1536, 280 tiles: 4 parts add 12 %), and at n = 2048
-    // (256 tiles) splitting gained 1.5 %. Three parts load the SMs unevenly and are slower than two.
+    // Split K (4 parts, 2 for K < 512) when one matrix fills less than 60 % of one wave (two CTAs per SM), or less than
+    // one wave with K >= 2048, where the partial tiles' round trip through HBM is small against the K loop. Measured on
+    // B200: n = 1024 (64 tiles) 20 TF/s unsplit, 34 with 4 parts; M = 512, N = 8960, K = 1536 (280 tiles): 4 parts cost
+    // 12 %; the K = 4096 band GEMMs of SYRK / TRMM (192-256 tiles) gain 8-11 % from splitting; n = 2048 1.5 %. Three
+    // parts load the SMs unevenly and are slower than two.
     int S = 1, kper = K;
     const long long tiles = (long long)tiles_m * tiles_n;
-    if (count == 1 && tiles * 10 < 2 * SMS * 6 && K >= 256) S = K >= 512 ? 4 : 2;
+    if (count == 1 && K >= 256 && (tiles * 10 < 2 * SMS * 6 || (tiles < 2 * SMS && K >= 2048))) S = K >= 512 ? 4 : 2;
     if (S > 1) {
         kper = ((K + S - 1) / S + BK - 1) / BK * BK;
         S = (K + kper - 1) / kper;
