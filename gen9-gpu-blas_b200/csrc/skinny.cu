@@ -161,6 +161,9 @@ __global__ void __launch_bounds__(WK_WARPS * 32, 2)
 wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *__restrict__ count) {
     constexpr bool F32A = MODE != ACT_F16;
     constexpr bool late = LAZY || MODE == ACT_SPLIT;   // activation fragments loaded right before their MMAs
+    // Dependents (the next skinny call, launched with programmatic stream serialization) may start as soon as this
+    // grid runs: they take SM slots as this grid's CTAs retire and stream their own weights meanwhile.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
     const int t0 = blockIdx.y * 16;
@@ -190,6 +193,10 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *_
             uint4 wv0[UNROLL], wv1[UNROLL], av0[UNROLL], av1[UNROLL];
             const uint4 z = make_uint4(0, 0, 0, 0);
             if constexpr (MODE == ACT_F16 && !late) {
+                if (!waited) {
+                    asm volatile("griddepcontrol.wait;" ::: "memory");
+                    waited = true;
+                }
 #pragma unroll
                 for (int u = 0; u < UNROLL; u++) {
                     const int k = (kc * UNROLL + u) * 32 + 8 * t;
@@ -207,7 +214,8 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *_
                     wv0[u] = in ? ldg_w16(w0 + k) : z;
                     wv1[u] = in ? ldg_w16(w1 + k) : z;
                 }
-                if (F32A && !waited) {   // activations, scales: written by the preceding split kernel
+                if (!waited) {   // everything but the weights may come from the preceding kernel (the split kernel,
+                                 // or the previous call of a decode chain): wait for it before the first access
                     asm volatile("griddepcontrol.wait;" ::: "memory");
                     waited = true;
                 }
@@ -522,6 +530,23 @@ static SkPlan sk_plan(int Mc, int Nc, int K, int unroll, int sm_count) {
     return q;
 }
 
+// Launch with programmatic stream serialization: the kernel may start while the preceding kernel of the stream
+// finishes (it must execute griddepcontrol.wait before touching anything that kernel writes).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 template <typename T>
 static int skinny_t(SkinnyArgs p, cudaStream_t st) {
     DevState *d = dev_state();
@@ -551,8 +576,17 @@ static int skinny_t(SkinnyArgs p, cudaStream_t st) {
                 G9_TRY(skinny_counters((size_t)q.mtiles * q.RB, &count));
                 float *part = (float *)((char *)scr + a_bytes);
                 dim3 grid((unsigned)q.ctas, q.mtiles);
-                if (p.Mc > 8) wk_f16_sk<true, 8, ACT_F16, true><<<grid, WK_WARPS * 32, 0, st>>>(p, q.KC, q.maxc, part, count);
-                else wk_f16_sk<false, 8, ACT_F16, true><<<grid, WK_WARPS * 32, 0, st>>>(p, q.KC, q.maxc, part, count);
+                // Single-device calls overlap the previous call's tail (programmatic dependent launch); the fused
+                // all-gather keeps ordinary stream order around its rank barrier.
+                const dim3 blk(WK_WARPS * 32);
+                if (p.ndst == 1) {
+                    if (p.Mc > 8) launch_pdl(wk_f16_sk<true, 8, ACT_F16, true>, grid, blk, st, p, q.KC, q.maxc, part, count);
+                    else launch_pdl(wk_f16_sk<false, 8, ACT_F16, true>, grid, blk, st, p, q.KC, q.maxc, part, count);
+                } else if (p.Mc > 8) {
+                    wk_f16_sk<true, 8, ACT_F16, true><<<grid, blk, 0, st>>>(p, q.KC, q.maxc, part, count);
+                } else {
+                    wk_f16_sk<false, 8, ACT_F16, true><<<grid, blk, 0, st>>>(p, q.KC, q.maxc, part, count);
+                }
                 return launched("skinny_wk_f16_sk");
             }
             const int mt = p.Mc <= 1 ? 1 : p.Mc <= 4 ? 4 : p.Mc <= 8 ? 8 : 16;
@@ -605,6 +639,7 @@ __global__ void __launch_bounds__(SPLIT_THREADS) split_f32_rows(const float *__r
                                                                __half *__restrict__ lo, long long rs,
                                                                float *__restrict__ tscale) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");   // A may be the previous call's output
     __shared__ float red[SPLIT_THREADS / 32];
     __shared__ float sc;
     const int m = blockIdx.x;
@@ -703,8 +738,10 @@ int launch_skinny_f32a(int M, int N, int K, const float *A, int lda, const void 
     p.a = hi;
     p.tscale = ts;
     const bool vec4 = ((uintptr_t)A & 15) == 0 && lda % 4 == 0;
-    if (paired) split_f32_rows<<<M, SPLIT_THREADS, 0, st>>>(A, lda, K, Kp, vec4, hi, hi + Kp, 2LL * Kp, ts);
-    else split_f32_rows<<<M, SPLIT_THREADS, 0, st>>>(A, lda, K, Kp, vec4, hi, hi + (size_t)M * Kp, Kp, ts);
+    if (paired) launch_pdl(split_f32_rows, dim3(M), dim3(SPLIT_THREADS), st, A, (long long)lda, K, Kp, vec4, hi, hi + Kp,
+                           2LL * Kp, ts);
+    else launch_pdl(split_f32_rows, dim3(M), dim3(SPLIT_THREADS), st, A, (long long)lda, K, Kp, vec4, hi,
+                    hi + (size_t)M * Kp, (long long)Kp, ts);
     G9_TRY(launched("skinny_split_f32"));
     float *part = (float *)((char *)scr + a_bytes + s_bytes);
     if (!paired) return launch_f32a_main<true, 8, ACT_SPLIT>(p, q, part, count, st);
