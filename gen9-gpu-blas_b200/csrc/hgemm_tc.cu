@@ -411,6 +411,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
     const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+    // The next GEMM of the stream (a programmatic dependent launch) may start as soon as this one runs; it takes SM
+    // slots as these CTAs retire and sets up its barriers and TMEM meanwhile.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
             mbar_init(&full[s], 1);
@@ -437,6 +440,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const int nk = (p.K + TC_BK - 1) / TC_BK;
+    // A, B, C, the split-K scratch and flags may belong to the preceding kernel: wait for it before any access.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     if (warp == 0 && lane == 0) {
         // ---------------- TMA producer (both CTAs): this CTA's halves, bytes counted on the leader's full[s]
@@ -659,7 +664,21 @@ static int launch_pair(const CUtensorMap &mA, const CUtensorMap &mB, const CUten
                                    PairCfg<BN>::SMEM));
         attr = true;
     }
-    hgemm_tc2_kernel<F16ACC, BN><<<grid, TC_THREADS, PairCfg<BN>::SMEM, st>>>(mA, mB, mC, p);
+    if (p.ndst == 1) {   // programmatic dependent launch (the fused all-gather keeps plain stream order)
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(grid);
+        cfg.blockDim = dim3(TC_THREADS);
+        cfg.dynamicSmemBytes = PairCfg<BN>::SMEM;
+        cfg.stream = st;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        cudaLaunchKernelEx(&cfg, hgemm_tc2_kernel<F16ACC, BN>, mA, mB, mC, p);
+    } else {
+        hgemm_tc2_kernel<F16ACC, BN><<<grid, TC_THREADS, PairCfg<BN>::SMEM, st>>>(mA, mB, mC, p);
+    }
     return launched("hgemm_tc2");
 }
 
