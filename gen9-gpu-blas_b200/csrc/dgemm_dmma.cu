@@ -98,6 +98,9 @@ dgemm_dmma_kernel(int M, int N, int K, double alpha, const double *__restrict__ 
                   const double *__restrict__ B, long long ldb, long long sB, double beta, double *C, long long ldc,
                   long long sC, int tiles_m, int tiles_n, int c_vec) {
     using namespace dmma;
+    // Programmatic dependent launch (see the SGEMM kernel): let the successor start, wait for the predecessor.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     constexpr int BN = CF::BN, BK = CF::BK, STAGES = CF::STAGES, KS = CF::KS, THREADS = CF::THREADS;
     extern __shared__ __align__(16) double smem[];
     constexpr int AS = CF::template a_stage<TA>(), BS = CF::template b_stage<TB>();
@@ -234,7 +237,8 @@ static int dmma_go(cudaStream_t st, int M, int N, int K, double alpha, const dou
         G9_CU(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         attr_set[dev & 63] = true;
     }
-    k<<<grid, CF::THREADS, smem, st>>>(M, N, K, alpha, A, lda, sA, B, ldb, sB, beta, C, ldc, sC, tiles_m, tiles_n, c_vec);
+    launch_pdl(k, grid, dim3(CF::THREADS), (size_t)smem, st, M, N, K, alpha, A, lda, sA, B, ldb, sB, beta, C, ldc, sC,
+               tiles_m, tiles_n, c_vec);
     return launched("dgemm_dmma");
 }
 

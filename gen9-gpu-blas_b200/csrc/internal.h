@@ -144,5 +144,23 @@ int skinny_threshold(int type);
 int launch_skinny_f32a(int M, int N, int K, const float *A, int lda, const void *W, int ldw, float *C, int ldc,
                        unsigned *nf, cudaStream_t st);
 
+// Launch with programmatic stream serialization: the kernel may start while the preceding kernel of the stream
+// finishes; it must execute griddepcontrol.wait before it touches anything that kernel may write.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 }  // namespace g9
 #pragma GCC visibility pop

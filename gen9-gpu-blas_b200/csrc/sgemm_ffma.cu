@@ -141,6 +141,10 @@ sgemm_ffma_kernel(int M, int N, int K, float alpha, const float *__restrict__ A,
                   const float *__restrict__ B, long long ldb, long long sB, float beta, float *C, long long ldc,
                   long long sC, int c_vec, int kper, float *__restrict__ partial) {
     using namespace sg;
+    // Programmatic dependent launch: the next kernel may start while this one runs (it waits before its own loads);
+    // this one waits for its predecessor before the first operand access.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     extern __shared__ __align__(16) float sg_smem[];
     float(*As)[BK][LDS_] = reinterpret_cast<float(*)[BK][LDS_]>(sg_smem);
     float(*Bs)[BK][LDS_] = reinterpret_cast<float(*)[BK][LDS_]>(sg_smem + STAGES * BK * LDS_);
@@ -283,8 +287,8 @@ static int sg_go(bool va, bool vb, dim3 grid, cudaStream_t st, int M, int N, int
             G9_CU(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));                         \
             attr[dev & 63] = true;                                                                                     \
         }                                                                                                              \
-        k<<<grid, sg::THREADS, smem, st>>>(M, N, K, alpha, a, lda, sA, b, ldb, sB, beta, c, ldc, sC, c_vec, kper,     \
-                                            partial);                                                                  \
+        launch_pdl(k, grid, dim3(sg::THREADS), smem, st, M, N, K, alpha, a, lda, sA, b, ldb, sB, beta, c, ldc, sC,     \
+                   c_vec, kper, partial);                                                                              \
     } while (0)
     if (va && vb) G9_SG(TA, !TB);
     else if (va) G9_SG(TA, false);

@@ -530,23 +530,6 @@ static SkPlan sk_plan(int Mc, int Nc, int K, int unroll, int sm_count) {
     return q;
 }
 
-// Launch with programmatic stream serialization: the kernel may start while the preceding kernel of the stream
-// finishes (it must execute griddepcontrol.wait before touching anything that kernel writes).
-template <typename... KArgs, typename... Args>
-static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = st;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, args...);
-}
-
 template <typename T>
 static int skinny_t(SkinnyArgs p, cudaStream_t st) {
     DevState *d = dev_state();
@@ -580,8 +563,8 @@ static int skinny_t(SkinnyArgs p, cudaStream_t st) {
                 // all-gather keeps ordinary stream order around its rank barrier.
                 const dim3 blk(WK_WARPS * 32);
                 if (p.ndst == 1) {
-                    if (p.Mc > 8) launch_pdl(wk_f16_sk<true, 8, ACT_F16, true>, grid, blk, st, p, q.KC, q.maxc, part, count);
-                    else launch_pdl(wk_f16_sk<false, 8, ACT_F16, true>, grid, blk, st, p, q.KC, q.maxc, part, count);
+                    if (p.Mc > 8) launch_pdl(wk_f16_sk<true, 8, ACT_F16, true>, grid, blk, 0, st, p, q.KC, q.maxc, part, count);
+                    else launch_pdl(wk_f16_sk<false, 8, ACT_F16, true>, grid, blk, 0, st, p, q.KC, q.maxc, part, count);
                 } else if (p.Mc > 8) {
                     wk_f16_sk<true, 8, ACT_F16, true><<<grid, blk, 0, st>>>(p, q.KC, q.maxc, part, count);
                 } else {
@@ -738,9 +721,9 @@ int launch_skinny_f32a(int M, int N, int K, const float *A, int lda, const void 
     p.a = hi;
     p.tscale = ts;
     const bool vec4 = ((uintptr_t)A & 15) == 0 && lda % 4 == 0;
-    if (paired) launch_pdl(split_f32_rows, dim3(M), dim3(SPLIT_THREADS), st, A, (long long)lda, K, Kp, vec4, hi, hi + Kp,
+    if (paired) launch_pdl(split_f32_rows, dim3(M), dim3(SPLIT_THREADS), 0, st, A, (long long)lda, K, Kp, vec4, hi, hi + Kp,
                            2LL * Kp, ts);
-    else launch_pdl(split_f32_rows, dim3(M), dim3(SPLIT_THREADS), st, A, (long long)lda, K, Kp, vec4, hi,
+    else launch_pdl(split_f32_rows, dim3(M), dim3(SPLIT_THREADS), 0, st, A, (long long)lda, K, Kp, vec4, hi,
                     hi + (size_t)M * Kp, (long long)Kp, ts);
     G9_TRY(launched("skinny_split_f32"));
     float *part = (float *)((char *)scr + a_bytes + s_bytes);
