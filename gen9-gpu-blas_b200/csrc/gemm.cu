@@ -32,6 +32,73 @@ int launch_gemm(int type, int tA, int tB, int M, int N, int K, double alpha, con
     return launch_sgemm(tA, tB, M, N, K, alpha, A, lda, sA, B, ldb, sB, beta, C, ldc, sC, count, st);
 }
 
+// Host memory (pageable or pinned) as seen by the CUDA runtime.
+static bool host_memory(const void *p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return true;
+    }
+    return a.type == cudaMemoryTypeHost || a.type == cudaMemoryTypeUnregistered;
+}
+
+// GEMM with A and C in host memory (the reference's common case: NumPy arrays), pipelined over row bands of C:
+// B goes to the device first (unless it is device-resident), then band i of A crosses PCIe on the copy-in stream
+// while band i - 1 is multiplied on the library's stream and band i - 2 of C returns on the copy-out stream. With
+// pinned host memory the H2D and D2H engines and the GEMM run concurrently; with pageable memory the copies are
+// synchronous for the host and the pipeline degrades to the plain sequence. Rows of C are copied with 2-D copies
+// (pitch ldc), so bytes between rows are never written.
+static int gemm_host_pipelined(int type, int tB, int M, int N, int K, double alpha, const void *A, int lda,
+                               const void *B, int ldb, double beta, void *C, int ldc) {
+    DevState *d = dev_state();
+    if (!d) return G.status;
+    G9_TRY(pipeline_streams(d));
+    const size_t es = elem_size(type);
+    const size_t bA = ((size_t)(M - 1) * lda + K) * es, bC = ((size_t)(M - 1) * ldc + N) * es;
+    const size_t bB = (tB ? (size_t)(N - 1) * ldb + K : (size_t)(K - 1) * ldb + N) * es;
+    const bool b_host = host_memory(B);
+    void *dA = nullptr, *dB = const_cast<void *>(B), *dC = nullptr;
+    G9_TRY(stage_buffer(0, bA, &dA));
+    if (b_host) G9_TRY(stage_buffer(1, bB, &dB));
+    G9_TRY(stage_buffer(2, bC, &dC));
+    cudaStream_t sm = stream(), si = d->copy_in, so = d->copy_out;
+    cudaEvent_t *ev = d->band_ev;
+    // the copy streams start after everything already queued on the library's stream
+    G9_CU(cudaEventRecord(ev[0], sm));
+    G9_CU(cudaStreamWaitEvent(si, ev[0], 0));
+    G9_CU(cudaStreamWaitEvent(so, ev[0], 0));
+    if (b_host) G9_CU(cudaMemcpyAsync(dB, B, bB, cudaMemcpyHostToDevice, si));
+    // bands of whole 256-row pair tiles, at most 16
+    int mb = (M + 7) / 8;
+    mb = (mb + 255) / 256 * 256;
+    const int nb = (M + mb - 1) / mb;
+    G.last_zc = (b_host ? 0 : 2);
+    timer_kernel();
+    for (int i = 0; i < nb; i++) {
+        const int r0 = i * mb, rows = M - r0 < mb ? M - r0 : mb;
+        const size_t oa = (size_t)r0 * lda * es, oc = (size_t)r0 * ldc * es;
+        G9_CU(cudaMemcpy2DAsync((char *)dA + oa, (size_t)lda * es, (const char *)A + oa, (size_t)lda * es, (size_t)K * es,
+                                rows, cudaMemcpyHostToDevice, si));
+        if (beta != 0.0)
+            G9_CU(cudaMemcpy2DAsync((char *)dC + oc, (size_t)ldc * es, (const char *)C + oc, (size_t)ldc * es,
+                                    (size_t)N * es, rows, cudaMemcpyHostToDevice, si));
+        G9_CU(cudaEventRecord(ev[1 + 2 * i], si));
+        G9_CU(cudaStreamWaitEvent(sm, ev[1 + 2 * i], 0));
+        G9_TRY(launch_gemm(type, 0, tB, rows, N, K, alpha, (const char *)dA + oa, lda, 0, dB, ldb, 0, beta,
+                           (char *)dC + oc, ldc, 0, 1, sm));
+        G9_CU(cudaEventRecord(ev[2 + 2 * i], sm));
+        G9_CU(cudaStreamWaitEvent(so, ev[2 + 2 * i], 0));
+        G9_CU(cudaMemcpy2DAsync((char *)C + oc, (size_t)ldc * es, (const char *)dC + oc, (size_t)ldc * es, (size_t)N * es,
+                                rows, cudaMemcpyDeviceToHost, so));
+    }
+    // the library's stream continues after the last copy back (later calls may reuse the staging buffers)
+    G9_CU(cudaEventRecord(ev[0], so));
+    G9_CU(cudaStreamWaitEvent(sm, ev[0], 0));
+    G9_CU(cudaStreamSynchronize(sm));
+    Operand none[1];
+    return finish_op(none, 0);
+}
+
 }  // namespace g9
 
 using namespace g9;
@@ -51,6 +118,13 @@ GEN9BLAS_API int gen9blas_gemm_batched(int type, int tA, int tB, int M, int N, i
     const size_t bB = (c1 * sB + (tB ? (size_t)(N - 1) * ldb + K : (size_t)(K - 1) * ldb + N)) * es;
     const size_t bC = (c1 * sC + (size_t)(M - 1) * ldc + N) * es;
     timer_start();
+    // Large single GEMMs on host A and C: banded pipeline of copies and kernels
+    if (count == 1 && !tA && M >= 1024 && N > skinny_threshold(type) && K > skinny_threshold(type) &&
+        bA + bC >= ((size_t)16 << 20) && host_memory(A) && host_memory(C)) {
+        int r = gemm_host_pipelined(type, tB, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc);
+        timer_stop();
+        return r;
+    }
     Operand op[3];
     G9_TRY(map_operand(op[0], A, bA, 0, true, false));
     G9_TRY(map_operand(op[1], B, bB, 1, true, false));

@@ -39,6 +39,8 @@ struct DevState {
     size_t l3_n = 0;
     void *l2x = nullptr;                                       // level-2 work vectors / unpacked triangles (grow-only)
     size_t l2x_n = 0;
+    cudaStream_t copy_in = nullptr, copy_out = nullptr;        // host-operand GEMM pipeline: H2D and D2H streams
+    cudaEvent_t band_ev[2 * 17] = {};                          // and its events (band inputs ready, band C done)
     unsigned long long *sv_msg = nullptr;                      // value messages of the look-back triangular solve
     size_t sv_msg_n = 0;                                       // (epoch-stamped 64-bit words, zeroed on growth)
     unsigned sv_epoch = 0;
@@ -99,6 +101,10 @@ int map_operand(Operand &op, const void *p, size_t bytes, int slot, bool copy_in
 int finish_op(Operand *ops, int n);
 // Scratch buffer of at least `bytes` on the current device (grow-only). Waits for queued work before growing.
 int scratch(size_t bytes, void **p);
+// Device buffer of staging slot `slot` (the one map_operand uses for host operands), at least `bytes` (grow-only).
+int stage_buffer(int slot, size_t bytes, void **p);
+// The copy streams and band events of the host-operand GEMM pipeline (created on first use).
+int pipeline_streams(DevState *d);
 // Triangular solve op(A)·X = alpha·B (left) or X·op(A) = alpha·B (right) on device pointers (level-3 TRSM; B is
 // overwritten). Uses the level-3 work buffer and the GEMM scratch.
 int launch_trsm_dev(int type, int left, int upper, int tA, int unit, int M, int N, double alpha, const void *A, int lda,

@@ -176,6 +176,22 @@ int scratch(size_t bytes, void **p) {
     return 0;
 }
 
+int stage_buffer(int slot, size_t bytes, void **p) {
+    DevState *d = dev_state();
+    if (!d) return G.status;
+    G9_TRY(ensure_dev_buf(&d->stage[slot], &d->stage_n[slot], bytes));
+    *p = d->stage[slot];
+    return 0;
+}
+
+int pipeline_streams(DevState *d) {
+    if (d->copy_in) return 0;
+    G9_CU(cudaStreamCreateWithFlags(&d->copy_in, cudaStreamNonBlocking));
+    G9_CU(cudaStreamCreateWithFlags(&d->copy_out, cudaStreamNonBlocking));
+    for (auto &e : d->band_ev) G9_CU(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    return 0;
+}
+
 int skinny_counters(size_t n, int **p) {
     DevState *d = dev_state();
     if (!d) return G.status;
