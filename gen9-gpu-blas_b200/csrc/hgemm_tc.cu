@@ -331,13 +331,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 // - a cluster barrier after the barrier setup and before TMEM is freed keeps both CTAs alive while the pair's MMAs
 //   read their shared memory. No TMA multicast is used.
 constexpr int T2_BM = 256;
-constexpr int T2_A_BYTES = 128 * TC_BK * 2;   // this CTA's 128 rows of A, 16 KiB
+// The pair kernel's ring stages hold 128 K (two 64-wide TMA boxes per operand) so that each barrier handshake feeds 8
+// MMAs: with 4 MMAs per stage the per-stage handshake (full-barrier wait, fence, commit, stage advance) left the
+// tensor pipe idle between stages (measured on B200 with the operand loads switched off: 1407 TF/s with 4 MMAs per
+// handshake, 1712 with 8).
+constexpr int T2_BK = 128;
+constexpr int T2_A_BYTES = 128 * T2_BK * 2;   // this CTA's 128 rows of A, 32 KiB
 
 // Tile width BN (256 or 128) sets the shared-memory ring and the number of TMEM accumulators (512 / BN columns).
 template <int BN> struct PairCfg {
-    static constexpr int B_BYTES = (BN / 2) * TC_BK * 2;          // this CTA's BN/2 columns of B
+    static constexpr int B_BYTES = (BN / 2) * T2_BK * 2;          // this CTA's BN/2 columns of B
+    static constexpr int B_BOX = (BN / 2) * TC_BK * 2;             // one 64-K box of the K-major B
     static constexpr int STAGE_BYTES = T2_A_BYTES + B_BYTES;
-    static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;   // 6 (BN 256) or 8 (BN 128)
+    static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;   // 3 (BN 256) or 4 (BN 128)
     static constexpr int NBUF = 512 / BN;                       // TMEM accumulators
     static constexpr int STAGING = 4 * 2 * 2048;                // epilogue: 4 warps × 2 buffers of 32 × 32 FP16
     static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 512 + STAGING;
@@ -439,7 +445,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     cluster_sync();   // both CTAs' barriers are initialised before any cross-CTA arrive
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    const int nk = (p.K + TC_BK - 1) / TC_BK;
+    const int nk = (p.K + T2_BK - 1) / T2_BK;
     // A, B, C, the split-K scratch and flags may belong to the preceding kernel: wait for it before any access.
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
@@ -460,18 +466,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
                 const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
                 uint8_t *a = sA + stage * T2_A_BYTES;
                 uint8_t *bb = sB + stage * Cfg::B_BYTES;
-                const int k0 = kb * TC_BK;
-                if (!p.a_mn) {
-                    tma_load_3d_pair(a, &tmA, bar, k0, m0, b);
-                } else {
-                    tma_load_3d_pair(a, &tmA, bar, m0, k0, b);
-                    tma_load_3d_pair(a + 8192, &tmA, bar, m0 + 64, k0, b);
-                }
-                if (!p.b_mn) {
-                    tma_load_3d_pair(bb, &tmB, bar, k0, n0, b);
-                } else {
+                const int k0 = kb * T2_BK;
+                // K-major operands: the two 64-K boxes back to back. MN-major operands: per 64-wide M (N) block, its
+                // 128 K rows contiguous (two boxes of 64 K), blocks 16 KiB apart.
 #pragma unroll
-                    for (int j = 0; j < BN / 128; j++) tma_load_3d_pair(bb + 8192 * j, &tmB, bar, n0 + 64 * j, k0, b);
+                for (int h = 0; h < 2; h++) {
+                    if (!p.a_mn) {
+                        tma_load_3d_pair(a + 16384 * h, &tmA, bar, k0 + 64 * h, m0, b);
+                    } else {
+                        tma_load_3d_pair(a + 8192 * h, &tmA, bar, m0, k0 + 64 * h, b);
+                        tma_load_3d_pair(a + 16384 + 8192 * h, &tmA, bar, m0 + 64, k0 + 64 * h, b);
+                    }
+                    if (!p.b_mn) {
+                        tma_load_3d_pair(bb + Cfg::B_BOX * h, &tmB, bar, k0 + 64 * h, n0, b);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < BN / 128; j++)
+                            tma_load_3d_pair(bb + 16384 * j + 8192 * h, &tmB, bar, n0 + 64 * j, k0 + 64 * h, b);
+                    }
                 }
                 issued++;
                 if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -508,12 +520,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
                 tc_fence_after();
                 const uint32_t a_base = smem_u32(sA + stage * T2_A_BYTES);
                 const uint32_t b_base = smem_u32(sB + stage * Cfg::B_BYTES);
+                const int k_left = p.K - kb * T2_BK;   // >= 1; 16-K steps wholly past K hold TMA zero fill: skipped
 #pragma unroll
-                for (int k = 0; k < TC_BK / 16; k++) {
-                    const uint64_t ad = p.a_mn ? smem_desc_sw128(a_base + k * 2048, 8192, 1024)
-                                               : smem_desc_sw128(a_base + k * 32, 16, 1024);
-                    const uint64_t bd = p.b_mn ? smem_desc_sw128(b_base + k * 2048, 8192, 1024)
-                                               : smem_desc_sw128(b_base + k * 32, 16, 1024);
+                for (int k = 0; k < T2_BK / 16; k++) {
+                    if (k * 16 >= k_left) break;
+                    const uint32_t kin = (uint32_t)(k & 3) * 32, kbox = (uint32_t)(k >> 2);
+                    const uint64_t ad = p.a_mn ? smem_desc_sw128(a_base + k * 2048, 16384, 1024)
+                                               : smem_desc_sw128(a_base + kbox * 16384 + kin, 16, 1024);
+                    const uint64_t bd = p.b_mn ? smem_desc_sw128(b_base + k * 2048, 16384, 1024)
+                                               : smem_desc_sw128(b_base + kbox * Cfg::B_BOX + kin, 16, 1024);
                     umma_f16_pair(d_tmem, ad, bd, idesc, (kb > w.kb0 || k > 0) ? 1u : 0u);
                 }
                 umma_commit_pair_mc(&empty[stage], 0x3);
@@ -751,7 +766,7 @@ int launch_hgemm_tc(int type, int tA, int tB, int M, int N, int K, double alpha,
     // 150 TF/s with 256, 174 with 128; at n = 2048, 64 tiles: 838 with 256, 575 with 128).
     const long long tiles256 = (long long)((M + T2_BM - 1) / T2_BM) * ((N + 255) / 256) * count;
     const int bn = pair_env == 128 || (pair_env == 1 && tiles256 * 4 <= pairs) ? 128 : 256;
-    const int nk = (K + TC_BK - 1) / TC_BK;
+    const int nk = (K + T2_BK - 1) / T2_BK;   // K blocks of the pair kernel's stages
     // Work plan of the pair kernel: whole tiles while full waves of CTA pairs remain; when the last wave would leave
     // at least half of the pairs idle, its tiles are split along K over them (split-K tail, FP32 partials). A single
     // partial wave is not split: there the partial-sum exchange through global memory costs more than the idle pairs
