@@ -60,8 +60,11 @@ struct TcParams {
     int ndst;
     long long col_off;
     // pair kernel, alpha = 1, beta = 0, one destination with a TMA-legal C: the epilogue stages each warp's 32 × 32
-    // FP16 block in shared memory and writes it with one TMA store (tmC)
+    // FP16 block in shared memory (64-byte swizzle) and writes it with one TMA store (tmC)
     int tma_c;
+    // with tma_c: the kernel computes Cᵀ (the host swapped the operands), so each staged block is written transposed
+    // and stored at the swapped coordinates
+    int c_t;
 };
 
 __device__ __forceinline__ void tile_coords(const TcParams &p, int tile, int &b, int &mb, int &nb) {
@@ -346,7 +349,7 @@ template <int BN> struct PairCfg {
     static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;   // 3 (BN 256) or 4 (BN 128)
     static constexpr int NBUF = 512 / BN;                       // TMEM accumulators
     static constexpr int STAGING = 4 * 2 * 2048;                // epilogue: 4 warps × 2 buffers of 32 × 32 FP16
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 512 + STAGING;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 1024 + STAGING;
 };
 
 __device__ __forceinline__ void tile_coords_pair(const TcParams &p, int tile, int &b, int &mb, int &nb) {
@@ -412,7 +415,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     uint64_t *drain = bars + 2 * STAGES + 2 * NBUF;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
-    uint8_t *staging = smem + STAGES * Cfg::STAGE_BYTES + 512;   // 128-byte aligned
+    uint8_t *staging = smem + STAGES * Cfg::STAGE_BYTES + 1024;   // 1024-byte aligned (64-byte swizzle atoms)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
@@ -605,12 +608,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
                     if (F16ACC) tmem_ld_32x32_pack16(t_row + c * 32, r);
                     else tmem_ld_32x32(t_row + c * 32, r);
                     tmem_ld_wait();
-                    if (w.part < 0 && p.tma_c) {
+                    if (p.tma_c) {
                         // FP16 block of this warp (32 rows × 32 columns) into its staging buffer, then one TMA store;
-                        // rows and columns past M and N are clipped by the store. The buffer used two chunks ago
-                        // must have been read by its store first.
+                        // rows and columns past M and N are clipped by the store. A split tile's finisher first adds
+                        // the other parts' FP32 partial sums. The buffer used two chunks ago must have been read by
+                        // its store first. Staging rows are 64 bytes with the map's 64-byte swizzle: 16-byte chunk j
+                        // of row r sits at chunk j ^ ((r >> 1) & 3), so a warp's row stores spread over all banks.
+                        if (!have) continue;
                         uint32_t h[16];
-                        if (F16ACC) {
+                        if (w.part == 0) {
+                            float v[32];
+                            acc_to_f32<F16ACC>(r, v);
+                            for (int j = 1; j < p.split; j++) {
+                                const float4 *s4 = reinterpret_cast<const float4 *>(
+                                    p.partial + (size_t)partial_slot(p, w.tile, j, rank) * (128 * BN) +
+                                    (size_t)row_local * BN + c * 32);
+#pragma unroll
+                                for (int e = 0; e < 8; e++) {
+                                    const float4 t = s4[e];
+                                    v[4 * e] += t.x; v[4 * e + 1] += t.y; v[4 * e + 2] += t.z; v[4 * e + 3] += t.w;
+                                }
+                            }
+#pragma unroll
+                            for (int k = 0; k < 16; k++) {
+                                const __half2 v2 = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+                                h[k] = *reinterpret_cast<const uint32_t *>(&v2);
+                            }
+                        } else if (F16ACC) {
 #pragma unroll
                             for (int k = 0; k < 16; k++) h[k] = r[k];
                         } else {
@@ -623,14 +647,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
                         uint8_t *stg = staging + ((q * 2) + (c & 1)) * 2048;
                         if (lane == 0) bulk_wait_read<1>();
                         __syncwarp();
-                        uint4 *d4 = reinterpret_cast<uint4 *>(stg + lane * 64);
+                        if (!p.c_t) {
 #pragma unroll
-                        for (int k = 0; k < 4; k++) d4[k] = make_uint4(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
+                            for (int k = 0; k < 4; k++)
+                                *reinterpret_cast<uint4 *>(stg + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4)) =
+                                    make_uint4(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
+                        } else {
+                            // this lane's row of the Cᵀ tile is column `lane` of the C block: element j goes to
+                            // staging row j, byte 2·lane
+#pragma unroll
+                            for (int k = 0; k < 16; k++) {
+#pragma unroll
+                                for (int e = 0; e < 2; e++) {
+                                    const int j = 2 * k + e;
+                                    *reinterpret_cast<uint16_t *>(stg + j * 64 + ((((lane >> 3) ^ (j >> 1)) & 3) << 4) +
+                                                                  (lane & 7) * 2) = (uint16_t)(h[k] >> (16 * e));
+                                }
+                            }
+                        }
                         fence_proxy_async();
                         __syncwarp();
                         const int row_w = mb * T2_BM + 128 * rank + q * 32;
                         if (lane == 0 && row_w < p.M && col0 < p.N) {
-                            tma_store_3d(&tmC, stg, col0, row_w, b);
+                            if (p.c_t) tma_store_3d(&tmC, stg, row_w, col0, b);
+                            else tma_store_3d(&tmC, stg, col0, row_w, b);
                             bulk_commit();
                         }
                         continue;
@@ -726,8 +766,8 @@ static int encode_map(CUtensorMap *m, const void *base, long long inner, long lo
     return 0;
 }
 
-// C as a TMA store target: FP16, {N, M, count} with row pitch ldc and batch stride sC (elements), 32 × 32 boxes, no
-// swizzle (the epilogue stages plain 64-byte rows).
+// C as a TMA store target: FP16, {N, M, count} with row pitch ldc and batch stride sC (elements), 32 × 32 boxes with
+// the 64-byte swizzle that the epilogue's staging writes follow.
 static int encode_c_map(CUtensorMap *m, void *base, long long N, long long M, long long ldc, long long count,
                         long long sC) {
     auto enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(tensor_map_encoder());
@@ -737,7 +777,7 @@ static int encode_c_map(CUtensorMap *m, void *base, long long N, long long M, lo
     cuuint32_t box[3] = {32, 32, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                     CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
         return fail(GEN9BLAS_ERR, "cuTensorMapEncodeTiled (C) failed (%d): N %lld M %lld ldc %lld", (int)r, N, M, ldc);
     return 0;
@@ -747,18 +787,25 @@ static bool tma_ok(const void *p, long long ld, long long s, int count) {
     return ((uintptr_t)p & 15) == 0 && (ld * 2) % 16 == 0 && (count == 1 || (s * 2) % 16 == 0);
 }
 
-int launch_hgemm_tc(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, long long sA,
-                    const void *B, int ldb, long long sB, double beta, void *C, int ldc, long long sC, int count,
-                    cudaStream_t st, void *const *peers, int npeers, long long col_off) {
-    DevState *d = dev_state();
-    if (!d) return G.status;
-    if (npeers > 8) return fail(GEN9BLAS_ERR_INVALID_ARG, "at most 8 ranks for the fused GEMM + all-gather");
-    // GEN9BLAS_HGEMM_PAIR: 0 keeps the one-CTA kernel, 128 / 256 force the pair tile width (comparisons).
+// GEN9BLAS_HGEMM_PAIR: 0 keeps the one-CTA kernel, 128 / 256 force the pair tile width (comparisons).
+static int pair_setting() {
     static int pair_env = -1;
     if (pair_env < 0) {
         const char *e = getenv("GEN9BLAS_HGEMM_PAIR");
         pair_env = e ? atoi(e) : 1;
     }
+    return pair_env;
+}
+
+// c_t: the operands arrive swapped (the call computes Cᵀ) and C (M × N here, pitch ldc) receives the transposed tiles;
+// only with the pair kernel's TMA-store epilogue.
+static int hgemm_tc_impl(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, long long sA,
+                         const void *B, int ldb, long long sB, double beta, void *C, int ldc, long long sC, int count,
+                         cudaStream_t st, void *const *peers, int npeers, long long col_off, int c_t) {
+    DevState *d = dev_state();
+    if (!d) return G.status;
+    if (npeers > 8) return fail(GEN9BLAS_ERR_INVALID_ARG, "at most 8 ranks for the fused GEMM + all-gather");
+    const int pair_env = pair_setting();
     const bool pair = (pair_env && M > 128) || npeers > 0;
     const int pairs = d->sm_count / 2;
     // Tile width: 256 feeds the tensor pipe best (L2 -> SMEM bytes per FLOP), but when 256×256 tiles would occupy at
@@ -850,10 +897,14 @@ int launch_hgemm_tc(int type, int tA, int tB, int M, int N, int K, double alpha,
 
     CUtensorMap mC = mB;   // unused unless p.tma_c
     p.tma_c = 0;
+    p.c_t = c_t;
     if (pair && p.plain && !(peers && npeers > 0) && p.c_vec && (count == 1 || (sC * 2) % 16 == 0)) {
-        G9_TRY(encode_c_map(&mC, C, N, M, ldc, count, count == 1 ? ((long long)M * ldc + 7) / 8 * 8 : sC));
+        // C's own shape: N × M (columns × rows) when the tiles are not transposed, M × N when they are
+        const long long cc = c_t ? M : N, cr = c_t ? N : M;
+        G9_TRY(encode_c_map(&mC, C, cc, cr, ldc, count, count == 1 ? (cr * ldc + 7) / 8 * 8 : sC));
         p.tma_c = 1;
     }
+    if (c_t && !p.tma_c) return fail(GEN9BLAS_ERR, "internal: transposed HGEMM tiles need the TMA-store epilogue");
     if (pair) {
         p.tiles_m = (M + T2_BM - 1) / T2_BM;
         p.tiles_n = (N + bn - 1) / bn;
@@ -897,6 +948,21 @@ int launch_hgemm_tc(int type, int tA, int tB, int M, int N, int K, double alpha,
         hgemm_tc_kernel<false><<<grid, TC_THREADS, TC_SMEM, st>>>(mA, mB, p);
     }
     return launched("hgemm_tc");
+}
+
+int launch_hgemm_tc(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, long long sA,
+                    const void *B, int ldb, long long sB, double beta, void *C, int ldc, long long sC, int count,
+                    cudaStream_t st, void *const *peers, int npeers, long long col_off) {
+    // Both operands transposed: the tensor pipe runs about 18 % slower when its A operand is MN-major (measured on
+    // B200, n = 4096), so C = Aᵀ·Bᵀ is computed as Cᵀ = B·A, with B (stored N × K, K-major) as the MMA's A operand and
+    // A (stored K × M) as its MN-major B operand, and the epilogue writes the transposed tiles into C.
+    const bool c_legal = ((uintptr_t)C & 15) == 0 && (ldc % 8) == 0 && (count == 1 || (sC % 8) == 0);
+    if (tA && tB && !(peers && npeers > 0) && alpha == 1.0 && beta == 0.0 && M > 128 && N > 128 && pair_setting() == 1 &&
+        c_legal)
+        return hgemm_tc_impl(type, 0, 0, N, M, K, alpha, B, ldb, sB, A, lda, sA, beta, C, ldc, sC, count, st, nullptr, 0,
+                             0, 1);
+    return hgemm_tc_impl(type, tA, tB, M, N, K, alpha, A, lda, sA, B, ldb, sB, beta, C, ldc, sC, count, st, peers, npeers,
+                         col_off, 0);
 }
 
 // ------------------------------------------------------------------------------------------------ wait self-test

@@ -192,6 +192,39 @@ def test_hgemm_split_k_tail(gpu_lib, t):
             assert mx <= 1e-3, (t, M, N, K, mx)
 
 
+@pytest.mark.parametrize("t", [abi.H, abi.HS])
+def test_hgemm_both_transposed(gpu_lib, t):
+    """C = Aᵀ·Bᵀ with alpha = 1, beta = 0 runs as Cᵀ = B·A with the epilogue writing transposed 32 × 32 blocks:
+    ragged edges in M, N and K, a split-K tail, 256×128 tiles, and a batch with padded strides; every element of C
+    (and nothing past it) is checked against FP64."""
+    rng = np.random.default_rng(23)
+    for (M, N, K) in ((129, 257, 65), (1000, 5000, 300), (3072, 1792, 1024), (300, 1100, 777), (2048, 2048, 2048)):
+        A = (rng.standard_normal((K, M)) / np.sqrt(K)).astype(np.float16)   # stored K × M
+        B = (rng.standard_normal((N, K)) / np.sqrt(K)).astype(np.float16)   # stored N × K
+        ldc = N + 8
+        C = np.full((M, ldc), 7.0, np.float16)
+        for _ in range(2):
+            assert gpu_lib.gemm(t, 1, 1, M, N, K, 1.0, A.ctypes.data, M, B.ctypes.data, K, 0.0, C.ctypes.data, ldc) == 0
+            a64, b64 = A.T.astype(np.float64), B.T.astype(np.float64)
+            avg, mx = gemm_error(C[:, :N], a64 @ b64, np.abs(a64) @ np.abs(b64))
+            assert mx <= 1e-3, (t, M, N, K, mx)
+            assert (C[:, N:] == 7.0).all()
+    cnt, M, N, K = 3, 384, 320, 200
+    sa, sb, sc = K * M + 64, N * K + 32, M * N + 128
+    A = rng.uniform(-1, 1, cnt * sa).astype(np.float16)
+    B = rng.uniform(-1, 1, cnt * sb).astype(np.float16)
+    C = np.full(cnt * sc, 7.0, np.float16)
+    assert gpu_lib.gemm_batched(t, 1, 1, M, N, K, 1.0, A.ctypes.data, M, sa, B.ctypes.data, K, sb, 0.0, C.ctypes.data,
+                                N, sc, cnt) == 0
+    for i in range(cnt):
+        a64 = A[i * sa:i * sa + K * M].reshape(K, M).T.astype(np.float64)
+        b64 = B[i * sb:i * sb + N * K].reshape(N, K).T.astype(np.float64)
+        c = C[i * sc:i * sc + M * N].reshape(M, N)
+        avg, mx = gemm_error(c, a64 @ b64, np.abs(a64) @ np.abs(b64))
+        assert mx <= 1e-3, (t, i, mx)
+        assert (C[i * sc + M * N:(i + 1) * sc] == 7.0).all()
+
+
 def test_gemm_allgather_writes_every_destination(gpu_lib):
     """The fused GEMM + all-gather epilogue on one GPU: two local buffers stand in for two ranks' C; each receives
     this rank's column block at col_offset and nothing else changes."""
