@@ -192,6 +192,29 @@ def test_hgemm_split_k_tail(gpu_lib, t):
             assert mx <= 1e-3, (t, M, N, K, mx)
 
 
+@pytest.mark.parametrize("t,dt", [(abi.H, np.float16), (abi.S, np.float32)])
+def test_host_operands_banded_pipeline(gpu_lib, t, dt):
+    """Host A and C large enough for the banded pipeline (row bands of A cross to the device while earlier bands are
+    multiplied and their C rows return): a ragged last band, leading dimensions that are not 16-byte multiples, beta
+    != 0 (C bands copied in too), and canary bytes between the rows of C that must survive."""
+    rng = np.random.default_rng(29)
+    M, N, K = 2500, 2000, 1500
+    lda, ldc = K + 5, N + 3
+    A = rng.uniform(-1, 1, (M, lda)).astype(dt)
+    B = (rng.uniform(-1, 1, (K, N)) / np.sqrt(K)).astype(dt)
+    C0 = rng.uniform(-1, 1, (M, ldc)).astype(dt)
+    C0[:, N:] = 7.0
+    C = C0.copy()
+    assert gpu_lib.gemm(t, 0, 0, M, N, K, 1.5, A.ctypes.data, lda, B.ctypes.data, N, 0.5, C.ctypes.data, ldc) == 0
+    rows = np.concatenate([np.arange(0, M, 37), np.arange(M - 200, M)])
+    a64, b64, c64 = A[rows, :K].astype(np.float64), B.astype(np.float64), C0[rows, :N].astype(np.float64)
+    ref = 1.5 * a64 @ b64 + 0.5 * c64
+    scale = 1.5 * np.abs(a64) @ np.abs(b64) + 0.5 * np.abs(c64)
+    avg, mx = gemm_error(C[rows, :N], ref, scale)
+    assert mx <= (1e-3 if dt == np.float16 else 1e-5), (t, mx)
+    assert (C[:, N:] == 7.0).all()
+
+
 @pytest.mark.parametrize("t", [abi.H, abi.HS])
 def test_hgemm_both_transposed(gpu_lib, t):
     """C = Aᵀ·Bᵀ with alpha = 1, beta = 0 runs as Cᵀ = B·A with the epilogue writing transposed 32 × 32 blocks:
