@@ -11,9 +11,10 @@
 //   epilogue writes alpha·P + beta·C on the uplo triangle only (the other triangle of C is not touched).
 // - TRSM: reduced to a lower-triangular left solve L·Z = alpha·R (an upper triangle by reversing the index order, the
 //   right side by transposition, as the reference does); inverses of the 128×128 diagonal blocks of L are computed in
-//   FP64 on the GPU (forward substitution, one CTA per block) and stored in the element type; then per block row i
-//   (right-looking): Y_i = inv(L_ii)·Y_i (GEMM) and Y[>i] -= L[>i, i]·Y_i (one large GEMM with K = 128, which fills
-//   the GPU where the reference's left-looking update of 128 rows would not); finally Z is written back into B.
+//   FP64 on the GPU (forward substitution, one CTA per block) and stored in the element type (FP32 / FP64 also compose
+//   them into 256- and 512-row inverses with small batched GEMMs); then a recursive halving solve: the top half, one
+//   GEMM Y[bottom] -= L[bottom, top]·Y[top] with K = half the range, the bottom half, down to leaves
+//   Y_i = inv(L_ii)·Y_i; finally Z is written back into B.
 // The work matrices live in a level-3 buffer of their own (the GEMMs use the general scratch buffer).
 #include "common.cuh"
 #include "internal.h"
@@ -145,6 +146,23 @@ __global__ void __launch_bounds__(l3::kTrsmNb) trsm_block_inverse(const T *__res
     }
 }
 
+// Composed inverse of a 2s × 2s diagonal block from the inverses I0, I1 of its two s × s halves and X = -I1·L10·I0
+// (already in place at rows s..2s-1, columns 0..s-1 of the output): copies I0 and I1 in and zeroes the upper right.
+// One CTA column per pair p (blockIdx.y).
+template <typename T>
+__global__ void trsm_compose(const T *__restrict__ Inv, int s, T *Out) {
+    const int p = blockIdx.y;
+    const T *I0 = Inv + (long long)(2 * p) * s * s, *I1 = I0 + (long long)s * s;
+    T *o = Out + (long long)p * 4 * s * s;
+    const long long total = (long long)s * s;
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total; e += (long long)gridDim.x * blockDim.x) {
+        const int i = (int)(e / s), j = (int)(e % s);
+        o[(long long)i * 2 * s + j] = I0[e];
+        o[(long long)i * 2 * s + s + j] = from_r<T>(0);
+        o[(long long)(s + i) * 2 * s + s + j] = I1[e];
+    }
+}
+
 static int grid_elems(long long n) {
     DevState *d = dev_state();
     long long g = (n + 255) / 256, cap = (long long)(d ? d->sm_count : 148) * 8;
@@ -239,15 +257,29 @@ static int trsm_t(int type, int left, int upper, int tA, int unit, int M, int N,
     const bool lower = !upper != (tr != 0);
     const int rev = lower ? 0 : 1;
     const int nbl = (n + NB - 1) / NB;
+    // Leaf size: FP32 and FP64 compose the 128-row inverses into 256- and 512-row ones (two small batched GEMMs per
+    // level), so that the serial leaves and the smallest updates -- GEMMs too narrow to fill the GPU -- are 4x fewer;
+    // FP16 keeps 128-row leaves (its products would round the composed inverses to FP16 twice more).
+    int levels = 0;
+    if (type == GEN9BLAS_S || type == GEN9BLAS_D) levels = n >= 1024 ? 2 : n >= 512 ? 1 : 0;
+    const int LB = NB << levels;
     auto al = [](size_t x) { return (x + 255) / 256 * 256; };
     const size_t bL = al((size_t)n * n * sizeof(T)), bY = al((size_t)n * m * sizeof(T));
-    const size_t bI = al((size_t)nbl * NB * NB * sizeof(T)), bT = al((size_t)NB * m * sizeof(T));
+    const size_t bI = al((size_t)nbl * NB * NB * sizeof(T)), bT = al((size_t)LB * m * sizeof(T));
+    size_t bC[2] = {0, 0}, bW = 0;   // composed inverses (256, 512) and the composition's work blocks
+    for (int l = 0; l < levels; l++) {
+        const int s2 = NB << (l + 1);
+        bC[l] = al((size_t)(n / s2) * s2 * s2 * sizeof(T));
+        bW = bW > bC[l] / 4 ? bW : al((size_t)(n / s2) * (s2 / 2) * (s2 / 2) * sizeof(T));
+    }
     void *buf = nullptr;
-    G9_TRY(l3_buffer(bL + bY + bI + bT, &buf));
+    G9_TRY(l3_buffer(bL + bY + bI + bT + bC[0] + bC[1] + bW, &buf));
     T *L = (T *)buf;
     T *Y = (T *)((char *)buf + bL);
     T *Inv = (T *)((char *)buf + bL + bY);
     T *Tmp = (T *)((char *)buf + bL + bY + bI);
+    T *Comp[2] = {(T *)((char *)buf + bL + bY + bI + bT), (T *)((char *)buf + bL + bY + bI + bT + bC[0])};
+    T *Work = (T *)((char *)buf + bL + bY + bI + bT + bC[0] + bC[1]);
     trsm_build_L<T><<<grid_elems((long long)n * n), 256, 0, st>>>(A, lda, n, tr, unit, rev, L);
     G9_TRY(launched("trsm_build_L"));
     trsm_build_Y<T><<<grid_elems((long long)n * m), 256, 0, st>>>(B, ldb, n, m, left, rev, (R)alpha, Y);
@@ -261,17 +293,51 @@ static int trsm_t(int type, int left, int upper, int tA, int unit, int M, int N,
     }
     trsm_block_inverse<T><<<nbl, NB, smem, st>>>(L, n, Inv);
     G9_TRY(launched("trsm_block_inverse"));
-    for (int bb = 0; bb < nbl; bb++) {   // right-looking: every update is one large GEMM with K = the block
-        const int i0 = bb * NB, b = n - i0 < NB ? n - i0 : NB, rest = n - i0 - b;
-        T *Yi = Y + (long long)i0 * m;
-        // Y_i = inv(L_ii) · Y_i
-        G9_TRY(launch_gemm(type, 0, 0, b, m, b, 1.0, Inv + (long long)bb * NB * NB, NB, 0, Yi, m, 0, 0.0, Tmp, m, 0, 1,
-                           st));
-        G9_CU(cudaMemcpyAsync(Yi, Tmp, (size_t)b * m * sizeof(T), cudaMemcpyDeviceToDevice, st));
-        if (rest > 0)   // Y[i0+b:] -= L[i0+b:, i0:i0+b] · Y_i
-            G9_TRY(launch_gemm(type, 0, 0, rest, m, b, -1.0, L + (long long)(i0 + b) * n + i0, n, 0, Yi, m, 0, 1.0,
-                               Yi + (long long)b * m, m, 0, 1, st));
+    // inv([L00 0; L10 L11]) = [I0 0; -I1·L10·I0 I1] for every full pair of s-row blocks (s = 128, then 256)
+    for (int l = 0; l < levels; l++) {
+        const int sz = NB << l, s2 = 2 * sz, np = n / s2;
+        if (np == 0) break;
+        const T *src = l == 0 ? Inv : Comp[0];
+        const long long ss = (long long)sz * sz;
+        // Work_p = L10 · I0 (L10 = L[(2p+1)s.., 2p·s..], pitch n)
+        G9_TRY(launch_gemm(type, 0, 0, sz, sz, sz, 1.0, L + (long long)sz * n, n, (long long)s2 * n + s2, src, sz,
+                           2 * ss, 0.0, Work, sz, ss, np, st));
+        // X_p = -I1 · Work_p, straight into rows s..2s-1, columns 0..s-1 of the composed block
+        G9_TRY(launch_gemm(type, 0, 0, sz, sz, sz, -1.0, src + ss, sz, 2 * ss, Work, sz, ss, 0.0,
+                           Comp[l] + (long long)sz * s2, s2, 4 * ss, np, st));
+        trsm_compose<T><<<dim3((unsigned)std::min<long long>((ss + 255) / 256, 64), np), 256, 0, st>>>(src, sz, Comp[l]);
+        G9_TRY(launched("trsm_compose"));
     }
+    // Recursive halving over power-of-two aligned ranges of rows: solve the top half, subtract its contribution from
+    // the bottom half with one GEMM (K = the top half's size), solve the bottom half. The updates are the right-looking
+    // ones grouped into few large GEMMs (n = 4096: 2048 × m × 2048 first), which run near the GEMM kernels' large-K
+    // rate instead of the K = 128 rate of one update per block (measured on B200, n = 4096: dtrsm 12.7 TF/s block by
+    // block). A leaf is Y_i = inv(L_ii) · Y_i with the largest inverse that covers the range exactly (LB rows for a
+    // full aligned block, else 128-row blocks; the last block may be shorter).
+    auto leaf = [&](int lo, int rows, const T *inv, int ld) -> int {
+        T *Yi = Y + (long long)lo * m;
+        G9_TRY(launch_gemm(type, 0, 0, rows, m, rows, 1.0, inv, ld, 0, Yi, m, 0, 0.0, Tmp, m, 0, 1, st));
+        G9_CU(cudaMemcpyAsync(Yi, Tmp, (size_t)rows * m * sizeof(T), cudaMemcpyDeviceToDevice, st));
+        return 0;
+    };
+    auto solve = [&](auto &&self, int lo, int size) -> int {   // rows [lo, min(lo + size, n)), lo a multiple of size
+        const int hi = lo + size < n ? lo + size : n;
+        if (size > NB && size <= LB && hi - lo == size) {
+            const int l = size == 2 * NB ? 0 : 1;
+            return leaf(lo, size, Comp[l] + (long long)(lo / size) * size * size, size);
+        }
+        if (size <= NB) return leaf(lo, hi - lo, Inv + (long long)(lo / NB) * NB * NB, NB);
+        const int mid = lo + size / 2;
+        if (mid >= n) return self(self, lo, size / 2);
+        G9_TRY(self(self, lo, size / 2));
+        // Y[mid:hi] -= L[mid:hi, lo:mid] · Y[lo:mid]
+        G9_TRY(launch_gemm(type, 0, 0, hi - mid, m, mid - lo, -1.0, L + (long long)mid * n + lo, n, 0,
+                           Y + (long long)lo * m, m, 0, 1.0, Y + (long long)mid * m, m, 0, 1, st));
+        return self(self, mid, size / 2);
+    };
+    int top = NB;
+    while (top < n) top *= 2;
+    G9_TRY(solve(solve, 0, top));
     trsm_write<T><<<grid_elems((long long)n * m), 256, 0, st>>>(Y, n, m, left, rev, B, ldb);
     return launched("trsm_write");
 }

@@ -116,6 +116,37 @@ def test_trsm(g9, dt, acc):
                         assert e <= tol, (np.dtype(dt).name, acc, side, uplo, ta, dg, M, N, e)
 
 
+@pytest.mark.parametrize("dt", [np.float64, np.float32])
+def test_trsm_large_recursive(g9, dt):
+    """Triangles large enough for the recursive solve with composed 256- and 512-row leaf inverses, at sizes that
+    leave ragged tails (n = 1300: 512-row leaves, then a 256-row leaf and a 20-row one; n = 700: 256-row leaves),
+    every side / triangle / transpose / diagonal combination."""
+    rng = np.random.default_rng(9)
+    tol = TRSM_TOL[(dt, False)]
+    for side, (M, N) in (("L", (1300, 96)), ("R", (80, 700))):
+        for uplo in "LU":
+            for ta in (False, True):
+                for dg in (False, True):
+                    n = M if side == "L" else N
+                    A = rng.uniform(-1, 1, (n, n))
+                    if dg:
+                        A *= 1.0 / n
+                        A[np.diag_indices(n)] = 123.0
+                    else:
+                        A[np.diag_indices(n)] = n
+                    A = A.astype(dt)
+                    B = rng.uniform(-1, 1, (M, N)).astype(dt)
+                    T = np.tril(f64(A)) if uplo == "L" else np.triu(f64(A))
+                    if dg:
+                        np.fill_diagonal(T, 1.0)
+                    T = T.T if ta else T
+                    Xr = (np.linalg.solve(T, 2.0 * f64(B)) if side == "L"
+                          else np.linalg.solve(T.T, 2.0 * f64(B).T).T)
+                    X = f64(g9.trsm(A, B, side, uplo, ta, dg, 2.0))
+                    e = np.abs(X - Xr).max() / np.abs(Xr).max()
+                    assert e <= tol, (np.dtype(dt).name, side, uplo, ta, dg, M, N, e)
+
+
 def test_views_and_degenerate(g9):
     """Transposed views of A (triangle and transA flip without a copy), K = 0 SYRK (C = beta·C on the triangle),
     empty shapes."""
