@@ -154,13 +154,27 @@ __device__ __forceinline__ uint32_t word(const uint4 &v, int i) {
 //   their fragments loaded right before use.
 // In both F32 modes the kernel is launched as the programmatic dependent of split_f32_rows: it issues its first weight
 // loads, then waits for the split (griddepcontrol.wait) before the first activation access.
-enum { ACT_F16 = 0, ACT_PAIRED = 1, ACT_SPLIT = 2 };
+// - ACT_F16S (9..16 tokens): FP16 activations staged per warp in shared memory: at each K chunk, after its weight
+//   loads, the warp copies its tokens' UNROLL·32 columns (cp.async, 16 bytes per lane and token row, one burst) into
+//   its own region and reads the MMA fragments from there, so the activation round trip to L2 is paid once per chunk
+//   rather than once per 32-wide step (two token tiles read 2 x 8 rows a step, and a 16 × K activation block no
+//   longer stays in L1). Measured on B200, M = 16, two boxes: W 4096² 12.3 -> 10.8-11.2 µs, 11008 × 4096 23.6 ->
+//   21.7-22.1, 4096 × 11008 22.7 -> 21.5-22.6, but 12288 × 4096 23.5 -> 24.2. With up to 8 tokens the fragments
+//   stay L1-resident and are read directly (ACT_F16, LAZY; staging them cost M = 1 up to 48 %).
+enum { ACT_F16 = 0, ACT_PAIRED = 1, ACT_SPLIT = 2, ACT_F16S = 3 };
+
+// ACT_F16S staging: per warp, one row per token of UNROLL·32 FP16 plus a 64-byte pad (the two token rows a
+// quarter-warp reads then fall on different banks).
+constexpr int SK_ROWB = 8 * 32 * 2 + 64;
+__host__ __device__ constexpr int sk_stage_bytes(bool two) { return WK_WARPS * (two ? 16 : 8) * SK_ROWB; }
 
 template <bool TWO_NTILES, int UNROLL, int MODE = ACT_F16, bool LAZY = false>
 __global__ void __launch_bounds__(WK_WARPS * 32, 2)
 wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *__restrict__ count) {
-    constexpr bool F32A = MODE != ACT_F16;
-    constexpr bool late = LAZY || MODE == ACT_SPLIT;   // activation fragments loaded right before their MMAs
+    constexpr bool F32A = MODE == ACT_PAIRED || MODE == ACT_SPLIT;
+    constexpr bool late = LAZY || MODE == ACT_SPLIT || MODE == ACT_F16S;   // fragments loaded right before their MMAs
+    static_assert(MODE != ACT_F16S || UNROLL == 8, "ACT_F16S staging rows hold 8 K steps");
+    extern __shared__ __align__(16) uint8_t sk_stage[];
     // Dependents (the next skinny call, launched with programmatic stream serialization) may start as soon as this
     // grid runs: they take SM slots as this grid's CTAs retire and stream their own weights meanwhile.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -219,6 +233,27 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *_
                     asm volatile("griddepcontrol.wait;" ::: "memory");
                     waited = true;
                 }
+                if constexpr (MODE == ACT_F16S) {
+                    // this warp's token rows of the chunk: lane l copies columns 8l .. 8l + 7 of every existing row (rows
+                    // past Mc are not copied: their MMA columns are never stored)
+                    __syncwarp();   // the previous chunk's fragments have been read by every lane
+                    uint8_t *sa = sk_stage + warp * (TWO_NTILES ? 16 : 8) * SK_ROWB;
+                    const int k = kc * UNROLL * 32 + 8 * lane;
+                    const bool in = k < p.K;
+                    const int rows = min(TWO_NTILES ? 16 : 8, p.Mc - t0);
+#pragma unroll
+                    for (int r = 0; r < (TWO_NTILES ? 16 : 8); r++) {
+                        if (r >= rows) break;
+                        const __half *src = A + (long long)(t0 + r) * p.sam + (in ? k : 0);
+                        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(
+                                         (unsigned)__cvta_generic_to_shared(sa + r * SK_ROWB + 16 * lane)),
+                                     "l"(src), "r"(in ? 16 : 0)
+                                     : "memory");
+                    }
+                    asm volatile("cp.async.commit_group;\n" ::: "memory");
+                    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+                    __syncwarp();
+                }
                 if constexpr (MODE == ACT_PAIRED && !late) {
 #pragma unroll
                     for (int u = 0; u < UNROLL; u++) {
@@ -232,7 +267,11 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *_
 #pragma unroll
             for (int u = 0; u < UNROLL; u++) {
                 uint4 lo0 = z, lo1 = z;
-                if constexpr (late) {
+                if constexpr (MODE == ACT_F16S) {
+                    const uint8_t *sa = sk_stage + warp * (TWO_NTILES ? 16 : 8) * SK_ROWB + (32 * u + 8 * t) * 2;
+                    av0[u] = *reinterpret_cast<const uint4 *>(sa + g * SK_ROWB);
+                    if (TWO_NTILES) av1[u] = *reinterpret_cast<const uint4 *>(sa + (g + 8) * SK_ROWB);
+                } else if constexpr (late) {
                     const int k = (kc * UNROLL + u) * 32 + 8 * t;
                     const bool in = k < p.K;
                     av0[u] = in ? __ldg(reinterpret_cast<const uint4 *>(a0 + k)) : z;
@@ -562,11 +601,19 @@ static int skinny_t(SkinnyArgs p, cudaStream_t st) {
                 // Single-device calls overlap the previous call's tail (programmatic dependent launch); the fused
                 // all-gather keeps ordinary stream order around its rank barrier.
                 const dim3 blk(WK_WARPS * 32);
+                const bool two = p.Mc > 8;
+                const int smem = two ? sk_stage_bytes(true) : 0;   // two token tiles: activations staged (ACT_F16S)
+                static bool attr[kMaxDevices] = {};
+                if (two && !attr[d->dev]) {
+                    G9_CU(cudaFuncSetAttribute(wk_f16_sk<true, 8, ACT_F16S, true>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+                    attr[d->dev] = true;
+                }
                 if (p.ndst == 1) {
-                    if (p.Mc > 8) launch_pdl(wk_f16_sk<true, 8, ACT_F16, true>, grid, blk, 0, st, p, q.KC, q.maxc, part, count);
+                    if (two) launch_pdl(wk_f16_sk<true, 8, ACT_F16S, true>, grid, blk, smem, st, p, q.KC, q.maxc, part, count);
                     else launch_pdl(wk_f16_sk<false, 8, ACT_F16, true>, grid, blk, 0, st, p, q.KC, q.maxc, part, count);
-                } else if (p.Mc > 8) {
-                    wk_f16_sk<true, 8, ACT_F16, true><<<grid, blk, 0, st>>>(p, q.KC, q.maxc, part, count);
+                } else if (two) {
+                    wk_f16_sk<true, 8, ACT_F16S, true><<<grid, blk, smem, st>>>(p, q.KC, q.maxc, part, count);
                 } else {
                     wk_f16_sk<false, 8, ACT_F16, true><<<grid, blk, 0, st>>>(p, q.KC, q.maxc, part, count);
                 }
