@@ -324,7 +324,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 // ------------------------------------------------------------------------------------------------ CTA-pair kernel
 // Same roles and bounded waits as hgemm_tc_kernel, on a cluster of 2 CTAs that computes 256×256 tiles with
 // tcgen05.mma.cta_group::2 (M = 256 across the pair's TMEM, N = 256). Each CTA stages only its half of the operands
-// per K-block (A: its 128 rows, B: its 128 of the 256 columns), 32 KiB per stage instead of 48 KiB for a 128×256
+// per K-block (A: its 128 rows, B: its 128 of the 256 columns), 32 KiB per 64 K instead of 48 KiB for a 128×256
 // tile: half the shared-memory fill traffic per FLOP. Protocol of the pair:
 // - full[s] of the leader (rank 0) counts the TMA bytes of both CTAs (cta_group::2 loads name the leader's
 //   barrier); the leader's producer arms it with the pair's byte count;
@@ -334,10 +334,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 // - a cluster barrier after the barrier setup and before TMEM is freed keeps both CTAs alive while the pair's MMAs
 //   read their shared memory. No TMA multicast is used.
 constexpr int T2_BM = 256;
-// The pair kernel's ring stages hold 128 K (two 64-wide TMA boxes per operand) so that each barrier handshake feeds 8
-// MMAs: with 4 MMAs per stage the per-stage handshake (full-barrier wait, fence, commit, stage advance) left the
-// tensor pipe idle between stages (measured on B200 with the operand loads switched off: 1407 TF/s with 4 MMAs per
-// handshake, 1712 with 8).
+// The pair kernel's ring stages hold 128 K (two 64-wide TMA boxes per operand, 64 KiB per stage with BN 256), so each
+// barrier handshake (full-barrier wait, fence, commit, stage advance) feeds 8 MMAs instead of 4. Measured on B200 at
+// full clock against 6 stages of 64 K in the same 192 KiB: n = 4096 1259 -> 1289-1305 TF/s, n = 8192 1384 -> 1441-1451,
+// n = 1024 206 -> 232.
 constexpr int T2_BK = 128;
 constexpr int T2_A_BYTES = 128 * T2_BK * 2;   // this CTA's 128 rows of A, 32 KiB
 
