@@ -326,8 +326,11 @@ __global__ void l2x_rank(const L2Mat m, typename Compute<T>::R alpha, const T *_
 // One cooperative kernel over blocks of 64 rows of op(A) in dependency order (op(A) upper: the rows are taken in
 // reversed order, which makes it lower). Every CTA owns blocks b = blockIdx.x, + gridDim.x, ...; for a block it
 // (1) inverts the diagonal block in FP64 in shared memory (independent of x, so it overlaps the earlier blocks),
-// (2) accumulates op(A)[block b][block c]·x_c over the earlier blocks c in order (band: only the blocks the band
-// reaches), streaming the next tile into registers while it waits for x_c and multiplies the current one,
+// (2) accumulates op(A)[block b][block c]·x_c over the earlier blocks c (band: only the blocks the band reaches):
+// groups of G tiles are loaded into registers together with one poll of their x messages, every thread accumulating
+// its elements across all groups, and the per-row sums are formed once after the walk; the last tile (block b - 1,
+// the chain's last dependency) is multiplied on its own afterwards, so that only its product separates x_{b-1} from
+// x_b (measured on B200, n = 16384: strsv 1.14 -> 0.62 ms, dtrsv 1.22 -> 0.85 ms against one tile at a time),
 // (3) writes x_b = inv·(b_b − acc) in place and publishes it. Publication is a message per value: a 64-bit word holding
 // the value's bits (FP32: the whole value; FP64: one half per word) and the launch's epoch, stored with one relaxed
 // 64-bit access, so a reader that sees the epoch sees the value -- one L2 round trip per dependency, no flag and no
@@ -377,7 +380,7 @@ template <typename T> constexpr size_t sv_smem_bytes() {
 }
 
 template <typename T>
-__global__ void __launch_bounds__(256) l2x_trsv_lb(const SvArgs a) {
+__global__ void __launch_bounds__(256, sizeof(T) == 8 ? 1 : 2) l2x_trsv_lb(const SvArgs a) {
     using R = typename Compute<T>::R;
     extern __shared__ __align__(16) unsigned char sv_smem[];
     auto inv = reinterpret_cast<double (*)[kSvNb + 1]>(sv_smem);
@@ -418,30 +421,112 @@ __global__ void __launch_bounds__(256) l2x_trsv_lb(const SvArgs a) {
                 __syncwarp();
             }
         }
-        // (2) earlier blocks
-        R acc = 0;
+        // (2) earlier blocks, G tiles at a time: every thread loads its 16 elements of each tile of the group into
+        // registers (consecutive threads along A's contiguous direction), the 256 threads poll the group's x
+        // messages (one word each) into shared memory, and after one barrier each thread accumulates its elements
+        // times their x in registers across all tiles; the per-row sums are formed once, after the walk.
+        // Non-transposed: a thread holds column j = tid % 64 of rows tid / 64 + 4u (16 partial sums);
+        // transposed: row tid % 64 of columns tid / 64 + 4u (one partial sum).
+        constexpr int G = sizeof(R) == 8 ? 2 : 4;   // tiles per group: G · 64 values · words per value = 256 words
+        constexpr int EPT = kSvNb * kSvNb / 256;    // elements of a tile per thread
+        R acc_r[EPT];
+#pragma unroll
+        for (int u = 0; u < EPT; u++) acc_r[u] = 0;
+        unsigned long long *xw = reinterpret_cast<unsigned long long *>(&tile[0][0]);   // [G][64][words]
+        __syncthreads();   // the inverse is complete (tile is reused for the group's x words)
         const int c_lo = a.back ? max(0, b - a.back) : 0;
-        R pre[kSvNb * kSvNb / 256];
-        auto fetch = [&](int c) {
+        // the immediate predecessor (tile b - 1, the last dependency) is taken apart after the walk and its reduction,
+        // so that only its own product lies on the chain from x_{b-1} to x_b
+        const int c_end = b - 1;
+        R plast[EPT];
+        if (c_lo <= c_end) {
 #pragma unroll
-            for (int u = 0; u < kSvNb * kSvNb / 256; u++) {
+            for (int u = 0; u < EPT; u++) {
                 int i, j;
                 tij(tid + 256 * u, i, j);
-                pre[u] = i < rows ? sv_at<T>(a, f0 + i, c * kSvNb + j) : R(0);
+                plast[u] = i < rows ? sv_at<T>(a, f0 + i, c_end * kSvNb + j) : R(0);
             }
-        };
-        if (c_lo < b) fetch(c_lo);
-        for (int c = c_lo; c < b; c++) {
-            __syncthreads();   // the previous tile and x block are consumed (and the inverse is complete)
+        }
+        for (int cg = c_lo; cg < c_end; cg += G) {
+            R pre[G][EPT];
 #pragma unroll
-            for (int u = 0; u < kSvNb * kSvNb / 256; u++) {
+            for (int t = 0; t < G; t++) {
+                const int c = cg + t;
+#pragma unroll
+                for (int u = 0; u < EPT; u++) {
+                    int i, j;
+                    tij(tid + 256 * u, i, j);
+                    pre[t][u] = (c < c_end && i < rows) ? sv_at<T>(a, f0 + i, c * kSvNb + j) : R(0);
+                }
+            }
+            {   // word tid of the group's messages: value (tile, row) = tid / words, half tid % words
+                const int vi = tid / sv_words<R>(), tt = vi / kSvNb, row = vi % kSvNb;
+                unsigned long long v = 0;
+                if (cg + tt < c_end) {
+                    const unsigned long long *w = a.msg + ((long long)(cg + tt) * kSvNb + row) * sv_words<R>() +
+                                                  tid % sv_words<R>();
+                    v = sv_ld_msg(w);
+                    if ((unsigned)(v >> 32) != a.epoch) {
+                        const unsigned long long t0 = sv_timer();
+                        for (unsigned it = 0; (unsigned)(v >> 32) != a.epoch; ++it) {
+                            v = sv_ld_msg(w);
+                            if ((it & 63) == 63 && sv_timer() - t0 > a.limit_ns) {
+                                go = 0;
+                                break;
+                            }
+                        }
+                    }
+                }
+                xw[tid] = v;
+            }
+            __syncthreads();
+            if (!go) {
+                if (tid == 0) *(volatile unsigned *)a.err = kDevErrWaitTimeout;
+                return;
+            }
+#pragma unroll
+            for (int t = 0; t < G; t++) {
+#pragma unroll
+                for (int u = 0; u < EPT; u++) {
+                    int i, j;
+                    tij(tid + 256 * u, i, j);
+                    R xv;
+                    if constexpr (sizeof(R) == 8) {
+                        const unsigned long long lo = xw[(t * kSvNb + j) * 2], hi = xw[(t * kSvNb + j) * 2 + 1];
+                        xv = __longlong_as_double((long long)((hi << 32) | (lo & 0xffffffffull)));
+                    } else {
+                        xv = __uint_as_float((unsigned)xw[t * kSvNb + j]);
+                    }
+                    if (tr) acc_r[0] = fma_r(pre[t][u], xv, acc_r[0]);
+                    else acc_r[u] = fma_r(pre[t][u], xv, acc_r[u]);
+                }
+            }
+            __syncthreads();   // the group's x words are consumed
+        }
+        // per-row sums: red[i][k] holds the partial of row i from thread slot k (64 slots), added in slot order
+        R acc = 0;
+        {
+            auto red = reinterpret_cast<R (*)[kSvNb + 1]>(&tile[0][0]);
+            if (!tr) {
+#pragma unroll
+                for (int u = 0; u < EPT; u++) red[(tid >> 6) + 4 * u][tid & 63] = acc_r[u];
+            } else {
+                red[tid & 63][tid >> 6] = acc_r[0];
+            }
+            __syncthreads();
+            const int nslot = tr ? 4 : kSvNb;
+            for (int k = q; k < nslot; k += 4) acc += red[r][k];
+        }
+        if (c_lo <= c_end) {   // tile b - 1: stored in shared memory, x_{b-1} polled by 64 threads, row sums
+            __syncthreads();   // the partial sums are read
+#pragma unroll
+            for (int u = 0; u < EPT; u++) {
                 int i, j;
                 tij(tid + 256 * u, i, j);
-                tile[i][j] = pre[u];
+                tile[i][j] = plast[u];
             }
-            if (c + 1 < b) fetch(c + 1);
-            if (tid < kSvNb) {   // x_c[tid]: poll its message word(s) until they carry this launch's epoch
-                const unsigned long long *w = a.msg + ((long long)c * kSvNb + tid) * sv_words<R>();
+            if (tid < kSvNb) {
+                const unsigned long long *w = a.msg + ((long long)c_end * kSvNb + tid) * sv_words<R>();
                 unsigned long long v0 = sv_ld_msg(w), v1 = sv_words<R>() == 2 ? sv_ld_msg(w + 1) : 0ull;
                 auto ready = [&]() {
                     return (unsigned)(v0 >> 32) == a.epoch && (sv_words<R>() == 1 || (unsigned)(v1 >> 32) == a.epoch);
@@ -467,10 +552,10 @@ __global__ void __launch_bounds__(256) l2x_trsv_lb(const SvArgs a) {
                 if (tid == 0) *(volatile unsigned *)a.err = kDevErrWaitTimeout;
                 return;
             }
-            R s = 0;
+            R s2 = 0;
 #pragma unroll
-            for (int j = q; j < kSvNb; j += 4) s = fma_r(tile[r][j], xs[j], s);
-            acc += s;
+            for (int j = q; j < kSvNb; j += 4) s2 = fma_r(tile[r][j], xs[j], s2);
+            acc += s2;
         }
         // (3) x_b = inv·(b_b − acc), FP64, 4 lanes per row; then the flag
         acc += __shfl_xor_sync(0xffffffffu, acc, 1);
