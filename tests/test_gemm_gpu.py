@@ -192,6 +192,34 @@ def test_hgemm_split_k_tail(gpu_lib, t):
             assert mx <= 1e-3, (t, M, N, K, mx)
 
 
+def test_sgemm_large_grid_all_layouts(gpu_lib):
+    """SGEMM on a grid of more than two waves: all four transposes, pitches that are and are not multiples of 4 floats
+    (16-byte and 4-byte copy paths), ragged M, N, K, alpha / beta, bytes past N untouched."""
+    rng = np.random.default_rng(37)
+    M, N, K = 2200, 4100, 333
+    for ta in (0, 1):
+        for tb in (0, 1):
+            for pad in (0, 1):
+                ra, ca = (K, M) if ta else (M, K)
+                rb, cb = (N, K) if tb else (K, N)
+                lda, ldb, ldc = ca + pad, cb + pad, N + 3
+                A = rng.uniform(-1, 1, (ra, lda)).astype(np.float32)
+                B = rng.uniform(-1, 1, (rb, ldb)).astype(np.float32)
+                C0 = rng.uniform(-1, 1, (M, ldc)).astype(np.float32)
+                C = C0.copy()
+                assert gpu_lib.gemm(abi.S, ta, tb, M, N, K, 1.5, A.ctypes.data, lda, B.ctypes.data, ldb, 0.5,
+                                    C.ctypes.data, ldc) == 0
+                a64 = (A[:, :ca].T if ta else A[:, :ca]).astype(np.float64)
+                b64 = (B[:, :cb].T if tb else B[:, :cb]).astype(np.float64)
+                rows = np.concatenate([np.arange(0, M, 37), np.arange(M - 130, M)])
+                c64 = C0[rows, :N].astype(np.float64)
+                ref = 1.5 * a64[rows] @ b64 + 0.5 * c64
+                scale = 1.5 * np.abs(a64[rows]) @ np.abs(b64) + 0.5 * np.abs(c64)
+                avg, mx = gemm_error(C[rows, :N], ref, scale)
+                assert avg <= 1e-6 and mx <= 1e-5, (ta, tb, pad, avg, mx)
+                assert (C[:, N:] == C0[:, N:]).all()
+
+
 @pytest.mark.parametrize("t,dt", [(abi.H, np.float16), (abi.S, np.float32)])
 def test_host_operands_banded_pipeline(gpu_lib, t, dt):
     """Host A and C large enough for the banded pipeline (row bands of A cross to the device while earlier bands are
