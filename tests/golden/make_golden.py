@@ -1,6 +1,6 @@
 """Generates the committed parity fixtures under tests/golden/ (run here, where the reference checkout exists).
 
-    python tests/golden/make_golden.py [REF=/root/reference]
+    python tests/golden/make_golden.py [path of the reference checkout]
 
 1. ref_golden_hashes.json: the reference's own golden digests of its BLAS layer (tools/golden/expected/uhd620-whl/
    lib.txt of kprzybys/gen9-gpu-blas) for the calls whose result bytes do not depend on the hardware's summation
