@@ -93,6 +93,10 @@ struct Operand {
     size_t bytes = 0;
     bool zc = true;               // used in place (device or managed memory)
     bool written = false;         // copied back at the end when staged
+    // strided vector (|inc| > 1): copied back element by element (rows elements of width bytes, pitch apart), so
+    // that the bytes between its elements -- possibly another operand's, e.g. swap(x[0::2], x[1::2]) -- are not
+    // rewritten with their staged values
+    size_t pitch = 0, width = 0, rows = 0;
 };
 // Maps an operand: device / managed memory in place, any other memory staged into slot (copy_in: with its contents).
 int map_operand(Operand &op, const void *p, size_t bytes, int slot, bool copy_in, bool written);
@@ -121,6 +125,15 @@ void timer_stop();
 void *tensor_map_encoder();
 
 // Elements of a strided vector region and offset of element 0 (inc < 0: pointer is the lowest address).
+// Marks a staged vector of n elements with increment inc for an element-wise copy back (see Operand).
+inline void vec_strided(Operand &op, int n, int inc, size_t es) {
+    const size_t a = (size_t)(inc < 0 ? -(long long)inc : inc);
+    if (!op.zc && a > 1 && n > 1) {
+        op.pitch = a * es;
+        op.width = es;
+        op.rows = (size_t)n;
+    }
+}
 inline size_t vec_span(int n, int inc) { return (size_t)(n - 1) * (size_t)(inc < 0 ? -(long long)inc : inc) + 1; }
 inline long long vec_off(int n, int inc) { return inc < 0 ? (long long)(n - 1) * (long long)(-inc) : 0; }
 

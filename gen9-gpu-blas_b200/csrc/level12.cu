@@ -587,6 +587,7 @@ GEN9BLAS_API int gen9blas_axpy(int type, int n, double a, const void *x, int inc
     Operand op[2];
     G9_TRY(map_operand(op[0], x, vec_span(n, incx) * es, 0, true, false));
     G9_TRY(map_operand(op[1], y, vec_span(n, incy) * es, 1, true, true));
+    vec_strided(op[1], n, incy, es);
     timer_kernel();
     G9_TRY(launch_axpy(l12_type(type), n, a, op[0].dptr, vec_off(n, incx), incx, op[1].dptr, vec_off(n, incy), incy, stream()));
     G.last_zc = op[0].zc | op[1].zc << 1;
@@ -664,6 +665,7 @@ GEN9BLAS_API int gen9blas_gemv(int type, int trans, int M, int N, double alpha, 
     G9_TRY(map_operand(op[1], x, vec_span(nx, incx) * es, 1, true, false));
     // y is read when beta != 0, and copied in when strided so the gaps survive the copy back.
     G9_TRY(map_operand(op[2], y, vec_span(ny, incy) * es, 2, beta != 0.0 || (incy != 1 && incy != -1), true));
+    vec_strided(op[2], ny, incy, es);
     timer_kernel();
     G9_TRY(launch_gemv(l12_type(type), trans ? 1 : 0, M, N, alpha, op[0].dptr, lda, op[1].dptr, vec_off(nx, incx), incx,
                        beta, op[2].dptr, vec_off(ny, incy), incy, stream()));

@@ -810,7 +810,11 @@ int l1x_call(int mode, int type, int n, void *x, int incx, void *y, int incy, do
     timer_start();
     Operand op[2];
     G9_TRY(map_operand(op[0], x, vec_span(n, incx) * es, 0, true, mode != 0));
-    if (two) G9_TRY(map_operand(op[1], y, vec_span(n, incy) * es, 1, mode != 0 || (incy != 1 && incy != -1), true));
+    vec_strided(op[0], n, incx, es);
+    if (two) {
+        G9_TRY(map_operand(op[1], y, vec_span(n, incy) * es, 1, mode != 0 || (incy != 1 && incy != -1), true));
+        vec_strided(op[1], n, incy, es);
+    }
     timer_kernel();
     const long long ox = vec_off(n, incx), oy = two ? vec_off(n, incy) : 0;
     cudaStream_t st = stream();
@@ -842,6 +846,7 @@ int mv_call(int type, int es, L2Mat m, size_t abytes, double alpha, const void *
     G9_TRY(map_operand(op[0], m.A, abytes, 0, true, false));
     G9_TRY(map_operand(op[1], x, vec_span(m.cols, incx) * es, 1, true, false));
     G9_TRY(map_operand(op[2], y, vec_span(m.rows, incy) * es, 2, beta != 0.0 || (incy != 1 && incy != -1), true));
+    vec_strided(op[2], m.rows, incy, es);
     timer_kernel();
     m.A = op[0].dptr;
     G9_TRY(L2X_DISPATCH(mv_t, m, alpha, op[1].dptr, vec_off(m.cols, incx), incx, beta, op[2].dptr, vec_off(m.rows, incy),
@@ -858,6 +863,7 @@ int mv_inplace_call(int type, int es, L2Mat m, size_t abytes, void *x, int incx)
     Operand op[2];
     G9_TRY(map_operand(op[0], m.A, abytes, 0, true, false));
     G9_TRY(map_operand(op[1], x, vec_span(m.rows, incx) * es, 1, true, true));
+    vec_strided(op[1], m.rows, incx, es);
     timer_kernel();
     m.A = op[0].dptr;
     G9_TRY(L2X_DISPATCH(mv_inplace_t, m, op[1].dptr, vec_off(m.rows, incx), incx, stream()));
@@ -873,6 +879,7 @@ int solve_call(int type, int es, L2Mat m, size_t abytes, void *x, int incx) {
     Operand op[2];
     G9_TRY(map_operand(op[0], m.A, abytes, 0, true, false));
     G9_TRY(map_operand(op[1], x, vec_span(m.n, incx) * es, 1, true, true));
+    vec_strided(op[1], m.n, incx, es);
     timer_kernel();
     m.A = op[0].dptr;
     G9_TRY(L2X_DISPATCH(trsv_lb_t, m, op[1].dptr, vec_off(m.n, incx), incx, stream()));

@@ -265,9 +265,14 @@ int finish_op(Operand *ops, int n) {
     bool all_zc = true;
     for (int i = 0; i < n; i++) all_zc = all_zc && ops[i].zc;
     if (G.nowait && all_zc) return 0;
-    for (int i = 0; i < n; i++)
-        if (ops[i].written && !ops[i].zc)
+    for (int i = 0; i < n; i++) {
+        if (!ops[i].written || ops[i].zc) continue;
+        if (ops[i].pitch)
+            G9_CU(cudaMemcpy2DAsync(const_cast<void *>(ops[i].user), ops[i].pitch, ops[i].dptr, ops[i].pitch,
+                                    ops[i].width, ops[i].rows, cudaMemcpyDeviceToHost, st));
+        else
             G9_CU(cudaMemcpyAsync(const_cast<void *>(ops[i].user), ops[i].dptr, ops[i].bytes, cudaMemcpyDeviceToHost, st));
+    }
     G9_CU(cudaStreamSynchronize(st));
     return check_dev_err(d);
 }
