@@ -37,8 +37,6 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.join(ROOT, "gen9-gpu-blas_b200")
 METRIC = "HGEMM/SGEMM/DGEMM TFLOPS at n=4096/8192; skinny GEMM µs & HBM GB/s at M=1..16"
-OPENBLAS_DIR = "/opt/prime-rl/.venv/lib/python3.12/site-packages/opencv_python_headless.libs"
-OPENBLAS = os.path.join(OPENBLAS_DIR, "libopenblasp-r0-59ffcd50.3.15.so")
 H, S, HS, D = 0, 1, 2, 3
 
 
@@ -180,14 +178,16 @@ class ClockSampler:
 # --------------------------------------------------------------------------------------------- reference CPU path
 def load_reference_cblas():
     """The reference's CBLAS layer in CPU mode (oracle/_ref) over OpenBLAS; None if it was not built here."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import cpu_blas   # the checkers' locator of OpenBLAS (GEN9BLAS_OPENBLAS or a wheel's bundled copy)
     so = os.path.join(ROOT, "oracle", "_ref", "libgen9blas_blas_ref.so")
-    if not os.path.exists(so) or not os.path.exists(OPENBLAS):
+    openblas = cpu_blas.openblas()
+    if not os.path.exists(so) or openblas is None:
         return None, "port"
     os.environ["GEN9BLAS_BLAS"] = "cpu"
-    os.environ["GEN9BLAS_BLAS_CPU"] = OPENBLAS
+    os.environ["GEN9BLAS_BLAS_CPU"] = openblas
     os.environ.setdefault("OPENBLAS_NUM_THREADS", str(os.cpu_count()))
-    for dep in ("libquadmath-2284e583.so.0.0.0", "libgfortran-83c28eba.so.5.0.0"):
-        ctypes.CDLL(os.path.join(OPENBLAS_DIR, dep), mode=ctypes.RTLD_GLOBAL)
+    cpu_blas.preload_openblas_deps()
     L = ctypes.CDLL(so)
     L.cblas_sgemm.argtypes = [ctypes.c_int] * 6 + [ctypes.c_float, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
                                                    ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_int]
@@ -288,13 +288,35 @@ def profile_traffic(name):
 
 
 def measured_peaks():
-    """(dense bf16 TF/s for a kernel timed inside a long power-capped run, HBM GB/s, kind). The timed loops of this
-    benchmark run for about half a second back to back, so the sustained figure is the denominator."""
+    """(dense bf16 TF/s burst, the same sustained under the power cap, HBM GB/s, kind) from MEASURED_PEAKS.json, or
+    the pool's earlier figures (kind "fallback") where that file is absent."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         d = json.load(open(p))
-        return d.get("bf16_tflops_sustained") or d.get("bf16_tflops"), d.get("hbm_gbs"), "measured"
-    return 1400.0, 6650.0, "fallback"
+        burst = d.get("bf16_tflops") or d.get("bf16_tflops_sustained")
+        return burst, d.get("bf16_tflops_sustained") or burst, d.get("hbm_gbs"), "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def tensor_peak(clk):
+    """The tensor-core denominator that fits the clocks sampled over the timed region: the burst figure (cuBLAS timed
+    alone at full clock) unless the samples show the power cap (sw_power_cap active, or a median SM clock below 97 %
+    of the maximum), then the sustained one (cuBLAS looped for seconds under the cap). Returns (peak, note, both)
+    where both = {"burst": ..., "sustained": ...} for the line's record."""
+    burst, sust, _, kind = measured_peaks()
+    capped, why = False, "no power cap in the clock samples"
+    if clk:
+        mhz, mx = clk.get("sm_mhz"), clk.get("sm_max_mhz")
+        if "sw_power_cap" in (clk.get("reasons") or []):
+            capped, why = True, "sw_power_cap active during the timed region"
+        elif mhz and mx and mhz < 0.97 * mx:
+            capped, why = True, f"median SM clock {mhz:.0f} of {mx:.0f} MHz"
+    else:
+        why = "no clock samples"
+    peak = sust if capped else burst
+    note = (f"{kind} cuBLAS bf16 dense, {'sustained' if capped else 'burst'} ({why}), "
+            f"{'MEASURED_PEAKS.json' if kind == 'measured' else 'fallback figures'}")
+    return peak, note, {"burst": burst, "sustained": sust}
 
 
 def run_ours(args):
@@ -385,13 +407,14 @@ def run_ours(args):
             e2e = {"value": round(flops * e2e_steps / dt / 1e12, 3), "unit": "TFLOP/s",
                    "h2d_bytes_per_step": 2 * n * n * 2, "d2h_bytes_per_step": n * n * 2,
                    "steps": e2e_steps, "path": "gen9blas_gemm(GEN9BLAS_H) on pinned host pointers"}
-        peak_t, _, peak_kind = measured_peaks()
+        peak_t, peak_note, both = tensor_peak(clk)
         traffic = profile_traffic("hgemm_tc2_n4096")
         roof = {"bound": "tensor", "achieved": round(value, 2), "peak": peak_t, "unit": "TFLOP/s",
                 "frac": round(value / peak_t, 4), "traffic": traffic, "kernel": "hgemm_tc2_kernel<true, 256> (CTA pair, 256x256 tiles)",
                 "algorithmic": f"2*n^3 = {flops:.4g} FLOP per launch, one launch per step",
-                "peak_kind": f"{peak_kind} cuBLAS bf16 dense, sustained (the timed loop runs ~0.5 s under the 1 kW "
-                             "power cap), MEASURED_PEAKS.json"}
+                "peak_kind": peak_note,
+                "frac_of_burst": round(value / both["burst"], 4), "frac_of_sustained": round(value / both["sustained"], 4),
+                "timed_region_ms": round(ms_total, 2)}
         cpu = None
         if rank == 0 and world == 1 and not args.no_cpu:
             v, kind, calls, threads, sample = cpu_sgemm_sample(n)
@@ -563,7 +586,7 @@ def run_scaleout(args, L, torch, stream, barrier, rank, world, local):
         peers.close()
         pw.close()
         bar.close()
-    peak_t, peak_hbm, peak_kind = measured_peaks()
+    peak_t, peak_note, both = tensor_peak(clk)
     return {"metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": steps,
             "warmup": warm, "ms_per_step": round(ms_total / steps, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic",
@@ -576,8 +599,9 @@ def run_scaleout(args, L, torch, stream, barrier, rank, world, local):
                        "n": n, "l2": "inputs larger than L2 (A alone 2 GiB)"},
             "roofline": {"bound": "tensor", "achieved": round(value / world, 2), "peak": peak_t, "unit": "TFLOP/s",
                          "frac": round(value / world / peak_t, 4), "traffic": None,
-                         "peak_kind": f"{peak_kind} cuBLAS bf16 dense sustained, per GPU; achieved = whole step per "
-                                      "GPU including the gather"},
+                         "peak_kind": peak_note + "; per GPU, achieved = whole step per GPU including the gather",
+                         "frac_of_burst": round(value / world / both["burst"], 4),
+                         "frac_of_sustained": round(value / world / both["sustained"], 4)},
             "skinny_tp": {"shape": "C(8x32768) = A(8x8192) * W^T, W 32768x8192 FP16 row-sharded", "us_per_step":
                           round(tp_us, 2), "weight_GBps_per_gpu": round(nr * Kw * 2 / (tp_us * 1e-6) / 1e9, 1),
                           "includes": ("fused: skinny kernel storing its outputs into every rank's C over NVLink + "
@@ -665,7 +689,7 @@ def run_rows(args, torch):
     L = load_lib()
     stream = torch.cuda.Stream()
     assert L.set_stream(ctypes.c_void_p(stream.cuda_stream)) == 0
-    peak_t, peak_hbm, peak_kind = measured_peaks()
+    _, _, peak_hbm, peak_kind = measured_peaks()
     mhz_max = 1965.0
     peak_ffma = 148 * 128 * 2 * mhz_max * 1e6 / 1e12
     peak_dmma = 148 * 64 * 2 * mhz_max * 1e6 / 1e12
@@ -734,7 +758,10 @@ def run_rows(args, torch):
                 chk(L.gemm(kind, ta, tb, n, n, n, alpha, A[j].data_ptr(), n, B[j].data_ptr(), n, beta, C[j].data_ptr(), n))
 
         reps = max(4, min(200, int(0.25 / (2 * n ** 3 / 50e12))))
+        clocks = ClockSampler(torch.cuda.current_device())
+        clocks.start()
         ms = queued_ms(call, reps)
+        clk = clocks.stop()
         # cuBLAS on the same operands (torch.matmul / addmm), TF32 off
         torch.backends.cuda.matmul.allow_tf32 = False
         with torch.cuda.stream(stream):
@@ -751,11 +778,12 @@ def run_rows(args, torch):
             e1.synchronize()
         ms_cublas = e0.elapsed_time(e1) / reps
         tf = 2 * n ** 3 / (ms * 1e-3) / 1e12
-        peak, note = {torch.float16: (peak_t, f"{peak_kind} cuBLAS bf16 dense sustained, MEASURED_PEAKS.json"),
+        peak, note = {torch.float16: tensor_peak(clk)[:2],
                       torch.float32: (peak_ffma, "FP32 FFMA nominal: 148 SMs x 128 lanes x 2 x 1965 MHz"),
                       torch.float64: (peak_dmma, "FP64 DMMA nominal: 148 SMs x 64 FMA/clk x 2 x 1965 MHz")}[dt]
         emit_row(row, label, tf, "TFLOP/s", ms, "tensor" if dt != torch.float32 else "ffma", tf, peak, "TFLOP/s", note,
-                 {"cublas_tflops": round(2 * n ** 3 / (ms_cublas * 1e-3) / 1e12, 2)}, cpu_key)
+                 {"cublas_tflops": round(2 * n ** 3 / (ms_cublas * 1e-3) / 1e12, 2),
+                  "clocks": {k: clk.get(k) for k in ("sm_mhz", "sm_max_mhz", "reasons")}}, cpu_key)
         del A, B, C
         torch.cuda.empty_cache()
 
@@ -884,12 +912,15 @@ def run_rows(args, torch):
             P = L.dll.gen9blas_pack_b(kind, 1, K, N, Wt.data_ptr(), K)
             assert P, L.error().decode()
             reps = max(4, min(200, int(0.25 / (2 * M * N * K / 50e12))))
+            clocks = ClockSampler(torch.cuda.current_device())
+            clocks.start()
             ms = queued_ms(lambda i: chk(L.dll.gen9blas_gemm_pb(0, M, 1.0, A.data_ptr(), K, P, 0.0, Cm.data_ptr(), N)),
                            reps)
+            clk = clocks.stop()
             ms_g = queued_ms(lambda i: chk(L.gemm(kind, 0, 1, M, N, K, 1.0, A.data_ptr(), K, Wt.data_ptr(), K, 0.0,
                                                   Cm.data_ptr(), N)), reps)
             tf = 2 * M * N * K / (ms * 1e-3) / 1e12
-            peak, note = ((peak_t, f"{peak_kind} cuBLAS bf16 dense sustained, MEASURED_PEAKS.json") if dt == torch.float16
+            peak, note = (tensor_peak(clk)[:2] if dt == torch.float16
                           else (peak_ffma, "FP32 FFMA nominal: 148 SMs x 128 lanes x 2 x 1965 MHz"))
             tag = {H: "h", HS: "hs", S: "s"}[kind]
             emit_row("PB", f"gemm_pb {tag} {M}x{N}x{K}", tf, "TFLOP/s", ms, "tensor" if dt == torch.float16 else "ffma",

@@ -230,13 +230,8 @@ static int dmma_go(cudaStream_t st, int M, int N, int K, double alpha, const dou
         return fail(GEN9BLAS_ERR_INVALID_ARG, "DGEMM grid too large (M %d, N %d, count %d)", M, N, count);
     dim3 grid((unsigned)tiles, 1, count);
     auto k = dgemm_dmma_kernel<CF, TA, TB, VA, VB>;
-    static bool attr_set[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!attr_set[dev & 63]) {
-        G9_CU(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        attr_set[dev & 63] = true;
-    }
+    static bool attr[kMaxDevices] = {};
+    G9_CU(smem_limit_once(k, smem, attr));
     launch_pdl(k, grid, dim3(CF::THREADS), (size_t)smem, st, M, N, K, alpha, A, lda, sA, B, ldb, sB, beta, C, ldc, sC,
                tiles_m, tiles_n, c_vec);
     return launched("dgemm_dmma");

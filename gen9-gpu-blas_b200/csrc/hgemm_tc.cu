@@ -713,12 +713,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
 template <bool F16ACC, int BN>
 static int launch_pair(const CUtensorMap &mA, const CUtensorMap &mB, const CUtensorMap &mC, const TcParams &p, int grid,
                        cudaStream_t st) {
-    static bool attr = false;
-    if (!attr) {
-        G9_CU(cudaFuncSetAttribute(hgemm_tc2_kernel<F16ACC, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   PairCfg<BN>::SMEM));
-        attr = true;
-    }
+    static bool attr[kMaxDevices] = {};
+    G9_CU(smem_limit_once(hgemm_tc2_kernel<F16ACC, BN>, PairCfg<BN>::SMEM, attr));
     if (p.ndst == 1) {   // programmatic dependent launch (the fused all-gather keeps plain stream order)
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(grid);
@@ -933,18 +929,12 @@ static int hgemm_tc_impl(int type, int tA, int tB, int M, int N, int K, double a
     p.total_tiles = p.tiles_m * p.tiles_n * count;
     const int grid = p.total_tiles < d->sm_count ? p.total_tiles : d->sm_count;
     if (type == GEN9BLAS_H) {
-        static bool attr = false;
-        if (!attr) {
-            G9_CU(cudaFuncSetAttribute(hgemm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM));
-            attr = true;
-        }
+        static bool attr[kMaxDevices] = {};
+        G9_CU(smem_limit_once(hgemm_tc_kernel<true>, TC_SMEM, attr));
         hgemm_tc_kernel<true><<<grid, TC_THREADS, TC_SMEM, st>>>(mA, mB, p);
     } else {
-        static bool attr = false;
-        if (!attr) {
-            G9_CU(cudaFuncSetAttribute(hgemm_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM));
-            attr = true;
-        }
+        static bool attr[kMaxDevices] = {};
+        G9_CU(smem_limit_once(hgemm_tc_kernel<false>, TC_SMEM, attr));
         hgemm_tc_kernel<false><<<grid, TC_THREADS, TC_SMEM, st>>>(mA, mB, p);
     }
     return launched("hgemm_tc");

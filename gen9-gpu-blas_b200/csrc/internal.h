@@ -65,6 +65,8 @@ extern CallState G;
 
 // Current device state; initialises it on first use. nullptr on failure (status set).
 DevState *dev_state();
+// The state of device dev if an earlier call has set it up, else nullptr; creates nothing (no stream, no buffer).
+DevState *dev_state_if_ready(int dev);
 cudaStream_t stream();
 
 int fail(int code, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
@@ -162,6 +164,21 @@ int skinny_threshold(int type);
 // *nf (device-visible word).
 int launch_skinny_f32a(int M, int N, int K, const float *A, int lda, const void *W, int ldw, float *C, int ldc,
                        unsigned *nf, cudaStream_t st);
+
+// Raises a kernel's dynamic shared-memory limit to `bytes` once per device. The attribute belongs to the current
+// device's context, so a process that calls the library on several devices (gen9blas_set_device) sets it on each;
+// `done` is the caller's per-kernel array of kMaxDevices flags.
+template <typename... KArgs>
+inline cudaError_t smem_limit_once(void (*kernel)(KArgs...), int bytes, bool *done) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    if (done[dev]) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) done[dev] = true;
+    return e;
+}
 
 // Launch with programmatic stream serialization: the kernel may start while the preceding kernel of the stream
 // finishes; it must execute griddepcontrol.wait before it touches anything that kernel may write.

@@ -794,7 +794,11 @@ extern "C" GEN9BLAS_API int gen9blas_gemv_noalloc(int type, int trans, int M, in
     G9_TRY(noalloc_scratch(dev, &P));
     int sm_count = 0;
     G9_CU(cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev));
-    cudaStream_t st = G.user_stream_set ? G.user_stream : cudaStreamPerThread;
+    // The library's stream of this device, so that the call is ordered with the other entry points' work and
+    // gen9blas_flush waits for it. Before any other call has set up the device there is no such stream (setting it
+    // up would allocate); the call then runs on the per-thread default stream and always waits for it.
+    DevState *ds = dev_state_if_ready(dev);
+    cudaStream_t st = G.user_stream_set ? G.user_stream : ds ? ds->own_stream : cudaStreamPerThread;
     const int nx = trans ? M : N, ny = trans ? N : M;
     const long long ox = vec_off(nx, incx), oy = vec_off(ny, incy);
     int r;
@@ -812,6 +816,6 @@ extern "C" GEN9BLAS_API int gen9blas_gemv_noalloc(int type, int trans, int M, in
                                    (__half *)y + oy, incy, sm_count, P, st);
     }
     if (r < 0) return r;
-    if (!G.nowait) G9_CU(cudaStreamSynchronize(st));
+    if (!G.nowait || st == cudaStreamPerThread) G9_CU(cudaStreamSynchronize(st));
     return 0;
 }

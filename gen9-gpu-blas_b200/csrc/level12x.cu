@@ -752,14 +752,12 @@ static int trsv_lb_t(const L2Mat &m, void *x, long long ox, long long ix, cudaSt
     if (++d->sv_epoch == 0) d->sv_epoch = 1;
     a.msg = d->sv_msg;
     a.epoch = d->sv_epoch;
-    static int per_sm[3] = {0, 0, 0};
-    const int slot = sizeof(T) == 8 ? 2 : sizeof(T) == 4 ? 1 : 0;
+    static int per_sm[kMaxDevices] = {};
+    static bool attr[kMaxDevices] = {};
     constexpr size_t smem = sv_smem_bytes<T>();
-    if (!per_sm[slot]) {
-        G9_CU(cudaFuncSetAttribute(l2x_trsv_lb<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        G9_CU(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm[slot], l2x_trsv_lb<T>, 256, smem));
-    }
-    int grid = per_sm[slot] * d->sm_count;
+    G9_CU(smem_limit_once(l2x_trsv_lb<T>, (int)smem, attr));
+    if (!per_sm[d->dev]) G9_CU(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm[d->dev], l2x_trsv_lb<T>, 256, smem));
+    int grid = per_sm[d->dev] * d->sm_count;
     if (grid > a.nb) grid = a.nb;
     if (grid < 1) return fail(GEN9BLAS_ERR, "triangular solve kernel does not fit on an SM");
     void *args[] = {&a};

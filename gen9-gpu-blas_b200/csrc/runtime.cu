@@ -112,6 +112,11 @@ DevState *dev_state() {
     return &d;
 }
 
+DevState *dev_state_if_ready(int dev) {
+    if (dev < 0 || dev >= kMaxDevices || !g_dev[dev].ready) return nullptr;
+    return &g_dev[dev];
+}
+
 cudaStream_t stream() {
     if (G.user_stream_set) return G.user_stream;
     DevState *d = dev_state();

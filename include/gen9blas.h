@@ -209,9 +209,9 @@ GEN9BLAS_API long long gen9blas_kernel_launches(void);
 GEN9BLAS_API int gen9blas_selftest_wait(double limit_ms);
 
 /* GEMV that allocates nothing: same arguments, results and error codes as gen9blas_gemv, for callers that must not
- * allocate GPU memory -- code recording or replaying a CUDA graph, a latency-critical loop that cannot afford the
- * device-wide synchronisation of cudaMalloc/cudaFree, or a process whose device memory is fully handed to its own
- * pool. No counterpart in the reference (lib/gen9blas.h has none: its host-memory design always stages).
+ * allocate GPU memory -- a latency-critical loop that cannot afford the device-wide synchronisation of
+ * cudaMalloc/cudaFree, or a process whose device memory is all handed to its own pool, where any allocation outside
+ * that pool fails. No counterpart in the reference (lib/gen9blas.h has none: its host-memory design always stages).
  * - A, x and y must be device (or managed) memory of the current device; nothing is staged (INVALID_ARG otherwise).
  * - The transposed product keeps its partial sums in an 8 MiB array inside the library's device image, which every
  *   GPU that loads the library holds until the process exits; trans with N above 2,097,152 (FP16/FP32) or 1,048,576
@@ -220,8 +220,11 @@ GEN9BLAS_API int gen9blas_selftest_wait(double limit_ms);
  *   make that first call before any stream capture.
  * - All calls share the one array: calls that overlap on the GPU (different streams, or no-wait calls from several
  *   threads) race on it. Every partial sum is written before it is read, so nothing needs clearing between calls.
- * - Runs on the stream set with gen9blas_set_stream, else on the per-thread default stream; waits for it unless
- *   no-wait mode is on. Calls no cudaMalloc, cudaFree or other allocating routine. */
+ * - Runs on the stream set with gen9blas_set_stream, else on the library's own stream of the device, so it is
+ *   ordered with the other entry points' work and gen9blas_flush waits for it; waits for that stream unless no-wait
+ *   mode is on. On a device where no other entry point has run yet, the library has no stream of its own (creating
+ *   it would allocate): the call then runs on the per-thread default stream and always waits for it.
+ * - Calls no cudaMalloc, cudaFree or other allocating routine. */
 GEN9BLAS_API int gen9blas_gemv_noalloc(int type, int trans, int M, int N, double alpha, const void *A, int lda,
                                        const void *x, int incx, double beta, void *y, int incy);
 

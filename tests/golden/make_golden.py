@@ -1,6 +1,10 @@
 """Generates the committed parity fixtures under tests/golden/ (run here, where the reference checkout exists).
 
-    python tests/golden/make_golden.py [path of the reference checkout]
+    python tests/golden/make_golden.py [--reference DIR] [--only hashes,cblas,config]
+
+The reference checkout is DIR, else GEN9BLAS_REFERENCE, else a checkout named "reference" beside this repository;
+the script stops with a message when none exists. OpenBLAS: GEN9BLAS_OPENBLAS, else a wheel's bundled copy
+(oracle/cpu_blas.py).
 
 1. ref_golden_hashes.json: the reference's own golden digests of its BLAS layer (tools/golden/expected/uhd620-whl/
    lib.txt of kprzybys/gen9-gpu-blas) for the calls whose result bytes do not depend on the hardware's summation
@@ -10,6 +14,10 @@
    DGEMM with all transposes, alpha/beta, non-tile-multiple sizes, gemv N/T, ger, axpy, dot, nrm2, asum, iamax, and
    the level-3 set on GEMM (row- and column-major SYMM, SYRK, SYR2K, TRMM, TRSM over every side / triangle /
    transpose / diagonal option; inputs from l3_inputs).
+3. ref_config_rows.npz: sampled rows of the reference layer's output at BASELINE config sizes: SGEMM n = 1024
+   row-major NN, alpha = 1, beta = 0, A and B uniform[-1,1] from seeds 1 and 2 (the speed section of
+   lib/test_basic.py); DGEMM n = 3000 column-major, every transA/transB pair, alpha = 1.5, beta = 0.5, C prefilled
+   uniform[-1,1] (inputs from gemm_inputs). The tests regenerate the inputs from the same seeds.
 The GPU box never reads the reference: the tests only read these files.
 """
 import ctypes
@@ -22,9 +30,10 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
-OPENBLAS_DIR = "/opt/prime-rl/.venv/lib/python3.12/site-packages/opencv_python_headless.libs"
-OPENBLAS = os.path.join(OPENBLAS_DIR, "libopenblasp-r0-59ffcd50.3.15.so")
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+import cpu_blas  # noqa: E402
+
+REF = None   # reference checkout, set by main()
 
 # Digests whose inputs and arithmetic are fully defined by element-wise rules (see tests/test_oracle_golden.py).
 PINNED = ["saxpy", "daxpy", "sger", "dger", "siamax", "diamax", "snrm2", "sasum"]
@@ -171,15 +180,69 @@ def vec_inputs(tag, what, *shape):
     return np.random.default_rng(hash_seed(tag, what, shape)).uniform(-1, 1, shape).astype(dt)
 
 
-def ref_outputs():
+def ref_layer():
+    """The reference's CBLAS layer built from its sources (oracle/Makefile), in CPU mode over OpenBLAS."""
     subprocess.run(["make", "-C", os.path.join(ROOT, "oracle"), "ref", f"REF={REF}"], check=True, capture_output=True)
+    openblas = cpu_blas.preload_openblas_deps()   # its dependencies, which the wheel folder keeps off the loader path
+    if openblas is None:
+        sys.exit("no OpenBLAS found: set GEN9BLAS_OPENBLAS to a libopenblas shared object with cblas_* names")
     os.environ["GEN9BLAS_BLAS"] = "cpu"
-    os.environ["GEN9BLAS_BLAS_CPU"] = OPENBLAS
+    os.environ["GEN9BLAS_BLAS_CPU"] = openblas
     os.environ["OPENBLAS_NUM_THREADS"] = "1"
-    # OpenBLAS's own dependencies, by full path and in dependency order (the wheel directory is not on the loader path)
-    for dep in ("libquadmath-2284e583.so.0.0.0", "libgfortran-83c28eba.so.5.0.0"):
-        ctypes.CDLL(os.path.join(OPENBLAS_DIR, dep), mode=ctypes.RTLD_GLOBAL)
-    L = ctypes.CDLL(os.path.join(ROOT, "oracle", "_ref", "libgen9blas_blas_ref.so"))
+    return ctypes.CDLL(os.path.join(ROOT, "oracle", "_ref", "libgen9blas_blas_ref.so"))
+
+
+# BASELINE config sizes of ref_config_rows.npz
+C0_N = 1024
+C3_N, C3_ALPHA, C3_BETA = 3000, 1.5, 0.5
+
+
+def c0_inputs():
+    """SGEMM n = 1024 inputs, A and B uniform[-1,1] FP32 from seeds 1 and 2 (lib/test_basic.py:86-87)."""
+    n = C0_N
+    A = np.random.default_rng(1).uniform(-1, 1, (n, n)).astype(np.float32)
+    B = np.random.default_rng(2).uniform(-1, 1, (n, n)).astype(np.float32)
+    return A, B
+
+
+def c0_rows():
+    return np.unique(np.concatenate([[0, C0_N - 1], np.random.default_rng(3).choice(C0_N, 32, replace=False)]))
+
+
+def c3_inputs(ta, tb):
+    """DGEMM n = 3000 column-major inputs (logical stored matrices, gemm_inputs' seeds)."""
+    return gemm_inputs("d", ColMajor, ta, tb, C3_N, C3_N, C3_N)
+
+
+def c3_rows():
+    return np.unique(np.concatenate([[0, C3_N - 1], np.random.default_rng(4).choice(C3_N, 4, replace=False)]))
+
+
+def config_outputs(L):
+    I, P = ctypes.c_int, ctypes.c_void_p
+    res = {}
+    f = L.cblas_sgemm
+    f.argtypes = [I, I, I, I, I, I, ctypes.c_float, P, I, P, I, ctypes.c_float, P, I]
+    A, B = c0_inputs()
+    n = C0_N
+    C = np.zeros((n, n), np.float32)
+    f(RowMajor, NoTrans, NoTrans, n, n, n, 1.0, A.ctypes.data, n, B.ctypes.data, n, 0.0, C.ctypes.data, n)
+    res["sgemm_c0_rows"] = C[c0_rows()]
+    f = L.cblas_dgemm
+    f.argtypes = [I, I, I, I, I, I, ctypes.c_double, P, I, P, I, ctypes.c_double, P, I]
+    n = C3_N
+    for ta in (NoTrans, Trans):
+        for tb in (NoTrans, Trans):
+            A, B, C0 = c3_inputs(ta, tb)
+            As, Bs, Cs = np.asfortranarray(A), np.asfortranarray(B), np.asfortranarray(C0.copy())
+            f(ColMajor, ta, tb, n, n, n, C3_ALPHA, As.ctypes.data, A.shape[0], Bs.ctypes.data, B.shape[0], C3_BETA,
+              Cs.ctypes.data, n)
+            res[f"dgemm_c3_t{ta}{tb}_rows"] = np.ascontiguousarray(Cs[c3_rows()])
+    return res
+
+
+def ref_outputs():
+    L = ref_layer()
     I, P = ctypes.c_int, ctypes.c_void_p
     res = {}
     for tag, F in (("s", ctypes.c_float), ("d", ctypes.c_double)):
@@ -241,9 +304,30 @@ def ref_outputs():
     return res
 
 
+def main():
+    import argparse
+    global REF
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=None, help="reference checkout (default: GEN9BLAS_REFERENCE, else a "
+                                                        "checkout named reference beside this repository)")
+    ap.add_argument("--only", default="hashes,cblas,config")
+    a = ap.parse_args()
+    REF = a.reference or cpu_blas.reference_dir()
+    if not REF or not os.path.exists(os.path.join(REF, "lib", "src", "cblas.c")):
+        sys.exit("reference checkout not found: pass --reference DIR or set GEN9BLAS_REFERENCE")
+    only = set(a.only.split(","))
+    if "hashes" in only:
+        h = golden_hashes()
+        with open(os.path.join(HERE, "ref_golden_hashes.json"), "w") as f:
+            json.dump(h, f, indent=1, sort_keys=True)
+        print("wrote", len(h), "golden hashes")
+    if "cblas" in only:
+        np.savez_compressed(os.path.join(HERE, "ref_cblas_outputs.npz"), **ref_outputs())
+        print("wrote ref_cblas_outputs.npz")
+    if "config" in only:
+        np.savez_compressed(os.path.join(HERE, "ref_config_rows.npz"), **config_outputs(ref_layer()))
+        print("wrote ref_config_rows.npz")
+
+
 if __name__ == "__main__":
-    h = golden_hashes()
-    with open(os.path.join(HERE, "ref_golden_hashes.json"), "w") as f:
-        json.dump(h, f, indent=1, sort_keys=True)
-    np.savez_compressed(os.path.join(HERE, "ref_cblas_outputs.npz"), **ref_outputs())
-    print("wrote", len(h), "golden hashes and ref_cblas_outputs.npz")
+    main()

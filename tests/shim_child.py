@@ -17,10 +17,12 @@ sys.path.insert(0, os.path.join(HERE, "golden"))
 from make_golden import (GEMM_CASES, L3_SYMM, L3_SYRK, L3_TRXM, ColMajor, Left, NoTrans, RowMajor, Trans,  # noqa: E402
                          Unit, Upper, gemm_inputs, l3_cases, l3_inputs, l3_key, run_l3, vec_inputs)
 
-OPENBLAS_DIR = "/opt/prime-rl/.venv/lib/python3.12/site-packages/opencv_python_headless.libs"
-for dep in ("libquadmath-2284e583.so.0.0.0", "libgfortran-83c28eba.so.5.0.0"):
-    ctypes.CDLL(os.path.join(OPENBLAS_DIR, dep), mode=ctypes.RTLD_GLOBAL)
-os.environ.setdefault("GEN9BLAS_BLAS_CPU", os.path.join(OPENBLAS_DIR, "libopenblasp-r0-59ffcd50.3.15.so"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+import cpu_blas  # noqa: E402
+_openblas = cpu_blas.preload_openblas_deps()
+if _openblas is None:
+    sys.exit("no OpenBLAS found: set GEN9BLAS_OPENBLAS to a libopenblas shared object with cblas_* names")
+os.environ.setdefault("GEN9BLAS_BLAS_CPU", _openblas)
 L = ctypes.CDLL(os.path.join(ROOT, "gen9-gpu-blas_b200", "libgen9blas_blas.so"))
 I, P = ctypes.c_int, ctypes.c_void_p
 REF = np.load(os.path.join(HERE, "golden", "ref_cblas_outputs.npz"))
@@ -339,7 +341,46 @@ def group_l2x():
     return out
 
 
+def group_config():
+    """BASELINE config sizes through the CBLAS entry points: cblas_sgemm configs[0] (n = 1024 row-major NN, alpha 1,
+    beta 0) and cblas_dgemm configs[3] (n = 3000 column-major, all four transposes, alpha 1.5, beta 0.5, C prefilled),
+    each against FP64 NumPy and against the reference layer's own rows (tests/golden/ref_config_rows.npz)."""
+    import make_golden as mg
+    fix = np.load(os.path.join(HERE, "golden", "ref_config_rows.npz"))
+    out = {}
+    f = L.cblas_sgemm
+    f.argtypes = [I, I, I, I, I, I, ctypes.c_float, P, I, P, I, ctypes.c_float, P, I]
+    A, B = mg.c0_inputs()
+    n = mg.C0_N
+    C = np.full((n, n), np.nan, np.float32)
+    f(RowMajor, NoTrans, NoTrans, n, n, n, 1.0, A.ctypes.data, n, B.ctypes.data, n, 0.0, C.ctypes.data, n)
+    a64, b64 = A.astype(np.float64), B.astype(np.float64)
+    scale = np.abs(a64) @ np.abs(b64)
+    out["sgemm_c0_vs_fp64"] = rel(C, a64 @ b64, scale)
+    rows = mg.c0_rows()
+    out["sgemm_c0_vs_ref_cblas"] = rel(C[rows], fix["sgemm_c0_rows"], scale[rows])
+    f = L.cblas_dgemm
+    f.argtypes = [I, I, I, I, I, I, ctypes.c_double, P, I, P, I, ctypes.c_double, P, I]
+    n = mg.C3_N
+    rows = mg.c3_rows()
+    w64 = w_ref = 0.0
+    for ta in (NoTrans, Trans):
+        for tb in (NoTrans, Trans):
+            A, B, C0 = mg.c3_inputs(ta, tb)
+            As, Bs, Cs = np.asfortranarray(A), np.asfortranarray(B), np.asfortranarray(C0.copy())
+            f(ColMajor, ta, tb, n, n, n, mg.C3_ALPHA, As.ctypes.data, A.shape[0], Bs.ctypes.data, B.shape[0],
+              mg.C3_BETA, Cs.ctypes.data, n)
+            opA = A if ta == NoTrans else A.T
+            opB = B if tb == NoTrans else B.T
+            ref = mg.C3_ALPHA * opA[rows] @ opB + mg.C3_BETA * C0[rows]
+            scale = mg.C3_ALPHA * np.abs(opA[rows]) @ np.abs(opB) + mg.C3_BETA * np.abs(C0[rows])
+            w64 = max(w64, rel(Cs[rows], ref, scale))
+            w_ref = max(w_ref, rel(Cs[rows], fix[f"dgemm_c3_t{ta}{tb}_rows"], scale))
+    out["dgemm_c3_vs_fp64"], out["dgemm_c3_vs_ref_cblas"] = w64, w_ref
+    return out
+
+
 if __name__ == "__main__":
     groups = {"cblas_gemm": group_cblas_gemm, "fortran_l12": group_fortran_and_l12, "forwarded": group_forwarded,
-              "level3": group_level3, "l2x": group_l2x}
+              "level3": group_level3, "l2x": group_l2x, "config": group_config}
     print(json.dumps(groups[sys.argv[1]]()))

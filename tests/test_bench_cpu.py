@@ -93,9 +93,25 @@ def test_roofline_inputs_from_committed_files():
     traffic = bench.profile_traffic("hgemm_tc2_n4096")
     assert traffic is not None and 80e6 < traffic < 120e6   # DRAM bytes of one n = 4096 launch (A + B + C ≈ 100.7 MB)
     assert bench.profile_traffic("no_such_profile") is None
-    peak_t, peak_hbm, kind = bench.measured_peaks()
+    burst, sust, peak_hbm, kind = bench.measured_peaks()
     if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")):
         d = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
-        assert kind == "measured" and peak_t == d["bf16_tflops_sustained"] and peak_hbm == d["hbm_gbs"]
+        assert kind == "measured" and burst == d["bf16_tflops"] and sust == d["bf16_tflops_sustained"]
+        assert peak_hbm == d["hbm_gbs"]
     else:
-        assert kind == "fallback"
+        assert kind == "fallback" and (burst, sust) == (1590.0, 1400.0)
+
+
+def test_tensor_peak_follows_the_sampled_clocks():
+    """Burst denominator for a region at full clock with no cap; sustained when the power cap shows or the median SM
+    clock sits below the maximum; burst (noted) when nothing was sampled."""
+    burst, sust, _, _ = bench.measured_peaks()
+    full = {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": []}
+    p, note, both = bench.tensor_peak(full)
+    assert p == burst and "burst" in note and both == {"burst": burst, "sustained": sust}
+    p, note, _ = bench.tensor_peak(dict(full, reasons=["sw_power_cap"]))
+    assert p == sust and "sw_power_cap" in note
+    p, note, _ = bench.tensor_peak(dict(full, sm_mhz=1357.0))
+    assert p == sust and "1357" in note
+    p, note, _ = bench.tensor_peak(None)
+    assert p == burst and "no clock samples" in note

@@ -8,7 +8,8 @@ import numpy as np
 import pytest
 
 import abi
-from conftest import gemm_error
+import make_golden as mg
+from conftest import ROOT, gemm_error
 
 pytestmark = pytest.mark.gpu
 
@@ -301,3 +302,83 @@ def test_gemm_allgather_writes_every_destination(gpu_lib):
             assert float(((blk - ref).abs() / scale).max()) <= 1e-3
             rest = torch.cat([C[:, :512], C[:, 768:]], 1)
             assert bool((rest == 7.0).all())
+
+
+# ---------------------------------------------------------------------------------------- BASELINE config sizes
+def config_fixture():
+    import os
+    return np.load(os.path.join(ROOT, "tests", "golden", "ref_config_rows.npz"))
+
+
+def test_baseline_c0_sgemm(gpu_lib):
+    """SGEMM n = 1024 row-major NN, alpha = 1, beta = 0, A and B uniform[-1,1] from seeds 1 and 2
+    (lib/test_basic.py:86-87). North-star limit max <= 1e-6 on every element against FP64, and within 1e-6 (same
+    metric) of the reference CBLAS layer's own output on the fixture rows; run twice (split-K partials are reused)."""
+    n = mg.C0_N
+    A, B = mg.c0_inputs()
+    a64, b64 = A.astype(np.float64), B.astype(np.float64)
+    ref, scale = a64 @ b64, np.abs(a64) @ np.abs(b64)
+    rows = mg.c0_rows()
+    want = config_fixture()["sgemm_c0_rows"]
+    for _ in range(2):
+        C = np.full((n, n), np.nan, np.float32)
+        assert gpu_lib.gemm(abi.S, 0, 0, n, n, n, 1.0, A.ctypes.data, n, B.ctypes.data, n, 0.0, C.ctypes.data, n) == 0
+        avg, mx = gemm_error(C, ref, scale)
+        print(f"sgemm n=1024: mean {avg:.2e} max {mx:.2e}")
+        assert mx <= 1e-6 and avg <= 1e-7, (avg, mx)
+        assert gemm_error(C[rows], want, scale[rows])[1] <= 1e-6
+
+
+@pytest.mark.parametrize("n", [1024, 2048, 3000, 8192])
+@pytest.mark.parametrize("accurate,limit", [(False, 1e-3), (True, 1e-4)])
+def test_baseline_c1_hgemm_sizes(gpu_lib, n, accurate, limit):
+    """configs[1] at the tile-remainder sizes (n = 1024: 256x128 pair tiles, single wave; 2048; 3000: ragged edges and
+    a split-K tail) and at the 70 % target size n = 8192: A, B iid N(0,1)/sqrt(n) in FP16, north-star max limits (fast
+    1e-3, accurate 1e-4) against FP64 on the FP16 inputs -- every row up to n = 2048, else a sample plus the last
+    rows (the ragged tile row)."""
+    rng = np.random.default_rng(1)
+    A = (rng.standard_normal((n, n)) / np.sqrt(n)).astype(np.float16)
+    B = (rng.standard_normal((n, n)) / np.sqrt(n)).astype(np.float16)
+    C = np.full((n, n), np.nan, np.float16)
+    t = abi.HS if accurate else abi.H
+    assert gpu_lib.gemm(t, 0, 0, n, n, n, 1.0, A.ctypes.data, n, B.ctypes.data, n, 0.0, C.ctypes.data, n) == 0
+    if n <= 2048:
+        rows = np.arange(n)
+    else:
+        rows = np.unique(np.concatenate([rng.choice(n, 384 if n < 8192 else 128, replace=False), np.arange(n - 64, n)]))
+    a64, b64 = A[rows].astype(np.float64), B.astype(np.float64)
+    avg, mx = gemm_error(C[rows], a64 @ b64, np.abs(a64) @ np.abs(b64))
+    print(f"hgemm n={n} accurate={accurate}: mean {avg:.2e} max {mx:.2e}")
+    assert mx <= limit, (n, accurate, avg, mx)
+
+
+def c3_call(lib, ta, tb, n, A, B, C):
+    """Column-major DGEMM through the row-major C ABI by the CBLAS swap identity: column-major C = op(A)·op(B) is
+    row-major Cᵀ = op(B)ᵀ·op(A)ᵀ on the same memory (the path the LD_PRELOAD library takes, lib/src/cblas.c:190)."""
+    As, Bs, Cs = np.asfortranarray(A), np.asfortranarray(B), np.asfortranarray(C)
+    r = lib.gemm(abi.D, int(tb == mg.Trans), int(ta == mg.Trans), n, n, n, mg.C3_ALPHA, Bs.ctypes.data, B.shape[0],
+                 As.ctypes.data, A.shape[0], mg.C3_BETA, Cs.ctypes.data, n)
+    return r, Cs
+
+
+@pytest.mark.parametrize("n", [3000, 4096])
+@pytest.mark.parametrize("ta,tb", [(mg.NoTrans, mg.NoTrans), (mg.Trans, mg.NoTrans), (mg.NoTrans, mg.Trans),
+                                   (mg.Trans, mg.Trans)])
+def test_baseline_c3_dgemm(gpu_lib, n, ta, tb):
+    """DGEMM n = 3000 and 4096, column-major, all four transposes, alpha = 1.5, beta = 0.5, C prefilled
+    uniform[-1,1]: max <= 1e-13 against FP64 on sampled rows; at n = 3000 also against the reference CBLAS layer's
+    own output rows (fixture)."""
+    A, B, C0 = mg.gemm_inputs("d", mg.ColMajor, ta, tb, n, n, n)
+    r, Cs = c3_call(gpu_lib, ta, tb, n, A, B, C0.copy())
+    assert r == 0, gpu_lib.error()
+    rng = np.random.default_rng(n)
+    rows = mg.c3_rows() if n == mg.C3_N else np.unique(np.concatenate([rng.choice(n, 16, replace=False), [0, n - 1]]))
+    opA = A if ta == mg.NoTrans else A.T
+    opB = B if tb == mg.NoTrans else B.T
+    ref = mg.C3_ALPHA * opA[rows] @ opB + mg.C3_BETA * C0[rows]
+    scale = mg.C3_ALPHA * np.abs(opA[rows]) @ np.abs(opB) + mg.C3_BETA * np.abs(C0[rows])
+    avg, mx = gemm_error(Cs[rows], ref, scale)
+    assert mx <= 1e-13, (n, ta, tb, mx)
+    if n == mg.C3_N:
+        want = config_fixture()[f"dgemm_c3_t{ta}{tb}_rows"]
+        assert gemm_error(Cs[rows], want, scale)[1] <= 1e-13

@@ -102,3 +102,41 @@ def test_fused_and_nccl_allgather_two_ranks():
         assert p.returncode == 0, e[-2000:]
         line = [ln for ln in o.splitlines() if ln.startswith("ERR")][0].split()
         assert all(float(v) <= 1e-3 for v in line[2:6]), line
+
+
+SWITCH_CHILD = r'''
+import ctypes, os, sys
+import numpy as np
+sys.path.insert(0, os.path.join(sys.argv[1], "tests"))
+import abi
+L = abi.bind(ctypes.CDLL(os.path.join(sys.argv[1], "gen9-gpu-blas_b200", "libgen9blas.so")), "gen9blas_")
+assert L.init() == 0, L.error()
+rng = np.random.default_rng(5)
+worst = 0.0
+for dev in (0, 1, 0, 1):
+    assert L.set_device(dev) == 0, L.error()
+    for t, (M, N, K) in ((abi.H, (1024, 1024, 512)), (abi.HS, (96, 640, 256)), (abi.S, (512, 384, 256)),
+                         (abi.D, (256, 320, 200))):
+        dt = np.float16 if t in (abi.H, abi.HS) else np.float32 if t == abi.S else np.float64
+        A = rng.uniform(-1, 1, (M, K)).astype(dt)
+        B = rng.uniform(-1, 1, (K, N)).astype(dt)
+        C = np.zeros((M, N), dt)
+        r = L.gemm(t, 0, 0, M, N, K, 1.0, A.ctypes.data, K, B.ctypes.data, N, 0.0, C.ctypes.data, N)
+        assert r == 0, (dev, t, L.error())
+        a64, b64 = A.astype(np.float64), B.astype(np.float64)
+        worst = max(worst, float((np.abs(C - a64 @ b64) / (np.abs(a64) @ np.abs(b64))).max()))
+print("WORST", worst)
+'''
+
+
+def test_one_process_switches_devices():
+    """One process runs the large-shared-memory kernels (tcgen05 HGEMM pair and 1-CTA kernels, SGEMM, DGEMM) on device
+    0, then device 1, then both again through gen9blas_set_device: each kernel's shared-memory limit is raised on
+    every device it runs on."""
+    torch = pytest.importorskip("torch")
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    r = subprocess.run([sys.executable, "-c", SWITCH_CHILD, ROOT], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    worst = float([ln for ln in r.stdout.splitlines() if ln.startswith("WORST")][0].split()[1])
+    assert worst <= 1e-3, worst

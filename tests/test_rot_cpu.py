@@ -3,23 +3,22 @@ no GPU involved) against OpenBLAS's srotg / srotmg -- the CPU BLAS the reference
 random and edge-case inputs."""
 import ctypes
 import os
+import sys
 
 import numpy as np
 import pytest
 
-from conftest import PKG
+from conftest import PKG, ROOT
 
-OPENBLAS_DIR = "/opt/prime-rl/.venv/lib/python3.12/site-packages/opencv_python_headless.libs"
-OPENBLAS = os.path.join(OPENBLAS_DIR, "libopenblasp-r0-59ffcd50.3.15.so")
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+import cpu_blas  # noqa: E402
 
 
 @pytest.fixture(scope="module")
 def libs():
-    if not os.path.exists(OPENBLAS):
-        pytest.skip("OpenBLAS wheel library not present")
-    for dep in ("libquadmath-2284e583.so.0.0.0", "libgfortran-83c28eba.so.5.0.0"):
-        ctypes.CDLL(os.path.join(OPENBLAS_DIR, dep), mode=ctypes.RTLD_GLOBAL)
-    ob = ctypes.CDLL(OPENBLAS)
+    ob = cpu_blas.load_openblas()
+    if ob is None:
+        pytest.skip("no OpenBLAS found (set GEN9BLAS_OPENBLAS)")
     g9 = ctypes.CDLL(os.path.join(PKG, "libgen9blas.so"))
     fp = ctypes.POINTER(ctypes.c_float)
     for lib, pre in ((ob, "cblas_s"), (g9, "gen9blas_")):

@@ -95,6 +95,24 @@ def test_gpu_gemm_matches_reference_cblas():
     assert "sgemm -> GPU" in err and "dgemm -> GPU" in err and "-> CPU" not in err
 
 
+def test_cpu_mode_config_sizes_are_the_reference_cblas():
+    """GEN9BLAS_BLAS=cpu: configs[0] / configs[3] through cblas_sgemm / cblas_dgemm reproduce the fixture rows."""
+    res, err = child("config", GEN9BLAS_BLAS="cpu", GEN9BLAS_BLAS_INFO="1")
+    assert res["sgemm_c0_vs_ref_cblas"] <= 1e-6 and res["dgemm_c3_vs_ref_cblas"] <= 1e-13, res
+    assert "-> GPU" not in err
+
+
+@pytest.mark.gpu
+def test_gpu_config_sizes_through_cblas():
+    """BASELINE configs[0] (cblas_sgemm n = 1024 row-major) and configs[3] (cblas_dgemm n = 3000 column-major, all
+    four transposes, alpha 1.5, beta 0.5, C prefilled) through the LD_PRELOAD library on the GPU: north-star limits
+    (SGEMM max 1e-6, DGEMM 1e-13) against FP64 and against the reference CBLAS layer's own output rows."""
+    res, err = child("config", GEN9BLAS_BLAS="gpu", GEN9BLAS_BLAS_INFO="1")
+    assert res["sgemm_c0_vs_fp64"] <= 1e-6 and res["sgemm_c0_vs_ref_cblas"] <= 1e-6, res
+    assert res["dgemm_c3_vs_fp64"] <= 1e-13 and res["dgemm_c3_vs_ref_cblas"] <= 1e-13, res
+    assert "sgemm -> GPU" in err and "dgemm -> GPU" in err and "-> CPU" not in err
+
+
 @pytest.mark.gpu
 def test_gpu_fortran_and_level12():
     res, err = child("fortran_l12", GEN9BLAS_BLAS_INFO="1")

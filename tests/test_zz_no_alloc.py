@@ -1,12 +1,14 @@
-"""gen9blas_gemv_noalloc: the gemv entry point for callers that must not allocate GPU memory (graph capture, loops
-that cannot take the device-wide synchronisation of cudaMalloc/cudaFree, processes that hand all device memory to
-their own pool). Its transposed product keeps the split-row partial sums in a fixed 8 MiB array of the library's
-device image instead of the grow-only scratch buffer that gen9blas_gemv uses.
+"""gen9blas_gemv_noalloc: the gemv entry point for callers that must not allocate GPU memory (loops that cannot take
+the device-wide synchronisation of cudaMalloc/cudaFree, processes that hand all device memory to their own pool).
+Its transposed product keeps the split-row partial sums in a fixed 8 MiB array of the library's device image
+instead of the grow-only scratch buffer that gen9blas_gemv uses.
 
 Checked through the C ABI on device-resident operands: two calls in a row, each equal (within the level-2
-tolerances) to the output of the existing gen9blas_gemv; no growth of device memory use across calls that would
-need more scratch; oversize N rejected with a clear error before any launch. This file sorts last so that a run
-that stops at the first failure has already run every other test; it also passes alone in a fresh process."""
+tolerances) to the output of the existing gen9blas_gemv and to alpha·op(A)·x + beta·y in FP64 NumPy; in no-wait
+mode, ordered after a gen9blas_gemm that writes its A and waited for by gen9blas_flush; no growth of device memory
+use across calls that would need more scratch; oversize N rejected with a clear error before any launch. This file
+sorts last so that a run that stops at the first failure has already run every other test; it also passes alone in
+a fresh process."""
 import ctypes
 
 import numpy as np
@@ -48,14 +50,47 @@ def test_noalloc_matches_gemv_twice(gpu_lib, torch, t, dtname):
         torch.cuda.synchronize()
         Ad = A[:, :N].double().cpu().numpy()
         xs = x.double().cpu().numpy()[::incx]
-        scale = 0.75 * (np.abs(Ad.T if trans else Ad) @ np.abs(xs))   # logical order of y
+        opA = Ad.T if trans else Ad
+        y0m = y0.double().cpu().numpy()[::abs(incy)]                     # memory order (incy < 0: element 0 is last)
+        y0l = y0m[::-1] if incy < 0 else y0m                              # logical order
+        ref64 = 0.75 * (opA @ xs) + beta * y0l
+        scale = 0.75 * (np.abs(opA) @ np.abs(xs))
         if incy < 0:
-            scale = scale[::-1]                                           # memory order (element 0 is last)
-        scale = scale + abs(beta) * np.abs(y0.double().cpu().numpy()[::abs(incy)])
+            ref64, scale = ref64[::-1], scale[::-1]
+        scale = scale + abs(beta) * np.abs(y0m)
         ref = y_ref.cpu().numpy()[::abs(incy)]
         for got in (y1, y2):
             g = got.cpu().numpy()[::abs(incy)]
-            assert scaled_error(g, ref, scale) <= TOL[t], (t, M, N, trans)
+            assert scaled_error(g, ref, scale) <= TOL[t], (t, M, N, trans)      # same as gen9blas_gemv
+            assert scaled_error(g, ref64, scale) <= TOL[t], (t, M, N, trans)    # and as FP64 NumPy
+
+
+def test_noalloc_nowait_orders_after_gemm_and_flush_waits(gpu_lib, torch):
+    """No-wait mode: a gen9blas_gemm writes the matrix that gen9blas_gemv_noalloc then reads; neither call waits, and
+    gen9blas_flush must cover both (the noalloc call runs on the library's stream once the device is set up)."""
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(11)
+    M, N, K = 2048, 3072, 256
+    P = torch.empty(M, K, device="cuda", dtype=torch.float32).uniform_(-1, 1, generator=gen)
+    Q = torch.empty(K, N, device="cuda", dtype=torch.float32).uniform_(-1, 1, generator=gen)
+    x = torch.empty(M, device="cuda", dtype=torch.float32).uniform_(-1, 1, generator=gen)
+    torch.cuda.synchronize()
+    for rep in range(2):
+        A = torch.full((M, N), float("nan"), device="cuda", dtype=torch.float32)
+        y = torch.full((N,), float("nan"), device="cuda", dtype=torch.float32)
+        torch.cuda.synchronize()
+        gpu_lib.set_nowait(1)
+        try:
+            assert gpu_lib.gemm(abi.S, 0, 0, M, N, K, 1.0, P.data_ptr(), K, Q.data_ptr(), N, 0.0, A.data_ptr(), N) == 0
+            assert gpu_lib.gemv_noalloc(abi.S, 1, M, N, 1.0, A.data_ptr(), N, x.data_ptr(), 1, 0.0, y.data_ptr(), 1) == 0
+            assert gpu_lib.flush() == 0, gpu_lib.error()
+        finally:
+            gpu_lib.set_nowait(0)
+        Ad = P.double().cpu().numpy() @ Q.double().cpu().numpy()
+        xs = x.double().cpu().numpy()
+        ref = Ad.T @ xs
+        scale = np.abs(Ad.T) @ np.abs(xs)
+        assert scaled_error(y.cpu().numpy(), ref, scale) <= 1e-5, rep
 
 
 def test_noalloc_uses_no_new_device_memory(gpu_lib, torch):
