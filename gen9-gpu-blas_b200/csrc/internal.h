@@ -46,6 +46,12 @@ struct DevState {
     unsigned sv_epoch = 0;
     int *sk_count = nullptr;                                   // arrival counters of the stream-K skinny kernel (zeroed;
     size_t sk_count_n = 0;                                     // every launch leaves them at zero)
+    // Device ranges written by no-wait calls still queued on the library's stream (since the last call or flush that
+    // waited for it); a kernel that reads an input before griddepcontrol.wait checks its input against them.
+    static constexpr int kQueuedRanges = 32;
+    uintptr_t queued_lo[kQueuedRanges] = {}, queued_hi[kQueuedRanges] = {};
+    int queued_n = 0;
+    bool queued_overflow = false;
 };
 
 // Process-wide call state (the caller serialises calls, as for the reference).
@@ -105,6 +111,12 @@ int map_operand(Operand &op, const void *p, size_t bytes, int slot, bool copy_in
 // Ends a call: waits for the stream (unless no-wait applies), copies staged written operands back, checks the
 // device error word. ops may be empty.
 int finish_op(Operand *ops, int n);
+// Ledger of the outputs of queued no-wait calls (see DevState::queued_lo): add a range, forget them all once the
+// library's stream has been waited for, and ask whether [p, p + bytes) may still be written by queued work (true also
+// when more ranges were queued than the ledger holds).
+void queued_writes_add(DevState *d, const void *p, size_t bytes);
+void queued_writes_clear(DevState *d);
+bool queued_writes_overlap(DevState *d, const void *p, size_t bytes);
 // Scratch buffer of at least `bytes` on the current device (grow-only). Waits for queued work before growing.
 int scratch(size_t bytes, void **p);
 // Device buffer of staging slot `slot` (the one map_operand uses for host operands), at least `bytes` (grow-only).

@@ -816,6 +816,10 @@ extern "C" GEN9BLAS_API int gen9blas_gemv_noalloc(int type, int trans, int M, in
                                    (__half *)y + oy, incy, sm_count, P, st);
     }
     if (r < 0) return r;
-    if (!G.nowait || st == cudaStreamPerThread) G9_CU(cudaStreamSynchronize(st));
+    if (!G.nowait || st == cudaStreamPerThread) {
+        G9_CU(cudaStreamSynchronize(st));
+    } else if (ds) {   // queued on the library's stream: later calls that read y early must know
+        queued_writes_add(ds, y, vec_span(ny, incy) * (size_t)es);
+    }
     return 0;
 }

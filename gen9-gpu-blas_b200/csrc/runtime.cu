@@ -263,13 +263,41 @@ static int check_dev_err(DevState *d) {
     return 0;
 }
 
+void queued_writes_add(DevState *d, const void *p, size_t bytes) {
+    if (!bytes) return;
+    if (d->queued_n == DevState::kQueuedRanges) {
+        d->queued_overflow = true;
+        return;
+    }
+    d->queued_lo[d->queued_n] = (uintptr_t)p;
+    d->queued_hi[d->queued_n] = (uintptr_t)p + bytes;
+    d->queued_n++;
+}
+
+void queued_writes_clear(DevState *d) {
+    d->queued_n = 0;
+    d->queued_overflow = false;
+}
+
+bool queued_writes_overlap(DevState *d, const void *p, size_t bytes) {
+    if (d->queued_overflow) return true;
+    const uintptr_t lo = (uintptr_t)p, hi = lo + bytes;
+    for (int i = 0; i < d->queued_n; i++)
+        if (lo < d->queued_hi[i] && d->queued_lo[i] < hi) return true;
+    return false;
+}
+
 int finish_op(Operand *ops, int n) {
     DevState *d = dev_state();
     if (!d) return G.status;
     cudaStream_t st = stream();
     bool all_zc = true;
     for (int i = 0; i < n; i++) all_zc = all_zc && ops[i].zc;
-    if (G.nowait && all_zc) return 0;
+    if (G.nowait && all_zc) {
+        for (int i = 0; i < n; i++)
+            if (ops[i].written) queued_writes_add(d, ops[i].dptr, ops[i].bytes);
+        return 0;
+    }
     for (int i = 0; i < n; i++) {
         if (!ops[i].written || ops[i].zc) continue;
         if (ops[i].pitch)
@@ -279,6 +307,7 @@ int finish_op(Operand *ops, int n) {
             G9_CU(cudaMemcpyAsync(const_cast<void *>(ops[i].user), ops[i].dptr, ops[i].bytes, cudaMemcpyDeviceToHost, st));
     }
     G9_CU(cudaStreamSynchronize(st));
+    queued_writes_clear(d);
     return check_dev_err(d);
 }
 
@@ -486,6 +515,7 @@ GEN9BLAS_API int gen9blas_ipc_close(void *peer_ptr) {
 GEN9BLAS_API int gen9blas_flush(void) {
     if (begin_op()) return G.status;
     G9_CU(cudaStreamSynchronize(stream()));
+    queued_writes_clear(dev_state());
     return check_dev_err(dev_state());
 }
 

@@ -54,6 +54,8 @@ struct SkinnyArgs {
     long long alo;
     const float *tscale;
     unsigned *nf;
+    // wk_f16_sk: the weights may be read before griddepcontrol.wait (no queued call writes them).
+    int early_w;
 };
 
 template <typename T>
@@ -167,6 +169,9 @@ enum { ACT_F16 = 0, ACT_PAIRED = 1, ACT_SPLIT = 2, ACT_F16S = 3 };
 // quarter-warp reads then fall on different banks).
 constexpr int SK_ROWB = 8 * 32 * 2 + 64;
 __host__ __device__ constexpr int sk_stage_bytes(bool two) { return WK_WARPS * (two ? 16 : 8) * SK_ROWB; }
+// Second-iteration weights prefetched into shared memory (the modes other than ACT_F16S): 16 rows per warp.
+constexpr int SK_PRE_ROWB = 8 * 32 * 2 + 64;
+constexpr int SK_PRE_BYTES = WK_WARPS * 16 * SK_PRE_ROWB;
 
 template <bool TWO_NTILES, int UNROLL, int MODE = ACT_F16, bool LAZY = false>
 __global__ void __launch_bounds__(WK_WARPS * 32, 2)
@@ -194,7 +199,34 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *_
     const __half *a1 = A + (long long)ta1 * p.sam;
     const __half *l0 = a0 + p.alo, *l1 = a1 + p.alo;   // ACT_SPLIT: lo parts
     const int Mout = MODE == ACT_PAIRED ? p.Mc / 2 : p.Mc;   // tokens stored
+    // The warp's second iteration goes to shared memory (cp.async) before the wait as well, so that with two
+    // iterations per warp every weight byte is requested while the preceding kernel finishes. Rows of 512 bytes
+    // padded to SK_PRE_ROWB: the two rows a quarter-warp reads then sit on different banks.
+    constexpr bool PRE = MODE != ACT_F16S && UNROLL == 8;
     bool waited = false;
+    if (!p.early_w) {   // a queued call may still write the weights: nothing is read before the wait
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        waited = true;
+    }
+    long long pre_it = -1;
+    if constexpr (PRE) {
+        if (it + 1 < it_end) {
+            pre_it = it + 1;
+            const int prb = (int)(pre_it / KC), pkc = (int)(pre_it % KC);
+            uint8_t *sw = sk_stage + warp * 16 * SK_PRE_ROWB;
+            const int k = pkc * UNROLL * 32 + 8 * lane;
+            const bool in = k < p.K;
+#pragma unroll
+            for (int r = 0; r < 16; r++) {
+                const __half *src = Wt + (long long)min(prb * 16 + r, p.Nc - 1) * p.swn + (in ? k : 0);
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(
+                                 (unsigned)__cvta_generic_to_shared(sw + r * SK_PRE_ROWB + 16 * lane)),
+                             "l"(src), "r"(in ? 16 : 0)
+                             : "memory");
+            }
+            asm volatile("cp.async.commit_group;\n" ::: "memory");
+        }
+    }
     while (it < it_end) {
         const int rb = (int)(it / KC), kc0 = (int)(it % KC);
         const int kc1 = (int)min((long long)KC, kc0 + (it_end - it));
@@ -221,12 +253,23 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *_
                     if (TWO_NTILES) av1[u] = in ? __ldg(reinterpret_cast<const uint4 *>(a1 + k)) : z;
                 }
             } else {
+                if (PRE && (long long)rb * KC + kc == pre_it) {
+                    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+                    __syncwarp();
+                    const uint8_t *sw = sk_stage + warp * 16 * SK_PRE_ROWB + 16 * t;
 #pragma unroll
-                for (int u = 0; u < UNROLL; u++) {
-                    const int k = (kc * UNROLL + u) * 32 + 8 * t;
-                    const bool in = k < p.K;
-                    wv0[u] = in ? ldg_w16(w0 + k) : z;
-                    wv1[u] = in ? ldg_w16(w1 + k) : z;
+                    for (int u = 0; u < UNROLL; u++) {
+                        wv0[u] = *reinterpret_cast<const uint4 *>(sw + g * SK_PRE_ROWB + 64 * u);
+                        wv1[u] = *reinterpret_cast<const uint4 *>(sw + (g + 8) * SK_PRE_ROWB + 64 * u);
+                    }
+                } else {
+#pragma unroll
+                    for (int u = 0; u < UNROLL; u++) {
+                        const int k = (kc * UNROLL + u) * 32 + 8 * t;
+                        const bool in = k < p.K;
+                        wv0[u] = in ? ldg_w16(w0 + k) : z;
+                        wv1[u] = in ? ldg_w16(w1 + k) : z;
+                    }
                 }
                 if (!waited) {   // everything but the weights may come from the preceding kernel (the split kernel,
                                  // or the previous call of a decode chain): wait for it before the first access
@@ -594,6 +637,7 @@ static int skinny_t(SkinnyArgs p, cudaStream_t st) {
                 p.sak = 1;
             }
             if (sizeof(T) == 2) {
+                p.early_w = !queued_writes_overlap(d, p.w, ((size_t)(p.Nc - 1) * p.swn + p.K) * sizeof(T));
                 int *count = nullptr;
                 G9_TRY(skinny_counters((size_t)q.mtiles * q.RB, &count));
                 float *part = (float *)((char *)scr + a_bytes);
@@ -609,13 +653,15 @@ static int skinny_t(SkinnyArgs p, cudaStream_t st) {
                                                cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
                     attr[d->dev] = true;
                 }
+                static bool attr1[kMaxDevices] = {};
+                if (!two) G9_CU(smem_limit_once(wk_f16_sk<false, 8, ACT_F16, true>, SK_PRE_BYTES, attr1));
                 if (p.ndst == 1) {
                     if (two) launch_pdl(wk_f16_sk<true, 8, ACT_F16S, true>, grid, blk, smem, st, p, q.KC, q.maxc, part, count);
-                    else launch_pdl(wk_f16_sk<false, 8, ACT_F16, true>, grid, blk, 0, st, p, q.KC, q.maxc, part, count);
+                    else launch_pdl(wk_f16_sk<false, 8, ACT_F16, true>, grid, blk, SK_PRE_BYTES, st, p, q.KC, q.maxc, part, count);
                 } else if (two) {
                     wk_f16_sk<true, 8, ACT_F16S, true><<<grid, blk, smem, st>>>(p, q.KC, q.maxc, part, count);
                 } else {
-                    wk_f16_sk<false, 8, ACT_F16, true><<<grid, blk, 0, st>>>(p, q.KC, q.maxc, part, count);
+                    wk_f16_sk<false, 8, ACT_F16, true><<<grid, blk, SK_PRE_BYTES, st>>>(p, q.KC, q.maxc, part, count);
                 }
                 return launched("skinny_wk_f16_sk");
             }
@@ -724,10 +770,12 @@ __global__ void __launch_bounds__(SPLIT_THREADS) split_f32_rows(const float *__r
 
 template <bool TWO_NTILES, int UNROLL, int MODE, bool LAZY = false>
 static int launch_f32a_main(const SkinnyArgs &p, const SkPlan &q, float *part, int *count, cudaStream_t st) {
+    static bool attr[kMaxDevices] = {};
+    G9_CU(smem_limit_once(wk_f16_sk<TWO_NTILES, UNROLL, MODE, LAZY>, SK_PRE_BYTES, attr));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)q.ctas, q.mtiles);
     cfg.blockDim = dim3(WK_WARPS * 32);
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = SK_PRE_BYTES;
     cfg.stream = st;
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -756,6 +804,7 @@ int launch_skinny_f32a(int M, int N, int K, const float *A, int lda, const void 
     p.sam = Kp; p.sak = 1;
     p.alo = paired ? 0 : (long long)M * Kp;
     p.nf = nf;
+    p.early_w = !queued_writes_overlap(d, W, ((size_t)(N - 1) * ldw + Kp) * sizeof(__half));
     const SkPlan q = sk_plan(p.Mc, N, Kp, 8, d->sm_count);
     // Scratch layout: [hi, lo (2·M rows of Kp FP16) | row scales | stream-K partial tiles (FP32)].
     const size_t a_bytes = ((size_t)2 * M * Kp * sizeof(__half) + 255) / 256 * 256, s_bytes = 256;
@@ -793,6 +842,7 @@ int launch_skinny(int type, int tA, int tB, int M, int N, int K, double alpha, c
     p.alo = 0;
     p.tscale = nullptr;
     p.nf = nullptr;
+    p.early_w = 0;
     if (peers && npeers > 0) {
         if (npeers > 8) return fail(GEN9BLAS_ERR_INVALID_ARG, "at most 8 ranks for the fused skinny GEMM + all-gather");
         for (int q = 0; q < npeers; q++) p.dst[q] = peers[q];

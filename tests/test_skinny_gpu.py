@@ -55,3 +55,31 @@ def test_decoder_shapes(g9, M):
         C = g9.hgemm(A, W.T)
         ref = A.astype(np.float64) @ W.astype(np.float64).T
         assert err(C, ref) <= 4e-3, (M, N, K)
+
+
+def test_nowait_chain_weights_written_by_previous_call(gpu_lib):
+    """No-wait mode: gen9blas_gemm writes W (N × K, FP16) and the next call, a skinny GEMM C = A·Wᵀ, uses W as its
+    weights. The skinny kernel may load weights before waiting for the preceding kernel only when no queued call
+    writes them, so every round must see the new W. Rounds of fresh data, then gen9blas_flush; FP64 reference."""
+    torch = pytest.importorskip("torch")
+    g = torch.Generator(device="cuda").manual_seed(17)
+    N, K, R, M = 4096, 2048, 256, 4
+    X = torch.randn(N, R, device="cuda", generator=g, dtype=torch.float32).mul_(0.1).half()
+    Y = torch.randn(R, K, device="cuda", generator=g, dtype=torch.float32).mul_(0.1).half()
+    A = torch.randn(M, K, device="cuda", generator=g, dtype=torch.float32).half()
+    torch.cuda.synchronize()
+    for rnd in range(4):
+        W = torch.full((N, K), float("nan"), device="cuda", dtype=torch.float16)
+        C = torch.full((M, N), float("nan"), device="cuda", dtype=torch.float16)
+        X.mul_(-1.0)   # new weights every round
+        torch.cuda.synchronize()
+        gpu_lib.set_nowait(1)
+        try:
+            assert gpu_lib.gemm(0, 0, 0, N, K, R, 1.0, X.data_ptr(), R, Y.data_ptr(), K, 0.0, W.data_ptr(), K) == 0
+            assert gpu_lib.gemm(0, 0, 1, M, N, K, 1.0, A.data_ptr(), K, W.data_ptr(), K, 0.0, C.data_ptr(), N) == 0
+            assert gpu_lib.flush() == 0, gpu_lib.error()
+        finally:
+            gpu_lib.set_nowait(0)
+        ref = A.double() @ W.double().t()
+        assert bool(torch.isfinite(C).all()), rnd
+        assert float((C.double() - ref).abs().max() / ref.abs().max()) <= 4e-3, rnd
