@@ -120,6 +120,14 @@ GEN9BLAS_API int gen9blas_gemm_batched(int type, int tA, int tB, int M, int N, i
     const size_t bB = (c1 * sB + (tB ? (size_t)(N - 1) * ldb + K : (size_t)(K - 1) * ldb + N)) * es;
     const size_t bC = (c1 * sC + (size_t)(M - 1) * ldc + N) * es;
     timer_start();
+    // Large single GEMMs over several devices (gen9blas_set_devices / GEN9BLAS_DEVICES): column blocks per device
+    if (count == 1) {
+        const int r = gemm_sharded(type, tA, tB, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc);
+        if (r <= 0) {
+            timer_stop();
+            return r;
+        }
+    }
     // Large single GEMMs on host A and C: banded pipeline of copies and kernels
     if (count == 1 && !tA && M >= 1024 && N > skinny_threshold(type) && K > skinny_threshold(type) &&
         bA + bC >= ((size_t)16 << 20) && host_memory(A) && host_memory(C)) {

@@ -52,6 +52,8 @@ struct DevState {
     uintptr_t queued_lo[kQueuedRanges] = {}, queued_hi[kQueuedRanges] = {};
     int queued_n = 0;
     bool queued_overflow = false;
+    void *shard = nullptr;                                     // operand copies of a column-sharded GEMM (grow-only)
+    size_t shard_n = 0;
 };
 
 // Process-wide call state (the caller serialises calls, as for the reference).
@@ -117,6 +119,14 @@ int finish_op(Operand *ops, int n);
 void queued_writes_add(DevState *d, const void *p, size_t bytes);
 void queued_writes_clear(DevState *d);
 bool queued_writes_overlap(DevState *d, const void *p, size_t bytes);
+// Turns the device error word of d (set by bounded device-side waits that gave up) into a status; clears it.
+int check_dev_err(DevState *d);
+// Grow-only device buffer of the current device (waits for the library's stream before it grows).
+int ensure_buffer(void **p, size_t *n, size_t bytes);
+// Column-sharded GEMM over the devices set with gen9blas_set_devices / GEN9BLAS_DEVICES: returns 1 when the call does
+// not qualify (fewer than two devices, batched, skinny or below the size threshold), else 0 or a negative status.
+int gemm_sharded(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, const void *B,
+                 int ldb, double beta, void *C, int ldc);
 // Scratch buffer of at least `bytes` on the current device (grow-only). Waits for queued work before growing.
 int scratch(size_t bytes, void **p);
 // Device buffer of staging slot `slot` (the one map_operand uses for host operands), at least `bytes` (grow-only).

@@ -173,6 +173,8 @@ static int ensure_dev_buf(void **p, size_t *n, size_t bytes) {
     return 0;
 }
 
+int ensure_buffer(void **p, size_t *n, size_t bytes) { return ensure_dev_buf(p, n, bytes); }
+
 int scratch(size_t bytes, void **p) {
     DevState *d = dev_state();
     if (!d) return G.status;
@@ -251,7 +253,7 @@ int map_operand(Operand &op, const void *p, size_t bytes, int slot, bool copy_in
     return 0;
 }
 
-static int check_dev_err(DevState *d) {
+int check_dev_err(DevState *d) {
     if (fault_mode() == kFaultWait) *(volatile unsigned *)d->err_host = kDevErrWaitTimeout;
     unsigned v = *(volatile unsigned *)d->err_host;
     if (v != kDevErrNone) {

@@ -171,6 +171,17 @@ GEN9BLAS_API int gen9blas_set_stream(void *cuda_stream);
  * (or any synchronisation of the stream). Calls with host operands still wait. */
 GEN9BLAS_API void gen9blas_set_nowait(int on);
 GEN9BLAS_API int gen9blas_flush(void);
+/* Several GPUs behind one process's calls (the reference's entry point, lib/src/gemm.c:177-180, drives one device).
+ * After gen9blas_set_devices(n, ids) with n >= 2 -- or with GEN9BLAS_DEVICES="0,1,..." in the environment, read at
+ * the first GEMM -- a gen9blas_gemm / gen9blas_hgemm / gen9blas_sgemm with count 1, min(M, N) above the skinny
+ * threshold and 2·M·N·K of at least GEN9BLAS_SHARD_MIN_FLOP (default 2·4096³) is split by column blocks of B and C
+ * (multiples of 256 columns) over the listed devices: each computes its block with its own kernels on its own
+ * memory, operands reach it by peer copies (NVLink) or host copies, and an operand already in a device's memory is
+ * read there in place. Such a call always waits for every device (no-wait mode does not apply to it). ids: CUDA
+ * device ordinals (at most 8, distinct, sm_100); n <= 1 turns sharding off. Returns 0 or GEN9BLAS_ERR_INVALID_ARG /
+ * GEN9BLAS_ERR_NO_DEVICE. gen9blas_get_devices copies up to max ids and returns how many are set (0: none). */
+GEN9BLAS_API int gen9blas_set_devices(int n, const int *ids);
+GEN9BLAS_API int gen9blas_get_devices(int *ids, int max);
 /* Multi-GPU, one process per GPU (no counterpart in the reference, which drives one device).
  * Device buffers that other ranks write into: any cudaMalloc memory (gen9blas_dev_alloc, torch tensors). For a
  * pointer into such memory gen9blas_ipc_handle fills a 64-byte CUDA IPC handle of its allocation and the pointer's

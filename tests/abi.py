@@ -20,6 +20,7 @@ SIGNATURES = {
     "ger": ([_i, _i, _i, _d, _p, _i, _p, _i, _p, _i], _i),
     "set_device": ([_i], _i), "get_device": ([], _i), "set_stream": ([_p], _i), "set_nowait": ([_i], None),
     "flush": ([], _i), "kernel_launches": ([], ctypes.c_longlong),
+    "set_devices": ([_i, ctypes.POINTER(_i)], _i), "get_devices": ([ctypes.POINTER(_i), _i], _i),
     "selftest_wait": ([_d], _i),
     "gemv_noalloc": ([_i, _i, _i, _i, _d, _p, _i, _p, _i, _d, _p, _i], _i),
     "peer_barrier": ([_p, _i, _i, _d], _i),

@@ -380,7 +380,37 @@ def group_config():
     return out
 
 
+def group_sharded():
+    """Large GEMMs through the CBLAS entry points, for a run with GEN9BLAS_DEVICES set (column blocks per GPU):
+    cblas_sgemm n = 8192 row-major and cblas_dgemm n = 4096 column-major with alpha 1.5, beta 0.5, against FP64 on
+    sampled rows."""
+    rng = np.random.default_rng(12)
+    out = {}
+    f = L.cblas_sgemm
+    f.argtypes = [I, I, I, I, I, I, ctypes.c_float, P, I, P, I, ctypes.c_float, P, I]
+    n = 8192
+    A = rng.uniform(-1, 1, (n, n)).astype(np.float32)
+    B = rng.uniform(-1, 1, (n, n)).astype(np.float32)
+    C = np.zeros((n, n), np.float32)
+    f(RowMajor, NoTrans, NoTrans, n, n, n, 1.0, A.ctypes.data, n, B.ctypes.data, n, 0.0, C.ctypes.data, n)
+    rows = rng.choice(n, 32, replace=False)
+    a64, b64 = A[rows].astype(np.float64), B.astype(np.float64)
+    out["sgemm_8192"] = rel(C[rows], a64 @ b64, np.abs(a64) @ np.abs(b64))
+    f = L.cblas_dgemm
+    f.argtypes = [I, I, I, I, I, I, ctypes.c_double, P, I, P, I, ctypes.c_double, P, I]
+    n = 4096
+    A, B, C0 = (np.asfortranarray(rng.uniform(-1, 1, (n, n))) for _ in range(3))
+    Cf = C0.copy(order="F")
+    f(ColMajor, NoTrans, Trans, n, n, n, 1.5, A.ctypes.data, n, B.ctypes.data, n, 0.5, Cf.ctypes.data, n)
+    rows = rng.choice(n, 16, replace=False)
+    ref = 1.5 * A[rows] @ B.T + 0.5 * C0[rows]
+    sc = 1.5 * np.abs(A[rows]) @ np.abs(B.T) + 0.5 * np.abs(C0[rows])
+    out["dgemm_4096_col"] = rel(Cf[rows], ref, sc)
+    return out
+
+
 if __name__ == "__main__":
     groups = {"cblas_gemm": group_cblas_gemm, "fortran_l12": group_fortran_and_l12, "forwarded": group_forwarded,
-              "level3": group_level3, "l2x": group_l2x, "config": group_config}
+              "level3": group_level3, "l2x": group_l2x, "config": group_config,
+              "sharded": group_sharded}
     print(json.dumps(groups[sys.argv[1]]()))

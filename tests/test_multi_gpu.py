@@ -140,3 +140,98 @@ def test_one_process_switches_devices():
     assert r.returncode == 0, r.stderr[-2000:]
     worst = float([ln for ln in r.stdout.splitlines() if ln.startswith("WORST")][0].split()[1])
     assert worst <= 1e-3, worst
+
+
+SHARD_CHILD = r'''
+import ctypes, os, sys
+import numpy as np
+import torch
+sys.path.insert(0, os.path.join(sys.argv[1], "tests"))
+sys.path.insert(0, os.path.join(sys.argv[1], "gen9-gpu-blas_b200"))
+import abi
+L = abi.bind(ctypes.CDLL(os.path.join(sys.argv[1], "gen9-gpu-blas_b200", "libgen9blas.so")), "gen9blas_")
+assert L.init() == 0, L.error()
+ids = (ctypes.c_int * 8)()
+assert L.get_devices(ids, 8) == 2 and list(ids[:2]) == [0, 1]       # from GEN9BLAS_DEVICES
+free1 = torch.cuda.mem_get_info(1)[0]
+rng = np.random.default_rng(3)
+out = {}
+def err(C, A64, B64, rows, alpha=1.0, beta=0.0, C0=None):
+    ref = alpha * A64[rows] @ B64 + (beta * C0[rows] if C0 is not None else 0)
+    sc = abs(alpha) * np.abs(A64[rows]) @ np.abs(B64) + (abs(beta) * np.abs(C0[rows]) if C0 is not None else 0)
+    return float((np.abs(C[rows].astype(np.float64) - ref) / sc).max())
+# FP16, host operands, n = 8192 (two 4096-column blocks)
+n = 8192
+A = (rng.standard_normal((n, n)) / np.sqrt(n)).astype(np.float16)
+B = (rng.standard_normal((n, n)) / np.sqrt(n)).astype(np.float16)
+C = np.zeros((n, n), np.float16)
+assert L.gemm(0, 0, 0, n, n, n, 1.0, A.ctypes.data, n, B.ctypes.data, n, 0.0, C.ctypes.data, n) == 0, L.error()
+rows = np.concatenate([rng.choice(n, 48, replace=False), [0, n - 1]])
+out["h_host"] = err(C, A.astype(np.float64), B.astype(np.float64), rows)
+out["dev1_used_mb"] = (free1 - torch.cuda.mem_get_info(1)[0]) / 2**20
+# FP32, ragged N (blocks of 4096 and 3904), transposed A, beta != 0 on a padded C, operands on device 0 (torch)
+M, N, K = 4100, 8000, 3000
+At = torch.rand(K, M, device="cuda:0", dtype=torch.float32) * 2 - 1      # stored K x M: op(A) = At^T
+Bd = torch.rand(K, N, device="cuda:0", dtype=torch.float32) * 2 - 1
+C0 = torch.rand(M, N + 5, device="cuda:0", dtype=torch.float32) * 2 - 1
+Cd = C0.clone()
+torch.cuda.synchronize()
+assert L.gemm(1, 1, 0, M, N, K, 1.5, At.data_ptr(), M, Bd.data_ptr(), N, 0.5, Cd.data_ptr(), N + 5) == 0, L.error()
+r2 = np.concatenate([rng.choice(M, 40, replace=False), [M - 1]])
+out["s_dev_ragged"] = err(Cd[:, :N].cpu().numpy(), At.t().double().cpu().numpy(), Bd.double().cpu().numpy(), r2,
+                          1.5, 0.5, C0[:, :N].double().cpu().numpy())
+out["s_padding_kept"] = bool((Cd[:, N:] == C0[:, N:]).all())
+# FP64 with B on device 1 (read there in place, copied to device 0 for the other block), transposed B
+Kd, Nd, Md = 2048, 4608, 4096
+Bt1 = torch.rand(Nd, Kd, device="cuda:1", dtype=torch.float64) * 2 - 1   # stored N x K: op(B) = Bt1^T
+A0 = torch.rand(Md, Kd, device="cuda:0", dtype=torch.float64) * 2 - 1
+C1 = torch.zeros(Md, Nd, device="cuda:0", dtype=torch.float64)
+torch.cuda.synchronize(0); torch.cuda.synchronize(1)
+assert L.gemm(3, 0, 1, Md, Nd, Kd, 1.0, A0.data_ptr(), Kd, Bt1.data_ptr(), Kd, 0.0, C1.data_ptr(), Nd) == 0, L.error()
+r3 = np.concatenate([rng.choice(Md, 32, replace=False), [Md - 1]])
+out["d_b_on_dev1"] = err(C1.cpu().numpy(), A0.cpu().numpy(), Bt1.t().cpu().numpy(), r3)
+# the NumPy module: hgemm on managed arrays (gen9blas.empty) at n = 8192
+import gen9blas
+Am = gen9blas.empty((n, n), np.float16); Am[...] = A
+Bm = gen9blas.empty((n, n), np.float16); Bm[...] = B
+Cm = gen9blas.hgemm(Am, Bm)
+out["h_module_managed"] = err(Cm, A.astype(np.float64), B.astype(np.float64), rows)
+# turning sharding off through the API
+assert L.set_devices(1, None) == 0 and L.get_devices(ids, 8) == 0
+bad = (ctypes.c_int * 2)(0, 0)
+assert L.set_devices(2, bad) == -3 and b"twice" in L.error()
+print("OUT", repr(out))
+'''
+
+
+def test_sharded_gemm_two_devices_one_process():
+    """GEN9BLAS_DEVICES=0,1 in one process: gen9blas_gemm splits large GEMMs by column blocks over both GPUs --
+    FP16 n = 8192 from host memory, FP32 with a ragged last block, transposed A, beta on a padded C, FP64 with B owned
+    by the second GPU, and the NumPy module on managed arrays -- each against FP64 with the north-star limits."""
+    torch = pytest.importorskip("torch")
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    env = dict(os.environ, GEN9BLAS_DEVICES="0,1", GEN9BLAS_SHARD_MIN_FLOP="1e10")
+    r = subprocess.run([sys.executable, "-c", SHARD_CHILD, ROOT], capture_output=True, text=True, timeout=600, env=env)
+    assert r.returncode == 0, r.stderr[-3000:]
+    import ast
+    out = ast.literal_eval([ln for ln in r.stdout.splitlines() if ln.startswith("OUT")][0][4:])
+    assert out["h_host"] <= 1e-3 and out["h_module_managed"] <= 1e-3, out
+    assert out["s_dev_ragged"] <= 1e-6 and out["s_padding_kept"], out
+    assert out["d_b_on_dev1"] <= 1e-13, out
+    assert out["dev1_used_mb"] > 100, out      # the second GPU held its operand copies
+
+
+def test_sharded_gemm_through_cblas_two_devices():
+    """The LD_PRELOAD library with GEN9BLAS_DEVICES=0,1: cblas_sgemm n = 8192 (row-major) and cblas_dgemm n = 4096
+    (column-major, alpha 1.5, beta 0.5) split over two GPUs, against FP64."""
+    torch = pytest.importorskip("torch")
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    env = dict(os.environ, GEN9BLAS_DEVICES="0,1", GEN9BLAS_BLAS="gpu")
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "tests", "shim_child.py"), "sharded"], capture_output=True,
+                       text=True, timeout=600, env=env)
+    assert r.returncode == 0, r.stderr[-3000:]
+    import json
+    res = json.loads(r.stdout.strip().splitlines()[-1])
+    assert res["sgemm_8192"] <= 1e-6 and res["dgemm_4096_col"] <= 1e-13, res
