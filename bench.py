@@ -329,10 +329,9 @@ def run_ours(args):
         return run_rows(args, torch)
     torch.cuda.set_device(local)
     if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+        sys.path.insert(0, PKG)
+        import g9dist   # process group with a finite timeout; failures raise g9dist.CommError with a status
+        g9dist.init_comm("nccl", timeout_s=120.0, device_id=torch.device("cuda", local))
     L = load_lib()
     assert L.set_device(local) == 0, L.error()
     stream = torch.cuda.Stream()

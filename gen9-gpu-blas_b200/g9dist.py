@@ -9,13 +9,86 @@ The reference is single-device (README.md:176-178); this module adds the scale-o
   C[:, rows_g] with the skinny kernel, then one all-gather of the small M × N/g outputs.
 The partition arithmetic (shard bounds, gather layout, re-layout) is plain Python/torch so that it can be tested with
 gloo ranks on the CPU (tests/test_dist_cpu.py) with a CPU stand-in for the local product.
+
+Failure detection (the analogue of the reference's bounded GPU wait, lib/kcl.c:361-372): init_comm starts the process
+group with a finite timeout, and every collective of these paths is waited for on the host with a deadline, polling the
+backend's completion (an error the backend records -- NCCL's asynchronous error, a failed peer -- surfaces there). A
+failure or a missed deadline raises CommError, whose `status` is the library's GEN9BLAS_ERR and `stage` says where
+("init", "collective" or "timeout"). GEN9BLAS_FAULT=nccl_init or nccl_op makes this rank fail there on purpose (host
+side only; the other ranks then see their deadline pass).
 """
 import ctypes
+import datetime
+import os
+import time
 
 import torch
 
 GEN9BLAS_H, GEN9BLAS_S, GEN9BLAS_HS, GEN9BLAS_D = 0, 1, 2, 3
+GEN9BLAS_ERR = -1   # status of a failed or timed-out collective (the 0.2 API's execution-error code)
 _KIND = {torch.float16: GEN9BLAS_H, torch.float32: GEN9BLAS_S, torch.float64: GEN9BLAS_D}
+DEFAULT_TIMEOUT_S = 60.0
+
+
+class CommError(RuntimeError):
+    """A collective of the multi-GPU path failed or missed its deadline. status: the gen9blas status code;
+    stage: "init", "collective" or "timeout"."""
+
+    def __init__(self, stage, message, status=GEN9BLAS_ERR):
+        super().__init__(f"{stage}: {message}")
+        self.stage, self.status = stage, status
+
+
+def _fault():
+    v = os.environ.get("GEN9BLAS_FAULT", "")
+    return v if v in ("nccl_init", "nccl_op") else ""
+
+
+def init_comm(backend="nccl", timeout_s=DEFAULT_TIMEOUT_S, **kwargs):
+    """torch.distributed.init_process_group(backend) with a finite timeout (rendezvous and collectives); a failure,
+    or GEN9BLAS_FAULT=nccl_init, raises CommError(stage "init")."""
+    if _fault() == "nccl_init":
+        raise CommError("init", "communicator initialisation failed (injected: GEN9BLAS_FAULT=nccl_init)")
+    try:
+        torch.distributed.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s), **kwargs)
+    except Exception as e:   # rendezvous timeout, backend error
+        raise CommError("init", f"init_process_group({backend}) failed: {e}") from e
+
+
+def _issue(fn, what):
+    """Starts one asynchronous collective; GEN9BLAS_FAULT=nccl_op makes this rank fail instead of taking part."""
+    if _fault() == "nccl_op":
+        raise CommError("collective", f"{what} failed (injected: GEN9BLAS_FAULT=nccl_op)")
+    try:
+        return fn()
+    except Exception as e:
+        raise CommError("collective", f"{what}: {e}") from e
+
+
+def _finish(works, timeout_s, what):
+    """Waits on the host for the given collectives until timeout_s (None: no deadline, stream-ordered wait only);
+    backend errors and a missed deadline raise CommError."""
+    if timeout_s is None:
+        for w in works:
+            w.wait()
+        return
+    deadline = time.monotonic() + timeout_s
+    for w in works:
+        while True:
+            try:
+                done = w.is_completed()
+            except Exception as e:
+                raise CommError("collective", f"{what}: {e}") from e
+            if done:
+                break
+            if time.monotonic() > deadline:
+                raise CommError("timeout", f"{what} did not complete within {timeout_s:g} s (a rank failed, left or "
+                                           "never joined)")
+            time.sleep(0.0002)
+        try:
+            w.wait()   # raises what the backend recorded for a failed collective
+        except Exception as e:
+            raise CommError("collective", f"{what}: {e}") from e
 
 
 def shard_bounds(n, world, align=1):
@@ -47,13 +120,15 @@ def gemm_local(lib, A, B, C, alpha=1.0, beta=0.0, accurate=False):
         raise RuntimeError(lib.gen9blas_error().decode())
 
 
-def column_sharded_gemm(A, B_shard, C, rank, world, local_gemm, group=None, chunks=4, comm_stream=None):
+def column_sharded_gemm(A, B_shard, C, rank, world, local_gemm, group=None, chunks=4, comm_stream=None,
+                        timeout_s=DEFAULT_TIMEOUT_S):
     """C (M × N, row-major, every rank) = A (M × K) · B, where this rank holds B_shard = B[:, cols_rank].
 
     All ranks hold equal-width shards (N divisible by world). The shard is computed in `chunks` column pieces into a
     chunk-major buffer; after each piece its all-gather starts on `comm_stream` while the next piece computes. The
     gathered pieces are then copied into C's row-major layout. local_gemm(A, B_piece, C_piece) computes one piece.
-    Returns C."""
+    The gathers are waited for on the host (deadline timeout_s; None: stream-ordered only); a failure raises
+    CommError. Returns C."""
     M = A.shape[0]
     nb = B_shard.shape[1]
     N = nb * world
@@ -75,18 +150,17 @@ def column_sharded_gemm(A, B_shard, C, rank, world, local_gemm, group=None, chun
     works = []
     for c, (a, b) in enumerate([ab for ab in bounds if ab[1] > ab[0]]):
         local_gemm(A, B_shard[:, a:b], Cs[c])
+        gather = (lambda c=c: torch.distributed.all_gather_into_tensor(Cg[c].view(world * M, cw), Cs[c], group=group,
+                                                                       async_op=True))
         if use_streams:
             ev = torch.cuda.Event()
             ev.record(main)
             comm_stream.wait_event(ev)
             with torch.cuda.stream(comm_stream):
-                works.append(torch.distributed.all_gather_into_tensor(Cg[c].view(world * M, cw), Cs[c], group=group,
-                                                                      async_op=True))
+                works.append(_issue(gather, f"all-gather of column piece {c}"))
         else:
-            works.append(torch.distributed.all_gather_into_tensor(Cg[c].view(world * M, cw), Cs[c], group=group,
-                                                                      async_op=True))
-    for w in works:
-        w.wait()
+            works.append(_issue(gather, f"all-gather of column piece {c}"))
+    _finish(works, timeout_s, "column all-gather")
     if use_streams:
         main.wait_stream(comm_stream)
     # gathered piece (chunk c, rank q) holds C[:, q*nb + c*cw : + cw]
@@ -94,9 +168,10 @@ def column_sharded_gemm(A, B_shard, C, rank, world, local_gemm, group=None, chun
     return C
 
 
-def row_sharded_skinny(A, W_shard, C, rank, world, local_skinny, group=None):
+def row_sharded_skinny(A, W_shard, C, rank, world, local_skinny, group=None, timeout_s=DEFAULT_TIMEOUT_S):
     """C (M × N) = A (M × K) · Wᵀ with W (N × K) split into row blocks: this rank holds W_shard = W[rows_rank] and
-    computes C[:, rows_rank]; one all-gather of the M × N/world outputs, then a re-layout. Returns C."""
+    computes C[:, rows_rank]; one all-gather of the M × N/world outputs (host deadline timeout_s, CommError on
+    failure), then a re-layout. Returns C."""
     M = A.shape[0]
     nr = W_shard.shape[0]
     N = nr * world
@@ -107,7 +182,9 @@ def row_sharded_skinny(A, W_shard, C, rank, world, local_skinny, group=None):
     Cs = torch.empty((M, nr), dtype=C.dtype, device=C.device)
     local_skinny(A, W_shard, Cs)
     Cg = torch.empty((world, M, nr), dtype=C.dtype, device=C.device)
-    torch.distributed.all_gather_into_tensor(Cg.view(world * M, nr), Cs, group=group)
+    w = _issue(lambda: torch.distributed.all_gather_into_tensor(Cg.view(world * M, nr), Cs, group=group,
+                                                                async_op=True), "all-gather of the output rows")
+    _finish([w], timeout_s, "output all-gather")
     C.view(M, world, nr).copy_(Cg.permute(1, 0, 2))
     return C
 
@@ -165,8 +242,8 @@ class PeerBarrier:
 
     def wait(self):
         r = self.lib.gen9blas_peer_barrier(self.arr, self.world, self.rank, self.timeout_ms)
-        if r != 0:
-            raise RuntimeError(self.lib.gen9blas_error().decode())
+        if r != 0:   # e.g. the device-side wait gave up: a rank never arrived
+            raise CommError("collective", "peer barrier: " + self.lib.gen9blas_error().decode(), status=r)
 
     def close(self):
         self.view.close()
@@ -204,7 +281,7 @@ def _allgather(lib, A, B, transB, C, peers, col_off, accurate):
                                     A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), arr, world,
                                     C.stride(0), col_off)
     if r != 0:
-        raise RuntimeError(lib.gen9blas_error().decode())
+        raise CommError("collective", "gen9blas_gemm_allgather: " + lib.gen9blas_error().decode(), status=r)
 
 
 def _meet(C, world, group, barrier):
@@ -212,7 +289,8 @@ def _meet(C, world, group, barrier):
     if world == 1:
         return
     if barrier is not None:
-        barrier.wait()
+        barrier.wait()   # bounded on the device: a rank that never arrives makes the call return GEN9BLAS_ERR
     else:
         flag = torch.ones(1, device=C.device)
-        torch.distributed.all_reduce(flag, group=group)
+        w = _issue(lambda: torch.distributed.all_reduce(flag, group=group, async_op=True), "rank meeting")
+        _finish([w], DEFAULT_TIMEOUT_S, "rank meeting")
