@@ -909,14 +909,8 @@ static int hgemm_tc_impl(int type, int tA, int tB, int M, int N, int K, double a
         p.split = split;
         p.units = (int)units;
         if (split > 1) {
-            if (!d->gemm_flags) {
-                G9_CU(cudaMalloc((void **)&d->gemm_flags, 4096 * sizeof(unsigned)));
-                G9_CU(cudaMemsetAsync(d->gemm_flags, 0, 4096 * sizeof(unsigned), st));
-            }
-            if (++d->gemm_epoch == 0) d->gemm_epoch = 1;
+            G9_TRY(gemm_handoff(d, st, &p.flags, &p.epoch));
             p.partial = (float *)((char *)scr + bytesA + bytesB);
-            p.flags = d->gemm_flags;
-            p.epoch = d->gemm_epoch;
         }
         const int grid2 = 2 * (int)(units < pairs ? units : pairs);
         if (type == GEN9BLAS_H) return bn == 256 ? launch_pair<true, 256>(mA, mB, mC, p, grid2, st)

@@ -119,6 +119,10 @@ int finish_op(Operand *ops, int n);
 void queued_writes_add(DevState *d, const void *p, size_t bytes);
 void queued_writes_clear(DevState *d);
 bool queued_writes_overlap(DevState *d, const void *p, size_t bytes);
+// Hand-over flags of the GEMM kernels that split tiles over CTAs (kGemmFlags zeroed words, created on first use) and
+// the epoch of the launch about to be enqueued (never 0).
+constexpr int kGemmFlags = 4096;
+int gemm_handoff(DevState *d, cudaStream_t st, unsigned **flags, unsigned *epoch);
 // Turns the device error word of d (set by bounded device-side waits that gave up) into a status; clears it.
 int check_dev_err(DevState *d);
 // Grow-only device buffer of the current device (waits for the library's stream before it grows).

@@ -175,6 +175,17 @@ static int ensure_dev_buf(void **p, size_t *n, size_t bytes) {
 
 int ensure_buffer(void **p, size_t *n, size_t bytes) { return ensure_dev_buf(p, n, bytes); }
 
+int gemm_handoff(DevState *d, cudaStream_t st, unsigned **flags, unsigned *epoch) {
+    if (!d->gemm_flags) {
+        G9_CU(cudaMalloc((void **)&d->gemm_flags, kGemmFlags * sizeof(unsigned)));
+        G9_CU(cudaMemsetAsync(d->gemm_flags, 0, kGemmFlags * sizeof(unsigned), st));
+    }
+    if (++d->gemm_epoch == 0) d->gemm_epoch = 1;
+    *flags = d->gemm_flags;
+    *epoch = d->gemm_epoch;
+    return 0;
+}
+
 int scratch(size_t bytes, void **p) {
     DevState *d = dev_state();
     if (!d) return G.status;

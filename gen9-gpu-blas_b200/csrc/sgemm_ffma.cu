@@ -132,38 +132,19 @@ template <bool KCONT, bool VEC, int BK> struct TileLoader {
     }
 };
 
-// partial == nullptr: C = alpha·op(A)·op(B) + beta·C over the whole K (blockIdx.z = batch index).
-// partial != nullptr: split K (count == 1): CTA z sums k in [z·kper, (z+1)·kper) and stores its raw tile to
-// partial[z] (M × N, dense).
+// Main loop of one 128 × 128 tile over k in [kbeg, kend): acc2[i][q] = outputs (row i, columns 2q and 2q + 1) of the
+// thread's 8 × 8 block as FP32 pairs, accumulated in k order. The shared-memory ring must be free on entry (the caller
+// synchronises between tiles); on return every cp.async group has completed.
 template <bool TA, bool TB, bool VA, bool VB, int BK, int STAGES>
-__global__ void __launch_bounds__(sg::THREADS, 2)
-sgemm_ffma_kernel(int M, int N, int K, float alpha, const float *__restrict__ A, long long lda, long long sA,
-                  const float *__restrict__ B, long long ldb, long long sB, float beta, float *C, long long ldc,
-                  long long sC, int c_vec, int kper, float *__restrict__ partial) {
+__device__ __forceinline__ void sg_mainloop(const float *A, long long lda, const float *B, long long ldb, int M, int N,
+                                            int m0, int n0, int kbeg, int kend, float *smem,
+                                            unsigned long long (&acc2)[8][4]) {
     using namespace sg;
-    // Programmatic dependent launch: the next kernel may start while this one runs (it waits before its own loads);
-    // this one waits for its predecessor before the first operand access.
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    extern __shared__ __align__(16) float sg_smem[];
-    float(*As)[BK][LDS_] = reinterpret_cast<float(*)[BK][LDS_]>(sg_smem);
-    float(*Bs)[BK][LDS_] = reinterpret_cast<float(*)[BK][LDS_]>(sg_smem + STAGES * BK * LDS_);
-
-    const int z = blockIdx.z;
-    int kbeg = 0, kend = K;
-    if (partial) {
-        kbeg = z * kper;
-        kend = min(K, kbeg + kper);
-    } else {
-        A += z * sA;
-        B += z * sB;
-        C += z * sC;
-    }
-    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    float(*As)[BK][LDS_] = reinterpret_cast<float(*)[BK][LDS_]>(smem);
+    float(*Bs)[BK][LDS_] = reinterpret_cast<float(*)[BK][LDS_]>(smem + STAGES * BK * LDS_);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int rm = (warp >> 1) * 16 + (lane >> 3) * 4;   // first row of the thread's upper quadrants
     const int cn = (warp & 1) * 32 + (lane & 7) * 4;     // first column of the thread's left quadrants
-
     TileLoader<!TA, VA, BK> la;
     TileLoader<TB, VB, BK> lb;
     la.init(A, lda, M, m0, kbeg, tid);
@@ -174,14 +155,10 @@ sgemm_ffma_kernel(int M, int N, int K, float alpha, const float *__restrict__ A,
         la.issue(&As[stage][0][0], t, krem);
         lb.issue(&Bs[stage][0][0], t, krem);
     };
-
-    // acc2[i][q]: outputs (row i, columns 2q and 2q + 1) of the thread's 8×8 block as one FP32 pair.
-    unsigned long long acc2[8][4];
 #pragma unroll
     for (int i = 0; i < 8; i++)
 #pragma unroll
         for (int q = 0; q < 4; q++) acc2[i][q] = 0ull;
-
     const int nk = (kend - kbeg + BK - 1) / BK;
 #pragma unroll
     for (int s = 0; s < STAGES - 1; s++) {
@@ -215,7 +192,15 @@ sgemm_ffma_kernel(int M, int N, int K, float alpha, const float *__restrict__ A,
         }
     }
     cp_wait<0>();
+}
 
+// Epilogue of a tile: C = alpha·acc + beta·C (beta = 0: C is not read), or (partial != nullptr) the raw sums into the
+// dense M × N partial matrix.
+__device__ __forceinline__ void sg_store(const unsigned long long (&acc2)[8][4], int M, int N, int m0, int n0,
+                                         float alpha, float beta, float *C, long long ldc, int c_vec, float *partial) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int rm = (warp >> 1) * 16 + (lane >> 3) * 4;
+    const int cn = (warp & 1) * 32 + (lane & 7) * 4;
 #pragma unroll
     for (int i = 0; i < 8; i++) {
         const int m = m0 + rm + (i & 3) + (i >> 2) * 64;
@@ -226,7 +211,7 @@ sgemm_ffma_kernel(int M, int N, int K, float alpha, const float *__restrict__ A,
             const float2 v01 = f2_unpack(acc2[i][2 * h]), v23 = f2_unpack(acc2[i][2 * h + 1]);
             const float v[4] = {v01.x, v01.y, v23.x, v23.y};
             if (partial) {
-                float *p = partial + ((long long)z * M + m) * N + n;
+                float *p = partial + (long long)m * N + n;
                 if (c_vec && n + 3 < N) {
                     *reinterpret_cast<float4 *>(p) = make_float4(v[0], v[1], v[2], v[3]);
                 } else {
@@ -256,6 +241,131 @@ sgemm_ffma_kernel(int M, int N, int K, float alpha, const float *__restrict__ A,
     }
 }
 
+// partial == nullptr: C = alpha·op(A)·op(B) + beta·C over the whole K (blockIdx.z = batch index).
+// partial != nullptr: split K (count == 1): CTA z sums k in [z·kper, (z+1)·kper) and stores its raw tile to
+// partial[z] (M × N, dense).
+template <bool TA, bool TB, bool VA, bool VB, int BK, int STAGES>
+__global__ void __launch_bounds__(sg::THREADS, 2)
+sgemm_ffma_kernel(int M, int N, int K, float alpha, const float *__restrict__ A, long long lda, long long sA,
+                  const float *__restrict__ B, long long ldb, long long sB, float beta, float *C, long long ldc,
+                  long long sC, int c_vec, int kper, float *__restrict__ partial) {
+    using namespace sg;
+    // Programmatic dependent launch: the next kernel may start while this one runs (it waits before its own loads);
+    // this one waits for its predecessor before the first operand access.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    extern __shared__ __align__(16) float sg_smem[];
+    const int z = blockIdx.z;
+    int kbeg = 0, kend = K;
+    if (partial) {
+        kbeg = z * kper;
+        kend = min(K, kbeg + kper);
+        partial += (long long)z * M * N;
+    } else {
+        A += z * sA;
+        B += z * sB;
+        C += z * sC;
+    }
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    unsigned long long acc2[8][4];
+    sg_mainloop<TA, TB, VA, VB, BK, STAGES>(A, lda, B, ldb, M, N, m0, n0, kbeg, kend, sg_smem, acc2);
+    sg_store(acc2, M, N, m0, n0, alpha, beta, C, ldc, c_vec, partial);
+}
+
+// Stream-K SGEMM for grids of less than one wave (count == 1): the tiles × KI iterations (KI = K chunks of BK) in
+// (tile, k) order are split evenly over a one-wave grid (CTA c owns [T·c/G, T·(c+1)/G)), so every SM does the same
+// number of FMAs whatever the tile count. A tile lying wholly in a CTA is stored directly. A tile shared by several
+// CTAs is finished by the CTA that owns its first chunk, which reaches it in its last segment: each later CTA meets
+// the tile in its first segment, leaves its FP32 partial sums in a slot of `part` and raises the slot's flag with
+// this launch's epoch (release); the finisher waits for the flags (acquire, bounded: 4 s, then the device error word
+// is set and the tile is not stored) and adds the slots in CTA order (deterministic) before the epilogue.
+template <bool TA, bool TB, bool VA, bool VB, int BK, int STAGES>
+__global__ void __launch_bounds__(sg::THREADS, 2)
+sgemm_sk_kernel(int M, int N, int K, float alpha, const float *__restrict__ A, long long lda,
+                const float *__restrict__ B, long long ldb, float beta, float *C, long long ldc, int c_vec, int tiles_n,
+                int KI, int maxc, float *__restrict__ part, unsigned *flags, unsigned epoch, unsigned *err) {
+    using namespace sg;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    extern __shared__ __align__(16) float sg_smem[];
+    __shared__ int abort_flag;
+    const int G_ = gridDim.x, c = blockIdx.x, tid = threadIdx.x;
+    const long long tiles = (long long)tiles_n * ((M + BM - 1) / BM);
+    const long long T = tiles * KI;
+    long long x = T * c / G_;
+    const long long x1 = T * (c + 1) / G_;
+    unsigned long long acc2[8][4];
+    while (x < x1) {
+        const long long tile = x / KI;
+        const int k0 = (int)(x % KI), k1 = (int)min((long long)KI, k0 + (x1 - x));
+        const int m0 = (int)(tile / tiles_n) * BM, n0 = (int)(tile % tiles_n) * BN;
+        __syncthreads();   // the previous segment's stages have been read
+        sg_mainloop<TA, TB, VA, VB, BK, STAGES>(A, lda, B, ldb, M, N, m0, n0, k0 * BK, min(K, k1 * BK), sg_smem, acc2);
+        const long long y0 = tile * KI;
+        const int cf = (int)(((y0 + 1) * G_ - 1) / T), cl = (int)(((y0 + KI) * G_ - 1) / T);   // first / last CTA
+        // slot layout: element pair q of thread tid at [q][tid] (coalesced float2 accesses)
+        if (k0 > 0) {   // a later part of the tile: hand the partial sums over
+            float2 *sl = reinterpret_cast<float2 *>(part + (tile * (maxc - 1) + (c - cf - 1)) * (long long)(BM * BN));
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+#pragma unroll
+                for (int q = 0; q < 4; q++) sl[(i * 4 + q) * THREADS + tid] = f2_unpack(acc2[i][q]);
+            __threadfence();
+            __syncthreads();
+            if (tid == 0) asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(flags + tile * (maxc - 1) + (c - cf - 1)),
+                                       "r"(epoch)
+                                       : "memory");
+        } else {
+            if (cl > c) {   // the finisher of a shared tile: the later parts, in CTA order
+                if (tid == 0) {
+                    abort_flag = 0;
+                    for (int q = c + 1; q <= cl; q++) {
+                        const unsigned *f = flags + tile * (maxc - 1) + (q - cf - 1);
+                        unsigned v;
+                        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+                        if (v != epoch) {
+                            unsigned long long t0, t;
+                            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+                            for (;;) {
+                                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+                                if (v == epoch) break;
+                                asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+                                if (t - t0 > 4000000000ull) {
+                                    abort_flag = 1;
+                                    break;
+                                }
+                            }
+                        }
+                        if (abort_flag) break;
+                    }
+                }
+                __syncthreads();
+                if (abort_flag) {
+                    if (tid == 0) *(volatile unsigned *)err = kDevErrWaitTimeout;
+                    x += k1 - k0;
+                    continue;
+                }
+                for (int q = c + 1; q <= cl; q++) {
+                    const float2 *sl =
+                        reinterpret_cast<const float2 *>(part + (tile * (maxc - 1) + (q - cf - 1)) * (long long)(BM * BN));
+#pragma unroll
+                    for (int i = 0; i < 8; i++)
+#pragma unroll
+                        for (int r = 0; r < 4; r++) {
+                            const float2 v = __ldcg(&sl[(i * 4 + r) * THREADS + tid]);
+                            float2 a = f2_unpack(acc2[i][r]);
+                            a.x += v.x;
+                            a.y += v.y;
+                            acc2[i][r] = f2_pack(a.x, a.y);
+                        }
+                }
+            }
+            sg_store(acc2, M, N, m0, n0, alpha, beta, C, ldc, c_vec, nullptr);
+        }
+        x += k1 - k0;
+    }
+}
+
 // C = alpha·Σ_z partial[z] + beta·C, partials summed in ascending z.
 __global__ void sgemm_splitk_sum(int M, int N, int S, float alpha, const float *__restrict__ partial, float beta, float *C,
                                  long long ldc) {
@@ -280,13 +390,8 @@ static int sg_go(bool va, bool vb, dim3 grid, cudaStream_t st, int M, int N, int
 #define G9_SG(VA_, VB_)                                                                                                \
     do {                                                                                                               \
         auto k = sgemm_ffma_kernel<TA, TB, VA_, VB_, BK, STAGES>;                                                      \
-        static bool attr[64] = {};                                                                                     \
-        int dev = 0;                                                                                                   \
-        cudaGetDevice(&dev);                                                                                           \
-        if (!attr[dev & 63]) {                                                                                         \
-            G9_CU(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));                         \
-            attr[dev & 63] = true;                                                                                     \
-        }                                                                                                              \
+        static bool attr[kMaxDevices] = {};                                                                            \
+        G9_CU(smem_limit_once(k, smem, attr));                                                                         \
         launch_pdl(k, grid, dim3(sg::THREADS), smem, st, M, N, K, alpha, a, lda, sA, b, ldb, sB, beta, c, ldc, sC,     \
                    c_vec, kper, partial);                                                                              \
     } while (0)
@@ -298,6 +403,29 @@ static int sg_go(bool va, bool vb, dim3 grid, cudaStream_t st, int M, int N, int
     return 0;
 }
 
+template <bool TA, bool TB, int BK, int STAGES>
+static int sk_go(bool va, bool vb, int grid, cudaStream_t st, int M, int N, int K, float alpha, const float *a, long long lda,
+                 const float *b, long long ldb, float beta, float *c, long long ldc, int c_vec, int tiles_n, int KI,
+                 int maxc, float *part, unsigned *flags, unsigned epoch, unsigned *err) {
+    constexpr int smem = 2 * STAGES * BK * sg::LDS_ * (int)sizeof(float);
+    va = TA && va;
+    vb = !TB && vb;
+#define G9_SK(VA_, VB_)                                                                                                \
+    do {                                                                                                               \
+        auto k = sgemm_sk_kernel<TA, TB, VA_, VB_, BK, STAGES>;                                                        \
+        static bool attr[kMaxDevices] = {};                                                                            \
+        G9_CU(smem_limit_once(k, smem, attr));                                                                         \
+        launch_pdl(k, dim3(grid), dim3(sg::THREADS), smem, st, M, N, K, alpha, a, lda, b, ldb, beta, c, ldc, c_vec,    \
+                   tiles_n, KI, maxc, part, flags, epoch, err);                                                        \
+    } while (0)
+    if (va && vb) G9_SK(TA, !TB);
+    else if (va) G9_SK(TA, false);
+    else if (vb) G9_SK(false, !TB);
+    else G9_SK(false, false);
+#undef G9_SK
+    return launched("sgemm_sk");
+}
+
 template <int BK, int STAGES>
 static int sg_cfg(int tA, int tB, int M, int N, int K, float al, const float *a, int lda, long long sA, const float *b,
                   int ldb, long long sB, float be, float *c, int ldc, long long sC, int count, cudaStream_t st,
@@ -306,6 +434,38 @@ static int sg_cfg(int tA, int tB, int M, int N, int K, float al, const float *a,
     const int tiles_n = (N + BN - 1) / BN, tiles_m = (M + BM - 1) / BM;
     if (tiles_m > 65535 || count > 65535)
         return fail(GEN9BLAS_ERR_INVALID_ARG, "SGEMM grid too large (M %d, count %d)", M, count);
+    // Stream-K for a single GEMM of less than one wave of tiles (two CTAs per SM) with K >= 256: the tile × K-chunk
+    // iterations are spread evenly over a one-wave grid (sgemm_sk_kernel), so no SM idles or does twice the work of
+    // another, and the partial sums of a shared tile stay in L2 until its finisher adds them.
+    {
+        DevState *d = dev_state();
+        if (!d) return G.status;
+        const long long tiles = (long long)tiles_m * tiles_n;
+        const int KI = (K + BK - 1) / BK, G_ = 2 * d->sm_count;
+        const long long T = tiles * KI;
+        if (count == 1 && K >= 256 && tiles < G_ && T / G_ >= 4) {
+            int maxc = 2;
+            for (long long t = 0; t < tiles; t++) {   // CTAs that share tile t: the first and last owners of its chunks
+                const long long y0 = t * KI;
+                const int cf = (int)(((y0 + 1) * G_ - 1) / T), cl = (int)(((y0 + KI) * G_ - 1) / T);
+                if (cl - cf + 1 > maxc) maxc = cl - cf + 1;
+            }
+            if (tiles * (maxc - 1) <= kGemmFlags) {
+                void *p = nullptr;
+                G9_TRY(scratch((size_t)tiles * (maxc - 1) * BM * BN * sizeof(float), &p));
+                unsigned *flags = nullptr, epoch = 0;
+                G9_TRY(gemm_handoff(d, st, &flags, &epoch));
+#define G9_SKT(TA_, TB_)                                                                                              \
+    return sk_go<TA_, TB_, BK, STAGES>(va, vb, G_, st, M, N, K, al, a, lda, b, ldb, be, c, ldc, c_vec, tiles_n, KI, maxc, \
+                                        (float *)p, flags, epoch, d->err_dev)
+                if (!tA && !tB) G9_SKT(false, false);
+                else if (tA && !tB) G9_SKT(true, false);
+                else if (!tA && tB) G9_SKT(false, true);
+                else G9_SKT(true, true);
+#undef G9_SKT
+            }
+        }
+    }
     // Split K (4 parts, 2 for K < 512) when one matrix fills less than 60 % of one wave (two CTAs per SM), or less than
     // one wave with K >= 2048, where the partial tiles' round trip through HBM is small against the K loop. Measured on
     // B200: n = 1024 (64 tiles) 20 TF/s unsplit, 34 with 4 parts; M = 512, N = 8960, K = 1536 (280 tiles): 4 parts cost
