@@ -541,6 +541,30 @@ def run_scaleout(args, L, torch, stream, barrier, rank, world, local):
     clk = clocks.stop()
     value = flops * steps / (ms_total * 1e-3) / 1e12
 
+    # The same n = 32768 GEMM on one GPU (rank 0, after the timed region; the other ranks wait at the barrier), so
+    # that the line carries its own strong-scaling reference: value / (n_gpus * single_gpu_same_workload).
+    single = None
+    if world > 1:
+        if rank == 0:
+            Bfull = torch.randn(n, n, device="cuda", generator=g, dtype=torch.float16).div_(n ** 0.5)
+            with torch.cuda.stream(stream):
+                local_gemm(A, Bfull, C)
+                clk1 = ClockSampler(local)
+                clk1.start()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for _ in range(2):
+                    local_gemm(A, Bfull, C)
+                e1.record(stream)
+                e1.synchronize()
+                c1 = clk1.stop()
+            single = {"tflops": round(2 * flops / (e0.elapsed_time(e1) * 1e-3) / 1e12, 2), "calls": 2,
+                      "clocks": {k: c1.get(k) for k in ("sm_mhz", "sm_max_mhz", "reasons")},
+                      "what": "rank 0 alone: gen9blas_gemm FP16 n=32768 (A . full B) on its GPU, CUDA events"}
+            del Bfull
+            torch.cuda.empty_cache()
+        barrier()
+
     # e2e through the public path with this rank's inputs in pinned host memory: every step copies A and the rank's
     # B block to the device, runs the sharded GEMM + gather, and reads the rank's block of C back (together the ranks
     # read all of C). Wall clock between barriers, max over ranks.
@@ -606,6 +630,7 @@ def run_scaleout(args, L, torch, stream, barrier, rank, world, local):
                           "includes": ("fused: skinny kernel storing its outputs into every rank's C over NVLink + "
                                        "NVLink flag barrier, replayed as one CUDA graph per step" if fused else
                                        "local skinny GEMM + NCCL all-gather of the outputs + re-layout")},
+            "single_gpu_same_workload": single,
             "cpu_baseline": None, "e2e": e2e, "gpu_launches": launches, "clocks": clk}
 
 
