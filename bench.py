@@ -11,6 +11,8 @@ Workloads:
   shapes × M = 1..16, level-1 n = 2^28 and level-2 32768² in FP32 and FP64; level 3 on GEMM at n = 4096; packed
   weights: gemm_pb_skinny on the weight shapes, gemm_pb against gemm), one JSON line per case with its
   roofline fraction, the cuBLAS time for GEMM shapes, and the reference's CPU path on a bounded sample per family.
+- case (N = 1, on request): one GEMM shape (--case TYPE:M:N:K[:tA:tB]) called back to back on device-resident
+  operands -- the workload of the single-kernel ncu captures in profiles/.
 - scaleout (default at N > 1, configs[4]): HGEMM n = 32768 with B and C column-sharded over the N ranks, A
   replicated, C all-gathered over NVLink (NCCL); one step = local GEMM of the rank's column block + all-gather +
   re-layout into the row-major C. Strong scaling (total work fixed).
@@ -46,7 +48,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=0)
     ap.add_argument("--warmup", type=int, default=0)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="auto", choices=["auto", "hgemm4096", "scaleout", "rows"],
+    ap.add_argument("--workload", default="auto", choices=["auto", "hgemm4096", "scaleout", "rows", "case"],
                     help="rows: one JSON line per BASELINE config row (GEMM, skinny, level 1/2), N = 1 only")
     ap.add_argument("--rows", default="C0,C1,C2,C3a,C3b,C3c,L3,L2X,PB",
                     help="rows workload: which config rows to measure (L3: level 3 on GEMM, L2X: rest of levels 1-2, "
@@ -55,6 +57,9 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample (profiling runs)")
     ap.add_argument("--gather", default="fused", choices=["fused", "nccl"],
                     help="scale-out exchange: fused GEMM + NVLink stores (default) or NCCL all-gather")
+    ap.add_argument("--case", default=None, metavar="TYPE:M:N:K[:tA:tB]",
+                    help="workload 'case': one GEMM shape (TYPE h|hs|s|d) called --steps times on device-resident "
+                         "operands after --warmup calls; one JSON line (for profiling a single kernel)")
     return ap.parse_args()
 
 
@@ -327,6 +332,10 @@ def run_ours(args):
         if world != 1:
             raise SystemExit("--workload rows runs on one GPU")
         return run_rows(args, torch)
+    if workload == "case":
+        if world != 1 or not args.case:
+            raise SystemExit("--workload case runs on one GPU and needs --case TYPE:M:N:K[:tA:tB]")
+        return run_case(args, torch)
     torch.cuda.set_device(local)
     if world > 1:
         sys.path.insert(0, PKG)
@@ -632,6 +641,55 @@ def run_scaleout(args, L, torch, stream, barrier, rank, world, local):
                                        "local skinny GEMM + NCCL all-gather of the outputs + re-layout")},
             "single_gpu_same_workload": single,
             "cpu_baseline": None, "e2e": e2e, "gpu_launches": launches, "clocks": clk}
+
+
+# --------------------------------------------------------------------------------------------- one GEMM shape
+def run_case(args, torch):
+    """One GEMM shape called back to back on device-resident operands (uniform[-1,1], N(0,1)/sqrt(K) for FP16), timed
+    with CUDA events, plus the max elementwise error of 16 sampled rows against FP64: the workload that the
+    single-kernel ncu captures in profiles/ run."""
+    parts = args.case.split(":")
+    kind = {"h": H, "hs": HS, "s": S, "d": D}[parts[0].lower()]
+    M, N, K = (int(v) for v in parts[1:4])
+    ta, tb = (int(parts[4]), int(parts[5])) if len(parts) >= 6 else (0, 0)
+    dt = {H: torch.float16, HS: torch.float16, S: torch.float32, D: torch.float64}[kind]
+    L = load_lib()
+    g = torch.Generator(device="cuda").manual_seed(1)
+    def mk(r, c):
+        if dt == torch.float16:
+            return torch.randn(r, c, device="cuda", generator=g, dtype=torch.float32).div_(K ** 0.5).to(dt)
+        return torch.rand(r, c, device="cuda", generator=g, dtype=dt).mul_(2).sub_(1)
+    A = mk(K, M) if ta else mk(M, K)
+    B = mk(N, K) if tb else mk(K, N)
+    C = torch.empty(M, N, device="cuda", dtype=dt)
+    stream = torch.cuda.Stream()
+    assert L.set_stream(ctypes.c_void_p(stream.cuda_stream)) == 0
+    L.set_nowait(1)
+
+    def call():
+        r = L.gemm(kind, ta, tb, M, N, K, 1.0, A.data_ptr(), A.shape[1], B.data_ptr(), B.shape[1], 0.0, C.data_ptr(), N)
+        if r:
+            raise RuntimeError(L.error().decode())
+
+    steps, warm = args.steps or 5, max(args.warmup or 3, 1)
+    with torch.cuda.stream(stream):
+        for _ in range(warm):
+            call()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            call()
+        e1.record(stream)
+        e1.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    rows = torch.randperm(M, generator=torch.Generator().manual_seed(2))[:16].tolist()
+    a64 = (A.t() if ta else A).double()[rows]
+    b64 = (B.t() if tb else B).double()
+    err = float(((C.double()[rows] - a64 @ b64).abs() / (a64.abs() @ b64.abs())).max())
+    emit({"workload": "case", "case": args.case, "ms_per_call": round(ms, 5),
+          "tflops": round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 2), "max_err_sampled_rows": err, "calls": steps})
+    return 0
 
 
 # --------------------------------------------------------------------------------------------- per-row measurements

@@ -46,10 +46,12 @@ struct DevState {
     unsigned sv_epoch = 0;
     int *sk_count = nullptr;                                   // arrival counters of the stream-K skinny kernel (zeroed;
     size_t sk_count_n = 0;                                     // every launch leaves them at zero)
-    // Device ranges written by no-wait calls still queued on the library's stream (since the last call or flush that
-    // waited for it); a kernel that reads an input before griddepcontrol.wait checks its input against them.
+    // Device ranges written by no-wait calls that may still be queued, each with an event recorded right after the
+    // call that wrote it (an entry whose event has completed is dropped); a kernel that reads an input before
+    // griddepcontrol.wait checks its input against them.
     static constexpr int kQueuedRanges = 32;
     uintptr_t queued_lo[kQueuedRanges] = {}, queued_hi[kQueuedRanges] = {};
+    cudaEvent_t queued_ev[kQueuedRanges] = {};
     int queued_n = 0;
     bool queued_overflow = false;
     void *shard = nullptr;                                     // operand copies of a column-sharded GEMM (grow-only)
@@ -116,7 +118,7 @@ int finish_op(Operand *ops, int n);
 // Ledger of the outputs of queued no-wait calls (see DevState::queued_lo): add a range, forget them all once the
 // library's stream has been waited for, and ask whether [p, p + bytes) may still be written by queued work (true also
 // when more ranges were queued than the ledger holds).
-void queued_writes_add(DevState *d, const void *p, size_t bytes);
+void queued_writes_add(DevState *d, const void *p, size_t bytes, cudaStream_t st);
 void queued_writes_clear(DevState *d);
 bool queued_writes_overlap(DevState *d, const void *p, size_t bytes);
 // Hand-over flags of the GEMM kernels that split tiles over CTAs (kGemmFlags zeroed words, created on first use) and

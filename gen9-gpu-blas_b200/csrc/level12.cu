@@ -819,7 +819,7 @@ extern "C" GEN9BLAS_API int gen9blas_gemv_noalloc(int type, int trans, int M, in
     if (!G.nowait || st == cudaStreamPerThread) {
         G9_CU(cudaStreamSynchronize(st));
     } else if (ds) {   // queued on the library's stream: later calls that read y early must know
-        queued_writes_add(ds, y, vec_span(ny, incy) * (size_t)es);
+        queued_writes_add(ds, y, vec_span(ny, incy) * (size_t)es, st);
     }
     return 0;
 }

@@ -276,15 +276,56 @@ int check_dev_err(DevState *d) {
     return 0;
 }
 
-void queued_writes_add(DevState *d, const void *p, size_t bytes) {
+// Drops entry i (its write has completed), keeping the others' order irrelevant: the last entry takes its place.
+static void queued_drop(DevState *d, int i) {
+    const int last = d->queued_n - 1;
+    if (i != last) {
+        d->queued_lo[i] = d->queued_lo[last];
+        d->queued_hi[i] = d->queued_hi[last];
+        cudaEvent_t e = d->queued_ev[i];
+        d->queued_ev[i] = d->queued_ev[last];
+        d->queued_ev[last] = e;
+    }
+    d->queued_n = last;
+}
+
+static bool queued_done(DevState *d, int i) {
+    const cudaError_t e = cudaEventQuery(d->queued_ev[i]);
+    if (e == cudaErrorNotReady) return false;
+    cudaGetLastError();
+    return e == cudaSuccess;
+}
+
+void queued_writes_add(DevState *d, const void *p, size_t bytes, cudaStream_t st) {
     if (!bytes) return;
-    if (d->queued_n == DevState::kQueuedRanges) {
-        d->queued_overflow = true;
+    const uintptr_t lo = (uintptr_t)p, hi = lo + bytes;
+    int slot = -1;
+    for (int i = 0; i < d->queued_n && slot < 0; i++)   // a range that overlaps or touches an entry widens it
+        if (lo <= d->queued_hi[i] && d->queued_lo[i] <= hi) slot = i;
+    if (slot < 0 && d->queued_n == DevState::kQueuedRanges)
+        for (int i = d->queued_n - 1; i >= 0; i--)       // full: forget the writes that have completed
+            if (queued_done(d, i)) queued_drop(d, i);
+    if (slot < 0) {
+        if (d->queued_n == DevState::kQueuedRanges) {    // still full: every later check answers "maybe written"
+            d->queued_overflow = true;
+            return;
+        }
+        slot = d->queued_n++;
+        d->queued_lo[slot] = lo;
+        d->queued_hi[slot] = hi;
+    } else {
+        if (lo < d->queued_lo[slot]) d->queued_lo[slot] = lo;
+        if (hi > d->queued_hi[slot]) d->queued_hi[slot] = hi;
+    }
+    if (!d->queued_ev[slot] && cudaEventCreateWithFlags(&d->queued_ev[slot], cudaEventDisableTiming) != cudaSuccess) {
+        cudaGetLastError();
+        d->queued_overflow = true;   // cannot tell when it completes: stay conservative
         return;
     }
-    d->queued_lo[d->queued_n] = (uintptr_t)p;
-    d->queued_hi[d->queued_n] = (uintptr_t)p + bytes;
-    d->queued_n++;
+    if (cudaEventRecord(d->queued_ev[slot], st) != cudaSuccess) {
+        cudaGetLastError();
+        d->queued_overflow = true;
+    }
 }
 
 void queued_writes_clear(DevState *d) {
@@ -295,8 +336,11 @@ void queued_writes_clear(DevState *d) {
 bool queued_writes_overlap(DevState *d, const void *p, size_t bytes) {
     if (d->queued_overflow) return true;
     const uintptr_t lo = (uintptr_t)p, hi = lo + bytes;
-    for (int i = 0; i < d->queued_n; i++)
-        if (lo < d->queued_hi[i] && d->queued_lo[i] < hi) return true;
+    for (int i = d->queued_n - 1; i >= 0; i--) {
+        if (!(lo < d->queued_hi[i] && d->queued_lo[i] < hi)) continue;
+        if (!queued_done(d, i)) return true;
+        queued_drop(d, i);   // that write has finished
+    }
     return false;
 }
 
@@ -308,7 +352,7 @@ int finish_op(Operand *ops, int n) {
     for (int i = 0; i < n; i++) all_zc = all_zc && ops[i].zc;
     if (G.nowait && all_zc) {
         for (int i = 0; i < n; i++)
-            if (ops[i].written) queued_writes_add(d, ops[i].dptr, ops[i].bytes);
+            if (ops[i].written) queued_writes_add(d, ops[i].dptr, ops[i].bytes, st);
         return 0;
     }
     for (int i = 0; i < n; i++) {
