@@ -172,6 +172,15 @@ __host__ __device__ constexpr int sk_stage_bytes(bool two) { return WK_WARPS * (
 // Second-iteration weights prefetched into shared memory (the modes other than ACT_F16S): 16 rows per warp.
 constexpr int SK_PRE_ROWB = 8 * 32 * 2 + 64;
 constexpr int SK_PRE_BYTES = WK_WARPS * 16 * SK_PRE_ROWB;
+// Both regions are 16 rows of SK_ROWB bytes per warp, whose last 64 bytes no copy touches: a warp keeps there (row r
+// of the tile in the pad of row r) its 16 x 16 FP32 partial tile of the first row block of its CTA when every
+// contributor of that block is a warp of the same CTA; the CTA adds those tiles after the main loop. The launch needs
+// no more shared memory than the regions (73,728 bytes), so a CTA of the next call still fits beside two of this one.
+static_assert(SK_PRE_ROWB == SK_ROWB && SK_ROWB - 8 * 32 * 2 == 64, "pad of 16 floats per staging row");
+constexpr int SK_SMEM_BYTES = WK_WARPS * 16 * SK_ROWB;
+__device__ __forceinline__ float *sk_pad_row(uint8_t *smem, int warp_local, int r) {
+    return reinterpret_cast<float *>(smem + (warp_local * 16 + r) * SK_ROWB + 8 * 32 * 2);
+}
 
 template <bool TWO_NTILES, int UNROLL, int MODE = ACT_F16, bool LAZY = false>
 __global__ void __launch_bounds__(WK_WARPS * 32, 2)
@@ -368,6 +377,18 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *_
             const int wf = (int)(((x0 + 1) * W - 1) / T), wl = (int)(((x1 + 1) * W - 1) / T);
             const int nc = wl - wf + 1;
             const long long blk = (long long)blockIdx.y * RB + rb;
+            const int cta_w0 = blockIdx.x * WK_WARPS;
+            if (wf >= cta_w0 && wl < cta_w0 + WK_WARPS && rb == (T * cta_w0 / W) / KC) {
+                // the CTA's first block and every contributor a warp of this CTA: the tile goes to this warp's pads,
+                // added after the loop
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    if (e >= nv) break;
+                    sk_pad_row(sk_stage, warp, vr[e])[vm[e]] = v[e];
+                }
+                it += kc1 - kc0;
+                continue;
+            }
             float *sp = part + (blk * maxc + (wg - wf)) * 256;
 #pragma unroll
             for (int e = 0; e < 8; e++) {
@@ -417,6 +438,22 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *_
             }
         }
         it += kc1 - kc0;
+    }
+    // The CTA's first row block, if all its contributors are this CTA's warps: their tiles are in their pads;
+    // thread (row, token) adds them in warp order (deterministic) and stores the element.
+    __syncthreads();
+    {
+        const int cta_w0 = blockIdx.x * WK_WARPS;
+        const long long cx0 = T * cta_w0 / W, cx1 = T * (cta_w0 + WK_WARPS) / W;
+        const long long b = cx0 / KC, y0 = b * KC, y1 = y0 + KC - 1;
+        const int wf = (int)(((y0 + 1) * W - 1) / T), wl = (int)(((y1 + 1) * W - 1) / T);
+        if (cx0 < cx1 && wf >= cta_w0 && wl < cta_w0 + WK_WARPS && wl > wf) {
+            const int row = threadIdx.x >> 4, tok = threadIdx.x & 15;
+            float acc = 0.0f;
+            for (int q = wf - cta_w0; q <= wl - cta_w0; q++) acc += sk_pad_row(sk_stage, q, row)[tok];
+            const int n = (int)b * 16 + row, m = t0 + tok;
+            if (n < p.Nc && m < Mout) skinny_out<F32A>(p, m, n, acc);
+        }
     }
     skinny_peer_fence(p);
 }
@@ -646,22 +683,18 @@ static int skinny_t(SkinnyArgs p, cudaStream_t st) {
                 // all-gather keeps ordinary stream order around its rank barrier.
                 const dim3 blk(WK_WARPS * 32);
                 const bool two = p.Mc > 8;
-                const int smem = two ? sk_stage_bytes(true) : 0;   // two token tiles: activations staged (ACT_F16S)
+                const int smem = SK_SMEM_BYTES;   // staging (two token tiles) or second-iteration weights, CTA tiles
                 static bool attr[kMaxDevices] = {};
-                if (two && !attr[d->dev]) {
-                    G9_CU(cudaFuncSetAttribute(wk_f16_sk<true, 8, ACT_F16S, true>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-                    attr[d->dev] = true;
-                }
+                if (two) G9_CU(smem_limit_once(wk_f16_sk<true, 8, ACT_F16S, true>, smem, attr));
                 static bool attr1[kMaxDevices] = {};
-                if (!two) G9_CU(smem_limit_once(wk_f16_sk<false, 8, ACT_F16, true>, SK_PRE_BYTES, attr1));
+                if (!two) G9_CU(smem_limit_once(wk_f16_sk<false, 8, ACT_F16, true>, SK_SMEM_BYTES, attr1));
                 if (p.ndst == 1) {
                     if (two) launch_pdl(wk_f16_sk<true, 8, ACT_F16S, true>, grid, blk, smem, st, p, q.KC, q.maxc, part, count);
-                    else launch_pdl(wk_f16_sk<false, 8, ACT_F16, true>, grid, blk, SK_PRE_BYTES, st, p, q.KC, q.maxc, part, count);
+                    else launch_pdl(wk_f16_sk<false, 8, ACT_F16, true>, grid, blk, SK_SMEM_BYTES, st, p, q.KC, q.maxc, part, count);
                 } else if (two) {
                     wk_f16_sk<true, 8, ACT_F16S, true><<<grid, blk, smem, st>>>(p, q.KC, q.maxc, part, count);
                 } else {
-                    wk_f16_sk<false, 8, ACT_F16, true><<<grid, blk, SK_PRE_BYTES, st>>>(p, q.KC, q.maxc, part, count);
+                    wk_f16_sk<false, 8, ACT_F16, true><<<grid, blk, SK_SMEM_BYTES, st>>>(p, q.KC, q.maxc, part, count);
                 }
                 return launched("skinny_wk_f16_sk");
             }
@@ -771,11 +804,11 @@ __global__ void __launch_bounds__(SPLIT_THREADS) split_f32_rows(const float *__r
 template <bool TWO_NTILES, int UNROLL, int MODE, bool LAZY = false>
 static int launch_f32a_main(const SkinnyArgs &p, const SkPlan &q, float *part, int *count, cudaStream_t st) {
     static bool attr[kMaxDevices] = {};
-    G9_CU(smem_limit_once(wk_f16_sk<TWO_NTILES, UNROLL, MODE, LAZY>, SK_PRE_BYTES, attr));
+    G9_CU(smem_limit_once(wk_f16_sk<TWO_NTILES, UNROLL, MODE, LAZY>, SK_SMEM_BYTES, attr));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)q.ctas, q.mtiles);
     cfg.blockDim = dim3(WK_WARPS * 32);
-    cfg.dynamicSmemBytes = SK_PRE_BYTES;
+    cfg.dynamicSmemBytes = SK_SMEM_BYTES;
     cfg.stream = st;
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
