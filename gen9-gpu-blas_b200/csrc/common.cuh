@@ -80,4 +80,17 @@ template <> __device__ __forceinline__ void store16<__half>(__half *p, const flo
 
 __device__ __forceinline__ bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
 
+// ggml GELU, tanh form, with the FP16 rounding of ggml-cpu's table (x <= -10: 0, x >= 10: x, else
+// fp16(gelu(fp16(x)))); written with explicit roundings so that no multiply-add is contracted. Shared by the
+// elementwise op and the fused GEMM epilogue, so that both give the same bits.
+__device__ __forceinline__ float gelu_ggml(float v) {
+    if (v <= -10.0f) return 0.0f;
+    if (v >= 10.0f) return v;
+    const float h = __half2float(__float2half_rn(v));
+    const float hh = __fmul_rn(h, h);
+    const float inner = __fmul_rn(__fmul_rn(0.79788456080286535588f, h), __fadd_rn(1.0f, __fmul_rn(0.044715f, hh)));
+    const float g = __fmul_rn(__fmul_rn(0.5f, h), __fadd_rn(1.0f, tanhf(inner)));
+    return __half2float(__float2half_rn(g));
+}
+
 }  // namespace g9

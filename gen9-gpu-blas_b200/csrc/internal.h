@@ -6,6 +6,7 @@
 // gen9blas_set_device. Everything in this header has hidden visibility.
 #pragma once
 #include "gen9blas.h"
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cstddef>
 #include <cstdint>
@@ -56,6 +57,11 @@ struct DevState {
     bool queued_overflow = false;
     void *shard = nullptr;                                     // operand copies of a column-sharded GEMM (grow-only)
     size_t shard_n = 0;
+    void *ml = nullptr;                                        // FP16 activations / results of the ML entry points
+    size_t ml_n = 0;                                           // (grow-only, apart from the GEMM scratch they feed)
+    static constexpr int kNowaitSlots = 4096;                  // overflow flags of queued ML calls (mapped pinned words),
+    unsigned *nw_host = nullptr, *nw_dev = nullptr;            // one per call until gen9blas_nowait_pending
+    int nw_used = 0;
 };
 
 // Process-wide call state (the caller serialises calls, as for the reference).
@@ -125,6 +131,11 @@ bool queued_writes_overlap(DevState *d, const void *p, size_t bytes);
 // the epoch of the launch about to be enqueued (never 0).
 constexpr int kGemmFlags = 4096;
 int gemm_handoff(DevState *d, cudaStream_t st, unsigned **flags, unsigned *epoch);
+// Work buffer of the ML entry points on the current device (grow-only, separate from the GEMM scratch).
+int ml_buffer(size_t bytes, void **p);
+// A flag word for one queued ML call (no-wait mode): its device address, or nullptr when all slots are taken (the
+// call then waits and reports through its own flag).
+unsigned *nowait_slot(DevState *d);
 // Turns the device error word of d (set by bounded device-side waits that gave up) into a status; clears it.
 int check_dev_err(DevState *d);
 // Grow-only device buffer of the current device (waits for the library's stream before it grows).
@@ -227,4 +238,13 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 }
 
 }  // namespace g9
+
+// A GEMM input written by gen9blas_layer_norm_pack: FP16 rows of Kp elements (zero past K), device memory of dev.
+struct gen9blas_packed_a {
+    unsigned magic;
+    int M, K, Kp, dev;
+    __half *rows;
+    size_t bytes;
+};
+constexpr unsigned kPackedAMagic = 0x67397061u;
 #pragma GCC visibility pop

@@ -175,6 +175,29 @@ static int ensure_dev_buf(void **p, size_t *n, size_t bytes) {
 
 int ensure_buffer(void **p, size_t *n, size_t bytes) { return ensure_dev_buf(p, n, bytes); }
 
+int ml_buffer(size_t bytes, void **p) {
+    DevState *d = dev_state();
+    if (!d) return G.status;
+    G9_TRY(ensure_dev_buf(&d->ml, &d->ml_n, bytes));
+    *p = d->ml;
+    return 0;
+}
+
+unsigned *nowait_slot(DevState *d) {
+    if (!d->nw_host) {
+        if (cudaHostAlloc((void **)&d->nw_host, DevState::kNowaitSlots * sizeof(unsigned), cudaHostAllocMapped) !=
+                cudaSuccess ||
+            cudaHostGetDevicePointer((void **)&d->nw_dev, d->nw_host, 0) != cudaSuccess) {
+            cudaGetLastError();
+            d->nw_host = nullptr;
+            return nullptr;
+        }
+        memset(d->nw_host, 0, DevState::kNowaitSlots * sizeof(unsigned));
+    }
+    if (d->nw_used == DevState::kNowaitSlots) return nullptr;
+    return d->nw_dev + d->nw_used++;
+}
+
 int gemm_handoff(DevState *d, cudaStream_t st, unsigned **flags, unsigned *epoch) {
     if (!d->gemm_flags) {
         G9_CU(cudaMalloc((void **)&d->gemm_flags, kGemmFlags * sizeof(unsigned)));

@@ -32,7 +32,27 @@ def test_header_declares_reference_surface():
                  "gen9blas_init", "gen9blas_error", "gen9blas_alloc", "gen9blas_spr2", "gen9blas_set_device",
                  "gen9blas_pack_b", "gen9blas_gemm_pb", "gen9blas_packed_b_free", "gen9blas_gemm_pb_skinny"):
         assert must in names
-    assert len(names) == 69   # 67 + gen9blas_set_devices / gen9blas_get_devices
+    assert len(names) == 101   # 67 + set_devices / get_devices + the 32 other entry points of lib/gen9blas_ml.h
+
+
+def test_ml_header_matches_the_reference_list():
+    """Every function of the reference's lib/gen9blas_ml.h (its 33 declarations; set_nowait and flush are declared in
+    gen9blas.h) is declared here, with the same parameter count."""
+    ml = open(HEADERS[1]).read()
+    expected = {   # name: parameters, from lib/gen9blas_ml.h:14-149
+        "gemm_pb_f16w": 7, "gemm_pb_f16w_h": 7, "gemm_pb_f16w_ex": 11, "gemm_pb_skinny": 7, "gemm_multi_f16w": 8,
+        "ffn_f16w": 9, "pack_b_q": 6, "packed_a_create": 0, "packed_a_free": 1, "layer_norm_pack": 11,
+        "gemm_pa_f16w_ex": 9, "nowait_pending": 0, "span": 3, "span_clear": 0, "rms_norm": 9, "layer_norm": 10,
+        "binop_rows": 11, "gelu": 4, "gelu_erf": 4, "relu": 4, "im2col": 20, "cvt_f16_heads": 8, "rope": 18,
+        "rope_multi": 19, "cpy_any": 9, "upscale_f32": 8, "set_rows_f16": 24, "attn_dec_supported": 3,
+        "attn_dec": 26, "attn_supported": 3, "attn_f16kv": 15, "attn_streams_supported": 3, "attn_f16kv_streams": 19,
+    }
+    for name, nparams in expected.items():
+        m = re.search(r"GEN9BLAS_API[^;(]*\bgen9blas_" + name + r"\s*\(([^)]*)\)", ml)
+        assert m, name
+        params = m.group(1).strip()
+        count = 0 if params in ("", "void") else params.count(",") + 1
+        assert count == nparams, (name, count)
 
 
 def test_library_exports_every_declared_function():
