@@ -45,8 +45,9 @@ struct DevState {
     unsigned long long *sv_msg = nullptr;                      // value messages of the look-back triangular solve
     size_t sv_msg_n = 0;                                       // (epoch-stamped 64-bit words, zeroed on growth)
     unsigned sv_epoch = 0;
-    int *sk_count = nullptr;                                   // arrival counters of the stream-K skinny kernel (zeroed;
-    size_t sk_count_n = 0;                                     // every launch leaves them at zero)
+    uint64_t *sk_part = nullptr;                               // epoch-tagged partial tiles of the stream-K skinny
+    size_t sk_part_n = 0;                                      // kernel (words; zeroed when created or grown)
+    unsigned sk_epoch = 0;                                     // launch counter written into those tags
     // Device ranges written by no-wait calls that may still be queued, each with an event recorded right after the
     // call that wrote it (an entry whose event has completed is dropped); a kernel that reads an input before
     // griddepcontrol.wait checks its input against them.
@@ -154,8 +155,9 @@ int pipeline_streams(DevState *d);
 // overwritten). Uses the level-3 work buffer and the GEMM scratch.
 int launch_trsm_dev(int type, int left, int upper, int tA, int unit, int M, int N, double alpha, const void *A, int lda,
                     void *B, int ldb, cudaStream_t st);
-// Arrival counters (n ints, all zero between launches) of the stream-K skinny kernel; grows (and zeroes) on demand.
-int skinny_counters(size_t n, int **p);
+// Partial-tile words of the stream-K skinny kernel (at least `words`, zeroed when created or grown) and the epoch of
+// the launch about to be enqueued (never 0; the words are zeroed again when the counter wraps).
+int skinny_slots(size_t words, uint64_t **p, unsigned *epoch);
 // Call timing: timer_start at entry (wall clock), timer_kernel right before the main kernels (GEN9BLAS_PROFILE=1:
 // CUDA event), timer_stop at the end: last_time_ms is the kernel time with profiling, else the whole call.
 void timer_start();

@@ -233,18 +233,21 @@ int pipeline_streams(DevState *d) {
     return 0;
 }
 
-int skinny_counters(size_t n, int **p) {
+int skinny_slots(size_t words, uint64_t **p, unsigned *epoch) {
     DevState *d = dev_state();
     if (!d) return G.status;
-    if (d->sk_count_n < n) {
-        void *buf = d->sk_count;
-        size_t bytes = d->sk_count_n * sizeof(int);
-        G9_TRY(ensure_dev_buf(&buf, &bytes, n * sizeof(int)));
+    const bool wrap = ++d->sk_epoch == 0;
+    if (wrap) d->sk_epoch = 1;
+    if (d->sk_part_n < words || wrap) {
+        void *buf = d->sk_part;
+        size_t bytes = d->sk_part_n * sizeof(uint64_t);
+        G9_TRY(ensure_dev_buf(&buf, &bytes, words * sizeof(uint64_t)));
         G9_CU(cudaMemsetAsync(buf, 0, bytes, stream()));
-        d->sk_count = (int *)buf;
-        d->sk_count_n = bytes / sizeof(int);
+        d->sk_part = (uint64_t *)buf;
+        d->sk_part_n = bytes / sizeof(uint64_t);
     }
-    *p = d->sk_count;
+    *p = d->sk_part;
+    *epoch = d->sk_epoch;
     return 0;
 }
 

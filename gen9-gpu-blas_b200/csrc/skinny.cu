@@ -11,8 +11,9 @@
 // - wk_f16_sk: weights FP16, contiguous along K. The (16-row block, K chunk) iterations are split evenly over every
 //   warp of a one-wave grid (stream-K), so all SMs stream the same number of weight bytes whatever the shape; each
 //   lane streams 16-byte loads of two weight rows (ld.global.nc, deep unroll) into mma.sync m16n8k16 (FP16 in, FP32
-//   accumulate). Row blocks shared by several warps are finished by the last warp to arrive, which sums the others'
-//   FP32 partial tiles in K order (deterministic, no waiting).
+//   accumulate). A row block shared by several warps is finished by the warp whose range ends in it (it meets the
+//   block last); the others leave epoch-tagged FP32 partial tiles without a fence and stream on, and the finisher adds
+//   them in K order (deterministic).
 // - wk_f32: weights FP32, contiguous along K, FFMA: a CTA owns 4 rows, 8 warps split K, lanes read float4, warp
 //   shuffle reduction, fixed-order combination across warps.
 // - wn_partial + wn_final: weights contiguous along N: split-K partial sums P[part][m][n] in FP32, then a fixed-order
@@ -56,6 +57,12 @@ struct SkinnyArgs {
     unsigned *nf;
     // wk_f16_sk: the weights may be read before griddepcontrol.wait (no queued call writes them).
     int early_w;
+    // wk_f16_sk: tag of this launch's partial tiles, and the device error word a finisher's bounded wait reports to.
+    unsigned epoch;
+    unsigned *err;
+    // wk_f16_sk: 1 = every CTA owns whole row blocks (its warps split them; partial tiles meet in shared memory),
+    // 0 = warps split the whole iteration space (partial tiles of blocks shared across CTAs go through global memory).
+    int aligned;
 };
 
 template <typename T>
@@ -123,6 +130,22 @@ __device__ __forceinline__ uint4 ldg_w16(const void *p) {
     return v;
 }
 
+// Stream-K hand-over words: a 64-bit relaxed store / load is single-copy atomic, so a value travels with its tag.
+__device__ __forceinline__ void st_relaxed_u64(uint64_t *a, uint64_t v) {
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t *a) {
+    uint64_t v;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+constexpr unsigned long long kSkWaitNs = 4000000000ull;   // a finisher's bound on waiting for a partial tile
+
 __device__ __forceinline__ uint32_t word(const uint4 &v, int i) {
     return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }
@@ -140,9 +163,12 @@ __device__ __forceinline__ uint32_t word(const uint4 &v, int i) {
 // Work is spread stream-K style over the whole GPU in one wave. The iteration space is (rb, kc): rb = block of 16
 // weight rows, kc = chunk of UNROLL·32 K elements; T = RB·KC iterations are split evenly over all warps of the grid
 // (warp w owns [T·w/W, T·(w+1)/W)), so every SM streams the same number of weight bytes whatever the shape. A warp that
-// covers a whole row block stores C directly. Otherwise each contributor of the block writes its FP32 partial tile to
-// its slot (slots ordered by K), and the last contributor to arrive (counter per block) sums the slots in slot order
-// and stores C -- deterministic, no spinning: nobody waits for anybody.
+// covers a whole row block stores C directly. Otherwise the warp whose range ends in the block (wf, the one owning its
+// first chunk) finishes it: the block is the last thing wf does, while the other contributors meet it at the start of
+// their ranges (or span it wholly). Each contributor writes its FP32 partial tile to its slot, every value tagged
+// with the launch's epoch in one relaxed 64-bit store, and goes on streaming -- no fence, no atomic, nothing that
+// leaves a warp without loads in flight. The finisher adds the slots to its own tile in slot order (deterministic),
+// waiting (bounded) only for values whose tag is still old; a timeout sets the device error word.
 //
 // Activation modes (the F32 ones serve gemm_pb_skinny, whose activations arrive split into two FP16 parts, a =
 // (hi + lo)·2^-s per row, written by split_f32_rows; both parts go through the MMA into FP32 accumulators, FP16
@@ -181,10 +207,14 @@ constexpr int SK_SMEM_BYTES = WK_WARPS * 16 * SK_ROWB;
 __device__ __forceinline__ float *sk_pad_row(uint8_t *smem, int warp_local, int r) {
     return reinterpret_cast<float *>(smem + (warp_local * 16 + r) * SK_ROWB + 8 * 32 * 2);
 }
+// After the main loop the copied part of a warp's rows is free: row r of its last block's tile sits at its start.
+__device__ __forceinline__ float *sk_last_row(uint8_t *smem, int warp_local, int r) {
+    return reinterpret_cast<float *>(smem + (warp_local * 16 + r) * SK_ROWB);
+}
 
 template <bool TWO_NTILES, int UNROLL, int MODE = ACT_F16, bool LAZY = false>
 __global__ void __launch_bounds__(WK_WARPS * 32, 2)
-wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *__restrict__ count) {
+wk_f16_sk(const SkinnyArgs p, int KC, int maxc, uint64_t *__restrict__ part) {
     constexpr bool F32A = MODE == ACT_PAIRED || MODE == ACT_SPLIT;
     constexpr bool late = LAZY || MODE == ACT_SPLIT || MODE == ACT_F16S;   // fragments loaded right before their MMAs
     static_assert(MODE != ACT_F16S || UNROLL == 8, "ACT_F16S staging rows hold 8 K steps");
@@ -199,8 +229,18 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *_
     const long long T = (long long)RB * KC;
     const int W = gridDim.x * WK_WARPS;
     const int wg = blockIdx.x * WK_WARPS + warp;
-    long long it = T * wg / W;
-    const long long it_end = T * (wg + 1) / W;
+    // aligned: CTA c owns row blocks [RB·c/G, RB·(c+1)/G), i.e. iterations [cs0, cs0 + cn), split evenly over its warps
+    long long it, it_end;
+    if (p.aligned) {
+        const long long cs0 = (long long)KC * ((long long)RB * blockIdx.x / gridDim.x);
+        const long long cn = (long long)KC * ((long long)RB * (blockIdx.x + 1) / gridDim.x) - cs0;
+        it = cs0 + cn * warp / WK_WARPS;
+        it_end = cs0 + cn * (warp + 1) / WK_WARPS;
+    } else {
+        it = T * wg / W;
+        it_end = T * (wg + 1) / W;
+    }
+    const int first_rb = (int)(it / KC);   // the warp's first row block
     const __half *Wt = (const __half *)p.w;
     const __half *A = (const __half *)p.a;
     const int ta0 = min(t0 + g, p.Mc - 1), ta1 = min(t0 + g + 8, p.Mc - 1);
@@ -218,6 +258,12 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *_
         waited = true;
     }
     long long pre_it = -1;
+    // The block this warp finishes (the last one of its range, when other warps contribute to it): its own tile, the
+    // block and its number of contributors, merged after the loop, where the streaming state is dead.
+    // (aligned mode: the tile of the warp's last row block when another warp shares it.)
+    float fin_v[8];
+    int fin_r0 = -1, fin_nc = 0;
+    long long fin_blk = 0;
     if constexpr (PRE) {
         if (it + 1 < it_end) {
             pre_it = it + 1;
@@ -372,6 +418,22 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *_
                 const int n = r0 + vr[e], m = t0 + vm[e];
                 if (n < p.Nc && m < Mout) skinny_out<F32A>(p, m, n, v[e]);
             }
+        } else if (p.aligned) {
+            // a block shared with other warps of this CTA: the first block of the range goes to the pads now, the
+            // last one (the end of the range) to fin_v; both are added after the loop
+            if (rb == first_rb) {
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    if (e >= nv) break;
+                    sk_pad_row(sk_stage, warp, vr[e])[vm[e]] = v[e];
+                }
+                it += kc1 - kc0;
+                continue;
+            }
+#pragma unroll
+            for (int e = 0; e < 8; e++) fin_v[e] = v[e];
+            fin_r0 = r0;
+            break;
         } else {
             const long long x0 = (long long)rb * KC, x1 = x0 + KC - 1;
             const int wf = (int)(((x0 + 1) * W - 1) / T), wl = (int)(((x1 + 1) * W - 1) / T);
@@ -389,55 +451,150 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, float *__restrict__ part, int *_
                 it += kc1 - kc0;
                 continue;
             }
-            float *sp = part + (blk * maxc + (wg - wf)) * 256;
+            // Slots of the block: contributor q = wg - wf writes value e of lane l at word e·32 + l of slot q, tagged
+            // with this launch's epoch in the upper 32 bits (one relaxed 64-bit store: single-copy atomic, so a tag
+            // that matches vouches for its value without any fence).
+            uint64_t *slots = part + blk * maxc * 256;
+            if (wg != wf) {
+                // contributor: the block's later chunks, at the start of this warp's range; it goes on streaming
+                uint64_t *sp = slots + (wg - wf) * 256 + lane;
 #pragma unroll
-            for (int e = 0; e < 8; e++) {
-                if (e >= nv) break;
-                sp[vr[e] * 16 + vm[e]] = v[e];
-            }
-            // Every lane orders its own partial stores at GPU scope (acq_rel fence) before lane 0 counts the warp's
-            // arrival (release); the last arriver's lanes fence again after lane 0's acquire, before they read the
-            // other warps' slots.
-            asm volatile("fence.acq_rel.gpu;" ::: "memory");
-            __syncwarp();
-            int prev = 0;
-            if (lane == 0)
-                asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(prev) : "l"(count + blk) : "memory");
-            prev = __shfl_sync(0xffffffffu, prev, 0);
-            if (prev == nc - 1) {
-                __syncwarp();
-                asm volatile("fence.acq_rel.gpu;" ::: "memory");
-                const int row = lane >> 1, tb = (lane & 1) * 8;
-                if (t0 + tb < Mout && r0 + row < p.Nc) {
-                    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                    const float4 *src0 = reinterpret_cast<const float4 *>(part + blk * maxc * 256 + row * 16 + tb);
-                    int q = 0;
-                    for (; q + 4 <= nc; q += 4) {   // four slots' loads in flight, summed in slot order
-                        float4 u[4][2];
-#pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            u[j][0] = __ldcg(src0 + (q + j) * 64);
-                            u[j][1] = __ldcg(src0 + (q + j) * 64 + 1);
-                        }
-#pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            acc[0] += u[j][0].x; acc[1] += u[j][0].y; acc[2] += u[j][0].z; acc[3] += u[j][0].w;
-                            acc[4] += u[j][1].x; acc[5] += u[j][1].y; acc[6] += u[j][1].z; acc[7] += u[j][1].w;
-                        }
-                    }
-                    for (; q < nc; q++) {
-                        const float4 u0 = __ldcg(src0 + q * 64), u1 = __ldcg(src0 + q * 64 + 1);
-                        acc[0] += u0.x; acc[1] += u0.y; acc[2] += u0.z; acc[3] += u0.w;
-                        acc[4] += u1.x; acc[5] += u1.y; acc[6] += u1.z; acc[7] += u1.w;
-                    }
-#pragma unroll
-                    for (int j = 0; j < 8; j++)
-                        if (t0 + tb + j < Mout) skinny_out<F32A>(p, t0 + tb + j, r0 + row, acc[j]);
+                for (int e = 0; e < 8; e++) {
+                    if (e >= nv) break;
+                    st_relaxed_u64(sp + e * 32, ((uint64_t)p.epoch << 32) | __float_as_uint(v[e]));
                 }
-                if (lane == 0) count[blk] = 0;   // ready for the next launch
+            } else {
+                // finisher: the block is the last of this warp's range; merged after the loop
+#pragma unroll
+                for (int e = 0; e < 8; e++) fin_v[e] = v[e];
+                fin_r0 = r0;
+                fin_nc = nc;
+                fin_blk = blk;
+                break;
             }
         }
         it += kc1 - kc0;
+    }
+    if (p.aligned) {
+        // Row blocks of this CTA shared by several of its warps: the last-block tiles go to the first 64 bytes of the
+        // warp's own staging rows (free now), then thread (row, token) adds the contributors' values in warp order
+        // (deterministic) and stores the element.
+        if (fin_r0 >= 0) {
+            int vm[8], vr[8], nv;
+            if constexpr (MODE == ACT_PAIRED) {
+                vr[0] = g; vm[0] = t; vr[1] = g + 8; vm[1] = t; vr[2] = g; vm[2] = 4 + t; vr[3] = g + 8; vm[3] = 4 + t;
+                nv = TWO_NTILES ? 4 : 2;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    vr[e] = g + ((e & 2) ? 8 : 0);
+                    vm[e] = 2 * t + (e & 1) + (e >= 4 ? 8 : 0);
+                }
+                nv = TWO_NTILES ? 8 : 4;
+            }
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                if (e >= nv) break;
+                sk_last_row(sk_stage, warp, vr[e])[vm[e]] = fin_v[e];
+            }
+        }
+        __syncthreads();
+        const int row = threadIdx.x >> 4, tok = threadIdx.x & 15;
+        const long long cs0 = (long long)KC * ((long long)RB * blockIdx.x / gridDim.x);
+        const long long cn = (long long)KC * ((long long)RB * (blockIdx.x + 1) / gridDim.x) - cs0;
+        const long long b0 = cs0 / KC, b1 = (cs0 + cn) / KC;
+        for (long long b = b0; b < b1; b++) {
+            const long long x0 = b * KC - cs0, x1 = x0 + KC - 1;   // the block's iterations, local to the CTA
+            const int wf = (int)(((x0 + 1) * WK_WARPS - 1) / cn), wl = (int)(((x1 + 1) * WK_WARPS - 1) / cn);
+            if (wf == wl) continue;   // one warp covered it and stored it
+            float acc = 0.0f;
+            for (int w = wf; w <= wl; w++) {
+                const long long ws = cn * w / WK_WARPS, we = cn * (w + 1) / WK_WARPS;
+                if (ws == we) continue;   // a warp without iterations
+                acc += (cs0 + ws) / KC == b ? sk_pad_row(sk_stage, w, row)[tok] : sk_last_row(sk_stage, w, row)[tok];
+            }
+            const int n = (int)b * 16 + row, m = t0 + tok;
+            if (n < p.Nc && m < Mout) skinny_out<F32A>(p, m, n, acc);
+        }
+        skinny_peer_fence(p);
+        return;
+    }
+    if (fin_r0 >= 0) {
+        // Finisher of block fin_blk (the warp whose range ends in it, so it meets the block last): it adds the other
+        // contributors' values to its own in slot order (deterministic), the loads of SB slots in flight at a time,
+        // and waits (bounded) only for values whose tag is not yet this launch's.
+        float v[8];
+        int vm[8], vr[8], nv;
+#pragma unroll
+        for (int e = 0; e < 8; e++) v[e] = fin_v[e];
+        if constexpr (MODE == ACT_PAIRED) {
+            vr[0] = g; vm[0] = t; vr[1] = g + 8; vm[1] = t; vr[2] = g; vm[2] = 4 + t; vr[3] = g + 8; vm[3] = 4 + t;
+            nv = TWO_NTILES ? 4 : 2;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                vr[e] = g + ((e & 2) ? 8 : 0);
+                vm[e] = 2 * t + (e & 1) + (e >= 4 ? 8 : 0);
+            }
+            nv = TWO_NTILES ? 8 : 4;
+        }
+        const int nc = fin_nc, r0 = fin_r0;
+        const uint64_t *mine = part + fin_blk * maxc * 256 + lane;
+        constexpr int SB = TWO_NTILES ? 2 : 4;
+        bool ok = true;
+        for (int q0 = 1; q0 < nc && ok; q0 += SB) {
+            uint64_t x[SB][8];
+            bool fresh = true;
+#pragma unroll
+            for (int j = 0; j < SB; j++) {
+#pragma unroll
+                for (int e = 0; e < 8; e++)
+                    if (q0 + j < nc && e < nv) x[j][e] = ld_relaxed_u64(mine + (q0 + j) * 256 + e * 32);
+            }
+#pragma unroll
+            for (int j = 0; j < SB; j++) {
+#pragma unroll
+                for (int e = 0; e < 8; e++)
+                    if (q0 + j < nc && e < nv) fresh = fresh && (unsigned)(x[j][e] >> 32) == p.epoch;
+            }
+            if (!fresh) {
+                // a contributor has not written yet: poll each value of the batch until its tag is current (tags never
+                // go back within a launch), then take the batch again
+#pragma unroll 1
+                for (int j = 0; j < SB && ok && q0 + j < nc; j++) {
+#pragma unroll 1
+                    for (int e = 0; e < nv && ok; e++) {
+                        const uint64_t *a = mine + (q0 + j) * 256 + e * 32;
+                        const unsigned long long t_start = global_ns();
+                        while ((unsigned)(ld_relaxed_u64(a) >> 32) != p.epoch)
+                            if (global_ns() - t_start > kSkWaitNs) { ok = false; break; }
+                    }
+                }
+                if (!ok) break;
+#pragma unroll
+                for (int j = 0; j < SB; j++) {
+#pragma unroll
+                    for (int e = 0; e < 8; e++)
+                        if (q0 + j < nc && e < nv) x[j][e] = ld_relaxed_u64(mine + (q0 + j) * 256 + e * 32);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < SB; j++) {
+#pragma unroll
+                for (int e = 0; e < 8; e++)
+                    if (q0 + j < nc && e < nv) v[e] += __uint_as_float((unsigned)x[j][e]);
+            }
+        }
+        if (__all_sync(0xffffffffu, ok)) {
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                if (e >= nv) break;
+                const int n = r0 + vr[e], m = t0 + vm[e];
+                if (n < p.Nc && m < Mout) skinny_out<F32A>(p, m, n, v[e]);
+            }
+        } else if (lane == 0) {
+            atomicExch(p.err, kDevErrWaitTimeout);
+        }
     }
     // The CTA's first row block, if all its contributors are this CTA's warps: their tiles are in their pads;
     // thread (row, token) adds them in warp order (deterministic) and stores the element.
@@ -628,24 +785,41 @@ __global__ void repack_small(const T *__restrict__ a, long long sam, long long s
 // Stream-K plan of wk_f16_sk: a one-wave grid of CTAs, K chunks of unroll·32 elements, and the partial-tile slots
 // per 16-row block (the most warps that can share one block).
 struct SkPlan {
-    int KC, RB, mtiles, maxc;
+    int KC, RB, mtiles, maxc, aligned;
     long long ctas;
-    size_t part_bytes;
+    size_t part_words;   // tagged partial-tile words (global mode): mtiles × RB × maxc slots of 256
 };
 
+// Launch plan of wk_f16_sk. Aligned mode (whole row blocks per CTA: the fewest blocks per CTA that keep the grid
+// within one wave and give each of the 8 warps a chunk, spread evenly -- 256 blocks: 256 CTAs of one; 768: 256 of
+// three) when that still gives at least one CTA per SM and either K spans at least 32 chunks or two token tiles run
+// with several blocks per CTA. Measured on B200, same box, µs (global / aligned): W 4096 x 11008 M = 1 19.7 / 17.9,
+// M = 16 25.0 / 21.4; 12288 x 4096 M = 16 26.3 / 24.6, M = 1 19.8 / 20.0; 11008 x 4096 equal; 4096 x 4096 M = 1
+// 8.0 / 9.1. Otherwise the whole iteration space is split over a one-wave grid with at least ~2 iterations per warp.
 static SkPlan sk_plan(int Mc, int Nc, int K, int unroll, int sm_count) {
     SkPlan q;
     q.KC = (K + unroll * 32 - 1) / (unroll * 32);
     q.RB = (Nc + 15) / 16;
     q.mtiles = (Mc + 15) / 16;
+    long long per = (q.RB + 2LL * sm_count - 1) / (2LL * sm_count);
+    if (per * q.KC < WK_WARPS) per = (WK_WARPS + q.KC - 1) / q.KC;
+    const long long g_al = (q.RB + per - 1) / per;
+    if (g_al >= sm_count && (q.KC >= 32 || (Mc > 8 && per >= 2))) {
+        q.aligned = 1;
+        q.ctas = g_al;
+        q.maxc = 0;
+        q.part_words = 0;
+        return q;
+    }
+    q.aligned = 0;
     const long long iters = (long long)q.RB * q.KC;
     long long ctas = (iters + 2 * WK_WARPS - 1) / (2 * WK_WARPS);   // at least ~2 iterations per warp
     if (ctas > 2 * sm_count) ctas = 2 * sm_count;
     if (ctas < 1) ctas = 1;
-    const long long per = iters / (ctas * WK_WARPS);
-    q.maxc = (int)(per == 0 ? q.KC : (q.KC / per + 2 < q.KC ? q.KC / per + 2 : q.KC));
+    const long long per_w = iters / (ctas * WK_WARPS);
+    q.maxc = (int)(per_w == 0 ? q.KC : (q.KC / per_w + 2 < q.KC ? q.KC / per_w + 2 : q.KC));
     q.ctas = ctas;
-    q.part_bytes = (size_t)q.mtiles * q.RB * q.maxc * 256 * sizeof(float);
+    q.part_words = (size_t)q.mtiles * q.RB * q.maxc * 256;
     return q;
 }
 
@@ -660,12 +834,11 @@ static int skinny_t(SkinnyArgs p, cudaStream_t st) {
         const bool w_ok = ((uintptr_t)p.w & 15) == 0 && (p.swn * es) % 16 == 0 && p.K % kq == 0;
         if (w_ok) {
             const bool a_ok = p.sak == 1 && ((uintptr_t)p.a & 15) == 0 && (p.sam * es) % 16 == 0;
-            // Scratch layout: [repacked small operand (when needed) | stream-K partial tiles (FP32)].
+            // Scratch: the repacked small operand (when needed); the partial tiles have their own buffer.
             const size_t a_bytes = a_ok ? 0 : ((size_t)p.Mc * p.K * es + 255) / 256 * 256;
             const SkPlan q = sk_plan(p.Mc, p.Nc, p.K, 8, d->sm_count);
-            const size_t part_bytes = sizeof(T) == 2 ? q.part_bytes : 0;
             void *scr = nullptr;
-            if (a_bytes + part_bytes) G9_TRY(scratch(a_bytes + part_bytes, &scr));
+            if (a_bytes) G9_TRY(scratch(a_bytes, &scr));
             if (!a_ok) {
                 repack_small<T><<<d->sm_count * 4, 256, 0, st>>>((const T *)p.a, p.sam, p.sak, p.Mc, p.K, p.K, (T *)scr);
                 G9_TRY(launched("repack_small"));
@@ -675,9 +848,10 @@ static int skinny_t(SkinnyArgs p, cudaStream_t st) {
             }
             if (sizeof(T) == 2) {
                 p.early_w = !queued_writes_overlap(d, p.w, ((size_t)(p.Nc - 1) * p.swn + p.K) * sizeof(T));
-                int *count = nullptr;
-                G9_TRY(skinny_counters((size_t)q.mtiles * q.RB, &count));
-                float *part = (float *)((char *)scr + a_bytes);
+                uint64_t *part = nullptr;
+                if (!q.aligned) G9_TRY(skinny_slots(q.part_words, &part, &p.epoch));
+                p.err = d->err_dev;
+                p.aligned = q.aligned;
                 dim3 grid((unsigned)q.ctas, q.mtiles);
                 // Single-device calls overlap the previous call's tail (programmatic dependent launch); the fused
                 // all-gather keeps ordinary stream order around its rank barrier.
@@ -689,12 +863,12 @@ static int skinny_t(SkinnyArgs p, cudaStream_t st) {
                 static bool attr1[kMaxDevices] = {};
                 if (!two) G9_CU(smem_limit_once(wk_f16_sk<false, 8, ACT_F16, true>, SK_SMEM_BYTES, attr1));
                 if (p.ndst == 1) {
-                    if (two) launch_pdl(wk_f16_sk<true, 8, ACT_F16S, true>, grid, blk, smem, st, p, q.KC, q.maxc, part, count);
-                    else launch_pdl(wk_f16_sk<false, 8, ACT_F16, true>, grid, blk, SK_SMEM_BYTES, st, p, q.KC, q.maxc, part, count);
+                    if (two) launch_pdl(wk_f16_sk<true, 8, ACT_F16S, true>, grid, blk, smem, st, p, q.KC, q.maxc, part);
+                    else launch_pdl(wk_f16_sk<false, 8, ACT_F16, true>, grid, blk, SK_SMEM_BYTES, st, p, q.KC, q.maxc, part);
                 } else if (two) {
-                    wk_f16_sk<true, 8, ACT_F16S, true><<<grid, blk, smem, st>>>(p, q.KC, q.maxc, part, count);
+                    wk_f16_sk<true, 8, ACT_F16S, true><<<grid, blk, smem, st>>>(p, q.KC, q.maxc, part);
                 } else {
-                    wk_f16_sk<false, 8, ACT_F16, true><<<grid, blk, SK_SMEM_BYTES, st>>>(p, q.KC, q.maxc, part, count);
+                    wk_f16_sk<false, 8, ACT_F16, true><<<grid, blk, SK_SMEM_BYTES, st>>>(p, q.KC, q.maxc, part);
                 }
                 return launched("skinny_wk_f16_sk");
             }
@@ -802,7 +976,7 @@ __global__ void __launch_bounds__(SPLIT_THREADS) split_f32_rows(const float *__r
 }
 
 template <bool TWO_NTILES, int UNROLL, int MODE, bool LAZY = false>
-static int launch_f32a_main(const SkinnyArgs &p, const SkPlan &q, float *part, int *count, cudaStream_t st) {
+static int launch_f32a_main(const SkinnyArgs &p, const SkPlan &q, uint64_t *part, cudaStream_t st) {
     static bool attr[kMaxDevices] = {};
     G9_CU(smem_limit_once(wk_f16_sk<TWO_NTILES, UNROLL, MODE, LAZY>, SK_SMEM_BYTES, attr));
     cudaLaunchConfig_t cfg = {};
@@ -815,7 +989,7 @@ static int launch_f32a_main(const SkinnyArgs &p, const SkPlan &q, float *part, i
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    cudaLaunchKernelEx(&cfg, wk_f16_sk<TWO_NTILES, UNROLL, MODE, LAZY>, p, q.KC, q.maxc, part, count);
+    cudaLaunchKernelEx(&cfg, wk_f16_sk<TWO_NTILES, UNROLL, MODE, LAZY>, p, q.KC, q.maxc, part);
     return launched("skinny_wk_f16_sk_f32a");
 }
 
@@ -839,12 +1013,14 @@ int launch_skinny_f32a(int M, int N, int K, const float *A, int lda, const void 
     p.nf = nf;
     p.early_w = !queued_writes_overlap(d, W, ((size_t)(N - 1) * ldw + Kp) * sizeof(__half));
     const SkPlan q = sk_plan(p.Mc, N, Kp, 8, d->sm_count);
-    // Scratch layout: [hi, lo (2·M rows of Kp FP16) | row scales | stream-K partial tiles (FP32)].
+    // Scratch layout: [hi, lo (2·M rows of Kp FP16) | row scales]; the partial tiles have their own buffer.
     const size_t a_bytes = ((size_t)2 * M * Kp * sizeof(__half) + 255) / 256 * 256, s_bytes = 256;
     void *scr = nullptr;
-    G9_TRY(scratch(a_bytes + s_bytes + q.part_bytes, &scr));
-    int *count = nullptr;
-    G9_TRY(skinny_counters((size_t)q.mtiles * q.RB, &count));
+    G9_TRY(scratch(a_bytes + s_bytes, &scr));
+    uint64_t *part = nullptr;
+    if (!q.aligned) G9_TRY(skinny_slots(q.part_words, &part, &p.epoch));
+    p.err = d->err_dev;
+    p.aligned = q.aligned;
     __half *hi = (__half *)scr;
     float *ts = (float *)((char *)scr + a_bytes);
     p.a = hi;
@@ -855,10 +1031,9 @@ int launch_skinny_f32a(int M, int N, int K, const float *A, int lda, const void 
     else launch_pdl(split_f32_rows, dim3(M), dim3(SPLIT_THREADS), 0, st, A, (long long)lda, K, Kp, vec4, hi,
                     hi + (size_t)M * Kp, (long long)Kp, ts);
     G9_TRY(launched("skinny_split_f32"));
-    float *part = (float *)((char *)scr + a_bytes + s_bytes);
-    if (!paired) return launch_f32a_main<true, 8, ACT_SPLIT>(p, q, part, count, st);
-    if (p.Mc > 8) return launch_f32a_main<true, 8, ACT_PAIRED, true>(p, q, part, count, st);
-    return launch_f32a_main<false, 8, ACT_PAIRED>(p, q, part, count, st);
+    if (!paired) return launch_f32a_main<true, 8, ACT_SPLIT>(p, q, part, st);
+    if (p.Mc > 8) return launch_f32a_main<true, 8, ACT_PAIRED, true>(p, q, part, st);
+    return launch_f32a_main<false, 8, ACT_PAIRED>(p, q, part, st);
 }
 
 int launch_skinny(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, const void *B,
@@ -876,6 +1051,9 @@ int launch_skinny(int type, int tA, int tB, int M, int N, int K, double alpha, c
     p.tscale = nullptr;
     p.nf = nullptr;
     p.early_w = 0;
+    p.epoch = 0;
+    p.err = nullptr;
+    p.aligned = 0;
     if (peers && npeers > 0) {
         if (npeers > 8) return fail(GEN9BLAS_ERR_INVALID_ARG, "at most 8 ranks for the fused skinny GEMM + all-gather");
         for (int q = 0; q < npeers; q++) p.dst[q] = peers[q];
