@@ -249,8 +249,9 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, uint64_t *__restrict__ part) {
     const __half *l0 = a0 + p.alo, *l1 = a1 + p.alo;   // ACT_SPLIT: lo parts
     const int Mout = MODE == ACT_PAIRED ? p.Mc / 2 : p.Mc;   // tokens stored
     // The warp's second iteration goes to shared memory (cp.async) before the wait as well, so that with two
-    // iterations per warp every weight byte is requested while the preceding kernel finishes. Rows of 512 bytes
-    // padded to SK_PRE_ROWB: the two rows a quarter-warp reads then sit on different banks.
+    // iterations per warp every weight byte is requested while the preceding kernel finishes (issued right after the
+    // first iteration's loads, below). Rows of 512 bytes padded to SK_PRE_ROWB: the two rows a quarter-warp reads then
+    // sit on different banks.
     constexpr bool PRE = MODE != ACT_F16S && UNROLL == 8;
     bool waited = false;
     if (!p.early_w) {   // a queued call may still write the weights: nothing is read before the wait
@@ -264,24 +265,6 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, uint64_t *__restrict__ part) {
     float fin_v[8];
     int fin_r0 = -1, fin_nc = 0;
     long long fin_blk = 0;
-    if constexpr (PRE) {
-        if (it + 1 < it_end) {
-            pre_it = it + 1;
-            const int prb = (int)(pre_it / KC), pkc = (int)(pre_it % KC);
-            uint8_t *sw = sk_stage + warp * 16 * SK_PRE_ROWB;
-            const int k = pkc * UNROLL * 32 + 8 * lane;
-            const bool in = k < p.K;
-#pragma unroll
-            for (int r = 0; r < 16; r++) {
-                const __half *src = Wt + (long long)min(prb * 16 + r, p.Nc - 1) * p.swn + (in ? k : 0);
-                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(
-                                 (unsigned)__cvta_generic_to_shared(sw + r * SK_PRE_ROWB + 16 * lane)),
-                             "l"(src), "r"(in ? 16 : 0)
-                             : "memory");
-            }
-            asm volatile("cp.async.commit_group;\n" ::: "memory");
-        }
-    }
     while (it < it_end) {
         const int rb = (int)(it / KC), kc0 = (int)(it % KC);
         const int kc1 = (int)min((long long)KC, kc0 + (it_end - it));
@@ -324,6 +307,25 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, uint64_t *__restrict__ part) {
                         const bool in = k < p.K;
                         wv0[u] = in ? ldg_w16(w0 + k) : z;
                         wv1[u] = in ? ldg_w16(w1 + k) : z;
+                    }
+                    // Right behind the warp's first chunk, its second one goes to shared memory (cp.async), also
+                    // before the wait -- after the first chunk, whose data the warp needs first (issued the other way
+                    // round, W 12288 x 4096 M = 1 took 19.6 instead of 19.1 µs, 11008 x 4096 18.8 instead of 18.2).
+                    if (PRE && pre_it < 0 && (long long)rb * KC + kc + 1 < it_end) {
+                        pre_it = (long long)rb * KC + kc + 1;
+                        const int prb = (int)(pre_it / KC), pkc = (int)(pre_it % KC);
+                        uint8_t *sw = sk_stage + warp * 16 * SK_PRE_ROWB;
+                        const int kp = pkc * UNROLL * 32 + 8 * lane;
+                        const bool inp = kp < p.K;
+#pragma unroll
+                        for (int r = 0; r < 16; r++) {
+                            const __half *src = Wt + (long long)min(prb * 16 + r, p.Nc - 1) * p.swn + (inp ? kp : 0);
+                            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(
+                                             (unsigned)__cvta_generic_to_shared(sw + r * SK_PRE_ROWB + 16 * lane)),
+                                         "l"(src), "r"(inp ? 16 : 0)
+                                         : "memory");
+                        }
+                        asm volatile("cp.async.commit_group;\n" ::: "memory");
                     }
                 }
                 if (!waited) {   // everything but the weights may come from the preceding kernel (the split kernel,
