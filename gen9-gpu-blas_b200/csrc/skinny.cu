@@ -617,6 +617,114 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, uint64_t *__restrict__ part) {
     skinny_peer_fence(p);
 }
 
+// ------------------------------------------------------------------------------------------------ FP16, one block per CTA
+// wk_f16_blk: the common decode plan written out -- one 16-row weight block per CTA, up to 8 FP16 tokens, warp w taking
+// K chunks [KC·w/8, KC·(w+1)/8) of 256. The warp requests its first chunk into registers and its second into its
+// staging rows (cp.async) before the wait, the rest in turn; its 16 × 8 FP32 tile goes to its pads and the CTA adds the
+// eight tiles after one barrier. Same MMA fragments, K permutation and stores as wk_f16_sk, without its stream-K
+// bookkeeping (W 4096 × 4096 M = 1, calls back to back on B200: 5.8 µs against 7.7 with wk_f16_sk; 4096 × 11008 15.0
+// against 17.5). A version looping over several blocks per CTA (next block's requests before the barrier, two pad
+// sets) was slower on every shape, including the one-block ones (7.0 and 16.8 µs).
+template <bool FULLK, bool TWO>
+__global__ void __launch_bounds__(WK_WARPS * 32, 2) wk_f16_blk(const SkinnyArgs p, int KC) {
+    extern __shared__ __align__(16) uint8_t sk_stage[];
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int r0 = blockIdx.x * 16;
+    const int c0 = KC * warp / WK_WARPS, c1 = KC * (warp + 1) / WK_WARPS;
+    const __half *Wt = (const __half *)p.w;
+    const __half *w0 = Wt + (long long)min(r0 + g, p.Nc - 1) * p.swn;
+    const __half *w1 = Wt + (long long)min(r0 + g + 8, p.Nc - 1) * p.swn;
+    const __half *a0 = (const __half *)p.a + (long long)min(g, p.Mc - 1) * p.sam;   // token g (clamped: not stored)
+    const __half *a1 = (const __half *)p.a + (long long)min(g + 8, p.Mc - 1) * p.sam;   // TWO: token g + 8
+    uint8_t *sw = sk_stage + warp * 16 * SK_ROWB;
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    if (!p.early_w) asm volatile("griddepcontrol.wait;" ::: "memory");
+    uint4 wv0[8], wv1[8];
+    if (c0 < c1) {
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int k = c0 * 256 + 32 * u + 8 * t;
+            const bool in = FULLK || k < p.K;
+            wv0[u] = in ? ldg_w16(w0 + k) : z;
+            wv1[u] = in ? ldg_w16(w1 + k) : z;
+        }
+        if (c0 + 1 < c1) {   // the second chunk: lane l copies 16 bytes of each of the 16 rows
+            const int kp = (c0 + 1) * 256 + 8 * lane;
+            const bool inp = FULLK || kp < p.K;
+#pragma unroll
+            for (int r = 0; r < 16; r++) {
+                const __half *src = Wt + (long long)min(r0 + r, p.Nc - 1) * p.swn + (inp ? kp : 0);
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(
+                                 (unsigned)__cvta_generic_to_shared(sw + r * SK_ROWB + 16 * lane)),
+                             "l"(src), "r"(inp ? 16 : 0)
+                             : "memory");
+            }
+            asm volatile("cp.async.commit_group;\n" ::: "memory");
+        }
+    }
+    if (p.early_w) asm volatile("griddepcontrol.wait;" ::: "memory");
+    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f}, d1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int c = c0; c < c1; c++) {
+        if (c == c0 + 1) {
+            asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+            __syncwarp();
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                wv0[u] = *reinterpret_cast<const uint4 *>(sw + g * SK_ROWB + 16 * t + 64 * u);
+                wv1[u] = *reinterpret_cast<const uint4 *>(sw + (g + 8) * SK_ROWB + 16 * t + 64 * u);
+            }
+        } else if (c > c0 + 1) {
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int k = c * 256 + 32 * u + 8 * t;
+                const bool in = FULLK || k < p.K;
+                wv0[u] = in ? ldg_w16(w0 + k) : z;
+                wv1[u] = in ? ldg_w16(w1 + k) : z;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int k = c * 256 + 32 * u + 8 * t;
+            const bool in = FULLK || k < p.K;
+            const uint4 av = in ? __ldg(reinterpret_cast<const uint4 *>(a0 + k)) : z;
+#pragma unroll
+            for (int j = 0; j < 2; j++)
+                mma_16816(d, word(wv0[u], 2 * j), word(wv1[u], 2 * j), word(wv0[u], 2 * j + 1), word(wv1[u], 2 * j + 1),
+                          word(av, 2 * j), word(av, 2 * j + 1));
+            if (TWO) {
+                const uint4 av1 = in ? __ldg(reinterpret_cast<const uint4 *>(a1 + k)) : z;
+#pragma unroll
+                for (int j = 0; j < 2; j++)
+                    mma_16816(d1, word(wv0[u], 2 * j), word(wv1[u], 2 * j), word(wv0[u], 2 * j + 1),
+                              word(wv1[u], 2 * j + 1), word(av1, 2 * j), word(av1, 2 * j + 1));
+            }
+        }
+    }
+    // D fragment: d[0..1] = (row g, tokens 2t, 2t+1), d[2..3] = (row g + 8, tokens 2t, 2t+1)
+    float *pg = sk_pad_row(sk_stage, warp, g), *pg8 = sk_pad_row(sk_stage, warp, g + 8);
+    pg[2 * t] = d[0];
+    pg[2 * t + 1] = d[1];
+    pg8[2 * t] = d[2];
+    pg8[2 * t + 1] = d[3];
+    if (TWO) {   // tokens 8 + 2t, 9 + 2t
+        pg[8 + 2 * t] = d1[0];
+        pg[9 + 2 * t] = d1[1];
+        pg8[8 + 2 * t] = d1[2];
+        pg8[9 + 2 * t] = d1[3];
+    }
+    __syncthreads();
+    const int row = threadIdx.x >> 4, tok = threadIdx.x & 15;
+    if (tok < p.Mc && r0 + row < p.Nc) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int w = 0; w < WK_WARPS; w++) acc += sk_pad_row(sk_stage, w, row)[tok];
+        skinny_store<__half>(p, tok, r0 + row, acc);
+    }
+    skinny_peer_fence(p);
+}
+
 // ------------------------------------------------------------------------------------------------ FP32, K-contiguous
 constexpr int WKF_ROWS = 4;
 
@@ -850,6 +958,20 @@ static int skinny_t(SkinnyArgs p, cudaStream_t st) {
             }
             if (sizeof(T) == 2) {
                 p.early_w = !queued_writes_overlap(d, p.w, ((size_t)(p.Nc - 1) * p.swn + p.K) * sizeof(T));
+                const int rb = (p.Nc + 15) / 16;
+                if (rb >= d->sm_count && q.KC >= WK_WARPS) {
+                    // one row block per CTA (several waves when the blocks outnumber two per SM)
+                    const bool fullk = p.K % 256 == 0, two_t = p.Mc > 8;
+                    const int smem = SK_SMEM_BYTES;
+                    static bool attr_b[4][kMaxDevices] = {};
+                    auto kern = fullk ? (two_t ? wk_f16_blk<true, true> : wk_f16_blk<true, false>)
+                                      : (two_t ? wk_f16_blk<false, true> : wk_f16_blk<false, false>);
+                    G9_CU(smem_limit_once(kern, smem, attr_b[(fullk ? 2 : 0) + (two_t ? 1 : 0)]));
+                    const dim3 grid((unsigned)rb), blk(WK_WARPS * 32);
+                    if (p.ndst == 1) launch_pdl(kern, grid, blk, smem, st, p, q.KC);
+                    else kern<<<grid, blk, smem, st>>>(p, q.KC);
+                    return launched("skinny_wk_f16_blk");
+                }
                 uint64_t *part = nullptr;
                 if (!q.aligned) G9_TRY(skinny_slots(q.part_words, &part, &p.epoch));
                 p.err = d->err_dev;

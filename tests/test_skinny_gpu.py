@@ -46,6 +46,25 @@ def test_reference_skinny_cases(g9, dt, usm):
         assert np.array_equal(big[mask], D0[mask]), "change outside the slice of C"
 
 
+@pytest.mark.parametrize("M,N,K", [(1, 3000, 2100), (3, 4100, 2056), (8, 2380, 4104), (5, 4736, 2048), (2, 4096, 8),
+                                   (4, 9000, 3000), (7, 14000, 2304), (1, 6000, 5000), (9, 3000, 2100),
+                                   (16, 4100, 2056), (12, 9000, 4096)])
+def test_whole_blocks_per_cta_plan(g9, M, N, K):
+    """At least one 16-row block per SM and K of at least 8 chunks of 256 take the kernel with one row block per CTA
+    (one or two token tiles, one or several waves): K off the chunk, edge rows past N, alpha/beta into a slice of C,
+    both operand orders (K = 8 stays on the stream-K kernel)."""
+    A = tab(g9, (M, K), np.float16, True)
+    W = tab(g9, (N, K), np.float16, True)
+    ref = A.astype(np.float64) @ W.astype(np.float64).T
+    assert err(g9.hgemm(A, W.T), ref) <= TOL[np.float16], (M, N, K)
+    assert err(g9.hgemm(W, A.T), ref.T) <= TOL[np.float16], (M, N, K, "swapped")
+    big = tab(g9, (M + 2, N + 5), np.float16, True)
+    C = big[1:M + 1, 2:N + 2]
+    C0 = C.astype(np.float64)
+    g9.hgemm(A, W.T, alpha=0.75, beta=-1.5, C=C)
+    assert err(C, 0.75 * ref - 1.5 * C0) <= TOL[np.float16]
+
+
 @pytest.mark.parametrize("M", [1, 2, 4, 8, 16])
 def test_decoder_shapes(g9, M):
     """W FP16 N(0,0.02) of the 7B shapes, A FP16 N(0,1); C = A·Wᵀ."""
