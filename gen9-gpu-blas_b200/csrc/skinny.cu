@@ -625,8 +625,10 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, uint64_t *__restrict__ part) {
 // bookkeeping (W 4096 × 4096 M = 1, calls back to back on B200: 5.8 µs against 7.7 with wk_f16_sk; 4096 × 11008 15.0
 // against 17.5). A version looping over several blocks per CTA (next block's requests before the barrier, two pad
 // sets) was slower on every shape, including the one-block ones (7.0 and 16.8 µs).
-template <bool FULLK, bool TWO>
+template <bool FULLK, bool TWO, int MODE = ACT_F16>
 __global__ void __launch_bounds__(WK_WARPS * 32, 2) wk_f16_blk(const SkinnyArgs p, int KC) {
+    static_assert(MODE == ACT_F16 || MODE == ACT_PAIRED || MODE == ACT_SPLIT, "token modes of this kernel");
+    constexpr bool F32A = MODE != ACT_F16;
     extern __shared__ __align__(16) uint8_t sk_stage[];
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -700,6 +702,20 @@ __global__ void __launch_bounds__(WK_WARPS * 32, 2) wk_f16_blk(const SkinnyArgs 
                     mma_16816(d1, word(wv0[u], 2 * j), word(wv1[u], 2 * j), word(wv0[u], 2 * j + 1),
                               word(wv1[u], 2 * j + 1), word(av1, 2 * j), word(av1, 2 * j + 1));
             }
+            if (MODE == ACT_SPLIT) {   // the lo parts of the same tokens into the same accumulators
+                const uint4 lv0 = in ? __ldg(reinterpret_cast<const uint4 *>(a0 + p.alo + k)) : z;
+#pragma unroll
+                for (int j = 0; j < 2; j++)
+                    mma_16816(d, word(wv0[u], 2 * j), word(wv1[u], 2 * j), word(wv0[u], 2 * j + 1), word(wv1[u], 2 * j + 1),
+                              word(lv0, 2 * j), word(lv0, 2 * j + 1));
+                if (TWO) {
+                    const uint4 lv1 = in ? __ldg(reinterpret_cast<const uint4 *>(a1 + p.alo + k)) : z;
+#pragma unroll
+                    for (int j = 0; j < 2; j++)
+                        mma_16816(d1, word(wv0[u], 2 * j), word(wv1[u], 2 * j), word(wv0[u], 2 * j + 1),
+                                  word(wv1[u], 2 * j + 1), word(lv1, 2 * j), word(lv1, 2 * j + 1));
+                }
+            }
         }
     }
     // D fragment: d[0..1] = (row g, tokens 2t, 2t+1), d[2..3] = (row g + 8, tokens 2t, 2t+1)
@@ -716,11 +732,22 @@ __global__ void __launch_bounds__(WK_WARPS * 32, 2) wk_f16_blk(const SkinnyArgs 
     }
     __syncthreads();
     const int row = threadIdx.x >> 4, tok = threadIdx.x & 15;
-    if (tok < p.Mc && r0 + row < p.Nc) {
+    if constexpr (MODE == ACT_PAIRED) {
+        // virtual token rows 2m (hi) and 2m + 1 (lo) of real token m: their sum is its value
+        if (tok < p.Mc / 2 && r0 + row < p.Nc) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int w = 0; w < WK_WARPS; w++) {
+                const float *pw = sk_pad_row(sk_stage, w, row);
+                acc += pw[2 * tok] + pw[2 * tok + 1];
+            }
+            skinny_out<true>(p, tok, r0 + row, acc);
+        }
+    } else if (tok < p.Mc && r0 + row < p.Nc) {
         float acc = 0.0f;
 #pragma unroll
         for (int w = 0; w < WK_WARPS; w++) acc += sk_pad_row(sk_stage, w, row)[tok];
-        skinny_store<__half>(p, tok, r0 + row, acc);
+        skinny_out<F32A>(p, tok, r0 + row, acc);
     }
     skinny_peer_fence(p);
 }
@@ -1155,6 +1182,16 @@ int launch_skinny_f32a(int M, int N, int K, const float *A, int lda, const void 
     else launch_pdl(split_f32_rows, dim3(M), dim3(SPLIT_THREADS), 0, st, A, (long long)lda, K, Kp, vec4, hi,
                     hi + (size_t)M * Kp, (long long)Kp, ts);
     G9_TRY(launched("skinny_split_f32"));
+    if ((N + 15) / 16 >= d->sm_count && q.KC >= WK_WARPS) {   // one row block per CTA, as the FP16-activation path
+        const bool fullk = Kp % 256 == 0;
+        auto kern = !paired ? (fullk ? wk_f16_blk<true, true, ACT_SPLIT> : wk_f16_blk<false, true, ACT_SPLIT>)
+                  : p.Mc > 8 ? (fullk ? wk_f16_blk<true, true, ACT_PAIRED> : wk_f16_blk<false, true, ACT_PAIRED>)
+                             : (fullk ? wk_f16_blk<true, false, ACT_PAIRED> : wk_f16_blk<false, false, ACT_PAIRED>);
+        static bool attr_b[6][kMaxDevices] = {};
+        G9_CU(smem_limit_once(kern, SK_SMEM_BYTES, attr_b[(!paired ? 0 : p.Mc > 8 ? 2 : 4) + (fullk ? 1 : 0)]));
+        launch_pdl(kern, dim3((unsigned)((N + 15) / 16)), dim3(WK_WARPS * 32), SK_SMEM_BYTES, st, p, q.KC);
+        return launched("skinny_wk_f16_blk_f32a");
+    }
     if (!paired) return launch_f32a_main<true, 8, ACT_SPLIT>(p, q, part, st);
     if (p.Mc > 8) return launch_f32a_main<true, 8, ACT_PAIRED, true>(p, q, part, st);
     return launch_f32a_main<false, 8, ACT_PAIRED>(p, q, part, st);

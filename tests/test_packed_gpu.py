@@ -185,9 +185,11 @@ def skinny_pb(L, M, A, P, N):
     return C, nf.value
 
 
-@pytest.mark.parametrize("N,K", [(1024, 1024), (256, 1024), (3072, 1024), (1024, 3072), (1000, 1000), (37, 96)])
+@pytest.mark.parametrize("N,K", [(1024, 1024), (256, 1024), (3072, 1024), (1024, 3072), (1000, 1000), (37, 96),
+                                 (3072, 2048), (4100, 2600)])
 def test_gemm_pb_skinny(gpu_lib, N, K):
-    """lib/test_skinny_pb.py:51-66: W[N][K] FP16 (N(0, 0.05)) packed as HS with transB = 1, A F32 N(0, 1)."""
+    """lib/test_skinny_pb.py:51-66: W[N][K] FP16 (N(0, 0.05)) packed as HS with transB = 1, A F32 N(0, 1). The last two
+    shapes (at least one 16-row block per SM, K of at least 2048) take the kernel with one row block per CTA."""
     L = gpu_lib
     rs = np.random.default_rng(11)
     W = (rs.standard_normal((N, K)) * 0.05).astype(np.float16)
@@ -205,11 +207,12 @@ def test_gemm_pb_skinny(gpu_lib, N, K):
         L.packed_b_free(P)
 
 
-def test_gemm_pb_skinny_scaling_and_nonfinite(gpu_lib):
+@pytest.mark.parametrize("N,K,M", [(512, 640, 6), (3000, 2048, 6), (3000, 2304, 12)])
+def test_gemm_pb_skinny_scaling_and_nonfinite(gpu_lib, N, K, M):
     """Rows of 1e-30 and 1e30 magnitude keep full accuracy (per-row power-of-two scaling of the FP16 parts); an inf
-    in one row flags the call and leaves the other rows exact."""
+    in one row flags the call and leaves the other rows exact (stream-K kernel, then the one-block-per-CTA kernel
+    with paired and with split token parts)."""
     L = gpu_lib
-    N, K, M = 512, 640, 6
     W = (rng.standard_normal((N, K)) * 0.05).astype(np.float16)
     P = pack(L, HS, W, 1)
     W64 = W.astype(np.float64)
