@@ -53,24 +53,26 @@ g9dist.fused_column_sharded_gemm(lib, A, Bs, C, peers, rank, world, barrier=bar)
 torch.cuda.synchronize()
 e3 = float(((C.double() - ref).abs() / scale).max())
 # tensor-parallel decode: weight rows split over the ranks, outputs stored into every rank's C, barrier; three rounds
-Mw, Kw, Nw = 8, 1024, 4096
-W = (torch.randn(Nw, Kw, device="cuda", generator=g) * 0.02).half()
-nr = Nw // world
-Ws = W[rank * nr:(rank + 1) * nr].contiguous()
-Cs = torch.zeros(Mw, Nw, device="cuda", dtype=torch.float16)
-pv = g9dist.PeerView(lib, Cs, rank, world)
+# per shape (2048 rows and K = 1024 per rank: the stream-K kernel; 4096 rows and K = 2048: one row block per CTA)
 e4 = 0.0
-for it in range(3):
-    X = torch.randn(Mw, Kw, device="cuda", generator=g, dtype=torch.float16)
-    torch.cuda.synchronize()
-    g9dist.fused_row_sharded_skinny(lib, X, Ws, Cs, pv, rank, world, barrier=bar)
-    torch.cuda.synchronize()
-    r4 = X.double() @ W.double().t()
-    s4 = X.double().abs() @ W.double().abs().t()
-    e4 = max(e4, float(((Cs.double() - r4).abs() / s4).max()))
-    dist.barrier()   # nobody overwrites Cs for the next round before every rank has checked this one
+for Mw, Kw, Nw in ((8, 1024, 4096), (8, 2048, 4096 * world)):
+    W = (torch.randn(Nw, Kw, device="cuda", generator=g) * 0.02).half()
+    nr = Nw // world
+    Ws = W[rank * nr:(rank + 1) * nr].contiguous()
+    Cs = torch.zeros(Mw, Nw, device="cuda", dtype=torch.float16)
+    pv = g9dist.PeerView(lib, Cs, rank, world)
+    for it in range(3):
+        X = torch.randn(Mw, Kw, device="cuda", generator=g, dtype=torch.float16)
+        torch.cuda.synchronize()
+        g9dist.fused_row_sharded_skinny(lib, X, Ws, Cs, pv, rank, world, barrier=bar)
+        torch.cuda.synchronize()
+        r4 = X.double() @ W.double().t()
+        s4 = X.double().abs() @ W.double().abs().t()
+        e4 = max(e4, float(((Cs.double() - r4).abs() / s4).max()))
+        dist.barrier()   # nobody overwrites Cs for the next round before every rank has checked this one
+    dist.barrier()
+    pv.close()
 dist.barrier()
-pv.close()
 bar.close()
 peers.close()
 dist.destroy_process_group()
