@@ -50,7 +50,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="auto", choices=["auto", "hgemm4096", "scaleout", "rows", "case"],
                     help="rows: one JSON line per BASELINE config row (GEMM, skinny, level 1/2), N = 1 only")
-    ap.add_argument("--rows", default="C0,C1,C2,C3a,C3b,C3c,L3,L2X,PB",
+    ap.add_argument("--rows", default="C0,C1,C2,C3a,C3b,C3c,L3,L2X,PB,ML",
                     help="rows workload: which config rows to measure (L3: level 3 on GEMM, L2X: rest of levels 1-2, "
                          "PB: packed weights)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) measurement")
@@ -1009,6 +1009,86 @@ def run_rows(args, torch):
                      tf, peak, "TFLOP/s", note, {"gemm_same_operands_tflops": round(2 * M * N * K / (ms_g * 1e-3) / 1e12, 2)})
             L.dll.gen9blas_packed_b_free(P)
             del A, Wt, Cm
+        torch.cuda.empty_cache()
+
+    # ML operations of gen9blas_ml.h on decode / prefill shapes, device-resident operands, queued (sync = 0 or no-wait
+    # mode). Every case here is bound by HBM at these sizes: the roofline is algorithmic bytes against the copy rate.
+    if "ML" in want:
+        def hbm_row(case, ms, nbytes, extra=None):
+            gbps = nbytes / (ms * 1e-3) / 1e9
+            emit_row("ML", case, ms * 1e3, "us", ms, "hbm", gbps, peak_hbm, "GB/s",
+                     f"{peak_kind} HBM copy, MEASURED_PEAKS.json", dict({"gbps": round(gbps, 1)}, **(extra or {})))
+
+        def packed(n, k):
+            W = torch.randn(n, k, device="cuda", generator=g).mul_(0.02).half()
+            torch.cuda.synchronize()   # the weights exist before the library's stream copies them
+            P = L.pack_b(HS, 1, k, n, W.data_ptr(), k)
+            assert P, L.error().decode()
+            return P
+
+        nfp = ctypes.c_int(0)
+        for N, K in ((4096, 4096), (11008, 4096)):
+            copies = max(2, int(512e6 // (N * K * 2)) + 1)
+            Ps = [packed(N, K) for _ in range(copies)]
+            for M in (1, 16, 64):
+                X = torch.randn(M, K, device="cuda", generator=g, dtype=torch.float32)
+                Y = torch.empty(M, N, device="cuda", dtype=torch.float32)
+                ms = queued_ms(lambda i, X=X, Y=Y, M=M: chk(L.gemm_pb_f16w(M, X.data_ptr(), K, Ps[i % copies],
+                                                                          Y.data_ptr(), N, ctypes.addressof(nfp))), 200)
+                L.flush()
+                L.nowait_pending()
+                hbm_row(f"gemm_pb_f16w M={M} W={N}x{K} (F32 act -> FP16, FP16 weights)", ms,
+                        N * K * 2 + M * K * 4 + M * N * 4)
+            for P in Ps:
+                L.packed_b_free(P)
+        # gated FFN of a 7B layer: gate and up 4096 -> 11008, down 11008 -> 4096
+        Pg = [packed(11008, 4096) for _ in range(2)]
+        Pu = [packed(11008, 4096) for _ in range(2)]
+        Pd = [packed(4096, 11008) for _ in range(2)]
+        for M in (1, 16):
+            X = torch.randn(M, 4096, device="cuda", generator=g, dtype=torch.float32)
+            Y = torch.empty(M, 4096, device="cuda", dtype=torch.float32)
+            ms = queued_ms(lambda i, X=X, Y=Y, M=M: chk(L.ffn_f16w(M, X.data_ptr(), 4096, Pg[i % 2], Pu[i % 2],
+                                                                  Pd[i % 2], Y.data_ptr(), 4096,
+                                                                  ctypes.addressof(nfp))), 100)
+            L.flush()
+            L.nowait_pending()
+            hbm_row(f"ffn_f16w M={M} 4096->11008->4096 (two weight sets)", ms, 3 * 11008 * 4096 * 2 + M * 4096 * 8)
+        for P in Pg + Pu + Pd:
+            L.packed_b_free(P)
+        # row / element operations at prefill size
+        R, Kr = 8192, 4096
+        Xs = [torch.randn(R, Kr, device="cuda", generator=g) for _ in range(2)]
+        Ys = [torch.empty(R, Kr, device="cuda") for _ in range(2)]
+        w = torch.randn(Kr, device="cuda", generator=g)
+        ms = queued_ms(lambda i: chk(L.rms_norm(R, Kr, Xs[i % 2].data_ptr(), Kr, w.data_ptr(), 1e-6,
+                                                Ys[i % 2].data_ptr(), Kr, 0)), 50)
+        hbm_row(f"rms_norm {R}x{Kr} F32 (with weight)", ms, 2 * R * Kr * 4 + Kr * 4)
+        ms = queued_ms(lambda i: chk(L.gelu(R * Kr, Xs[i % 2].data_ptr(), Ys[i % 2].data_ptr(), 0)), 50)
+        hbm_row(f"gelu {R * Kr} F32", ms, 2 * R * Kr * 4)
+        nt, nh, nd = 8192, 32, 128
+        pos = torch.arange(nt, device="cuda", dtype=torch.int32)
+        corr = (ctypes.c_float * 2)(0.0, 0.0)
+        Xr = Xs[0].view(-1)[:nt * nh * nd]
+        ms = queued_ms(lambda i: chk(L.rope(nd, nh, nt, Xr.data_ptr(), nd, nh * nd, Xr.data_ptr(), nd, nh * nd,
+                                            pos.data_ptr(), None, 1, 10000.0, 1.0, 0.0, 1.0,
+                                            ctypes.addressof(corr), 0)), 50)
+        hbm_row(f"rope NEOX {nt} tokens x {nh} heads x {nd} (in place)", ms, 2 * nt * nh * nd * 4 + nt * 4)
+        del Xs, Ys
+        # decoding attention over a KV cache: 8 streams, one new token each, H 32 / HKV 8, D 128, 4096 keys
+        ns, nk, H, HKV, D = 8, 4096, 32, 8, 128
+        Kc = [torch.randn(ns, nk, HKV, D, device="cuda", generator=g).half() for _ in range(2)]
+        Vc = [torch.randn(ns, nk, HKV, D, device="cuda", generator=g).half() for _ in range(2)]
+        Q = torch.randn(ns, 1, H, D, device="cuda", generator=g)
+        O = torch.empty(ns, 1, H, D, device="cuda")
+        vis = torch.full((ns,), nk, device="cuda", dtype=torch.int32)
+        kk, kh, ks = HKV * D, D, nk * HKV * D
+        ms = queued_ms(lambda i: chk(L.attn_dec(D, H, HKV, ns, 1, nk, Q.data_ptr(), H * D, D, H * D,
+                                                Kc[i % 2].data_ptr(), kk, kh, ks, Kc[0].numel() * 2,
+                                                Vc[i % 2].data_ptr(), kk, kh, ks, Vc[0].numel() * 2, O.data_ptr(),
+                                                D ** -0.5, vis.data_ptr(), 0, 256, 0)), 50)
+        hbm_row(f"attn_dec {ns} streams x {nk} keys, H {H} / HKV {HKV}, D {D}", ms, 2 * ns * nk * HKV * D * 2)
+        del Kc, Vc
         torch.cuda.empty_cache()
 
     # rest of levels 1-2 (the scope table's next row): level 1 at n = 2^28, level 2 at n = 16384 (dense, band K = 64,

@@ -203,6 +203,13 @@ int skinny_threshold(int type);
 // Skinny GEMM with FP32 activations and FP16 weights (gemm_pb_skinny): C (M × N, FP32) = A (M × K, FP32) · Wᵀ with W
 // N rows of ldw FP16 elements (ldw >= K rounded up to 8, zero past K, rows 16-byte aligned). A non-finite result sets
 // *nf (device-visible word).
+// gemm_pb_f16w's product in one kernel when its shape takes the one-row-block-per-CTA skinny kernel (M <= 16, N at
+// least 16 rows per SM, K >= 2048 and a multiple of 8, 16-byte aligned rows): activations (F32, or FP16 with ahalf)
+// rounded to FP16, FP32 sums rounded to FP16, then bias / GELU / residual, F32 C; *nf set on a non-finite FP16 result.
+// Returns 1 (nothing enqueued) when the shape does not qualify.
+int launch_skinny_f16w(int M, const void *A, bool ahalf, long long lda, const void *W, int K, int N, long long ldw,
+                       float *C, long long ldc, const float *bias, int gelu, const float *R, long long ldr, unsigned *nf,
+                       cudaStream_t st);
 int launch_skinny_f32a(int M, int N, int K, const float *A, int lda, const void *W, int ldw, float *C, int ldc,
                        unsigned *nf, cudaStream_t st);
 

@@ -495,6 +495,18 @@ int gemm_pb_f16w_any(bool ahalf, int M, const void *A, int lda, const gen9blas_p
         flag = d->err_dev + 1;
     }
     timer_kernel();
+    // M <= 16 on a wide enough, deep enough weight matrix: one kernel (FP16 rounding of the activations as they are
+    // loaded, the product, this epilogue), the same arithmetic as the three kernels below
+    const int one = launch_skinny_f16w(M, pa ? (const void *)pa->rows : op[0].dptr, pa || ahalf, pa ? Kp : lda, P->w,
+                                       pa ? Kp : K, N, Kp, (float *)op[1].dptr, ldc, bias, ext ? ext->gelu : 0, R,
+                                       ext ? ext->ldr : 0, flag, st);
+    if (one < 0) return one;
+    if (one == 0) {
+        int r = finish_op(op, 2);
+        timer_stop();
+        if (r == 0 && !queued && nonfinite) *nonfinite = *(volatile unsigned *)(d->err_host + 1) != 0u;
+        return r;
+    }
     if (pa) {
     } else if (ahalf) act_to_f16<__half><<<grid_for((long long)M * Kp, d->sm_count), 256, 0, st>>>((const __half *)op[0].dptr, lda,
                                                                                             M, K, Kp, a16);

@@ -22,6 +22,7 @@
 #include "common.cuh"
 #include "internal.h"
 #include <cstdlib>
+#include <cstring>
 
 namespace g9 {
 
@@ -63,6 +64,12 @@ struct SkinnyArgs {
     // wk_f16_sk: 1 = every CTA owns whole row blocks (its warps split them; partial tiles meet in shared memory),
     // 0 = warps split the whole iteration space (partial tiles of blocks shared across CTAs go through global memory).
     int aligned;
+    // wk_f16_blk with the gemm_pb_f16w epilogue: the FP32 sum rounded to FP16 once (a non-finite one sets *nf), then
+    // [+ bias[n]] [gelu] [+ R[m·ldr + n]], stored as F32 at C[m·scm + n].
+    const float *bias;
+    const float *R;
+    long long ldr;
+    int gelu;
 };
 
 template <typename T>
@@ -189,7 +196,9 @@ __device__ __forceinline__ uint32_t word(const uint4 &v, int i) {
 //   longer stays in L1). Measured on B200, M = 16, two boxes: W 4096² 12.3 -> 10.8-11.2 µs, 11008 × 4096 23.6 ->
 //   21.7-22.1, 4096 × 11008 22.7 -> 21.5-22.6, but 12288 × 4096 23.5 -> 24.2. With up to 8 tokens the fragments
 //   stay L1-resident and are read directly (ACT_F16, LAZY; staging them cost M = 1 up to 48 %).
-enum { ACT_F16 = 0, ACT_PAIRED = 1, ACT_SPLIT = 2, ACT_F16S = 3 };
+enum { ACT_F16 = 0, ACT_PAIRED = 1, ACT_SPLIT = 2, ACT_F16S = 3, ACT_F32H = 4 };
+// ACT_F32H (wk_f16_blk only): F32 activations rounded to FP16 (nearest even) as their fragments are loaded, the
+// gemm_pb_f16w semantics.
 
 // ACT_F16S staging: per warp, one row per token of UNROLL·32 FP16 plus a 64-byte pad (the two token rows a
 // quarter-warp reads then fall on different banks).
@@ -617,6 +626,22 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, uint64_t *__restrict__ part) {
     skinny_peer_fence(p);
 }
 
+// The 8 K-consecutive token values of a fragment (16 bytes of FP16): FP16 activations as stored, or F32 activations
+// rounded to FP16 (ACT_F32H; two 16-byte loads).
+template <int MODE>
+__device__ __forceinline__ uint4 act_frag(const SkinnyArgs &p, int m, int k) {
+    if constexpr (MODE == ACT_F32H) {
+        const float4 *f = reinterpret_cast<const float4 *>((const float *)p.a + (long long)m * p.sam + k);
+        const float4 x = __ldg(f), y = __ldg(f + 1);
+        const __half2 h0 = __floats2half2_rn(x.x, x.y), h1 = __floats2half2_rn(x.z, x.w);
+        const __half2 h2 = __floats2half2_rn(y.x, y.y), h3 = __floats2half2_rn(y.z, y.w);
+        return make_uint4(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1),
+                          *reinterpret_cast<const uint32_t *>(&h2), *reinterpret_cast<const uint32_t *>(&h3));
+    } else {
+        return __ldg(reinterpret_cast<const uint4 *>((const __half *)p.a + (long long)m * p.sam + k));
+    }
+}
+
 // ------------------------------------------------------------------------------------------------ FP16, one block per CTA
 // wk_f16_blk: the common decode plan written out -- one 16-row weight block per CTA, up to 8 FP16 tokens, warp w taking
 // K chunks [KC·w/8, KC·(w+1)/8) of 256. The warp requests its first chunk into registers and its second into its
@@ -625,10 +650,11 @@ wk_f16_sk(const SkinnyArgs p, int KC, int maxc, uint64_t *__restrict__ part) {
 // bookkeeping (W 4096 × 4096 M = 1, calls back to back on B200: 5.8 µs against 7.7 with wk_f16_sk; 4096 × 11008 15.0
 // against 17.5). A version looping over several blocks per CTA (next block's requests before the barrier, two pad
 // sets) was slower on every shape, including the one-block ones (7.0 and 16.8 µs).
-template <bool FULLK, bool TWO, int MODE = ACT_F16>
+template <bool FULLK, bool TWO, int MODE = ACT_F16, bool F16W = false>
 __global__ void __launch_bounds__(WK_WARPS * 32, 2) wk_f16_blk(const SkinnyArgs p, int KC) {
-    static_assert(MODE == ACT_F16 || MODE == ACT_PAIRED || MODE == ACT_SPLIT, "token modes of this kernel");
-    constexpr bool F32A = MODE != ACT_F16;
+    static_assert(MODE == ACT_F16 || MODE == ACT_PAIRED || MODE == ACT_SPLIT || MODE == ACT_F32H, "token modes");
+    static_assert(!F16W || MODE == ACT_F16 || MODE == ACT_F32H, "the f16w epilogue takes FP16-rounded tokens");
+    constexpr bool F32A = MODE == ACT_PAIRED || MODE == ACT_SPLIT;
     extern __shared__ __align__(16) uint8_t sk_stage[];
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -690,13 +716,13 @@ __global__ void __launch_bounds__(WK_WARPS * 32, 2) wk_f16_blk(const SkinnyArgs 
         for (int u = 0; u < 8; u++) {
             const int k = c * 256 + 32 * u + 8 * t;
             const bool in = FULLK || k < p.K;
-            const uint4 av = in ? __ldg(reinterpret_cast<const uint4 *>(a0 + k)) : z;
+            const uint4 av = in ? act_frag<MODE>(p, min(g, p.Mc - 1), k) : z;
 #pragma unroll
             for (int j = 0; j < 2; j++)
                 mma_16816(d, word(wv0[u], 2 * j), word(wv1[u], 2 * j), word(wv0[u], 2 * j + 1), word(wv1[u], 2 * j + 1),
                           word(av, 2 * j), word(av, 2 * j + 1));
             if (TWO) {
-                const uint4 av1 = in ? __ldg(reinterpret_cast<const uint4 *>(a1 + k)) : z;
+                const uint4 av1 = in ? act_frag<MODE>(p, min(g + 8, p.Mc - 1), k) : z;
 #pragma unroll
                 for (int j = 0; j < 2; j++)
                     mma_16816(d1, word(wv0[u], 2 * j), word(wv1[u], 2 * j), word(wv0[u], 2 * j + 1),
@@ -747,7 +773,18 @@ __global__ void __launch_bounds__(WK_WARPS * 32, 2) wk_f16_blk(const SkinnyArgs 
         float acc = 0.0f;
 #pragma unroll
         for (int w = 0; w < WK_WARPS; w++) acc += sk_pad_row(sk_stage, w, row)[tok];
-        skinny_out<F32A>(p, tok, r0 + row, acc);
+        if constexpr (F16W) {
+            // as gemm_pb_f16w's separate epilogue, operation for operation: the FP16 result, then bias / GELU / residual
+            const int n = r0 + row;
+            float v = __half2float(__float2half_rn(acc));
+            if (!isfinite(v)) *(volatile unsigned *)p.nf = 1u;
+            if (p.bias) v = __fadd_rn(v, p.bias[n]);
+            if (p.gelu) v = gelu_ggml(v);
+            if (p.R) v = __fadd_rn(v, p.R[(long long)tok * p.ldr + n]);
+            reinterpret_cast<float *>(p.C)[(long long)tok * p.scm + n] = v;
+        } else {
+            skinny_out<F32A>(p, tok, r0 + row, acc);
+        }
     }
     skinny_peer_fence(p);
 }
@@ -1152,6 +1189,7 @@ int launch_skinny_f32a(int M, int N, int K, const float *A, int lda, const void 
     if (ldw < Kp || ldw % 8 != 0 || ((uintptr_t)W & 15) != 0)
         return fail(GEN9BLAS_ERR_INVALID_ARG, "F32-activation skinny GEMM: weight rows must be padded, 16-byte aligned");
     SkinnyArgs p;
+    memset(&p, 0, sizeof(p));
     const bool paired = M <= 8;
     p.Mc = paired ? 2 * M : M;   // ACT_PAIRED: virtual token rows (hi, lo interleaved)
     p.Nc = N; p.K = Kp;
@@ -1197,6 +1235,40 @@ int launch_skinny_f32a(int M, int N, int K, const float *A, int lda, const void 
     return launch_f32a_main<false, 8, ACT_PAIRED>(p, q, part, st);
 }
 
+int launch_skinny_f16w(int M, const void *A, bool ahalf, long long lda, const void *W, int K, int N, long long ldw,
+                       float *C, long long ldc, const float *bias, int gelu, const float *R, long long ldr, unsigned *nf,
+                       cudaStream_t st) {
+    DevState *d = dev_state();
+    if (!d) return G.status;
+    const int es = ahalf ? 2 : 4;
+    const int KC = (K + 255) / 256;
+    if (M < 1 || M > 16 || (N + 15) / 16 < d->sm_count || KC < WK_WARPS || K % 8 != 0 || ((uintptr_t)A & 15) != 0 ||
+        (lda * es) % 16 != 0 || ((uintptr_t)W & 15) != 0 || (ldw * 2) % 16 != 0)
+        return 1;
+    SkinnyArgs p;
+    memset(&p, 0, sizeof(p));
+    p.Mc = M; p.Nc = N; p.K = K;
+    p.alpha = 1.0f; p.beta = 0.0f;
+    p.a = A; p.sam = lda; p.sak = 1;
+    p.w = W; p.swn = ldw; p.swk = 1;
+    p.C = C; p.scm = ldc; p.scn = 1;
+    p.dst[0] = C; p.ndst = 1;
+    p.nf = nf;
+    p.bias = bias; p.gelu = gelu; p.R = R; p.ldr = ldr;
+    p.early_w = !queued_writes_overlap(d, W, ((size_t)(N - 1) * ldw + K) * sizeof(__half));
+    const bool fullk = K % 256 == 0, two = M > 8;
+    using Kern = void (*)(const SkinnyArgs, int);
+    Kern kern;
+    if (ahalf) kern = fullk ? (two ? wk_f16_blk<true, true, ACT_F16, true> : wk_f16_blk<true, false, ACT_F16, true>)
+                            : (two ? wk_f16_blk<false, true, ACT_F16, true> : wk_f16_blk<false, false, ACT_F16, true>);
+    else kern = fullk ? (two ? wk_f16_blk<true, true, ACT_F32H, true> : wk_f16_blk<true, false, ACT_F32H, true>)
+                      : (two ? wk_f16_blk<false, true, ACT_F32H, true> : wk_f16_blk<false, false, ACT_F32H, true>);
+    static bool attr[8][kMaxDevices] = {};
+    G9_CU(smem_limit_once(kern, SK_SMEM_BYTES, attr[(ahalf ? 4 : 0) + (fullk ? 2 : 0) + (two ? 1 : 0)]));
+    launch_pdl(kern, dim3((unsigned)((N + 15) / 16)), dim3(WK_WARPS * 32), SK_SMEM_BYTES, st, p, KC);
+    return launched("skinny_wk_f16_blk_f16w");
+}
+
 int launch_skinny(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, const void *B,
                   int ldb, double beta, void *C, int ldc, cudaStream_t st, void *const *peers, int npeers,
                   long long col_off) {
@@ -1215,6 +1287,7 @@ int launch_skinny(int type, int tA, int tB, int M, int N, int K, double alpha, c
     p.epoch = 0;
     p.err = nullptr;
     p.aligned = 0;
+    p.bias = nullptr; p.R = nullptr; p.ldr = 0; p.gelu = 0;
     if (peers && npeers > 0) {
         if (npeers > 8) return fail(GEN9BLAS_ERR_INVALID_ARG, "at most 8 ranks for the fused skinny GEMM + all-gather");
         for (int q = 0; q < npeers; q++) p.dst[q] = peers[q];

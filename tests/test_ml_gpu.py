@@ -119,6 +119,45 @@ def test_gemm_pb_f16w_ex_equals_unfused_ops(gpu_lib):
         gpu_lib.packed_b_free(P)
 
 
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 2048), (5, 3000, 2304), (16, 2500, 4104), (9, 4096, 2048)])
+def test_gemm_pb_f16w_single_kernel_shapes(gpu_lib, M, N, K):
+    """Shapes that run the FP16-weight product as one kernel (M <= 16, at least 16 weight rows per SM, K >= 2048):
+    the same bits as the FP16-accumulating-in-FP32 GEMM (gen9blas_gemm, GEN9BLAS_HS) of the FP16-rounded activations,
+    as the FP16-activation entry point, and as the unfused bias / GELU / residual chain; the oracle's bound; a
+    non-finite result flagged."""
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    W = (rng.standard_normal((N, K)) * 0.05).astype(np.float16)
+    bias = rng.standard_normal(N).astype(np.float32)
+    R = rng.standard_normal((M, N)).astype(np.float32)
+    P = pack_hs(gpu_lib, W)
+    try:
+        nf, nfp = nf_ptr()
+        C = np.full((M, N), np.nan, np.float32)
+        assert gpu_lib.gemm_pb_f16w(M, ptr(A), K, P, ptr(C), N, nfp) == 0, gpu_lib.error()
+        A16 = A.astype(np.float16)
+        G16 = np.zeros((M, N), np.float16)
+        assert gpu_lib.gemm(HS, 0, 1, M, N, K, 1.0, ptr(A16), K, ptr(W), K, 0.0, ptr(G16), N) == 0, gpu_lib.error()
+        assert nf.value == 0 and np.array_equal(C, G16.astype(np.float32))
+        want, _ = ml_ref.gemm_f16w(A, W)
+        ok, worst = f16w_close(C, A, W, want)
+        assert ok, worst
+        C2 = np.full((M, N), np.nan, np.float32)
+        assert gpu_lib.gemm_pb_f16w_h(M, ptr(A16), K, P, ptr(C2), N, nfp) == 0
+        assert np.array_equal(C2, C)
+        Cx = dev(R)                                   # fused bias + GELU + in-place residual on device memory
+        assert gpu_lib.gemm_pb_f16w_ex(M, ptr(dev(A)), K, P, ptr(Cx), N, ptr(dev(bias)), 1, ptr(Cx), N, nfp) == 0
+        U = C.copy()
+        assert gpu_lib.binop_rows(0, M, N, ptr(U), N, ptr(bias), 0, 1, ptr(U), N, 1) == 0
+        assert gpu_lib.gelu(M * N, ptr(U), ptr(U), 1) == 0
+        assert gpu_lib.binop_rows(0, M, N, ptr(U), N, ptr(R), N, 1, ptr(U), N, 1) == 0
+        assert np.array_equal(host(Cx, gpu_lib), U)
+        A[0, :] = 3000.0 * np.sign(W[0].astype(np.float32))   # C[0, 0] = 3000 · Σ|w|: beyond FP16
+        assert gpu_lib.gemm_pb_f16w(M, ptr(A), K, P, ptr(C), N, nfp) == 0
+        assert nf.value == 1
+    finally:
+        gpu_lib.packed_b_free(P)
+
+
 def test_gemm_pb_f16w_overflow_sets_nonfinite(gpu_lib):
     M, N, K = 4, 64, 256
     A = np.full((M, K), 200.0, np.float32)
