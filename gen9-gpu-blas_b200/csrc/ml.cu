@@ -121,6 +121,75 @@ __global__ void __launch_bounds__(256) rms_norm_k(const float *__restrict__ x, l
     }
 }
 
+// The same two norms with 16-byte accesses, for rows (and w, b) 16-byte aligned and K % 4 == 0: the same FP32
+// operations per element; the FP64 partial sums are taken four elements at a time.
+__global__ void __launch_bounds__(256) rms_norm_v4_k(const float *__restrict__ x, long long ldx, const float *__restrict__ w,
+                                                     float eps, float *__restrict__ y, long long ldy, int K) {
+    __shared__ double sh[8];
+    const float4 *xr = reinterpret_cast<const float4 *>(x + blockIdx.x * ldx);
+    const int K4 = K / 4;
+    double s = 0.0;
+    for (int i = threadIdx.x; i < K4; i += blockDim.x) {
+        const float4 v = xr[i];
+        s += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+    }
+    s = block_sum(s, sh);
+    const float mean = (float)(s / K);
+    const float scale = __frcp_rn(__fsqrt_rn(__fadd_rn(mean, eps)));
+    float4 *yr = reinterpret_cast<float4 *>(y + blockIdx.x * ldy);
+    const float4 *w4 = reinterpret_cast<const float4 *>(w);
+    for (int i = threadIdx.x; i < K4; i += blockDim.x) {
+        const float4 v = xr[i];
+        float4 o = make_float4(__fmul_rn(v.x, scale), __fmul_rn(v.y, scale), __fmul_rn(v.z, scale), __fmul_rn(v.w, scale));
+        if (w) {
+            const float4 q = w4[i];
+            o = make_float4(__fmul_rn(o.x, q.x), __fmul_rn(o.y, q.y), __fmul_rn(o.z, q.z), __fmul_rn(o.w, q.w));
+        }
+        yr[i] = o;
+    }
+}
+
+__global__ void __launch_bounds__(256) layer_norm_v4_k(const float *__restrict__ x, long long ldx,
+                                                       const float *__restrict__ w, const float *__restrict__ b,
+                                                       float eps, float *__restrict__ y, long long ldy, int K) {
+    __shared__ double sh[8];
+    const float4 *xr = reinterpret_cast<const float4 *>(x + blockIdx.x * ldx);
+    const int K4 = K / 4;
+    double s = 0.0;
+    for (int i = threadIdx.x; i < K4; i += blockDim.x) {
+        const float4 v = xr[i];
+        s += (double)v.x + (double)v.y + (double)v.z + (double)v.w;
+    }
+    s = block_sum(s, sh);
+    const float mean = (float)(s / K);
+    double v2 = 0.0;
+    for (int i = threadIdx.x; i < K4; i += blockDim.x) {
+        const float4 v = xr[i];
+        const double d0 = __fsub_rn(v.x, mean), d1 = __fsub_rn(v.y, mean), d2 = __fsub_rn(v.z, mean),
+                     d3 = __fsub_rn(v.w, mean);
+        v2 += d0 * d0 + d1 * d1 + d2 * d2 + d3 * d3;
+    }
+    v2 = block_sum(v2, sh);
+    const float scale = __frcp_rn(__fsqrt_rn(__fadd_rn((float)(v2 / K), eps)));
+    float4 *yr = reinterpret_cast<float4 *>(y + blockIdx.x * ldy);
+    for (int i = threadIdx.x; i < K4; i += blockDim.x) {
+        const float4 v = xr[i];
+        float o[4] = {__fmul_rn(__fsub_rn(v.x, mean), scale), __fmul_rn(__fsub_rn(v.y, mean), scale),
+                      __fmul_rn(__fsub_rn(v.z, mean), scale), __fmul_rn(__fsub_rn(v.w, mean), scale)};
+        if (w) {
+            const float4 q = reinterpret_cast<const float4 *>(w)[i];
+            o[0] = __fmul_rn(o[0], q.x); o[1] = __fmul_rn(o[1], q.y); o[2] = __fmul_rn(o[2], q.z); o[3] = __fmul_rn(o[3], q.w);
+        }
+        if (b) {
+            const float4 q = reinterpret_cast<const float4 *>(b)[i];
+            o[0] = __fadd_rn(o[0], q.x); o[1] = __fadd_rn(o[1], q.y); o[2] = __fadd_rn(o[2], q.z); o[3] = __fadd_rn(o[3], q.w);
+        }
+        yr[i] = make_float4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+bool on16(const void *p) { return ((uintptr_t)p & 15) == 0; }
+
 // ggml NORM (+ MUL by w, ADD b): mean and variance over the row (FP64 sums, FP32 mean / scale),
 // y = (x − mean) · scale [· w] [+ b]; pack: also FP16 rows of Kp (zero past K) for a following GEMM.
 __global__ void __launch_bounds__(256) layer_norm_k(const float *__restrict__ x, long long ldx, const float *__restrict__ w,
@@ -418,6 +487,7 @@ struct AttnArgs {
     float qscale;
     float *part;
     float *O;
+    int csteps;   // tensor-core kernel: 32-key steps per warp (a chunk is 4 warps x csteps x 32 keys)
 };
 
 __global__ void __launch_bounds__(256) attn_part_k(AttnArgs a) {
@@ -485,26 +555,307 @@ __global__ void __launch_bounds__(256) attn_part_k(AttnArgs a) {
         if (live && d0 + i < a.D) pp[2 + d0 + i] = acc[i];
 }
 
-// O[s][t][h][d] = Σ_c acc_c 2^(m_c − M) / Σ_c l_c 2^(m_c − M) over the chunks with l > 0, in chunk order.
-__global__ void attn_merge_k(AttnArgs a) {
-    const long long n = (long long)a.ns * a.nq * a.H * a.D;
-    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
-        const int d = (int)(e % a.D);
-        const long long row = e / a.D;   // (s · nq + t) · H + h
-        const float *pb = a.part + row * a.nchunk * (2 + a.D);
-        float M = -INFINITY;
-        for (int c = 0; c < a.nchunk; c++)
-            if (pb[(long long)c * (2 + a.D) + 1] > 0.0f) M = fmaxf(M, pb[(long long)c * (2 + a.D)]);
-        float L = 0.0f, acc = 0.0f;
-        for (int c = 0; c < a.nchunk; c++) {
-            const float *pc = pb + (long long)c * (2 + a.D);
-            if (pc[1] > 0.0f) {
-                const float w = exp2f(pc[0] - M);
-                L += pc[1] * w;
-                acc += pc[2 + d] * w;
+// O[s][t][h][d] = Σ_c acc_c 2^(m_c − M) / Σ_c l_c 2^(m_c − M) over the chunks with l > 0 (M their largest m). One
+// 128-thread CTA per output row (s, t, h): the threads reduce M over the chunks, then thread d walks the chunks in
+// chunk order (eight chunks' loads in flight) adding its dimension and, redundantly in every thread, the denominator.
+// A chunk whose l is not positive is skipped by a select, so whatever its other words hold never enters the sums.
+__global__ void __launch_bounds__(128) attn_merge_k(AttnArgs a) {
+    __shared__ float red[4];
+    const long long row = blockIdx.x;   // (s · nq + t) · H + h
+    const int D = a.D, stride = 2 + D, nc = a.nchunk, d = threadIdx.x;
+    const float *pb = a.part + row * nc * stride;
+    float M = -INFINITY;
+    for (int c = threadIdx.x; c < nc; c += 128)
+        if (pb[(long long)c * stride + 1] > 0.0f) M = fmaxf(M, pb[(long long)c * stride]);
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = M;
+    __syncthreads();
+    M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    const int dd = d < D ? d : 0;
+    float L = 0.0f, acc = 0.0f;
+#pragma unroll 8
+    for (int c = 0; c < nc; c++) {
+        const float *pc = pb + (long long)c * stride;
+        const float lc = pc[1], mc = pc[0], xc = pc[2 + dd];
+        const bool use = lc > 0.0f;
+        const float w = use ? exp2f(mc - M) : 0.0f;
+        L = use ? fmaf(lc, w, L) : L;
+        acc = use ? fmaf(xc, w, acc) : acc;
+    }
+    if (d < D) a.O[row * D + d] = acc / L;
+}
+
+// Grouped split-K decoding attention on the tensor cores (D % 16 == 0, D <= 128, G = H / HKV <= 8, 16-byte aligned
+// K / V rows). CTA = (chunk of 4 · csteps · 32 keys, KV head g, stream-token); each of its 4 warps takes csteps steps of
+// 32 keys for all G query heads of g (the 8 head slots of the MMA's N side), so every K / V row is read from memory once.
+// Per step, with the 32 K rows and V rows in padded shared rows (cp.async, 16 bytes per copy; rows past the visible
+// keys are zero-filled):
+//   scores  Sᵀ[32 keys × 8 heads] = K · Qᵀ by mma.sync m16n8k16, K from the shared rows (ldmatrix) as A, the query as
+//           B in two FP16 parts (hi = fp16(q), lo = fp16(q − hi)) after scaling each head's query by a power of two
+//           that puts its largest |q| in [2^13, 2^14), so both parts stay normal and the products keep 22 of the
+//           query's 24 bits; FP32 accumulation, the power of two divided out of every score exactly;
+//   softmax running max per head over the lanes that hold the head, p = 2^(s − m) in FP32, per-lane partial sums;
+//   values  Oᵀ[D × 8 heads] += Vᵀ · Pᵀ, V from the shared rows by ldmatrix.trans as A, P in two FP16 parts as B
+//           (movmatrix turns the scores' accumulator layout into the B layout).
+// The next step's K rows are requested once this step's are scored and its V rows once these are summed, so each load
+// overlaps the other half of the step. The warps' (m, l, acc) are merged in shared memory into one partial per (head,
+// chunk), in the layout attn_merge_k reads.
+constexpr int AT2_WARPS = 4, AT2_KEYS = 32, AT2_GMAX = 8, AT2_SMAX = 8;
+__host__ __device__ constexpr int at2_rowb(int D) { return D * 2 + 16; }
+__host__ __device__ constexpr size_t at2_smem(int D) { return (size_t)AT2_WARPS * 2 * AT2_KEYS * at2_rowb(D); }
+
+__device__ __forceinline__ void at_ldsm(unsigned addr, unsigned (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr) : "memory");
+}
+__device__ __forceinline__ void at_ldsm_t(unsigned addr, unsigned (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr) : "memory");
+}
+__device__ __forceinline__ unsigned at_movt(unsigned x) {
+    unsigned y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(y) : "r"(x));
+    return y;
+}
+__device__ __forceinline__ void at_mma(float (&c)[4], const unsigned (&a)[4], unsigned b0, unsigned b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};\n"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// (x0, x1) as FP16 hi and lo parts: hi = fp16(x), lo = fp16(x − hi), element 0 in the low half of each word
+__device__ __forceinline__ void at_split(float x0, float x1, unsigned &hi, unsigned &lo) {
+    const __half2 h = __floats2half2_rn(x0, x1);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
+    hi = *reinterpret_cast<const unsigned *>(&h);
+    lo = *reinterpret_cast<const unsigned *>(&l);
+}
+__device__ __forceinline__ float at_pow2(int e) { return __uint_as_float((unsigned)(e + 127) << 23); }   // |e| <= 126
+
+template <int DT>
+__global__ void __launch_bounds__(AT2_WARPS * 32, 3) attn_tc_k(AttnArgs a) {
+    constexpr int D = DT * 16, ROWB = at2_rowb(D), PIECES = D / 8;
+    extern __shared__ __align__(16) uint8_t at_sm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
+    const int G = a.H / a.HKV;
+    const int c = blockIdx.x, g = blockIdx.y, st = blockIdx.z;
+    const int t = st % a.nq, s = st / a.nq;
+    uint8_t *kst = at_sm + (size_t)warp * 2 * AT2_KEYS * ROWB;   // this warp's K rows, then its V rows
+    uint8_t *vst = kst + AT2_KEYS * ROWB;
+    int vt = a.vis[s] + a.dvis * t;
+    vt = vt < a.nk ? vt : a.nk;
+    const int span = AT2_KEYS * a.csteps;
+    const int kw0 = (c * AT2_WARPS + warp) * span;
+    const int kw1 = min(kw0 + span, vt);
+    const int nsteps = kw1 > kw0 ? (kw1 - kw0 + AT2_KEYS - 1) / AT2_KEYS : 0;
+    const __half *Kb = a.K + s * a.ks + g * a.kh, *Vb = a.V + s * a.vs + g * a.vh;
+    // the 32 rows of step `step` of one tensor into its staging rows (zeros past the visible keys), one commit group
+    auto stage = [&](const __half *base, long long rs, uint8_t *dst, int step) {
+        const int r0 = kw0 + step * AT2_KEYS;
+#pragma unroll
+        for (int it = 0; it < PIECES; it++) {
+            const int i = it * 32 + lane, r = i / PIECES, q = i % PIECES;
+            uint8_t *sp = dst + r * ROWB + q * 16;
+            if (r0 + r < kw1)
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(
+                                 (unsigned)__cvta_generic_to_shared(sp)),
+                             "l"(base + (long long)(r0 + r) * rs + q * 8) : "memory");
+            else
+                *reinterpret_cast<uint4 *>(sp) = make_uint4(0u, 0u, 0u, 0u);
+        }
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+    };
+    if (nsteps > 0) {
+        stage(Kb, a.kk, kst, 0);
+        stage(Vb, a.vk, vst, 0);
+    }
+    // query fragments (B of the scores): lane holds head slot gq, dims 16kt + 2tq + {0, 1} and {8, 9}
+    float qv[DT][4];
+    float qmax = 0.0f;
+    const bool hlive = gq < G;
+    const float *qp = a.Q + s * a.qs + t * a.qt + (long long)(g * G + (hlive ? gq : 0)) * a.qh;
+#pragma unroll
+    for (int kt = 0; kt < DT; kt++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float x = hlive ? qp[16 * kt + 2 * tq + (i & 1) + (i >> 1) * 8] * a.qscale : 0.0f;
+            qv[kt][i] = x;
+            qmax = fmaxf(qmax, fabsf(x));
+        }
+    qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, 1));
+    qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, 2));   // the four lanes of head slot gq
+    int ex = 0;
+    if (qmax > 0.0f) {
+        const int be = (int)((__float_as_uint(qmax) >> 23) & 0xffu);   // qmax < 2^(be − 126)
+        ex = min(max(140 - be, -126), 126);                              // qmax · 2^ex < 2^14
+    }
+    const float qsc = at_pow2(ex), qinv = at_pow2(-ex);
+    unsigned qh[DT][2], ql[DT][2];
+#pragma unroll
+    for (int kt = 0; kt < DT; kt++)
+#pragma unroll
+        for (int j = 0; j < 2; j++) at_split(qv[kt][2 * j] * qsc, qv[kt][2 * j + 1] * qsc, qh[kt][j], ql[kt][j]);
+    // this lane's score columns are head slots 2tq and 2tq + 1; their scale factors live in lanes 8tq and 8tq + 4
+    const float inv[2] = {__shfl_sync(0xffffffffu, qinv, 8 * tq), __shfl_sync(0xffffffffu, qinv, 8 * tq + 4)};
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f};
+    float o[DT][4];
+#pragma unroll
+    for (int dt = 0; dt < DT; dt++) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.0f;
+    const unsigned kbase = (unsigned)__cvta_generic_to_shared(kst), vbase = (unsigned)__cvta_generic_to_shared(vst);
+    const unsigned koff = ((lane & 7) + ((lane >> 3) & 1) * 8) * ROWB + (lane >> 4) * 16;   // A = K rows
+    const unsigned voff = ((lane & 7) + (lane >> 4) * 8) * ROWB + ((lane >> 3) & 1) * 16;   // A = Vᵀ (trans)
+    for (int step = 0; step < nsteps; step++) {
+        const int r0 = kw0 + step * AT2_KEYS;
+        const bool more = step + 1 < nsteps;
+        asm volatile("cp.async.wait_group 1;\n" ::: "memory");   // this step's K rows (its V rows may be in flight)
+        __syncwarp();
+        float sc[2][4];
+#pragma unroll
+        for (int mt = 0; mt < 2; mt++) {
+            sc[mt][0] = sc[mt][1] = sc[mt][2] = sc[mt][3] = 0.0f;
+#pragma unroll
+            for (int kt = 0; kt < DT; kt++) {
+                unsigned af[4];
+                at_ldsm(kbase + koff + mt * 16 * ROWB + kt * 32, af);
+                at_mma(sc[mt], af, qh[kt][0], qh[kt][1]);
+                at_mma(sc[mt], af, ql[kt][0], ql[kt][1]);
             }
         }
-        a.O[e] = acc / L;
+        __syncwarp();   // every lane's K fragments are in registers before the next step's copy overwrites the rows
+        if (more) stage(Kb, a.kk, kst, step + 1);
+        // sc[mt][2·hh + j]: key r0 + 16mt + gq + 8hh, head slot 2tq + j
+        float pr[2][4];
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            float x[4];
+            float mx = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int mt = i >> 1, hh = i & 1;
+                x[i] = r0 + 16 * mt + gq + 8 * hh < kw1 ? sc[mt][2 * hh + j] * inv[j] : -INFINITY;
+                mx = fmaxf(mx, x[i]);
+            }
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            const float mn = fmaxf(m[j], mx);
+            const float alpha = exp2f(m[j] - mn);   // 0 on the first step (m = -inf)
+            float ps = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float p = exp2f(x[i] - mn);
+                pr[i >> 1][2 * (i & 1) + j] = p;
+                ps += p;
+            }
+            l[j] = fmaf(l[j], alpha, ps);
+#pragma unroll
+            for (int dt = 0; dt < DT; dt++) {
+                o[dt][j] *= alpha;
+                o[dt][2 + j] *= alpha;
+            }
+            m[j] = mn;
+        }
+        if (more) asm volatile("cp.async.wait_group 1;\n" ::: "memory");   // this step's V rows
+        else asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+        __syncwarp();
+#pragma unroll
+        for (int ks = 0; ks < 2; ks++) {
+            unsigned h01, l01, h23, l23;
+            at_split(pr[ks][0], pr[ks][1], h01, l01);   // key 16ks + gq, head slots 2tq, 2tq + 1
+            at_split(pr[ks][2], pr[ks][3], h23, l23);   // key 16ks + gq + 8
+            const unsigned bh0 = at_movt(h01), bh1 = at_movt(h23), bl0 = at_movt(l01), bl1 = at_movt(l23);
+#pragma unroll
+            for (int dt = 0; dt < DT; dt++) {
+                unsigned af[4];
+                at_ldsm_t(vbase + voff + ks * 16 * ROWB + dt * 32, af);
+                at_mma(o[dt], af, bh0, bh1);
+                at_mma(o[dt], af, bl0, bl1);
+            }
+        }
+        __syncwarp();   // every lane's V fragments are in registers before the next step's copy overwrites the rows
+        if (more) stage(Vb, a.vk, vst, step + 1);
+    }
+#pragma unroll
+    for (int j = 0; j < 2; j++) {   // the per-lane sums over the 8 lanes of each head slot
+        l[j] += __shfl_xor_sync(0xffffffffu, l[j], 4);
+        l[j] += __shfl_xor_sync(0xffffffffu, l[j], 8);
+        l[j] += __shfl_xor_sync(0xffffffffu, l[j], 16);
+    }
+    // merge the four warps: (m, l) per warp and head slot, acc per warp, head slot and dimension
+    __syncthreads();   // every warp is done with its staging rows
+    float *mw = reinterpret_cast<float *>(at_sm);   // [warp][slot]: m, then l
+    float *lw = mw + AT2_WARPS * AT2_GMAX;
+    float *aw = lw + AT2_WARPS * AT2_GMAX;         // [warp][slot][D]
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        const int hs = 2 * tq + j;
+        if (hs >= G) continue;
+        if (gq == 0) {
+            mw[warp * AT2_GMAX + hs] = m[j];
+            lw[warp * AT2_GMAX + hs] = l[j];
+        }
+        float *ap = aw + (warp * AT2_GMAX + hs) * D + gq;
+#pragma unroll
+        for (int dt = 0; dt < DT; dt++) {
+            ap[16 * dt] = o[dt][j];
+            ap[16 * dt + 8] = o[dt][2 + j];
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * D; i += AT2_WARPS * 32) {
+        const int h = i / D, d = i - h * D;
+        float M = -INFINITY;
+        for (int w = 0; w < AT2_WARPS; w++)
+            if (lw[w * AT2_GMAX + h] > 0.0f) M = fmaxf(M, mw[w * AT2_GMAX + h]);
+        float L = 0.0f, acc = 0.0f;
+        if (M > -INFINITY) {
+            for (int w = 0; w < AT2_WARPS; w++) {
+                if (!(lw[w * AT2_GMAX + h] > 0.0f)) continue;
+                const float f = exp2f(mw[w * AT2_GMAX + h] - M);
+                L += lw[w * AT2_GMAX + h] * f;
+                acc += aw[(w * AT2_GMAX + h) * D + d] * f;
+            }
+        }
+        float *pp = a.part + (((long long)st * a.H + g * G + h) * a.nchunk + c) * (2 + D);
+        pp[2 + d] = acc;
+        if (d == 0) {
+            pp[0] = M;
+            pp[1] = L;
+        }
+    }
+}
+
+// Launch of the tensor-core kernel for D = 16·DT; `plan` only reports its resident CTAs per SM (occupancy query once
+// per device) and launches nothing.
+template <int DT>
+int attn_tc_run(const AttnArgs &a, cudaStream_t st, bool plan, int *per_sm) {
+    static bool attr[kMaxDevices] = {};
+    static int occ[kMaxDevices] = {};
+    G9_CU(smem_limit_once(attn_tc_k<DT>, (int)at2_smem(DT * 16), attr));
+    DevState *d = dev_state();
+    if (plan) {
+        if (!occ[d->dev])
+            G9_CU(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ[d->dev], attn_tc_k<DT>, AT2_WARPS * 32,
+                                                                at2_smem(DT * 16)));
+        *per_sm = std::max(occ[d->dev], 1);
+        return 0;
+    }
+    attn_tc_k<DT><<<dim3((unsigned)a.nchunk, (unsigned)a.HKV, (unsigned)(a.ns * a.nq)), AT2_WARPS * 32,
+                    at2_smem(DT * 16), st>>>(a);
+    return launched("attn_tc");
+}
+
+int attn_tc(const AttnArgs &a, cudaStream_t st, bool plan, int *per_sm) {
+    switch (a.D / 16) {
+    case 1: return attn_tc_run<1>(a, st, plan, per_sm);
+    case 2: return attn_tc_run<2>(a, st, plan, per_sm);
+    case 3: return attn_tc_run<3>(a, st, plan, per_sm);
+    case 4: return attn_tc_run<4>(a, st, plan, per_sm);
+    case 5: return attn_tc_run<5>(a, st, plan, per_sm);
+    case 6: return attn_tc_run<6>(a, st, plan, per_sm);
+    case 7: return attn_tc_run<7>(a, st, plan, per_sm);
+    default: return attn_tc_run<8>(a, st, plan, per_sm);
     }
 }
 
@@ -518,21 +869,49 @@ int attention(AttnArgs a, int sync, const char *who) {
     if (!d) return G.status;
     if (!on_device(a.Q) || !on_device(a.K) || !on_device(a.V) || !on_device(a.O))
         return fail(GEN9BLAS_ERR_INVALID_ARG, "%s: Q, K, V and O must be device or managed memory", who);
-    a.nchunk = (a.nk + ATT_CHUNK - 1) / ATT_CHUNK;
+    // the tensor-core kernel when D is a multiple of 16, rows are 16-byte vectors and a KV head serves at most 8
+    // query heads; otherwise the per-head CUDA-core kernel
+    const bool tc = a.D % 16 == 0 && a.H / a.HKV <= AT2_GMAX && a.ns * a.nq <= 65535 && a.HKV <= 65535 &&
+                    ((uintptr_t)a.K & 15) == 0 && ((uintptr_t)a.V & 15) == 0 && (a.kk * 2) % 16 == 0 &&
+                    (a.kh * 2) % 16 == 0 && (a.ks * 2) % 16 == 0 && (a.vk * 2) % 16 == 0 && (a.vh * 2) % 16 == 0 &&
+                    (a.vs * 2) % 16 == 0;
+    cudaStream_t st = stream();
+    if (tc) {
+        // steps per warp: the fewest waves × (steps + a CTA's fixed cost of about a quarter step)
+        int per_sm = 1;
+        G9_TRY(attn_tc(a, st, true, &per_sm));
+        const long long slots = (long long)per_sm * d->sm_count, rows = (long long)a.HKV * a.ns * a.nq;
+        double best = 1e300;
+        for (int S = 1; S <= AT2_SMAX; S++) {
+            const long long span = (long long)AT2_WARPS * AT2_KEYS * S;
+            const long long ctas = (a.nk + span - 1) / span * rows;
+            const double cost = (double)((ctas + slots - 1) / slots) * (S + 0.25);
+            if (cost < best) {
+                best = cost;
+                a.csteps = S;
+            }
+        }
+        a.nchunk = (int)((a.nk + (long long)AT2_WARPS * AT2_KEYS * a.csteps - 1) / (AT2_WARPS * AT2_KEYS * a.csteps));
+    } else {
+        a.nchunk = (a.nk + ATT_CHUNK - 1) / ATT_CHUNK;
+    }
     const long long warps = (long long)a.ns * a.nq * a.H * a.nchunk;
     const size_t part_bytes = round256((size_t)warps * (2 + a.D) * sizeof(float));
     void *buf = nullptr;
     G9_TRY(ml_buffer(part_bytes + (size_t)a.ns * sizeof(int), &buf));
     a.part = (float *)buf;
-    cudaStream_t st = stream();
     if (!on_device(a.vis)) {   // the visible counts (ns ints) behind the partial results
         int *vd = (int *)((char *)buf + part_bytes);
         G9_CU(cudaMemcpyAsync(vd, a.vis, (size_t)a.ns * sizeof(int), cudaMemcpyHostToDevice, st));
         a.vis = vd;
     }
-    attn_part_k<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(a);
-    G9_TRY(launched("attn_part"));
-    attn_merge_k<<<grid_n((long long)a.ns * a.nq * a.H * a.D, d->sm_count), 256, 0, st>>>(a);
+    if (tc) {
+        G9_TRY(attn_tc(a, st, false, nullptr));
+    } else {
+        attn_part_k<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(a);
+        G9_TRY(launched("attn_part"));
+    }
+    attn_merge_k<<<(unsigned)((long long)a.ns * a.nq * a.H), 128, 0, st>>>(a);
     G9_TRY(launched("attn_merge"));
     Operand out;
     out.user = out.dptr = a.O;
@@ -573,7 +952,10 @@ GEN9BLAS_API int gen9blas_rms_norm(int M, int K, const float *X, int ldx, const 
     G9_TRY(c.big(Y, ((size_t)(M - 1) * ldy + K) * 4, X == Y || ldy != K, true, &y));
     G9_TRY(c.reserve(w ? round256((size_t)K * 4) : 0));
     G9_TRY(c.in(w, (size_t)K * 4, &wd, st));
-    rms_norm_k<<<M, 256, 0, st>>>((const float *)x, ldx, (const float *)wd, eps, (float *)y, ldy, K);
+    if (K % 4 == 0 && ldx % 4 == 0 && ldy % 4 == 0 && on16(x) && on16(y) && (!wd || on16(wd)))
+        rms_norm_v4_k<<<M, 256, 0, st>>>((const float *)x, ldx, (const float *)wd, eps, (float *)y, ldy, K);
+    else
+        rms_norm_k<<<M, 256, 0, st>>>((const float *)x, ldx, (const float *)wd, eps, (float *)y, ldy, K);
     G9_TRY(launched("rms_norm"));
     return c.finish(sync);
 }
@@ -594,8 +976,13 @@ GEN9BLAS_API int gen9blas_layer_norm(int M, int K, const float *X, int ldx, cons
     G9_TRY(c.reserve(2 * round256((size_t)K * 4)));
     G9_TRY(c.in(w, (size_t)K * 4, &wd, st));
     G9_TRY(c.in(b, (size_t)K * 4, &bd, st));
-    layer_norm_k<<<M, 256, 0, st>>>((const float *)x, ldx, (const float *)wd, (const float *)bd, eps, (float *)y, ldy, K,
-                                    nullptr, 0);
+    if (K % 4 == 0 && ldx % 4 == 0 && ldy % 4 == 0 && on16(x) && on16(y) && (!wd || on16(wd)) &&
+        (!bd || on16(bd)))
+        layer_norm_v4_k<<<M, 256, 0, st>>>((const float *)x, ldx, (const float *)wd, (const float *)bd, eps, (float *)y,
+                                           ldy, K);
+    else
+        layer_norm_k<<<M, 256, 0, st>>>((const float *)x, ldx, (const float *)wd, (const float *)bd, eps, (float *)y, ldy,
+                                        K, nullptr, 0);
     G9_TRY(launched("layer_norm"));
     return c.finish(sync);
 }
@@ -935,7 +1322,7 @@ GEN9BLAS_API int gen9blas_attn_dec(int D, int H, int HKV, int ns, int nq, int nk
                                    float scale, const int *vis, int dvis, int chunk, int sync) {
     (void)k_bytes;
     (void)v_bytes;
-    (void)chunk;   // the chunk length is this build's own (ATT_CHUNK keys)
+    (void)chunk;   // the chunk length is this build's own (chosen per call from the grid it gives)
     if (int e = begin_op()) return e;
     if (!vis) return fail(GEN9BLAS_ERR_INVALID_ARG, "attn_dec: no visible counts");
     AttnArgs a{D, H, HKV, ns, nq, nk, 0, dvis, Q, qt, qh, qs, (const __half *)K, kk, kh, ks, (const __half *)V, vk, vh, vs,

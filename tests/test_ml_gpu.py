@@ -314,9 +314,10 @@ def test_layer_norm_pack_feeds_gemm_pa(gpu_lib):
 
 
 # ------------------------------------------------------------------------------------------- elementwise ops
+@pytest.mark.parametrize("K,ld", [(4099, 4100), (4096, 4100)])   # scalar rows; 16-byte rows (vector kernels)
 @pytest.mark.parametrize("on_dev", [False, True])
-def test_norms(gpu_lib, on_dev):
-    M, K, ld = 33, 4096 + 3, 4100
+def test_norms(gpu_lib, on_dev, K, ld):
+    M = 33
     Xf = rng.standard_normal((M, ld)).astype(np.float32) * 3
     w, b = rng.standard_normal(K).astype(np.float32), rng.standard_normal(K).astype(np.float32)
     for fn in ("rms", "ln"):
@@ -509,9 +510,12 @@ def _close_attn(got, want):
     return np.max(np.abs(got - want)) <= 2e-5 * max(1.0, np.max(np.abs(want)))
 
 
-@pytest.mark.parametrize("D,H,HKV", [(128, 32, 8), (128, 8, 8), (64, 12, 2)])
-def test_attn_dec_streams(gpu_lib, D, H, HKV):
-    ns, nq, nk, pad = 3, 2, 700, 5
+@pytest.mark.parametrize("pad", [5, 8])
+@pytest.mark.parametrize("D,H,HKV", [(128, 32, 8), (128, 8, 8), (64, 12, 2), (96, 16, 2), (128, 36, 4)])
+def test_attn_dec_streams(gpu_lib, D, H, HKV, pad):
+    """Row padding 8 (16-byte rows, D a multiple of 16, at most 8 query heads per KV head) takes the tensor-core
+    kernel, padding 5 and the 9-heads-per-KV-head case the per-head one."""
+    ns, nq, nk = 3, 2, 700
     Q = dev(rng.standard_normal((ns, nq, H, D)).astype(np.float32))
     # llama.cpp cache layout with padding: [s][key][g][D + pad]
     Kc = rng.standard_normal((ns, nk + 9, HKV, D + pad)).astype(np.float16)
@@ -530,6 +534,49 @@ def test_attn_dec_streams(gpu_lib, D, H, HKV):
         want = ml_ref.attention(Qh[s], Kc[s, :nk, :, :D], Vc[s, :nk, :, :D], scale,
                                 [min(vis[s] + t, nk) for t in range(nq)])
         assert _close_attn(got[s], want), s
+
+
+@pytest.mark.parametrize("qmul", [1e-6, 1.0, 3e3])
+def test_attn_dec_query_scales(gpu_lib, qmul):
+    """Tiny and huge queries: the tensor-core kernel splits each head's scaled query into two FP16 parts after a
+    power-of-two normalisation, so neither underflows nor overflows; 3e3 makes the softmax nearly one-hot."""
+    D, H, HKV, ns, nq, nk = 64, 8, 2, 2, 1, 300
+    Q = dev((rng.standard_normal((ns, nq, H, D)) * qmul).astype(np.float32))
+    Kc = rng.standard_normal((ns, nk, HKV, D)).astype(np.float16)
+    Vc = rng.standard_normal((ns, nk, HKV, D)).astype(np.float16)
+    Kd, Vd = dev(Kc), dev(Vc)
+    O = dev(np.full((ns, nq, H, D), np.nan, np.float32))
+    vis = np.array([77, 300], np.int32)
+    kk, kh, ks, scale = HKV * D, D, nk * HKV * D, 0.125
+    assert gpu_lib.attn_dec(D, H, HKV, ns, nq, nk, ptr(Q), H * D, D, nq * H * D, ptr(Kd), kk, kh, ks, Kd.numel() * 2,
+                            ptr(Vd), kk, kh, ks, Vd.numel() * 2, ptr(O), scale, ptr(vis), 0, 64, 1) == 0, gpu_lib.error()
+    got = host(O, gpu_lib)
+    Qh = Q.cpu().numpy()
+    for s in range(ns):
+        want = ml_ref.attention(Qh[s], Kc[s], Vc[s], scale, [int(vis[s])])
+        assert _close_attn(got[s], want), (s, np.max(np.abs(got[s] - want)))
+
+
+def test_attn_dec_long_chunks(gpu_lib):
+    """Enough (stream, KV head) rows that the planner gives each warp several 32-key steps (the copy of the next
+    step's rows overlapping this step's MMAs), with visible counts that end inside a step, a warp and a chunk."""
+    D, H, HKV, ns, nq, nk = 128, 32, 8, 16, 1, 8192
+    g = torch.Generator(device="cuda")
+    g.manual_seed(21)
+    Kd = torch.randn(ns, nk, HKV, D, device="cuda", generator=g).half()
+    Vd = torch.randn(ns, nk, HKV, D, device="cuda", generator=g).half()
+    Q = torch.randn(ns, nq, H, D, device="cuda", generator=g)
+    O = torch.full((ns, nq, H, D), float("nan"), device="cuda")
+    vis = np.array([8192, 1, 31, 33, 127, 129, 640, 641, 1000, 2047, 4097, 5000, 6143, 7777, 8191, 3], np.int32)
+    kk, kh, ks, scale = HKV * D, D, nk * HKV * D, D ** -0.5
+    assert gpu_lib.attn_dec(D, H, HKV, ns, nq, nk, Q.data_ptr(), H * D, D, nq * H * D, Kd.data_ptr(), kk, kh, ks,
+                            Kd.numel() * 2, Vd.data_ptr(), kk, kh, ks, Vd.numel() * 2, O.data_ptr(), scale, ptr(vis),
+                            0, 64, 1) == 0, gpu_lib.error()
+    got = O.cpu().numpy()
+    Qh, Kh, Vh = Q.cpu().numpy(), Kd.cpu().numpy(), Vd.cpu().numpy()
+    for s in range(ns):
+        want = ml_ref.attention(Qh[s], Kh[s], Vh[s], scale, [int(vis[s])])
+        assert _close_attn(got[s], want), (s, int(vis[s]), np.max(np.abs(got[s] - want)))
 
 
 def test_attn_f16kv_prefill_causal_and_streams(gpu_lib):
