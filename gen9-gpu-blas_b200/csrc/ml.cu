@@ -14,6 +14,7 @@
 #include "common.cuh"
 #include "gen9blas_ml.h"
 #include "internal.h"
+#include "sm100.cuh"
 #include <cmath>
 #include <cstring>
 #include <new>
@@ -487,7 +488,12 @@ struct AttnArgs {
     float qscale;
     float *part;
     float *O;
-    int csteps;   // tensor-core kernel: 32-key steps per warp (a chunk is 4 warps x csteps x 32 keys)
+    // tensor-core kernel (stream-K over the 32-key steps of all rows r = (stream-token, KV head)): steps per row,
+    // their total over the rows, the grid size, and the device error word a timed-out wait sets
+    int nsr;
+    long long total;
+    int nblk;
+    unsigned *err;
 };
 
 __global__ void __launch_bounds__(256) attn_part_k(AttnArgs a) {
@@ -555,18 +561,38 @@ __global__ void __launch_bounds__(256) attn_part_k(AttnArgs a) {
         if (live && d0 + i < a.D) pp[2 + d0 + i] = acc[i];
 }
 
-// O[s][t][h][d] = Σ_c acc_c 2^(m_c − M) / Σ_c l_c 2^(m_c − M) over the chunks with l > 0 (M their largest m). One
-// 128-thread CTA per output row (s, t, h): the threads reduce M over the chunks, then thread d walks the chunks in
-// chunk order (eight chunks' loads in flight) adding its dimension and, redundantly in every thread, the denominator.
-// A chunk whose l is not positive is skipped by a select, so whatever its other words hold never enters the sums.
+// CTA of the stream-K split (grid B over T steps) that holds step x: the last b with ⌊b·T / B⌋ <= x.
+__host__ __device__ __forceinline__ long long at_blk_of(long long x, long long T, long long B) { return (x * B + B - 1) / T; }
+
+// O[s][t][h][d] = Σ_c acc_c 2^(m_c − M) / Σ_c l_c 2^(m_c − M) over the partials c with l > 0 (M their largest m). One
+// 128-thread CTA per output row (s, t, h): the threads reduce M over the partials, then thread d walks them in key
+// order (eight partials' loads in flight) adding its dimension and, redundantly in every thread, the denominator. A
+// partial whose l is not positive is skipped by a select, so whatever its other words hold never enters the sums.
+// SK: the partials of the tensor-core kernel, slots b + r for the CTAs b that held steps of row r = (s, t, KV head),
+// [head slot] inside a slot; otherwise the per-head kernel's [row][chunk].
+template <bool SK>
 __global__ void __launch_bounds__(128) attn_merge_k(AttnArgs a) {
     __shared__ float red[4];
     const long long row = blockIdx.x;   // (s · nq + t) · H + h
-    const int D = a.D, stride = 2 + D, nc = a.nchunk, d = threadIdx.x;
-    const float *pb = a.part + row * nc * stride;
+    const int D = a.D, stride = 2 + D, d = threadIdx.x;
+    const float *pb;
+    long long pstride;
+    int nc;
+    if (SK) {
+        const int G = a.H / a.HKV, h = (int)(row % a.H);
+        const long long r = row / a.H * a.HKV + h / G;
+        const long long b0 = at_blk_of(r * a.nsr, a.total, a.nblk), b1 = at_blk_of((r + 1) * a.nsr - 1, a.total, a.nblk);
+        pb = a.part + ((b0 + r) * G + h % G) * stride;
+        pstride = (long long)G * stride;
+        nc = (int)(b1 - b0 + 1);
+    } else {
+        pb = a.part + row * a.nchunk * stride;
+        pstride = stride;
+        nc = a.nchunk;
+    }
     float M = -INFINITY;
     for (int c = threadIdx.x; c < nc; c += 128)
-        if (pb[(long long)c * stride + 1] > 0.0f) M = fmaxf(M, pb[(long long)c * stride]);
+        if (pb[c * pstride + 1] > 0.0f) M = fmaxf(M, pb[c * pstride]);
     for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = M;
     __syncthreads();
@@ -575,7 +601,7 @@ __global__ void __launch_bounds__(128) attn_merge_k(AttnArgs a) {
     float L = 0.0f, acc = 0.0f;
 #pragma unroll 8
     for (int c = 0; c < nc; c++) {
-        const float *pc = pb + (long long)c * stride;
+        const float *pc = pb + c * pstride;
         const float lc = pc[1], mc = pc[0], xc = pc[2 + dd];
         const bool use = lc > 0.0f;
         const float w = use ? exp2f(mc - M) : 0.0f;
@@ -585,11 +611,13 @@ __global__ void __launch_bounds__(128) attn_merge_k(AttnArgs a) {
     if (d < D) a.O[row * D + d] = acc / L;
 }
 
-// Grouped split-K decoding attention on the tensor cores (D % 16 == 0, D <= 128, G = H / HKV <= 8, 16-byte aligned
-// K / V rows). CTA = (chunk of 4 · csteps · 32 keys, KV head g, stream-token); each of its 4 warps takes csteps steps of
-// 32 keys for all G query heads of g (the 8 head slots of the MMA's N side), so every K / V row is read from memory once.
-// Per step, with the 32 K rows and V rows in padded shared rows (cp.async, 16 bytes per copy; rows past the visible
-// keys are zero-filled):
+// Decoding attention on the tensor cores (D % 16 == 0, D <= 128, G = H / HKV <= 8, 16-byte aligned K / V rows).
+// Work: the 32-key steps of all rows r = (stream-token, KV head), ⌈nk / 32⌉ per row and T in all, split stream-K over a
+// one-wave grid of B CTAs: CTA b takes steps [⌊bT/B⌋, ⌊(b+1)T/B⌋), a row segment at a time, its 4 warps taking every
+// fourth step of the segment (steps past the visible keys are skipped) for all G query heads of the row's KV head (the
+// 8 head slots of the MMA's N side), so every K / V row is read from memory once. Per step, with the 32 K rows and V
+// rows in this warp's padded shared rows (one 1-D bulk copy per row, issued by the lane of that row and completing on
+// the warp's K or V mbarrier; rows past the visible keys are zero-filled):
 //   scores  Sᵀ[32 keys × 8 heads] = K · Qᵀ by mma.sync m16n8k16, K from the shared rows (ldmatrix) as A, the query as
 //           B in two FP16 parts (hi = fp16(q), lo = fp16(q − hi)) after scaling each head's query by a power of two
 //           that puts its largest |q| in [2^13, 2^14), so both parts stay normal and the products keep 22 of the
@@ -597,12 +625,14 @@ __global__ void __launch_bounds__(128) attn_merge_k(AttnArgs a) {
 //   softmax running max per head over the lanes that hold the head, p = 2^(s − m) in FP32, per-lane partial sums;
 //   values  Oᵀ[D × 8 heads] += Vᵀ · Pᵀ, V from the shared rows by ldmatrix.trans as A, P in two FP16 parts as B
 //           (movmatrix turns the scores' accumulator layout into the B layout).
-// The next step's K rows are requested once this step's are scored and its V rows once these are summed, so each load
-// overlaps the other half of the step. The warps' (m, l, acc) are merged in shared memory into one partial per (head,
-// chunk), in the layout attn_merge_k reads.
-constexpr int AT2_WARPS = 4, AT2_KEYS = 32, AT2_GMAX = 8, AT2_SMAX = 8;
+// The next step's K rows are requested once this step's are scored and its V rows once these are summed, so each copy
+// overlaps the other half of the step. At the end of a segment the warps' (m, l, acc) are merged in shared memory
+// into one partial per head slot, written to slot b + r (distinct for every (b, r) pair that shares a step).
+constexpr int AT2_WARPS = 4, AT2_KEYS = 32, AT2_GMAX = 8;
+constexpr uint64_t AT2_WAIT_NS = 2000000000ull;   // a 256-byte row copy that has not landed after 2 s is an error
 __host__ __device__ constexpr int at2_rowb(int D) { return D * 2 + 16; }
-__host__ __device__ constexpr size_t at2_smem(int D) { return (size_t)AT2_WARPS * 2 * AT2_KEYS * at2_rowb(D); }
+__host__ __device__ constexpr size_t at2_stage(int D) { return (size_t)AT2_WARPS * 2 * AT2_KEYS * at2_rowb(D); }
+__host__ __device__ constexpr size_t at2_smem(int D) { return at2_stage(D) + AT2_WARPS * 2 * sizeof(uint64_t); }
 
 __device__ __forceinline__ void at_ldsm(unsigned addr, unsigned (&r)[4]) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];\n"
@@ -632,197 +662,243 @@ __device__ __forceinline__ void at_split(float x0, float x1, unsigned &hi, unsig
     lo = *reinterpret_cast<const unsigned *>(&l);
 }
 __device__ __forceinline__ float at_pow2(int e) { return __uint_as_float((unsigned)(e + 127) << 23); }   // |e| <= 126
+// one contiguous row of `bytes` bytes (multiple of 16, both addresses 16-byte aligned) into shared memory, completing on
+// the mbarrier; no multicast
+__device__ __forceinline__ void at_bulk_row(void *dst, const void *src, unsigned bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                     sm100::smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(sm100::smem_u32(bar))
+                 : "memory");
+}
 
 template <int DT>
 __global__ void __launch_bounds__(AT2_WARPS * 32, 3) attn_tc_k(AttnArgs a) {
-    constexpr int D = DT * 16, ROWB = at2_rowb(D), PIECES = D / 8;
+    using namespace sm100;
+    constexpr int D = DT * 16, ROWB = at2_rowb(D);
     extern __shared__ __align__(16) uint8_t at_sm[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
     const int G = a.H / a.HKV;
-    const int c = blockIdx.x, g = blockIdx.y, st = blockIdx.z;
-    const int t = st % a.nq, s = st / a.nq;
     uint8_t *kst = at_sm + (size_t)warp * 2 * AT2_KEYS * ROWB;   // this warp's K rows, then its V rows
     uint8_t *vst = kst + AT2_KEYS * ROWB;
-    int vt = a.vis[s] + a.dvis * t;
-    vt = vt < a.nk ? vt : a.nk;
-    const int span = AT2_KEYS * a.csteps;
-    const int kw0 = (c * AT2_WARPS + warp) * span;
-    const int kw1 = min(kw0 + span, vt);
-    const int nsteps = kw1 > kw0 ? (kw1 - kw0 + AT2_KEYS - 1) / AT2_KEYS : 0;
-    const __half *Kb = a.K + s * a.ks + g * a.kh, *Vb = a.V + s * a.vs + g * a.vh;
-    // the 32 rows of step `step` of one tensor into its staging rows (zeros past the visible keys), one commit group
-    auto stage = [&](const __half *base, long long rs, uint8_t *dst, int step) {
-        const int r0 = kw0 + step * AT2_KEYS;
-#pragma unroll
-        for (int it = 0; it < PIECES; it++) {
-            const int i = it * 32 + lane, r = i / PIECES, q = i % PIECES;
-            uint8_t *sp = dst + r * ROWB + q * 16;
-            if (r0 + r < kw1)
-                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(
-                                 (unsigned)__cvta_generic_to_shared(sp)),
-                             "l"(base + (long long)(r0 + r) * rs + q * 8) : "memory");
-            else
-                *reinterpret_cast<uint4 *>(sp) = make_uint4(0u, 0u, 0u, 0u);
-        }
-        asm volatile("cp.async.commit_group;\n" ::: "memory");
-    };
-    if (nsteps > 0) {
-        stage(Kb, a.kk, kst, 0);
-        stage(Vb, a.vk, vst, 0);
+    uint64_t *kbar = reinterpret_cast<uint64_t *>(at_sm + at2_stage(D)) + 2 * warp, *vbar = kbar + 1;
+    if (lane == 0) {
+        mbar_init(kbar, 1);
+        mbar_init(vbar, 1);
+        fence_barrier_init();
     }
-    // query fragments (B of the scores): lane holds head slot gq, dims 16kt + 2tq + {0, 1} and {8, 9}
-    float qv[DT][4];
-    float qmax = 0.0f;
-    const bool hlive = gq < G;
-    const float *qp = a.Q + s * a.qs + t * a.qt + (long long)(g * G + (hlive ? gq : 0)) * a.qh;
-#pragma unroll
-    for (int kt = 0; kt < DT; kt++)
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const float x = hlive ? qp[16 * kt + 2 * tq + (i & 1) + (i >> 1) * 8] * a.qscale : 0.0f;
-            qv[kt][i] = x;
-            qmax = fmaxf(qmax, fabsf(x));
-        }
-    qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, 1));
-    qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, 2));   // the four lanes of head slot gq
-    int ex = 0;
-    if (qmax > 0.0f) {
-        const int be = (int)((__float_as_uint(qmax) >> 23) & 0xffu);   // qmax < 2^(be − 126)
-        ex = min(max(140 - be, -126), 126);                              // qmax · 2^ex < 2^14
-    }
-    const float qsc = at_pow2(ex), qinv = at_pow2(-ex);
-    unsigned qh[DT][2], ql[DT][2];
-#pragma unroll
-    for (int kt = 0; kt < DT; kt++)
-#pragma unroll
-        for (int j = 0; j < 2; j++) at_split(qv[kt][2 * j] * qsc, qv[kt][2 * j + 1] * qsc, qh[kt][j], ql[kt][j]);
-    // this lane's score columns are head slots 2tq and 2tq + 1; their scale factors live in lanes 8tq and 8tq + 4
-    const float inv[2] = {__shfl_sync(0xffffffffu, qinv, 8 * tq), __shfl_sync(0xffffffffu, qinv, 8 * tq + 4)};
-    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f};
-    float o[DT][4];
-#pragma unroll
-    for (int dt = 0; dt < DT; dt++) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.0f;
-    const unsigned kbase = (unsigned)__cvta_generic_to_shared(kst), vbase = (unsigned)__cvta_generic_to_shared(vst);
+    __syncwarp();
+    unsigned kph = 0, vph = 0;          // parity of the next phase of each barrier
+    bool kpend = false, vpend = false;  // a phase with copies that have not been waited for
+    bool ok = true;
+    __shared__ int bad;
+    if (threadIdx.x == 0) bad = 0;
+    const unsigned kbase = smem_u32(kst), vbase = smem_u32(vst);
     const unsigned koff = ((lane & 7) + ((lane >> 3) & 1) * 8) * ROWB + (lane >> 4) * 16;   // A = K rows
     const unsigned voff = ((lane & 7) + (lane >> 4) * 8) * ROWB + ((lane >> 3) & 1) * 16;   // A = Vᵀ (trans)
-    for (int step = 0; step < nsteps; step++) {
-        const int r0 = kw0 + step * AT2_KEYS;
-        const bool more = step + 1 < nsteps;
-        asm volatile("cp.async.wait_group 1;\n" ::: "memory");   // this step's K rows (its V rows may be in flight)
-        __syncwarp();
-        float sc[2][4];
+    const long long T = a.total, B = gridDim.x, b = blockIdx.x;
+    const long long lo = b * T / B, hi = (b + 1) * T / B;
+    __syncthreads();
+    for (long long r = lo / a.nsr; r * a.nsr < hi; r++) {
+        const long long rs0 = r * a.nsr;
+        const int g = (int)(r % a.HKV), st = (int)(r / a.HKV);
+        const int t = st % a.nq, s = st / a.nq;
+        int vt = a.vis[s] + a.dvis * t;
+        vt = max(min(vt, a.nk), 0);
+        const long long sb = max(lo, rs0) - rs0;                                   // this segment's steps in the row
+        const long long se = min(min(hi, rs0 + a.nsr) - rs0, (long long)((vt + AT2_KEYS - 1) / AT2_KEYS));
+        const int nmy = se > sb + warp ? (int)((se - sb - warp + AT2_WARPS - 1) / AT2_WARPS) : 0;
+        const __half *Kb = a.K + s * a.ks + g * a.kh, *Vb = a.V + s * a.vs + g * a.vh;
+        // the 32 rows of this warp's i-th step of one tensor: lane j copies key row j, or zero-fills it past vt
+        auto stage = [&](const __half *base, long long rs, uint8_t *dst, uint64_t *bar, int i) {
+            const int k0 = (int)((sb + warp + (long long)AT2_WARPS * i) * AT2_KEYS);
+            const int nrows = min(AT2_KEYS, vt - k0);
+            fence_proxy_async();   // earlier zero-fill stores to these rows come before the copies
+            if (lane == 0) mbar_arrive_expect_tx(bar, (unsigned)(nrows * D * 2));
+            __syncwarp();
+            if (lane < nrows) {
+                at_bulk_row(dst + lane * ROWB, base + (long long)(k0 + lane) * rs, D * 2, bar);
+            } else {
 #pragma unroll
-        for (int mt = 0; mt < 2; mt++) {
-            sc[mt][0] = sc[mt][1] = sc[mt][2] = sc[mt][3] = 0.0f;
+                for (int q = 0; q < D / 8; q++) *reinterpret_cast<uint4 *>(dst + lane * ROWB + q * 16) = make_uint4(0u, 0u, 0u, 0u);
+            }
+        };
+        float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f};
+        float o[DT][4];
 #pragma unroll
-            for (int kt = 0; kt < DT; kt++) {
-                unsigned af[4];
-                at_ldsm(kbase + koff + mt * 16 * ROWB + kt * 32, af);
-                at_mma(sc[mt], af, qh[kt][0], qh[kt][1]);
-                at_mma(sc[mt], af, ql[kt][0], ql[kt][1]);
+        for (int dt = 0; dt < DT; dt++) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.0f;
+        if (nmy > 0 && ok) {
+            stage(Kb, a.kk, kst, kbar, 0);
+            stage(Vb, a.vk, vst, vbar, 0);
+            kpend = vpend = true;
+            // query fragments (B of the scores): lane holds head slot gq, dims 16kt + 2tq + {0, 1} and {8, 9}
+            float qv[DT][4];
+            float qmax = 0.0f;
+            const bool hlive = gq < G;
+            const float *qp = a.Q + s * a.qs + t * a.qt + (long long)(g * G + (hlive ? gq : 0)) * a.qh;
+#pragma unroll
+            for (int kt = 0; kt < DT; kt++)
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const float x = hlive ? qp[16 * kt + 2 * tq + (i & 1) + (i >> 1) * 8] * a.qscale : 0.0f;
+                    qv[kt][i] = x;
+                    qmax = fmaxf(qmax, fabsf(x));
+                }
+            qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, 1));
+            qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, 2));   // the four lanes of head slot gq
+            int ex = 0;
+            if (qmax > 0.0f) {
+                const int be = (int)((__float_as_uint(qmax) >> 23) & 0xffu);   // qmax < 2^(be − 126)
+                ex = min(max(140 - be, -126), 126);                              // qmax · 2^ex < 2^14
+            }
+            const float qsc = at_pow2(ex), qinv = at_pow2(-ex);
+            unsigned qh[DT][2], ql[DT][2];
+#pragma unroll
+            for (int kt = 0; kt < DT; kt++)
+#pragma unroll
+                for (int j = 0; j < 2; j++) at_split(qv[kt][2 * j] * qsc, qv[kt][2 * j + 1] * qsc, qh[kt][j], ql[kt][j]);
+            // this lane's score columns are head slots 2tq and 2tq + 1; their scale factors sit in lanes 8tq, 8tq + 4
+            const float inv[2] = {__shfl_sync(0xffffffffu, qinv, 8 * tq), __shfl_sync(0xffffffffu, qinv, 8 * tq + 4)};
+            for (int i = 0; i < nmy; i++) {
+                const int r0 = (int)((sb + warp + (long long)AT2_WARPS * i) * AT2_KEYS);
+                const bool more = i + 1 < nmy;
+                if (!mbar_wait(kbar, kph, &bad, AT2_WAIT_NS)) {
+                    ok = false;
+                    break;
+                }
+                kph ^= 1u;
+                kpend = false;
+                float sc[2][4];
+#pragma unroll
+                for (int mt = 0; mt < 2; mt++) {
+                    sc[mt][0] = sc[mt][1] = sc[mt][2] = sc[mt][3] = 0.0f;
+#pragma unroll
+                    for (int kt = 0; kt < DT; kt++) {
+                        unsigned af[4];
+                        at_ldsm(kbase + koff + mt * 16 * ROWB + kt * 32, af);
+                        at_mma(sc[mt], af, qh[kt][0], qh[kt][1]);
+                        at_mma(sc[mt], af, ql[kt][0], ql[kt][1]);
+                    }
+                }
+                __syncwarp();   // every lane's K fragments are in registers before the next copy overwrites the rows
+                if (more) {
+                    stage(Kb, a.kk, kst, kbar, i + 1);
+                    kpend = true;
+                }
+                // sc[mt][2·hh + j]: key r0 + 16mt + gq + 8hh, head slot 2tq + j
+                float pr[2][4];
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    float x[4];
+                    float mx = -INFINITY;
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const int mt = e >> 1, hh = e & 1;
+                        x[e] = r0 + 16 * mt + gq + 8 * hh < vt ? sc[mt][2 * hh + j] * inv[j] : -INFINITY;
+                        mx = fmaxf(mx, x[e]);
+                    }
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                    const float mn = fmaxf(m[j], mx);
+                    const float alpha = exp2f(m[j] - mn);   // 0 on the first step (m = -inf)
+                    float ps = 0.0f;
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const float p = exp2f(x[e] - mn);
+                        pr[e >> 1][2 * (e & 1) + j] = p;
+                        ps += p;
+                    }
+                    l[j] = fmaf(l[j], alpha, ps);
+#pragma unroll
+                    for (int dt = 0; dt < DT; dt++) {
+                        o[dt][j] *= alpha;
+                        o[dt][2 + j] *= alpha;
+                    }
+                    m[j] = mn;
+                }
+                if (!mbar_wait(vbar, vph, &bad, AT2_WAIT_NS)) {
+                    ok = false;
+                    break;
+                }
+                vph ^= 1u;
+                vpend = false;
+#pragma unroll
+                for (int ks = 0; ks < 2; ks++) {
+                    unsigned h01, l01, h23, l23;
+                    at_split(pr[ks][0], pr[ks][1], h01, l01);   // key 16ks + gq, head slots 2tq, 2tq + 1
+                    at_split(pr[ks][2], pr[ks][3], h23, l23);   // key 16ks + gq + 8
+                    const unsigned bh0 = at_movt(h01), bh1 = at_movt(h23), bl0 = at_movt(l01), bl1 = at_movt(l23);
+#pragma unroll
+                    for (int dt = 0; dt < DT; dt++) {
+                        unsigned af[4];
+                        at_ldsm_t(vbase + voff + ks * 16 * ROWB + dt * 32, af);
+                        at_mma(o[dt], af, bh0, bh1);
+                        at_mma(o[dt], af, bl0, bl1);
+                    }
+                }
+                __syncwarp();   // every lane's V fragments are in registers before the next copy overwrites the rows
+                if (more) {
+                    stage(Vb, a.vk, vst, vbar, i + 1);
+                    vpend = true;
+                }
+            }
+            if (!ok) {   // report, then wait (bounded again) for this warp's copies still in flight
+                if (lane == 0) *(volatile unsigned *)a.err = kDevErrWaitTimeout;
+                if (kpend && mbar_wait(kbar, kph, &bad, AT2_WAIT_NS)) kph ^= 1u;
+                if (vpend && mbar_wait(vbar, vph, &bad, AT2_WAIT_NS)) vph ^= 1u;
+                kpend = vpend = false;
             }
         }
-        __syncwarp();   // every lane's K fragments are in registers before the next step's copy overwrites the rows
-        if (more) stage(Kb, a.kk, kst, step + 1);
-        // sc[mt][2·hh + j]: key r0 + 16mt + gq + 8hh, head slot 2tq + j
-        float pr[2][4];
+#pragma unroll
+        for (int j = 0; j < 2; j++) {   // the per-lane sums over the 8 lanes of each head slot
+            l[j] += __shfl_xor_sync(0xffffffffu, l[j], 4);
+            l[j] += __shfl_xor_sync(0xffffffffu, l[j], 8);
+            l[j] += __shfl_xor_sync(0xffffffffu, l[j], 16);
+        }
+        // merge the four warps: (m, l) per warp and head slot, acc per warp, head slot and dimension
+        __syncthreads();   // every warp is done with its staging rows
+        float *mw = reinterpret_cast<float *>(at_sm);   // [warp][slot]: m, then l
+        float *lw = mw + AT2_WARPS * AT2_GMAX;
+        float *aw = lw + AT2_WARPS * AT2_GMAX;         // [warp][slot][D]
 #pragma unroll
         for (int j = 0; j < 2; j++) {
-            float x[4];
-            float mx = -INFINITY;
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const int mt = i >> 1, hh = i & 1;
-                x[i] = r0 + 16 * mt + gq + 8 * hh < kw1 ? sc[mt][2 * hh + j] * inv[j] : -INFINITY;
-                mx = fmaxf(mx, x[i]);
+            const int hs = 2 * tq + j;
+            if (hs >= G) continue;
+            if (gq == 0) {
+                mw[warp * AT2_GMAX + hs] = m[j];
+                lw[warp * AT2_GMAX + hs] = l[j];
             }
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-            const float mn = fmaxf(m[j], mx);
-            const float alpha = exp2f(m[j] - mn);   // 0 on the first step (m = -inf)
-            float ps = 0.0f;
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const float p = exp2f(x[i] - mn);
-                pr[i >> 1][2 * (i & 1) + j] = p;
-                ps += p;
-            }
-            l[j] = fmaf(l[j], alpha, ps);
+            float *ap = aw + (warp * AT2_GMAX + hs) * D + gq;
 #pragma unroll
             for (int dt = 0; dt < DT; dt++) {
-                o[dt][j] *= alpha;
-                o[dt][2 + j] *= alpha;
-            }
-            m[j] = mn;
-        }
-        if (more) asm volatile("cp.async.wait_group 1;\n" ::: "memory");   // this step's V rows
-        else asm volatile("cp.async.wait_group 0;\n" ::: "memory");
-        __syncwarp();
-#pragma unroll
-        for (int ks = 0; ks < 2; ks++) {
-            unsigned h01, l01, h23, l23;
-            at_split(pr[ks][0], pr[ks][1], h01, l01);   // key 16ks + gq, head slots 2tq, 2tq + 1
-            at_split(pr[ks][2], pr[ks][3], h23, l23);   // key 16ks + gq + 8
-            const unsigned bh0 = at_movt(h01), bh1 = at_movt(h23), bl0 = at_movt(l01), bl1 = at_movt(l23);
-#pragma unroll
-            for (int dt = 0; dt < DT; dt++) {
-                unsigned af[4];
-                at_ldsm_t(vbase + voff + ks * 16 * ROWB + dt * 32, af);
-                at_mma(o[dt], af, bh0, bh1);
-                at_mma(o[dt], af, bl0, bl1);
+                ap[16 * dt] = o[dt][j];
+                ap[16 * dt + 8] = o[dt][2 + j];
             }
         }
-        __syncwarp();   // every lane's V fragments are in registers before the next step's copy overwrites the rows
-        if (more) stage(Vb, a.vk, vst, step + 1);
-    }
-#pragma unroll
-    for (int j = 0; j < 2; j++) {   // the per-lane sums over the 8 lanes of each head slot
-        l[j] += __shfl_xor_sync(0xffffffffu, l[j], 4);
-        l[j] += __shfl_xor_sync(0xffffffffu, l[j], 8);
-        l[j] += __shfl_xor_sync(0xffffffffu, l[j], 16);
-    }
-    // merge the four warps: (m, l) per warp and head slot, acc per warp, head slot and dimension
-    __syncthreads();   // every warp is done with its staging rows
-    float *mw = reinterpret_cast<float *>(at_sm);   // [warp][slot]: m, then l
-    float *lw = mw + AT2_WARPS * AT2_GMAX;
-    float *aw = lw + AT2_WARPS * AT2_GMAX;         // [warp][slot][D]
-#pragma unroll
-    for (int j = 0; j < 2; j++) {
-        const int hs = 2 * tq + j;
-        if (hs >= G) continue;
-        if (gq == 0) {
-            mw[warp * AT2_GMAX + hs] = m[j];
-            lw[warp * AT2_GMAX + hs] = l[j];
-        }
-        float *ap = aw + (warp * AT2_GMAX + hs) * D + gq;
-#pragma unroll
-        for (int dt = 0; dt < DT; dt++) {
-            ap[16 * dt] = o[dt][j];
-            ap[16 * dt + 8] = o[dt][2 + j];
-        }
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < G * D; i += AT2_WARPS * 32) {
-        const int h = i / D, d = i - h * D;
-        float M = -INFINITY;
-        for (int w = 0; w < AT2_WARPS; w++)
-            if (lw[w * AT2_GMAX + h] > 0.0f) M = fmaxf(M, mw[w * AT2_GMAX + h]);
-        float L = 0.0f, acc = 0.0f;
-        if (M > -INFINITY) {
-            for (int w = 0; w < AT2_WARPS; w++) {
-                if (!(lw[w * AT2_GMAX + h] > 0.0f)) continue;
-                const float f = exp2f(mw[w * AT2_GMAX + h] - M);
-                L += lw[w * AT2_GMAX + h] * f;
-                acc += aw[(w * AT2_GMAX + h) * D + d] * f;
+        __syncthreads();
+        float *pslot = a.part + (b + r) * G * (2 + D);
+        for (int i = threadIdx.x; i < G * D; i += AT2_WARPS * 32) {
+            const int h = i / D, d = i - h * D;
+            float M = -INFINITY;
+            for (int w = 0; w < AT2_WARPS; w++)
+                if (lw[w * AT2_GMAX + h] > 0.0f) M = fmaxf(M, mw[w * AT2_GMAX + h]);
+            float L = 0.0f, acc = 0.0f;
+            if (M > -INFINITY) {
+                for (int w = 0; w < AT2_WARPS; w++) {
+                    if (!(lw[w * AT2_GMAX + h] > 0.0f)) continue;
+                    const float f = exp2f(mw[w * AT2_GMAX + h] - M);
+                    L += lw[w * AT2_GMAX + h] * f;
+                    acc += aw[(w * AT2_GMAX + h) * D + d] * f;
+                }
+            }
+            float *pp = pslot + h * (2 + D);
+            pp[2 + d] = acc;
+            if (d == 0) {
+                pp[0] = M;
+                pp[1] = L;
             }
         }
-        float *pp = a.part + (((long long)st * a.H + g * G + h) * a.nchunk + c) * (2 + D);
-        pp[2 + d] = acc;
-        if (d == 0) {
-            pp[0] = M;
-            pp[1] = L;
-        }
+        __syncthreads();   // the merge area is read before the next segment's copies land in the staging rows
     }
 }
 
@@ -841,8 +917,7 @@ int attn_tc_run(const AttnArgs &a, cudaStream_t st, bool plan, int *per_sm) {
         *per_sm = std::max(occ[d->dev], 1);
         return 0;
     }
-    attn_tc_k<DT><<<dim3((unsigned)a.nchunk, (unsigned)a.HKV, (unsigned)(a.ns * a.nq)), AT2_WARPS * 32,
-                    at2_smem(DT * 16), st>>>(a);
+    attn_tc_k<DT><<<(unsigned)a.nblk, AT2_WARPS * 32, at2_smem(DT * 16), st>>>(a);
     return launched("attn_tc");
 }
 
@@ -876,27 +951,22 @@ int attention(AttnArgs a, int sync, const char *who) {
                     (a.kh * 2) % 16 == 0 && (a.ks * 2) % 16 == 0 && (a.vk * 2) % 16 == 0 && (a.vh * 2) % 16 == 0 &&
                     (a.vs * 2) % 16 == 0;
     cudaStream_t st = stream();
+    size_t part_bytes;
     if (tc) {
-        // steps per warp: the fewest waves × (steps + a CTA's fixed cost of about a quarter step)
+        // stream-K over all rows' 32-key steps on one wave of CTAs (never more CTAs than steps, so every CTA's
+        // range is non-empty and every slot b + r the merge reads is written)
         int per_sm = 1;
         G9_TRY(attn_tc(a, st, true, &per_sm));
-        const long long slots = (long long)per_sm * d->sm_count, rows = (long long)a.HKV * a.ns * a.nq;
-        double best = 1e300;
-        for (int S = 1; S <= AT2_SMAX; S++) {
-            const long long span = (long long)AT2_WARPS * AT2_KEYS * S;
-            const long long ctas = (a.nk + span - 1) / span * rows;
-            const double cost = (double)((ctas + slots - 1) / slots) * (S + 0.25);
-            if (cost < best) {
-                best = cost;
-                a.csteps = S;
-            }
-        }
-        a.nchunk = (int)((a.nk + (long long)AT2_WARPS * AT2_KEYS * a.csteps - 1) / (AT2_WARPS * AT2_KEYS * a.csteps));
+        const long long rows = (long long)a.HKV * a.ns * a.nq;
+        a.nsr = (a.nk + AT2_KEYS - 1) / AT2_KEYS;
+        a.total = rows * a.nsr;
+        a.nblk = (int)std::min<long long>((long long)per_sm * d->sm_count, a.total);
+        a.err = d->err_dev;
+        part_bytes = round256((size_t)(a.nblk + rows) * (a.H / a.HKV) * (2 + a.D) * sizeof(float));
     } else {
         a.nchunk = (a.nk + ATT_CHUNK - 1) / ATT_CHUNK;
+        part_bytes = round256((size_t)a.ns * a.nq * a.H * a.nchunk * (2 + a.D) * sizeof(float));
     }
-    const long long warps = (long long)a.ns * a.nq * a.H * a.nchunk;
-    const size_t part_bytes = round256((size_t)warps * (2 + a.D) * sizeof(float));
     void *buf = nullptr;
     G9_TRY(ml_buffer(part_bytes + (size_t)a.ns * sizeof(int), &buf));
     a.part = (float *)buf;
@@ -908,10 +978,13 @@ int attention(AttnArgs a, int sync, const char *who) {
     if (tc) {
         G9_TRY(attn_tc(a, st, false, nullptr));
     } else {
-        attn_part_k<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(a);
+        attn_part_k<<<(unsigned)(((long long)a.ns * a.nq * a.H * a.nchunk + 7) / 8), 256, 0, st>>>(a);
         G9_TRY(launched("attn_part"));
     }
-    attn_merge_k<<<(unsigned)((long long)a.ns * a.nq * a.H), 128, 0, st>>>(a);
+    if (tc)
+        attn_merge_k<true><<<(unsigned)((long long)a.ns * a.nq * a.H), 128, 0, st>>>(a);
+    else
+        attn_merge_k<false><<<(unsigned)((long long)a.ns * a.nq * a.H), 128, 0, st>>>(a);
     G9_TRY(launched("attn_merge"));
     Operand out;
     out.user = out.dptr = a.O;
