@@ -48,6 +48,8 @@ struct DevState {
     uint64_t *sk_part = nullptr;                               // epoch-tagged partial tiles of the stream-K skinny
     size_t sk_part_n = 0;                                      // kernel (words; zeroed when created or grown)
     unsigned sk_epoch = 0;                                     // launch counter written into those tags
+    unsigned *at_cnt = nullptr;                                // per-row arrival counters of the attention kernel
+    size_t at_cnt_n = 0;                                       // (zeroed when created or grown; each call leaves 0)
     // Device ranges written by no-wait calls that may still be queued, each with an event recorded right after the
     // call that wrote it (an entry whose event has completed is dropped); a kernel that reads an input before
     // griddepcontrol.wait checks its input against them.
@@ -158,6 +160,8 @@ int launch_trsm_dev(int type, int left, int upper, int tA, int unit, int M, int 
 // Partial-tile words of the stream-K skinny kernel (at least `words`, zeroed when created or grown) and the epoch of
 // the launch about to be enqueued (never 0; the words are zeroed again when the counter wraps).
 int skinny_slots(size_t words, uint64_t **p, unsigned *epoch);
+// n zero-initialised arrival counters for the attention kernel's rows (each call returns every counter it uses to 0).
+int attn_counters(size_t n, unsigned **p);
 // Call timing: timer_start at entry (wall clock), timer_kernel right before the main kernels (GEN9BLAS_PROFILE=1:
 // CUDA event), timer_stop at the end: last_time_ms is the kernel time with profiling, else the whole call.
 void timer_start();

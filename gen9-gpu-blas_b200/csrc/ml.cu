@@ -494,6 +494,8 @@ struct AttnArgs {
     long long total;
     int nblk;
     unsigned *err;
+    unsigned *cnt;   // per-row arrival counters (zero before and after each launch)
+    int early;       // no queued call writes K or V: the first copies may precede griddepcontrol.wait
 };
 
 __global__ void __launch_bounds__(256) attn_part_k(AttnArgs a) {
@@ -564,32 +566,17 @@ __global__ void __launch_bounds__(256) attn_part_k(AttnArgs a) {
 // CTA of the stream-K split (grid B over T steps) that holds step x: the last b with ⌊b·T / B⌋ <= x.
 __host__ __device__ __forceinline__ long long at_blk_of(long long x, long long T, long long B) { return (x * B + B - 1) / T; }
 
-// O[s][t][h][d] = Σ_c acc_c 2^(m_c − M) / Σ_c l_c 2^(m_c − M) over the partials c with l > 0 (M their largest m). One
-// 128-thread CTA per output row (s, t, h): the threads reduce M over the partials, then thread d walks them in key
-// order (eight partials' loads in flight) adding its dimension and, redundantly in every thread, the denominator. A
-// partial whose l is not positive is skipped by a select, so whatever its other words hold never enters the sums.
-// SK: the partials of the tensor-core kernel, slots b + r for the CTAs b that held steps of row r = (s, t, KV head),
-// [head slot] inside a slot; otherwise the per-head kernel's [row][chunk].
-template <bool SK>
+// O[s][t][h][d] = Σ_c acc_c 2^(m_c − M) / Σ_c l_c 2^(m_c − M) over the chunks c with l > 0 (M their largest m), for
+// the per-head kernel's [row][chunk] partials. One 128-thread CTA per output row (s, t, h): the threads reduce M over
+// the chunks, then thread d walks them in chunk order (eight chunks' loads in flight) adding its dimension and,
+// redundantly in every thread, the denominator. A chunk whose l is not positive is skipped by a select, so whatever
+// its other words hold never enters the sums.
 __global__ void __launch_bounds__(128) attn_merge_k(AttnArgs a) {
     __shared__ float red[4];
     const long long row = blockIdx.x;   // (s · nq + t) · H + h
-    const int D = a.D, stride = 2 + D, d = threadIdx.x;
-    const float *pb;
-    long long pstride;
-    int nc;
-    if (SK) {
-        const int G = a.H / a.HKV, h = (int)(row % a.H);
-        const long long r = row / a.H * a.HKV + h / G;
-        const long long b0 = at_blk_of(r * a.nsr, a.total, a.nblk), b1 = at_blk_of((r + 1) * a.nsr - 1, a.total, a.nblk);
-        pb = a.part + ((b0 + r) * G + h % G) * stride;
-        pstride = (long long)G * stride;
-        nc = (int)(b1 - b0 + 1);
-    } else {
-        pb = a.part + row * a.nchunk * stride;
-        pstride = stride;
-        nc = a.nchunk;
-    }
+    const int D = a.D, stride = 2 + D, d = threadIdx.x, nc = a.nchunk;
+    const float *pb = a.part + row * nc * stride;
+    const long long pstride = stride;
     float M = -INFINITY;
     for (int c = threadIdx.x; c < nc; c += 128)
         if (pb[c * pstride + 1] > 0.0f) M = fmaxf(M, pb[c * pstride]);
@@ -691,23 +678,31 @@ __global__ void __launch_bounds__(AT2_WARPS * 32, 3) attn_tc_k(AttnArgs a) {
     bool kpend = false, vpend = false;  // a phase with copies that have not been waited for
     bool ok = true;
     __shared__ int bad;
+    __shared__ bool last;
     if (threadIdx.x == 0) bad = 0;
     const unsigned kbase = smem_u32(kst), vbase = smem_u32(vst);
     const unsigned koff = ((lane & 7) + ((lane >> 3) & 1) * 8) * ROWB + (lane >> 4) * 16;   // A = K rows
     const unsigned voff = ((lane & 7) + (lane >> 4) * 8) * ROWB + ((lane >> 3) & 1) * 16;   // A = Vᵀ (trans)
     const long long T = a.total, B = gridDim.x, b = blockIdx.x;
     const long long lo = b * T / B, hi = (b + 1) * T / B;
+    // launched with programmatic stream serialization: the next kernel may start as this one's CTAs leave; this
+    // kernel touches Q, the visible counts, the slots, the counters and O only after griddepcontrol.wait (the slots
+    // and counters are shared with the previous call of this kernel), K and V before it only when a.early says so
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    bool waited = false;
+    if (!a.early) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        waited = true;
+    }
     __syncthreads();
     for (long long r = lo / a.nsr; r * a.nsr < hi; r++) {
         const long long rs0 = r * a.nsr;
         const int g = (int)(r % a.HKV), st = (int)(r / a.HKV);
         const int t = st % a.nq, s = st / a.nq;
-        int vt = a.vis[s] + a.dvis * t;
-        vt = max(min(vt, a.nk), 0);
-        const long long sb = max(lo, rs0) - rs0;                                   // this segment's steps in the row
-        const long long se = min(min(hi, rs0 + a.nsr) - rs0, (long long)((vt + AT2_KEYS - 1) / AT2_KEYS));
-        const int nmy = se > sb + warp ? (int)((se - sb - warp + AT2_WARPS - 1) / AT2_WARPS) : 0;
+        const long long sb = max(lo, rs0) - rs0;   // this segment's steps in the row: [sb, sn), capped below at the
+        const long long sn = min(hi, rs0 + a.nsr) - rs0;   // visible keys once their count is known
         const __half *Kb = a.K + s * a.ks + g * a.kh, *Vb = a.V + s * a.vs + g * a.vh;
+        int vt = a.nk;   // rows past vt are zero-filled instead of copied; all nk rows exist in the caller's buffers
         // the 32 rows of this warp's i-th step of one tensor: lane j copies key row j, or zero-fills it past vt
         auto stage = [&](const __half *base, long long rs, uint8_t *dst, uint64_t *bar, int i) {
             const int k0 = (int)((sb + warp + (long long)AT2_WARPS * i) * AT2_KEYS);
@@ -722,14 +717,25 @@ __global__ void __launch_bounds__(AT2_WARPS * 32, 3) attn_tc_k(AttnArgs a) {
                 for (int q = 0; q < D / 8; q++) *reinterpret_cast<uint4 *>(dst + lane * ROWB + q * 16) = make_uint4(0u, 0u, 0u, 0u);
             }
         };
+        // the first step is requested before the visible count is read, bounded by nk: its K rows past the count are
+        // masked in the scores and its V rows past it are zeroed once they land
+        if (ok && sb + warp < sn) {
+            stage(Kb, a.kk, kst, kbar, 0);
+            stage(Vb, a.vk, vst, vbar, 0);
+            kpend = vpend = true;
+        }
+        if (!waited) {
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            waited = true;
+        }
+        vt = max(min(a.vis[s] + a.dvis * t, a.nk), 0);
+        const long long se = min(sn, (long long)((vt + AT2_KEYS - 1) / AT2_KEYS));
+        const int nmy = se > sb + warp ? (int)((se - sb - warp + AT2_WARPS - 1) / AT2_WARPS) : 0;
         float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f};
         float o[DT][4];
 #pragma unroll
         for (int dt = 0; dt < DT; dt++) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.0f;
         if (nmy > 0 && ok) {
-            stage(Kb, a.kk, kst, kbar, 0);
-            stage(Vb, a.vk, vst, vbar, 0);
-            kpend = vpend = true;
             // query fragments (B of the scores): lane holds head slot gq, dims 16kt + 2tq + {0, 1} and {8, 9}
             float qv[DT][4];
             float qmax = 0.0f;
@@ -822,6 +828,11 @@ __global__ void __launch_bounds__(AT2_WARPS * 32, 3) attn_tc_k(AttnArgs a) {
                 }
                 vph ^= 1u;
                 vpend = false;
+                if (i == 0 && r0 + lane >= vt) {   // first step: V rows past the visible keys were copied (rows < nk)
+#pragma unroll
+                    for (int q = 0; q < D / 8; q++) *reinterpret_cast<uint4 *>(vst + lane * ROWB + q * 16) = make_uint4(0u, 0u, 0u, 0u);
+                }
+                __syncwarp();
 #pragma unroll
                 for (int ks = 0; ks < 2; ks++) {
                     unsigned h01, l01, h23, l23;
@@ -842,13 +853,18 @@ __global__ void __launch_bounds__(AT2_WARPS * 32, 3) attn_tc_k(AttnArgs a) {
                     vpend = true;
                 }
             }
-            if (!ok) {   // report, then wait (bounded again) for this warp's copies still in flight
-                if (lane == 0) *(volatile unsigned *)a.err = kDevErrWaitTimeout;
-                if (kpend && mbar_wait(kbar, kph, &bad, AT2_WAIT_NS)) kph ^= 1u;
-                if (vpend && mbar_wait(vbar, vph, &bad, AT2_WAIT_NS)) vph ^= 1u;
-                kpend = vpend = false;
-            }
         }
+        if (!ok && lane == 0) *(volatile unsigned *)a.err = kDevErrWaitTimeout;
+        // copies still in flight: a first step past the visible keys, or a wait that gave up (bounded again)
+        if (kpend) {
+            if (mbar_wait(kbar, kph, &bad, AT2_WAIT_NS)) kph ^= 1u;
+            else if (lane == 0) *(volatile unsigned *)a.err = kDevErrWaitTimeout;
+        }
+        if (vpend) {
+            if (mbar_wait(vbar, vph, &bad, AT2_WAIT_NS)) vph ^= 1u;
+            else if (lane == 0) *(volatile unsigned *)a.err = kDevErrWaitTimeout;
+        }
+        kpend = vpend = false;
 #pragma unroll
         for (int j = 0; j < 2; j++) {   // the per-lane sums over the 8 lanes of each head slot
             l[j] += __shfl_xor_sync(0xffffffffu, l[j], 4);
@@ -898,6 +914,95 @@ __global__ void __launch_bounds__(AT2_WARPS * 32, 3) attn_tc_k(AttnArgs a) {
                 pp[1] = L;
             }
         }
+        // arrival on the row's counter; the CTA that completes the row merges its slots b0 + r .. b1 + r into O
+        __syncthreads();   // every slot word is written (and the merge area read) before the arrival
+        const long long b0 = at_blk_of(rs0, T, B), b1 = at_blk_of(rs0 + a.nsr - 1, T, B);
+        const int nsl = (int)(b1 - b0 + 1);
+        if (threadIdx.x == 0) {
+            __threadfence();   // release of the CTA's slot words (ordered before by the barrier)
+            last = atomicAdd(a.cnt + r, 1u) + 1u == (unsigned)nsl;
+            __threadfence();   // acquire of the other CTAs' slot words
+        }
+        __syncthreads();
+        if (last) {
+            // thread i's outputs: (head slot, dim) = i + 128k for k < AT2_GMAX·D / 128 while below G·D; the values of
+            // the first four slots are requested before the weights are known, so the loads overlap
+            constexpr int NO = AT2_GMAX * D / (AT2_WARPS * 32), NJ = 4;
+            const float *pb = a.part + (b0 + r) * G * (2 + D);   // [slot][head slot][2 + D], slots in key order
+            float *wm = reinterpret_cast<float *>(at_sm);         // [slot][head slot]: 2^(m − M), −1 when l <= 0
+            float *hl = wm + nsl * G;                             // [head slot]: the denominator
+            float xv[NJ][NO];
+#pragma unroll
+            for (int jj = 0; jj < NJ; jj++)
+#pragma unroll
+                for (int k = 0; k < NO; k++) {
+                    const int i = threadIdx.x + AT2_WARPS * 32 * k, h = i / D, d = i - h * D;
+                    xv[jj][k] = jj < nsl && i < G * D ? __ldcg(pb + ((long long)jj * G + h) * (2 + D) + 2 + d) : 0.0f;
+                }
+            for (int h = warp; h < G; h += AT2_WARPS) {   // warp: the weights and denominator of head slots h
+                float M = -INFINITY, L = 0.0f;
+                for (int j0 = 0; j0 < nsl; j0 += 32) {
+                    const int j = j0 + lane;
+                    float mj = -INFINITY, lj = 0.0f;
+                    if (j < nsl) {
+                        const float *pp = pb + ((long long)j * G + h) * (2 + D);
+                        mj = __ldcg(pp);
+                        lj = __ldcg(pp + 1);
+                    }
+                    float mx = lj > 0.0f ? mj : -INFINITY;
+                    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                    const float Mn = fmaxf(M, mx);
+                    const float w = lj > 0.0f ? exp2f(mj - Mn) : -1.0f;
+                    if (j < nsl) wm[j * G + h] = w;
+                    float ls = lj > 0.0f ? lj * w : 0.0f;
+                    for (int o = 16; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+                    // slots of earlier rounds were weighted against M: rescale them to Mn (rows of > 32 slots only)
+                    __syncwarp();   // this round's weights are in shared memory for every lane
+                    if (j0 > 0 && Mn > M) {
+                        const float f = exp2f(M - Mn);
+                        for (int q = lane; q < j0; q += 32)
+                            if (wm[q * G + h] >= 0.0f) wm[q * G + h] *= f;
+                        L *= f;
+                    }
+                    L += ls;
+                    M = Mn;
+                    __syncwarp();
+                }
+                if (lane == 0) hl[h] = L;
+            }
+            __syncthreads();
+            float acc[NO];
+#pragma unroll
+            for (int k = 0; k < NO; k++) acc[k] = 0.0f;
+            for (int j0 = 0; j0 < nsl; j0 += NJ) {
+#pragma unroll
+                for (int jj = 0; jj < NJ; jj++)
+#pragma unroll
+                    for (int k = 0; k < NO; k++) {
+                        const int i = threadIdx.x + AT2_WARPS * 32 * k, h = i / D;
+                        if (j0 + jj < nsl && i < G * D) {
+                            const float w = wm[(j0 + jj) * G + h];
+                            acc[k] = w >= 0.0f ? fmaf(xv[jj][k], w, acc[k]) : acc[k];
+                        }
+                    }
+                if (j0 + NJ < nsl) {   // the next four slots' values
+#pragma unroll
+                    for (int jj = 0; jj < NJ; jj++)
+#pragma unroll
+                        for (int k = 0; k < NO; k++) {
+                            const int i = threadIdx.x + AT2_WARPS * 32 * k, h = i / D, d = i - h * D;
+                            const int j = j0 + NJ + jj;
+                            xv[jj][k] = j < nsl && i < G * D ? __ldcg(pb + ((long long)j * G + h) * (2 + D) + 2 + d) : 0.0f;
+                        }
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < NO; k++) {
+                const int i = threadIdx.x + AT2_WARPS * 32 * k, h = i / D, d = i - h * D;
+                if (i < G * D) a.O[((long long)st * a.H + g * G + h) * D + d] = acc[k] / hl[h];
+            }
+            if (threadIdx.x == 0) a.cnt[r] = 0u;   // the next call finds the counter at zero
+        }
         __syncthreads();   // the merge area is read before the next segment's copies land in the staging rows
     }
 }
@@ -917,7 +1022,7 @@ int attn_tc_run(const AttnArgs &a, cudaStream_t st, bool plan, int *per_sm) {
         *per_sm = std::max(occ[d->dev], 1);
         return 0;
     }
-    attn_tc_k<DT><<<(unsigned)a.nblk, AT2_WARPS * 32, at2_smem(DT * 16), st>>>(a);
+    G9_CU(launch_pdl(attn_tc_k<DT>, dim3((unsigned)a.nblk), dim3(AT2_WARPS * 32), at2_smem(DT * 16), st, a));
     return launched("attn_tc");
 }
 
@@ -960,8 +1065,15 @@ int attention(AttnArgs a, int sync, const char *who) {
         const long long rows = (long long)a.HKV * a.ns * a.nq;
         a.nsr = (a.nk + AT2_KEYS - 1) / AT2_KEYS;
         a.total = rows * a.nsr;
-        a.nblk = (int)std::min<long long>((long long)per_sm * d->sm_count, a.total);
+        // the merging CTA keeps one weight per (slot, head slot) of a row in the staging area
+        const long long fit = (long long)(at2_stage(a.D) / sizeof(float)) / (a.H / a.HKV) - 2;
+        a.nblk = (int)std::min(std::min<long long>((long long)per_sm * d->sm_count, a.total), fit);
         a.err = d->err_dev;
+        G9_TRY(attn_counters((size_t)rows, &a.cnt));
+        // bytes of K and V the kernel may read: every (stream, KV head, key) row of D elements
+        const size_t kext = ((size_t)(a.ns - 1) * a.ks + (size_t)(a.HKV - 1) * a.kh + (size_t)(a.nk - 1) * a.kk + a.D) * 2;
+        const size_t vext = ((size_t)(a.ns - 1) * a.vs + (size_t)(a.HKV - 1) * a.vh + (size_t)(a.nk - 1) * a.vk + a.D) * 2;
+        a.early = !queued_writes_overlap(d, a.K, kext) && !queued_writes_overlap(d, a.V, vext);
         part_bytes = round256((size_t)(a.nblk + rows) * (a.H / a.HKV) * (2 + a.D) * sizeof(float));
     } else {
         a.nchunk = (a.nk + ATT_CHUNK - 1) / ATT_CHUNK;
@@ -981,11 +1093,10 @@ int attention(AttnArgs a, int sync, const char *who) {
         attn_part_k<<<(unsigned)(((long long)a.ns * a.nq * a.H * a.nchunk + 7) / 8), 256, 0, st>>>(a);
         G9_TRY(launched("attn_part"));
     }
-    if (tc)
-        attn_merge_k<true><<<(unsigned)((long long)a.ns * a.nq * a.H), 128, 0, st>>>(a);
-    else
-        attn_merge_k<false><<<(unsigned)((long long)a.ns * a.nq * a.H), 128, 0, st>>>(a);
-    G9_TRY(launched("attn_merge"));
+    if (!tc) {
+        attn_merge_k<<<(unsigned)((long long)a.ns * a.nq * a.H), 128, 0, st>>>(a);
+        G9_TRY(launched("attn_merge"));
+    }
     Operand out;
     out.user = out.dptr = a.O;
     out.bytes = (size_t)a.ns * a.nq * a.H * a.D * sizeof(float);

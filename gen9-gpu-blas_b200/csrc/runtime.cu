@@ -251,6 +251,21 @@ int skinny_slots(size_t words, uint64_t **p, unsigned *epoch) {
     return 0;
 }
 
+int attn_counters(size_t n, unsigned **p) {
+    DevState *d = dev_state();
+    if (!d) return G.status;
+    if (d->at_cnt_n < n) {
+        void *buf = d->at_cnt;
+        size_t bytes = d->at_cnt_n * sizeof(unsigned);
+        G9_TRY(ensure_dev_buf(&buf, &bytes, n * sizeof(unsigned)));
+        G9_CU(cudaMemsetAsync(buf, 0, bytes, stream()));
+        d->at_cnt = (unsigned *)buf;
+        d->at_cnt_n = bytes / sizeof(unsigned);
+    }
+    *p = d->at_cnt;
+    return 0;
+}
+
 int map_operand(Operand &op, const void *p, size_t bytes, int slot, bool copy_in, bool written) {
     op.user = p;
     op.bytes = bytes;

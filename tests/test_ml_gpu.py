@@ -557,6 +557,34 @@ def test_attn_dec_query_scales(gpu_lib, qmul):
         assert _close_attn(got[s], want), (s, np.max(np.abs(got[s] - want)))
 
 
+def test_attn_dec_nan_past_visible(gpu_lib):
+    """Cache rows past each stream's visible count hold NaN (an unwritten llama.cpp cache may): the tensor-core kernel
+    may copy them (its first step is requested before the count is read) but masks their scores and zeroes their
+    values, so the outputs stay finite and equal the oracle's over the visible rows."""
+    D, H, HKV, ns, nq, nk = 128, 32, 8, 4, 1, 200
+    Q = dev(rng.standard_normal((ns, nq, H, D)).astype(np.float32))
+    Kc = rng.standard_normal((ns, nk, HKV, D)).astype(np.float16)
+    Vc = rng.standard_normal((ns, nk, HKV, D)).astype(np.float16)
+    vis = np.array([1, 37, 200, 96], np.int32)
+    Kn, Vn = Kc.copy(), Vc.copy()
+    for s_ in range(ns):
+        Kn[s_, vis[s_]:] = np.nan
+        Vn[s_, vis[s_]:] = np.nan
+    Kd, Vd = dev(Kn), dev(Vn)
+    O = dev(np.full((ns, nq, H, D), np.nan, np.float32))
+    kk, kh, ks, scale = HKV * D, D, nk * HKV * D, D ** -0.5
+    for _ in range(2):   # twice: the per-row arrival counters are back at zero after a call
+        assert gpu_lib.attn_dec(D, H, HKV, ns, nq, nk, ptr(Q), H * D, D, nq * H * D, ptr(Kd), kk, kh, ks,
+                                Kd.numel() * 2, ptr(Vd), kk, kh, ks, Vd.numel() * 2, ptr(O), scale, ptr(vis), 0, 64,
+                                1) == 0, gpu_lib.error()
+        got = host(O, gpu_lib)
+        assert np.all(np.isfinite(got))
+        Qh = Q.cpu().numpy()
+        for s_ in range(ns):
+            want = ml_ref.attention(Qh[s_], Kc[s_], Vc[s_], scale, [int(vis[s_])])
+            assert _close_attn(got[s_], want), (s_, np.max(np.abs(got[s_] - want)))
+
+
 def test_attn_dec_long_chunks(gpu_lib):
     """Enough (stream, KV head) rows that the planner gives each warp several 32-key steps (the copy of the next
     step's rows overlapping this step's MMAs), with visible counts that end inside a step, a warp and a chunk."""
