@@ -244,6 +244,65 @@ __global__ void unary_k(int op, long long n, const float *x, float *y) {
     }
 }
 
+// GELU table: gelu_ggml of every FP16 bit pattern, the function's values on (−10, 10) being fp16(gelu(fp16(x))), a
+// function of fp16(x) alone (ggml-cpu reads the same kind of table). Built once per device by gelu_tab_k from the
+// same device function as the fused GEMM epilogue, so a lookup gives the bits the computation gives.
+__device__ __half g_gelu_tab[65536];
+
+__global__ void gelu_tab_k() {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < 65536) g_gelu_tab[i] = __float2half_rn(gelu_ggml(__half2float(__ushort_as_half((unsigned short)i))));
+}
+
+template <int OP>
+__device__ __forceinline__ float unary_f(float v, const __half *tab) {
+    if (OP == 0) {
+        if (v <= -10.0f) return 0.0f;
+        if (v >= 10.0f) return v;
+        return __half2float(tab[__half_as_ushort(__float2half_rn(v))]);
+    } else if (OP == 1) {
+        return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, erff(__fmul_rn(v, 0.70710678118654752440f))));
+    }
+    return v > 0.0f ? v : 0.0f;
+}
+
+// Elementwise op over 16-byte aligned float4 vectors: grid-stride with four vectors in flight per thread, the last
+// n % 4 elements by the first threads of CTA 0. OP 0 (GELU) first copies the 128 KB table into shared memory (one
+// 1024-thread CTA per SM).
+template <int OP>
+__global__ void __launch_bounds__(1024) unary_v_k(long long n, const float *x, float *y) {
+    extern __shared__ __align__(16) uint8_t ut_sm[];
+    const __half *tab = nullptr;
+    if (OP == 0) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(g_gelu_tab);
+        uint4 *dst = reinterpret_cast<uint4 *>(ut_sm);
+        for (int i = threadIdx.x; i < 65536 * 2 / 16; i += blockDim.x) dst[i] = src[i];
+        __syncthreads();
+        tab = reinterpret_cast<const __half *>(ut_sm);
+    }
+    const long long n4 = n >> 2, stride = (long long)gridDim.x * blockDim.x;
+    const float4 *x4 = reinterpret_cast<const float4 *>(x);
+    float4 *y4 = reinterpret_cast<float4 *>(y);
+    long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    for (; i + 3 * stride < n4; i += 4 * stride) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) v[u] = x4[i + u * stride];
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+            y4[i + u * stride] = make_float4(unary_f<OP>(v[u].x, tab), unary_f<OP>(v[u].y, tab), unary_f<OP>(v[u].z, tab),
+                                             unary_f<OP>(v[u].w, tab));
+    }
+    for (; i < n4; i += stride) {
+        const float4 v = x4[i];
+        y4[i] = make_float4(unary_f<OP>(v.x, tab), unary_f<OP>(v.y, tab), unary_f<OP>(v.z, tab), unary_f<OP>(v.w, tab));
+    }
+    if (blockIdx.x == 0 && threadIdx.x < (n & 3)) {
+        const long long e = n4 * 4 + threadIdx.x;
+        y[e] = unary_f<OP>(x[e], tab);
+    }
+}
+
 __global__ void cvt_heads_k(int rows, int H, int D, const float *__restrict__ x, long long s_row, long long s_head,
                             __half *__restrict__ y) {
     const long long n = (long long)rows * H * D;
@@ -1207,7 +1266,24 @@ static int unary(int op, size_t n, const float *X, float *Y, int sync) {
     } else {
         G9_TRY(c.big(Y, n * 4, false, true, &y));
     }
-    unary_k<<<grid_n((long long)n, d->sm_count), 256, 0, st>>>(op, (long long)n, (const float *)x, (float *)y);
+    if (((uintptr_t)x & 15) == 0 && ((uintptr_t)y & 15) == 0) {
+        if (op == 0) {
+            static bool tab[kMaxDevices] = {}, attr[kMaxDevices] = {};
+            if (!tab[d->dev]) {
+                gelu_tab_k<<<64, 1024, 0, st>>>();
+                G9_TRY(launched("gelu_tab"));
+                tab[d->dev] = true;
+            }
+            G9_CU(smem_limit_once(unary_v_k<0>, 65536 * 2, attr));
+            unary_v_k<0><<<d->sm_count, 1024, 65536 * 2, st>>>((long long)n, (const float *)x, (float *)y);
+        } else if (op == 1) {
+            unary_v_k<1><<<2 * d->sm_count, 512, 0, st>>>((long long)n, (const float *)x, (float *)y);
+        } else {
+            unary_v_k<2><<<4 * d->sm_count, 512, 0, st>>>((long long)n, (const float *)x, (float *)y);
+        }
+    } else {
+        unary_k<<<grid_n((long long)n, d->sm_count), 256, 0, st>>>(op, (long long)n, (const float *)x, (float *)y);
+    }
     G9_TRY(launched("unary"));
     return c.finish(sync);
 }

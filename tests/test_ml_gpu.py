@@ -372,6 +372,25 @@ def test_activations(gpu_lib):
     assert np.array_equal(y, ml_ref.relu(x))
 
 
+def test_gelu_table_equals_computed(gpu_lib):
+    """16-byte aligned operands take the table kernel (fp16(x) indexes a 64K-entry table built on the device from the
+    same GELU function), others the computing kernel: the two agree bit for bit on every FP16 value, NaN and the
+    infinities included, and on random floats around the ±10 cut."""
+    x = np.concatenate([np.arange(65536, dtype=np.uint16).view(np.float16).astype(np.float32),
+                        (rng.standard_normal(100003) * 6).astype(np.float32),
+                        np.array([-10.0, 10.0, np.nextafter(-10.0, 0, dtype=np.float32),
+                                  np.nextafter(10.0, 0, dtype=np.float32), np.inf, -np.inf, np.nan], np.float32)])
+    n = x.size
+    buf = dev(np.concatenate([np.zeros(1, np.float32), x]))   # x at a 4-byte offset: not 16-byte aligned
+    out = dev(np.zeros(n + 1, np.float32))
+    xa = dev(x)
+    ya = dev(np.zeros(n, np.float32))
+    assert gpu_lib.gelu(n, ptr(xa), ptr(ya), 1) == 0
+    assert gpu_lib.gelu(n, buf.data_ptr() + 4, out.data_ptr() + 4, 1) == 0
+    a, m = host(ya, gpu_lib), host(out, gpu_lib)[1:]
+    assert np.array_equal(a.view(np.uint32), m.view(np.uint32)) or np.array_equal(a, m, equal_nan=True)
+
+
 def test_cvt_f16_heads(gpu_lib):
     rows, H, D = 11, 6, 40
     X = (rng.standard_normal((rows, H * 64 + 7)) * 3e4).astype(np.float32)   # beyond FP16: saturated
