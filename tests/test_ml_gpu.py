@@ -442,8 +442,9 @@ def test_rope(gpu_lib, neox, use_ff, ext, fs):
 
 @pytest.mark.parametrize("vision,sections", [(0, (16, 8, 8, 0)), (0, (11, 5, 0, 3)), (1, (16, 16, 0, 0)),
                                              (1, (8, 0, 12, 12))])
-def test_rope_multi(gpu_lib, vision, sections):
-    n_tok, nh, n_dims = 6, 3, 64
+@pytest.mark.parametrize("nh", [3, 9])   # 9: groups of four heads and a remainder
+def test_rope_multi(gpu_lib, vision, sections, nh):
+    n_tok, n_dims = 6, 64
     ne0 = 2 * n_dims if vision else n_dims
     X = rng.standard_normal((n_tok, nh, ne0)).astype(np.float32)
     pos = rng.integers(0, 600, 4 * n_tok).astype(np.int32)
