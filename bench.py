@@ -1076,18 +1076,18 @@ def run_rows(args, torch):
         hbm_row(f"rope NEOX {nt} tokens x {nh} heads x {nd} (in place)", ms, 2 * nt * nh * nd * 4 + nt * 4)
         del Xs, Ys
         # decoding attention over a KV cache: 8 streams, one new token each, H 32 / HKV 8, D 128, 4096 keys
-        ns, nk, H, HKV, D = 8, 4096, 32, 8, 128
-        Kc = [torch.randn(ns, nk, HKV, D, device="cuda", generator=g).half() for _ in range(2)]
-        Vc = [torch.randn(ns, nk, HKV, D, device="cuda", generator=g).half() for _ in range(2)]
-        Q = torch.randn(ns, 1, H, D, device="cuda", generator=g)
-        O = torch.empty(ns, 1, H, D, device="cuda")
+        ns, nk, nhq, nhkv, hd = 8, 4096, 32, 8, 128
+        Kc = [torch.randn(ns, nk, nhkv, hd, device="cuda", generator=g).half() for _ in range(2)]
+        Vc = [torch.randn(ns, nk, nhkv, hd, device="cuda", generator=g).half() for _ in range(2)]
+        Q = torch.randn(ns, 1, nhq, hd, device="cuda", generator=g)
+        O = torch.empty(ns, 1, nhq, hd, device="cuda")
         vis = torch.full((ns,), nk, device="cuda", dtype=torch.int32)
-        kk, kh, ks = HKV * D, D, nk * HKV * D
-        ms = queued_ms(lambda i: chk(L.attn_dec(D, H, HKV, ns, 1, nk, Q.data_ptr(), H * D, D, H * D,
+        kk, kh, ks = nhkv * hd, hd, nk * nhkv * hd
+        ms = queued_ms(lambda i: chk(L.attn_dec(hd, nhq, nhkv, ns, 1, nk, Q.data_ptr(), nhq * hd, hd, nhq * hd,
                                                 Kc[i % 2].data_ptr(), kk, kh, ks, Kc[0].numel() * 2,
                                                 Vc[i % 2].data_ptr(), kk, kh, ks, Vc[0].numel() * 2, O.data_ptr(),
-                                                D ** -0.5, vis.data_ptr(), 0, 256, 0)), 50)
-        hbm_row(f"attn_dec {ns} streams x {nk} keys, H {H} / HKV {HKV}, D {D}", ms, 2 * ns * nk * HKV * D * 2)
+                                                hd ** -0.5, vis.data_ptr(), 0, 256, 0)), 50)
+        hbm_row(f"attn_dec {ns} streams x {nk} keys, H {nhq} / HKV {nhkv}, D {hd}", ms, 2 * ns * nk * nhkv * hd * 2)
         del Kc, Vc
         torch.cuda.empty_cache()
 
