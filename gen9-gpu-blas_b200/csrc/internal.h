@@ -48,8 +48,9 @@ struct DevState {
     uint64_t *sk_part = nullptr;                               // epoch-tagged partial tiles of the stream-K skinny
     size_t sk_part_n = 0;                                      // kernel (words; zeroed when created or grown)
     unsigned sk_epoch = 0;                                     // launch counter written into those tags
-    unsigned *at_cnt = nullptr;                                // per-row arrival counters of the attention kernel
-    size_t at_cnt_n = 0;                                       // (zeroed when created or grown; each call leaves 0)
+    unsigned *at_cnt = nullptr;                                // arrival counters of the attention kernel's rows and
+    size_t at_cnt_n = 0;                                       // the FFN gate / up pairs (zeroed when created or
+                                                               // grown; each call leaves every counter it used at 0)
     // Device ranges written by no-wait calls that may still be queued, each with an event recorded right after the
     // call that wrote it (an entry whose event has completed is dropped); a kernel that reads an input before
     // griddepcontrol.wait checks its input against them.
@@ -160,8 +161,9 @@ int launch_trsm_dev(int type, int left, int upper, int tA, int unit, int M, int 
 // Partial-tile words of the stream-K skinny kernel (at least `words`, zeroed when created or grown) and the epoch of
 // the launch about to be enqueued (never 0; the words are zeroed again when the counter wraps).
 int skinny_slots(size_t words, uint64_t **p, unsigned *epoch);
-// n zero-initialised arrival counters for the attention kernel's rows (each call returns every counter it uses to 0).
-int attn_counters(size_t n, unsigned **p);
+// n zero-initialised arrival counters (attention rows, FFN gate / up pairs); each call returns every counter it uses
+// to 0, and calls on one stream run in order, so the kernels of successive calls share them.
+int arrival_counters(size_t n, unsigned **p);
 // Call timing: timer_start at entry (wall clock), timer_kernel right before the main kernels (GEN9BLAS_PROFILE=1:
 // CUDA event), timer_stop at the end: last_time_ms is the kernel time with profiling, else the whole call.
 void timer_start();
@@ -211,6 +213,8 @@ int skinny_threshold(int type);
 // least 16 rows per SM, K >= 2048 and a multiple of 8, 16-byte aligned rows): activations (F32, or FP16 with ahalf)
 // rounded to FP16, FP32 sums rounded to FP16, then bias / GELU / residual, F32 C; *nf set on a non-finite FP16 result.
 // Returns 1 (nothing enqueued) when the shape does not qualify.
+int launch_skinny_swiglu(int M, const float *X, long long ldx, const void *Wg, const void *Wu, int K, int N, long long ldw,
+                         __half *g16, __half *u16, __half *h16, long long ldh, unsigned *nf, cudaStream_t st);
 int launch_skinny_f16w(int M, const void *A, bool ahalf, long long lda, const void *W, int K, int N, long long ldw,
                        float *C, long long ldc, const float *bias, int gelu, const float *R, long long ldr, unsigned *nf,
                        cudaStream_t st);

@@ -1128,7 +1128,7 @@ int attention(AttnArgs a, int sync, const char *who) {
         const long long fit = (long long)(at2_stage(a.D) / sizeof(float)) / (a.H / a.HKV) - 2;
         a.nblk = (int)std::min(std::min<long long>((long long)per_sm * d->sm_count, a.total), fit);
         a.err = d->err_dev;
-        G9_TRY(attn_counters((size_t)rows, &a.cnt));
+        G9_TRY(arrival_counters((size_t)rows, &a.cnt));
         // bytes of K and V the kernel may read: every (stream, KV head, key) row of D elements
         const size_t kext = ((size_t)(a.ns - 1) * a.ks + (size_t)(a.HKV - 1) * a.kh + (size_t)(a.nk - 1) * a.kk + a.D) * 2;
         const size_t vext = ((size_t)(a.ns - 1) * a.vs + (size_t)(a.HKV - 1) * a.vh + (size_t)(a.nk - 1) * a.vk + a.D) * 2;

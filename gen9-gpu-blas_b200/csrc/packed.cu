@@ -650,16 +650,36 @@ GEN9BLAS_API int gen9blas_ffn_f16w(int M, const float *X, int ldx, const gen9bla
         flag = d->err_dev + 1;
     }
     timer_kernel();
-    act_to_f16<float><<<grid_for((long long)M * Kp, d->sm_count), 256, 0, st>>>((const float *)op[0].dptr, ldx, M, K, Kp, x16);
-    G9_TRY(launched("act_to_f16"));
-    G9_TRY(f16w_gemm(x16, M, Pg, g16, st));
-    G9_TRY(f16w_gemm(x16, M, Pu, u16, st));
-    swiglu_f16<<<grid_for((long long)M * Kpd, d->sm_count), 256, 0, st>>>(g16, u16, M, N, h16, Kpd, flag);
-    G9_TRY(launched("swiglu_f16"));
-    G9_TRY(f16w_gemm(h16, M, Pd, y16, st));
-    f16w_epilogue<<<grid_for((long long)M * Nd, d->sm_count), 256, 0, st>>>(y16, Nd, M, Nd, (float *)op[1].dptr, ldy, nullptr,
-                                                                            0, nullptr, 0, flag);
-    G9_TRY(launched("f16w_epilogue"));
+    // decode sizes: gate and up in one launch whose pairs apply SWIGLU, then the down GEMM with the F32 epilogue in
+    // its kernel (two launches; the same operations and roundings as the general chain below)
+    int fused = 1;
+    if (M <= 16) {
+        fused = launch_skinny_swiglu(M, (const float *)op[0].dptr, ldx, Pg->w, Pu->w, K, N, Kp, g16, u16, h16, Kpd, flag, st);
+        if (fused < 0) return fused;
+        if (fused == 0) {
+            const int r2 = launch_skinny_f16w(M, h16, true, Kpd, Pd->w, Kpd, Nd, Kpd, (float *)op[1].dptr, ldy, nullptr, 0,
+                                              nullptr, 0, flag, st);
+            if (r2 < 0) return r2;
+            if (r2 == 1) {
+                G9_TRY(f16w_gemm(h16, M, Pd, y16, st));
+                f16w_epilogue<<<grid_for((long long)M * Nd, d->sm_count), 256, 0, st>>>(
+                    y16, Nd, M, Nd, (float *)op[1].dptr, ldy, nullptr, 0, nullptr, 0, flag);
+                G9_TRY(launched("f16w_epilogue"));
+            }
+        }
+    }
+    if (fused) {
+        act_to_f16<float><<<grid_for((long long)M * Kp, d->sm_count), 256, 0, st>>>((const float *)op[0].dptr, ldx, M, K, Kp, x16);
+        G9_TRY(launched("act_to_f16"));
+        G9_TRY(f16w_gemm(x16, M, Pg, g16, st));
+        G9_TRY(f16w_gemm(x16, M, Pu, u16, st));
+        swiglu_f16<<<grid_for((long long)M * Kpd, d->sm_count), 256, 0, st>>>(g16, u16, M, N, h16, Kpd, flag);
+        G9_TRY(launched("swiglu_f16"));
+        G9_TRY(f16w_gemm(h16, M, Pd, y16, st));
+        f16w_epilogue<<<grid_for((long long)M * Nd, d->sm_count), 256, 0, st>>>(y16, Nd, M, Nd, (float *)op[1].dptr, ldy,
+                                                                                nullptr, 0, nullptr, 0, flag);
+        G9_TRY(launched("f16w_epilogue"));
+    }
     int r = finish_op(op, 2);
     timer_stop();
     if (r == 0 && !queued && nonfinite) *nonfinite = *(volatile unsigned *)(d->err_host + 1) != 0u;

@@ -251,7 +251,7 @@ int skinny_slots(size_t words, uint64_t **p, unsigned *epoch) {
     return 0;
 }
 
-int attn_counters(size_t n, unsigned **p) {
+int arrival_counters(size_t n, unsigned **p) {
     DevState *d = dev_state();
     if (!d) return G.status;
     if (d->at_cnt_n < n) {

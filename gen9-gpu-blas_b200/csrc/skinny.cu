@@ -70,6 +70,15 @@ struct SkinnyArgs {
     const float *R;
     long long ldr;
     int gelu;
+    // wk_f16_blk gate / up pair (ffn_f16w): CTA 2b takes row block b of w (gate, FP16 result to C) and CTA 2b + 1 the
+    // same block of w2 (up, FP16 result to c2), both with pitch scm; the second of the two to finish writes
+    // h = fp16(silu(g)·u) for those rows into hsw (pitch ldh, zero from column Nc to ldh), sets *nf for a non-finite
+    // g, u or h or |h| beyond FP16, and returns cnt[b] to zero.
+    const void *w2;
+    void *c2;
+    __half *hsw;
+    long long ldh;
+    unsigned *cnt;
 };
 
 template <typename T>
@@ -650,18 +659,20 @@ __device__ __forceinline__ uint4 act_frag(const SkinnyArgs &p, int m, int k) {
 // bookkeeping (W 4096 × 4096 M = 1, calls back to back on B200: 5.8 µs against 7.7 with wk_f16_sk; 4096 × 11008 15.0
 // against 17.5). A version looping over several blocks per CTA (next block's requests before the barrier, two pad
 // sets) was slower on every shape, including the one-block ones (7.0 and 16.8 µs).
-template <bool FULLK, bool TWO, int MODE = ACT_F16, bool F16W = false>
+template <bool FULLK, bool TWO, int MODE = ACT_F16, bool F16W = false, bool SWI = false>
 __global__ void __launch_bounds__(WK_WARPS * 32, 2) wk_f16_blk(const SkinnyArgs p, int KC) {
     static_assert(MODE == ACT_F16 || MODE == ACT_PAIRED || MODE == ACT_SPLIT || MODE == ACT_F32H, "token modes");
     static_assert(!F16W || MODE == ACT_F16 || MODE == ACT_F32H, "the f16w epilogue takes FP16-rounded tokens");
+    static_assert(!SWI || ((MODE == ACT_F16 || MODE == ACT_F32H) && !F16W), "the gate / up pair stores FP16 results");
     constexpr bool F32A = MODE == ACT_PAIRED || MODE == ACT_SPLIT;
     extern __shared__ __align__(16) uint8_t sk_stage[];
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
-    const int r0 = blockIdx.x * 16;
+    const int blk = SWI ? blockIdx.x >> 1 : blockIdx.x, which = SWI ? blockIdx.x & 1 : 0;   // SWI: 0 gate, 1 up
+    const int r0 = blk * 16;
     const int c0 = KC * warp / WK_WARPS, c1 = KC * (warp + 1) / WK_WARPS;
-    const __half *Wt = (const __half *)p.w;
+    const __half *Wt = (const __half *)(which ? p.w2 : p.w);
     const __half *w0 = Wt + (long long)min(r0 + g, p.Nc - 1) * p.swn;
     const __half *w1 = Wt + (long long)min(r0 + g + 8, p.Nc - 1) * p.swn;
     const __half *a0 = (const __half *)p.a + (long long)min(g, p.Mc - 1) * p.sam;   // token g (clamped: not stored)
@@ -782,8 +793,45 @@ __global__ void __launch_bounds__(WK_WARPS * 32, 2) wk_f16_blk(const SkinnyArgs 
             if (p.gelu) v = gelu_ggml(v);
             if (p.R) v = __fadd_rn(v, p.R[(long long)tok * p.ldr + n]);
             reinterpret_cast<float *>(p.C)[(long long)tok * p.scm + n] = v;
+        } else if constexpr (SWI) {   // the GEMM's FP16 result, as skinny_store with alpha = 1, beta = 0
+            reinterpret_cast<__half *>(which ? p.c2 : p.C)[(long long)tok * p.scm + r0 + row] = __float2half_rn(acc);
         } else {
             skinny_out<F32A>(p, tok, r0 + row, acc);
+        }
+    }
+    if constexpr (SWI) {
+        // arrival of this half of the pair; the second arrival applies SWIGLU to the block's rows (the operations of
+        // ffn_f16w's separate swiglu_f16, element for element)
+        __shared__ int sw_last;
+        __syncthreads();   // every FP16 result of this CTA is stored (the release below covers them)
+        if (threadIdx.x == 0) {
+            __threadfence();
+            sw_last = atomicAdd(p.cnt + blk, 1u) == 1u;
+            __threadfence();
+        }
+        __syncthreads();
+        if (sw_last) {
+            const int n = r0 + row;
+            if (tok < p.Mc && n < p.ldh) {
+                float h = 0.0f;
+                bool bad = false;
+                if (n < p.Nc) {
+                    const long long o = (long long)tok * p.scm + n;
+                    const float gv = __half2float(__ushort_as_half(__ldcg(reinterpret_cast<const unsigned short *>(p.C) + o)));
+                    const float uv = __half2float(__ushort_as_half(__ldcg(reinterpret_cast<const unsigned short *>(p.c2) + o)));
+                    h = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv);
+                    bad = !isfinite(gv) || !isfinite(uv) || !(fabsf(h) <= 65504.0f);
+                }
+                p.hsw[(long long)tok * p.ldh + n] = __float2half_rn(h);
+                if (bad) *(volatile unsigned *)p.nf = 1u;
+            }
+            const int nb = (int)(gridDim.x >> 1);
+            if (blk == nb - 1) {   // columns past the last block, up to the pitch: zero
+                const long long w0 = (long long)nb * 16, wn = p.ldh - w0;
+                for (long long i = threadIdx.x; i < (long long)p.Mc * wn; i += blockDim.x)
+                    p.hsw[(i / wn) * p.ldh + w0 + i % wn] = __float2half_rn(0.0f);
+            }
+            if (threadIdx.x == 0) p.cnt[blk] = 0u;   // the next call finds the counter at zero
         }
     }
     skinny_peer_fence(p);
@@ -1267,6 +1315,40 @@ int launch_skinny_f16w(int M, const void *A, bool ahalf, long long lda, const vo
     G9_CU(smem_limit_once(kern, SK_SMEM_BYTES, attr[(ahalf ? 4 : 0) + (fullk ? 2 : 0) + (two ? 1 : 0)]));
     launch_pdl(kern, dim3((unsigned)((N + 15) / 16)), dim3(WK_WARPS * 32), SK_SMEM_BYTES, st, p, KC);
     return launched("skinny_wk_f16_blk_f16w");
+}
+
+// ffn_f16w's gate and up GEMMs in one launch (M <= 16 F32 tokens rounded to FP16 as loaded, the one-block kernel's
+// plan): g16 = fp16(X·Wgᵀ), u16 = fp16(X·Wuᵀ) (pitch N) and h16 = fp16(silu(g)·u) (pitch ldh, zero past N). Returns 1,
+// launching nothing, where launch_skinny_f16w would decline the shape or layout.
+int launch_skinny_swiglu(int M, const float *X, long long ldx, const void *Wg, const void *Wu, int K, int N, long long ldw,
+                         __half *g16, __half *u16, __half *h16, long long ldh, unsigned *nf, cudaStream_t st) {
+    DevState *d = dev_state();
+    if (!d) return G.status;
+    const int KC = (K + 255) / 256, RB = (N + 15) / 16;
+    if (M < 1 || M > 16 || RB < d->sm_count || KC < WK_WARPS || K % 8 != 0 || ((uintptr_t)X & 15) != 0 ||
+        (ldx * 4) % 16 != 0 || ((uintptr_t)Wg & 15) != 0 || ((uintptr_t)Wu & 15) != 0 || (ldw * 2) % 16 != 0 || ldh < N)
+        return 1;
+    SkinnyArgs p;
+    memset(&p, 0, sizeof(p));
+    p.Mc = M; p.Nc = N; p.K = K;
+    p.alpha = 1.0f; p.beta = 0.0f;
+    p.a = X; p.sam = ldx; p.sak = 1;
+    p.w = Wg; p.w2 = Wu; p.swn = ldw; p.swk = 1;
+    p.C = g16; p.c2 = u16; p.scm = N; p.scn = 1;
+    p.dst[0] = g16; p.ndst = 1;
+    p.hsw = h16; p.ldh = ldh;
+    p.nf = nf;
+    G9_TRY(arrival_counters((size_t)RB, &p.cnt));
+    const size_t wext = ((size_t)(N - 1) * ldw + K) * sizeof(__half);
+    p.early_w = !queued_writes_overlap(d, Wg, wext) && !queued_writes_overlap(d, Wu, wext);
+    const bool fullk = K % 256 == 0, two = M > 8;
+    using Kern = void (*)(const SkinnyArgs, int);
+    const Kern kern = fullk ? (two ? wk_f16_blk<true, true, ACT_F32H, false, true> : wk_f16_blk<true, false, ACT_F32H, false, true>)
+                            : (two ? wk_f16_blk<false, true, ACT_F32H, false, true> : wk_f16_blk<false, false, ACT_F32H, false, true>);
+    static bool attr[4][kMaxDevices] = {};
+    G9_CU(smem_limit_once(kern, SK_SMEM_BYTES, attr[(fullk ? 2 : 0) + (two ? 1 : 0)]));
+    launch_pdl(kern, dim3((unsigned)(2 * RB)), dim3(WK_WARPS * 32), SK_SMEM_BYTES, st, p, KC);
+    return launched("skinny_wk_f16_blk_swiglu");
 }
 
 int launch_skinny(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, const void *B,

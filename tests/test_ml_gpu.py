@@ -246,6 +246,43 @@ def test_ffn_f16w(gpu_lib, M):
             gpu_lib.packed_b_free(P)
 
 
+@pytest.fixture(scope="module")
+def ffn_7b(gpu_lib):
+    """Gate, up (11008 x 4096) and down (4096 x 11008) FP16 weights of a 7B layer, packed once for the module."""
+    K, N, Nd = 4096, 11008, 4096
+    r = np.random.default_rng(77)
+    Wg, Wu = [(r.standard_normal((N, K), np.float32) * 0.02).astype(np.float16) for _ in range(2)]
+    Wd = (r.standard_normal((Nd, N), np.float32) * 0.02).astype(np.float16)
+    Ps = [pack_hs(gpu_lib, W) for W in (Wg, Wu, Wd)]
+    yield (K, N, Nd), Ps
+    for P in Ps:
+        gpu_lib.packed_b_free(P)
+
+
+@pytest.mark.parametrize("M", [1, 5, 16])
+@pytest.mark.parametrize("scale", [1.0, 300.0])
+def test_ffn_f16w_decode_fused_equals_chain(gpu_lib, ffn_7b, M, scale):
+    """At decode sizes (M <= 16, 16-byte aligned activation rows) ffn_f16w runs gate and up in one launch whose CTA
+    pairs apply SWIGLU, then the down GEMM with its epilogue in the kernel; an activation pitch that is not a multiple
+    of four floats takes the general six-kernel chain. Both give the same bits and the same non-finite flag (scale
+    300 drives |silu(g)·u| past FP16)."""
+    (K, N, Nd), (Pg, Pu, Pd) = ffn_7b
+    X = (rng.standard_normal((M, K)) * scale).astype(np.float32)
+    Xp = np.zeros((M, K + 1), np.float32)
+    Xp[:, :K] = X
+    Yf, Yc = np.zeros((M, Nd), np.float32), np.zeros((M, Nd), np.float32)
+    nf1, nfp1 = nf_ptr()
+    nf2, nfp2 = nf_ptr()
+    assert gpu_lib.ffn_f16w(M, ptr(X), K, Pg, Pu, Pd, ptr(Yf), Nd, nfp1) == 0, gpu_lib.error()
+    assert gpu_lib.ffn_f16w(M, ptr(Xp), K + 1, Pg, Pu, Pd, ptr(Yc), Nd, nfp2) == 0, gpu_lib.error()
+    assert np.array_equal(Yf.view(np.uint32), Yc.view(np.uint32))
+    assert nf1.value == nf2.value == (1 if scale > 1 else 0)
+    for _ in range(2):   # repeated calls: the pairs' arrival counters return to zero
+        Yr = np.zeros((M, Nd), np.float32)
+        assert gpu_lib.ffn_f16w(M, ptr(X), K, Pg, Pu, Pd, ptr(Yr), Nd, None) == 0, gpu_lib.error()
+        assert np.array_equal(Yr.view(np.uint32), Yf.view(np.uint32))
+
+
 @pytest.mark.parametrize("qtype", [0, 1, 2])
 def test_pack_b_q_dequantizes_bit_exactly(gpu_lib, qtype):
     """The packed FP16 weights equal ggml's dequantize_row_* + FP16 rounding: read back through an identity product
