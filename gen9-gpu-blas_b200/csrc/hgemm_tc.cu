@@ -65,6 +65,11 @@ struct TcParams {
     // with tma_c: the kernel computes Cᵀ (the host swapped the operands), so each staged block is written transposed
     // and stored at the swapped coordinates
     int c_t;
+    // 1-CTA kernel, split K (FP32 accumulation, one matrix): unit u = (tile u / ks, K part u % ks), part q taking K
+    // blocks [nk·q/ks, nk·(q+1)/ks) and storing its FP32 tile into kpart + q·M·N (dense M × N); hgemm_ksum adds the
+    // parts in order and applies alpha / beta. ks = 1: whole tiles straight into C.
+    int ks;
+    float *kpart;
 };
 
 __device__ __forceinline__ void tile_coords(const TcParams &p, int tile, int &b, int &mb, int &nb) {
@@ -205,11 +210,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         uint32_t phase = 0;
         long long issued = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
+        for (int u = blockIdx.x; u < p.total_tiles * p.ks && ok; u += gridDim.x) {
+            const int tile = u / p.ks, part = u - tile * p.ks;
             int b, mb, nb;
             tile_coords(p, tile, b, mb, nb);
             const int m0 = mb * TC_BM, n0 = nb * TC_BN;
-            for (int kb = 0; kb < nk; kb++) {
+            const int kb0 = nk * part / p.ks, kb1 = nk * (part + 1) / p.ks;
+            for (int kb = kb0; kb < kb1; kb++) {
                 if (!mbar_wait(&empty[stage], phase ^ 1, abort, TC_WAIT_NS)) { ok = false; break; }
                 mbar_arrive_expect_tx(&full[stage], TC_STAGE_BYTES);
                 uint8_t *a = sA + stage * TC_A_BYTES;
@@ -250,13 +257,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         uint32_t phase = 0;
         int local = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, local++) {
+        for (int u = blockIdx.x; u < p.total_tiles * p.ks && ok; u += gridDim.x, local++) {
+            const int part = u % p.ks;
+            const int kb0 = nk * part / p.ks, kb1 = nk * (part + 1) / p.ks;
             const int buf = local & 1;
             const uint32_t acc_phase = (local >> 1) & 1;
             if (!mbar_wait(&tempty[buf], acc_phase ^ 1, abort, TC_WAIT_NS)) { ok = false; break; }
             tc_fence_after();
             const uint32_t d_tmem = tmem_base + buf * TC_BN;
-            for (int kb = 0; kb < nk; kb++) {
+            for (int kb = kb0; kb < kb1; kb++) {
                 if (!mbar_wait(&full[stage], phase, abort, TC_WAIT_NS)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t a_base = smem_u32(sA + stage * TC_A_BYTES);
@@ -269,7 +278,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                                                : smem_desc_sw128(a_base + k * 32, 16, 1024);
                     const uint64_t bd = p.b_mn ? smem_desc_sw128(b_base + k * 2048, 8192, 1024)
                                                : smem_desc_sw128(b_base + k * 32, 16, 1024);
-                    umma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0);
+                    umma_f16(d_tmem, ad, bd, idesc, kb != kb0 || k != 0);
                 }
                 umma_commit(&empty[stage]);
                 if (++stage == TC_STAGES) { stage = 0; phase ^= 1; }
@@ -287,7 +296,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int q = warp & 3;                 // TMEM lane quarter this warp may access
         const int row_in_tile = q * 32 + lane;
         int local = 0;
-        for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, local++) {
+        for (int u = blockIdx.x; u < p.total_tiles * p.ks; u += gridDim.x, local++) {
+            const int tile = u / p.ks, part = u - tile * p.ks;
             int b, mb, nb;
             tile_coords(p, tile, b, mb, nb);
             const int buf = local & 1;
@@ -300,6 +310,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const int row = mb * TC_BM + row_in_tile;
             const bool row_ok = row < p.M;
             __half *crow = p.C + (long long)b * p.sC + (long long)(row_ok ? row : 0) * p.ldc;
+            float *prow = p.ks > 1 ? p.kpart + ((long long)part * p.M + (row_ok ? row : 0)) * p.N : nullptr;
             const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + buf * TC_BN;
 #pragma unroll 1
             for (int c = 0; c < TC_BN / 32; c++) {
@@ -308,7 +319,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 if (F16ACC) tmem_ld_32x32_pack16(t_row + c * 32, r);
                 else tmem_ld_32x32(t_row + c * 32, r);
                 tmem_ld_wait();
-                if (col0 < p.N) store_chunk<F16ACC>(p, r, crow, col0, row_ok);
+                if (col0 >= p.N) continue;
+                if (!F16ACC && prow) {   // split K: the FP32 part (fixed indices keep r in registers)
+                    if (row_ok) {
+                        if (col0 + 32 <= p.N && (p.N & 3) == 0) {
+                            float4 *d4 = reinterpret_cast<float4 *>(prow + col0);
+#pragma unroll
+                            for (int j = 0; j < 8; j++)
+                                d4[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                                    __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; j++)
+                                if (col0 + j < p.N) prow[col0 + j] = __uint_as_float(r[j]);
+                        }
+                    }
+                } else {
+                    store_chunk<F16ACC>(p, r, crow, col0, row_ok);
+                }
             }
             tc_fence_before();
             mbar_arrive(&tempty[buf]);
@@ -318,6 +346,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, TC_TMEM_COLS);
+    }
+}
+
+// C = alpha·Σ_q part[q] + beta·C over the ks K parts of the 1-CTA kernel (in part order), rounded to FP16 as store_vals
+// rounds: element i of the dense M × N parts is C[i / N][i % N].
+__global__ void hgemm_ksum(const float *__restrict__ part, int ks, int M, int N, float alpha, float beta, __half *C,
+                           long long ldc) {
+    const long long mn = (long long)M * N;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < mn; i += (long long)gridDim.x * blockDim.x) {
+        float s = part[i];
+        for (int q = 1; q < ks; q++) s += part[q * mn + i];
+        __half *c = C + (i / N) * ldc + i % N;
+        const float o = beta != 0.0f ? __fmaf_rn(beta, __half2float(*c), alpha * s) : alpha * s;
+        *c = __float2half_rn(o);
     }
 }
 
@@ -828,6 +870,16 @@ static int hgemm_tc_impl(int type, int tA, int tB, int M, int N, int K, double a
         units = dp + (tiles - dp) * split;
     }
     const size_t partial_bytes = pair && split > 1 ? (size_t)(tiles - dp) * (split - 1) * 2 * 128 * bn * sizeof(float) : 0;
+    // 1-CTA kernel (M <= 128) with at most half the SMs' worth of tiles: K split over them (FP32 accumulation, one
+    // matrix, C only), ks parts per tile, each of at least 4 K blocks, summed in order by hgemm_ksum. Measured on
+    // B200, gemm_pb_f16w M = 64 (HS, F32 tokens rounded to FP16): see the design notes' ML rows.
+    int ks = 1;
+    if (!pair && type == GEN9BLAS_HS && count == 1 && !(peers && npeers > 0) && !c_t) {
+        const long long t1 = (long long)((M + TC_BM - 1) / TC_BM) * ((N + TC_BN - 1) / TC_BN);
+        const int nkb = (K + TC_BK - 1) / TC_BK;
+        if (2 * t1 <= d->sm_count && nkb >= 8) ks = (int)std::min<long long>(std::min<long long>(d->sm_count / t1, nkb / 4), 16);
+    }
+    const size_t kpart_bytes = ks > 1 ? ((size_t)ks * M * N * sizeof(float) + 255) / 256 * 256 : 0;
 
     // Stored shapes: A is rowsA × colsA with pitch lda (tA: K × M, else M × K); B is rowsB × colsB (tB: N × K, else K × N).
     const long long rowsA = tA ? K : M, colsA = tA ? M : K;
@@ -839,7 +891,8 @@ static int hgemm_tc_impl(int type, int tA, int tB, int M, int N, int K, double a
     const long long bytesA = okA ? 0 : (rowsA * pa * count * 2 + 255) / 256 * 256;
     const long long bytesB = okB ? 0 : (rowsB * pb * count * 2 + 255) / 256 * 256;
     void *scr = nullptr;
-    if (bytesA + bytesB + (long long)partial_bytes > 0) G9_TRY(scratch((size_t)(bytesA + bytesB) + partial_bytes, &scr));
+    if (bytesA + bytesB + (long long)(partial_bytes + kpart_bytes) > 0)
+        G9_TRY(scratch((size_t)(bytesA + bytesB) + partial_bytes + kpart_bytes, &scr));
     if (bytesA) {
         repack_f16<<<d->sm_count * 8, 256, 0, st>>>((const __half *)A, lda, sA, (int)rowsA, (int)colsA, (__half *)scr, pa,
                                                    rowsA * pa, count);
@@ -870,6 +923,8 @@ static int hgemm_tc_impl(int type, int tA, int tB, int M, int N, int K, double a
     p.c_vec = ((uintptr_t)C & 15) == 0 && (ldc % 8) == 0 && (count == 1 || (sC % 8) == 0);
     p.err = d->err_dev;
     p.dp_tiles = p.split = p.units = 0;
+    p.ks = ks;
+    p.kpart = ks > 1 ? (float *)((char *)scr + bytesA + bytesB + partial_bytes) : nullptr;
     p.partial = nullptr;
     p.flags = nullptr;
     p.epoch = 0;
@@ -921,7 +976,8 @@ static int hgemm_tc_impl(int type, int tA, int tB, int M, int N, int K, double a
     p.tiles_m = (M + TC_BM - 1) / TC_BM;
     p.tiles_n = (N + TC_BN - 1) / TC_BN;
     p.total_tiles = p.tiles_m * p.tiles_n * count;
-    const int grid = p.total_tiles < d->sm_count ? p.total_tiles : d->sm_count;
+    const int units1 = p.total_tiles * ks;
+    const int grid = units1 < d->sm_count ? units1 : d->sm_count;
     if (type == GEN9BLAS_H) {
         static bool attr[kMaxDevices] = {};
         G9_CU(smem_limit_once(hgemm_tc_kernel<true>, TC_SMEM, attr));
@@ -931,7 +987,12 @@ static int hgemm_tc_impl(int type, int tA, int tB, int M, int N, int K, double a
         G9_CU(smem_limit_once(hgemm_tc_kernel<false>, TC_SMEM, attr));
         hgemm_tc_kernel<false><<<grid, TC_THREADS, TC_SMEM, st>>>(mA, mB, p);
     }
-    return launched("hgemm_tc");
+    G9_TRY(launched("hgemm_tc"));
+    if (ks > 1) {
+        hgemm_ksum<<<4 * d->sm_count, 256, 0, st>>>(p.kpart, ks, M, N, (float)alpha, (float)beta, (__half *)C, ldc);
+        return launched("hgemm_ksum");
+    }
+    return 0;
 }
 
 int launch_hgemm_tc(int type, int tA, int tB, int M, int N, int K, double alpha, const void *A, int lda, long long sA,

@@ -47,6 +47,18 @@ def case(g9, dt, accurate, M, N, K, al, be, ta, tb, zc, seed=0):
     return gemm_error(W, ref, scale) + (g9.last_zero_copy(),)
 
 
+@pytest.mark.parametrize("M", [17, 64, 128])
+@pytest.mark.parametrize("al,be,ta,tb", [(1.0, 0.0, 0, 0), (0.75, -0.5, 1, 1), (1.0, 0.0, 0, 1)])
+def test_hgemm_accurate_small_m_split_k(g9, M, al, be, ta, tb):
+    """FP32-accumulating HGEMM with M <= 128 and few column tiles (N = 4096: 16 tiles of 256) splits K over the idle
+    SMs: FP32 parts summed in part order by a second kernel, which applies alpha / beta and the FP16 rounding. The
+    reference's accurate-mode limits (mean 1e-4, max 1e-3 of the |A|·|B| scale)."""
+    avg, mx, _ = case(g9, np.float16, True, M, 4096, 4096, al, be, ta, tb, 0, seed=M)
+    assert avg <= 1e-4 and mx <= 1e-3, (M, al, be, ta, tb, avg, mx)
+    avg, mx, _ = case(g9, np.float16, True, M, 1000, 2050, al, be, ta, tb, 1, seed=M + 1)   # ragged N and K
+    assert avg <= 1e-4 and mx <= 1e-3, (M, al, be, ta, tb, avg, mx)
+
+
 @pytest.mark.parametrize("name,dt,accurate,tol_avg,tol_max", KINDS)
 def test_reference_cases(g9, name, dt, accurate, tol_avg, tol_max):
     worst = []
