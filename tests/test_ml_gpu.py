@@ -654,6 +654,7 @@ def test_attn_dec_long_chunks(gpu_lib):
     O = torch.full((ns, nq, H, D), float("nan"), device="cuda")
     vis = np.array([8192, 1, 31, 33, 127, 129, 640, 641, 1000, 2047, 4097, 5000, 6143, 7777, 8191, 3], np.int32)
     kk, kh, ks, scale = HKV * D, D, nk * HKV * D, D ** -0.5
+    torch.cuda.synchronize()   # the tensors are written by torch's stream; the library runs on its own
     assert gpu_lib.attn_dec(D, H, HKV, ns, nq, nk, Q.data_ptr(), H * D, D, nq * H * D, Kd.data_ptr(), kk, kh, ks,
                             Kd.numel() * 2, Vd.data_ptr(), kk, kh, ks, Vd.numel() * 2, O.data_ptr(), scale, ptr(vis),
                             0, 64, 1) == 0, gpu_lib.error()
