@@ -213,8 +213,11 @@ int skinny_threshold(int type);
 // least 16 rows per SM, K >= 2048 and a multiple of 8, 16-byte aligned rows): activations (F32, or FP16 with ahalf)
 // rounded to FP16, FP32 sums rounded to FP16, then bias / GELU / residual, F32 C; *nf set on a non-finite FP16 result.
 // Returns 1 (nothing enqueued) when the shape does not qualify.
-int launch_skinny_swiglu(int M, const float *X, long long ldx, const void *Wg, const void *Wu, int K, int N, long long ldw,
-                         __half *g16, __half *u16, __half *h16, long long ldh, unsigned *nf, cudaStream_t st);
+int launch_skinny_swiglu(int M, const void *X, bool xhalf, long long ldx, const void *Wg, const void *Wu, int K, int N,
+                         long long ldw, __half *g16, __half *u16, __half *h16, long long ldh, unsigned *nf,
+                         cudaStream_t st);
+// The shapes launch_skinny_f16w takes (M <= 16, at least one 16-row block per SM, K >= 2048 in 8s, aligned weights).
+bool skinny_f16w_fits(int M, int K, int N, long long ldw, const void *W);
 int launch_skinny_f16w(int M, const void *A, bool ahalf, long long lda, const void *W, int K, int N, long long ldw,
                        float *C, long long ldc, const float *bias, int gelu, const float *R, long long ldr, unsigned *nf,
                        cudaStream_t st);

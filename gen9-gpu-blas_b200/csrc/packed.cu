@@ -496,10 +496,26 @@ int gemm_pb_f16w_any(bool ahalf, int M, const void *A, int lda, const gen9blas_p
     }
     timer_kernel();
     // M <= 16 on a wide enough, deep enough weight matrix: one kernel (FP16 rounding of the activations as they are
-    // loaded, the product, this epilogue), the same arithmetic as the three kernels below
-    const int one = launch_skinny_f16w(M, pa ? (const void *)pa->rows : op[0].dptr, pa || ahalf, pa ? Kp : lda, P->w,
-                                       pa ? Kp : K, N, Kp, (float *)op[1].dptr, ldc, bias, ext ? ext->gelu : 0, R,
-                                       ext ? ext->ldr : 0, flag, st);
+    // loaded, the product, this epilogue), the same arithmetic as the three kernels below. From 9 tokens on, with at
+    // least four 16-row weight blocks per SM, F32 activations are rounded to FP16 rows first (act_to_f16, as the
+    // chain below does) so that the kernel reads half the activation bytes; it prefetches its weights while the
+    // conversion runs (dependent launch). Measured on B200 at M = 16: W 11008 x 4096 28.2 -> 27.2 us; with fewer
+    // blocks the conversion's latency shows (W 4096^2 9.96 -> 12.3 us), so those keep the direct F32 loads.
+    const void *a1 = pa ? (const void *)pa->rows : op[0].dptr;
+    bool h1 = pa || ahalf;
+    long long l1 = pa ? Kp : lda;
+    int k1 = pa ? Kp : K;
+    if (!pa && !ahalf && M > 8 && (N + 15) / 16 >= 4 * d->sm_count && skinny_f16w_fits(M, Kp, N, Kp, P->w)) {
+        act_to_f16<float><<<grid_for((long long)M * Kp, d->sm_count), 256, 0, st>>>((const float *)op[0].dptr, lda, M, K,
+                                                                                     Kp, a16);
+        G9_TRY(launched("act_to_f16"));
+        a1 = a16;
+        h1 = true;
+        l1 = Kp;
+        k1 = Kp;
+    }
+    const int one = launch_skinny_f16w(M, a1, h1, l1, P->w, k1, N, Kp, (float *)op[1].dptr, ldc, bias,
+                                       ext ? ext->gelu : 0, R, ext ? ext->ldr : 0, flag, st);
     if (one < 0) return one;
     if (one == 0) {
         int r = finish_op(op, 2);
@@ -654,7 +670,16 @@ GEN9BLAS_API int gen9blas_ffn_f16w(int M, const float *X, int ldx, const gen9bla
     // its kernel (two launches; the same operations and roundings as the general chain below)
     int fused = 1;
     if (M <= 16) {
-        fused = launch_skinny_swiglu(M, (const float *)op[0].dptr, ldx, Pg->w, Pu->w, K, N, Kp, g16, u16, h16, Kpd, flag, st);
+        // from 9 tokens on the F32 rows are rounded to FP16 first: half the activation bytes for the pair kernel, whose
+        // 2 x 688 CTAs at 7B shapes hide the conversion (M = 16: 81.5 -> 75.7 us on B200)
+        const bool pre = M > 8 && skinny_f16w_fits(M, Kp, N, Kp, Pg->w);
+        if (pre) {
+            act_to_f16<float><<<grid_for((long long)M * Kp, d->sm_count), 256, 0, st>>>((const float *)op[0].dptr, ldx, M, K,
+                                                                                         Kp, x16);
+            G9_TRY(launched("act_to_f16"));
+        }
+        fused = pre ? launch_skinny_swiglu(M, x16, true, Kp, Pg->w, Pu->w, Kp, N, Kp, g16, u16, h16, Kpd, flag, st)
+                    : launch_skinny_swiglu(M, op[0].dptr, false, ldx, Pg->w, Pu->w, K, N, Kp, g16, u16, h16, Kpd, flag, st);
         if (fused < 0) return fused;
         if (fused == 0) {
             const int r2 = launch_skinny_f16w(M, h16, true, Kpd, Pd->w, Kpd, Nd, Kpd, (float *)op[1].dptr, ldy, nullptr, 0,

@@ -1283,6 +1283,12 @@ int launch_skinny_f32a(int M, int N, int K, const float *A, int lda, const void 
     return launch_f32a_main<false, 8, ACT_PAIRED>(p, q, part, st);
 }
 
+bool skinny_f16w_fits(int M, int K, int N, long long ldw, const void *W) {
+    DevState *d = dev_state();
+    return d && M >= 1 && M <= 16 && (N + 15) / 16 >= d->sm_count && (K + 255) / 256 >= WK_WARPS && K % 8 == 0 &&
+           ((uintptr_t)W & 15) == 0 && (ldw * 2) % 16 == 0;
+}
+
 int launch_skinny_f16w(int M, const void *A, bool ahalf, long long lda, const void *W, int K, int N, long long ldw,
                        float *C, long long ldc, const float *bias, int gelu, const float *R, long long ldr, unsigned *nf,
                        cudaStream_t st) {
@@ -1290,9 +1296,7 @@ int launch_skinny_f16w(int M, const void *A, bool ahalf, long long lda, const vo
     if (!d) return G.status;
     const int es = ahalf ? 2 : 4;
     const int KC = (K + 255) / 256;
-    if (M < 1 || M > 16 || (N + 15) / 16 < d->sm_count || KC < WK_WARPS || K % 8 != 0 || ((uintptr_t)A & 15) != 0 ||
-        (lda * es) % 16 != 0 || ((uintptr_t)W & 15) != 0 || (ldw * 2) % 16 != 0)
-        return 1;
+    if (!skinny_f16w_fits(M, K, N, ldw, W) || ((uintptr_t)A & 15) != 0 || (lda * es) % 16 != 0) return 1;
     SkinnyArgs p;
     memset(&p, 0, sizeof(p));
     p.Mc = M; p.Nc = N; p.K = K;
@@ -1317,16 +1321,18 @@ int launch_skinny_f16w(int M, const void *A, bool ahalf, long long lda, const vo
     return launched("skinny_wk_f16_blk_f16w");
 }
 
-// ffn_f16w's gate and up GEMMs in one launch (M <= 16 F32 tokens rounded to FP16 as loaded, the one-block kernel's
-// plan): g16 = fp16(X·Wgᵀ), u16 = fp16(X·Wuᵀ) (pitch N) and h16 = fp16(silu(g)·u) (pitch ldh, zero past N). Returns 1,
+// ffn_f16w's gate and up GEMMs in one launch (M <= 16 tokens: F32 rounded to FP16 as loaded, or FP16 rows (xhalf);
+// the one-block kernel's plan): g16 = fp16(X·Wgᵀ), u16 = fp16(X·Wuᵀ) (pitch N) and h16 = fp16(silu(g)·u) (pitch ldh, zero past N). Returns 1,
 // launching nothing, where launch_skinny_f16w would decline the shape or layout.
-int launch_skinny_swiglu(int M, const float *X, long long ldx, const void *Wg, const void *Wu, int K, int N, long long ldw,
-                         __half *g16, __half *u16, __half *h16, long long ldh, unsigned *nf, cudaStream_t st) {
+int launch_skinny_swiglu(int M, const void *X, bool xhalf, long long ldx, const void *Wg, const void *Wu, int K, int N,
+                         long long ldw, __half *g16, __half *u16, __half *h16, long long ldh, unsigned *nf,
+                         cudaStream_t st) {
     DevState *d = dev_state();
     if (!d) return G.status;
     const int KC = (K + 255) / 256, RB = (N + 15) / 16;
     if (M < 1 || M > 16 || RB < d->sm_count || KC < WK_WARPS || K % 8 != 0 || ((uintptr_t)X & 15) != 0 ||
-        (ldx * 4) % 16 != 0 || ((uintptr_t)Wg & 15) != 0 || ((uintptr_t)Wu & 15) != 0 || (ldw * 2) % 16 != 0 || ldh < N)
+        (ldx * (xhalf ? 2 : 4)) % 16 != 0 || ((uintptr_t)Wg & 15) != 0 || ((uintptr_t)Wu & 15) != 0 ||
+        (ldw * 2) % 16 != 0 || ldh < N)
         return 1;
     SkinnyArgs p;
     memset(&p, 0, sizeof(p));
@@ -1343,10 +1349,13 @@ int launch_skinny_swiglu(int M, const float *X, long long ldx, const void *Wg, c
     p.early_w = !queued_writes_overlap(d, Wg, wext) && !queued_writes_overlap(d, Wu, wext);
     const bool fullk = K % 256 == 0, two = M > 8;
     using Kern = void (*)(const SkinnyArgs, int);
-    const Kern kern = fullk ? (two ? wk_f16_blk<true, true, ACT_F32H, false, true> : wk_f16_blk<true, false, ACT_F32H, false, true>)
-                            : (two ? wk_f16_blk<false, true, ACT_F32H, false, true> : wk_f16_blk<false, false, ACT_F32H, false, true>);
-    static bool attr[4][kMaxDevices] = {};
-    G9_CU(smem_limit_once(kern, SK_SMEM_BYTES, attr[(fullk ? 2 : 0) + (two ? 1 : 0)]));
+    Kern kern;
+    if (xhalf) kern = fullk ? (two ? wk_f16_blk<true, true, ACT_F16, false, true> : wk_f16_blk<true, false, ACT_F16, false, true>)
+                            : (two ? wk_f16_blk<false, true, ACT_F16, false, true> : wk_f16_blk<false, false, ACT_F16, false, true>);
+    else kern = fullk ? (two ? wk_f16_blk<true, true, ACT_F32H, false, true> : wk_f16_blk<true, false, ACT_F32H, false, true>)
+                      : (two ? wk_f16_blk<false, true, ACT_F32H, false, true> : wk_f16_blk<false, false, ACT_F32H, false, true>);
+    static bool attr[8][kMaxDevices] = {};
+    G9_CU(smem_limit_once(kern, SK_SMEM_BYTES, attr[(xhalf ? 4 : 0) + (fullk ? 2 : 0) + (two ? 1 : 0)]));
     launch_pdl(kern, dim3((unsigned)(2 * RB)), dim3(WK_WARPS * 32), SK_SMEM_BYTES, st, p, KC);
     return launched("skinny_wk_f16_blk_swiglu");
 }
