@@ -872,7 +872,7 @@ static int hgemm_tc_impl(int type, int tA, int tB, int M, int N, int K, double a
     const size_t partial_bytes = pair && split > 1 ? (size_t)(tiles - dp) * (split - 1) * 2 * 128 * bn * sizeof(float) : 0;
     // 1-CTA kernel (M <= 128) with at most half the SMs' worth of tiles: K split over them (FP32 accumulation, one
     // matrix, C only), ks parts per tile, each of at least 4 K blocks, summed in order by hgemm_ksum. Measured on
-    // B200, gemm_pb_f16w M = 64 (HS, F32 tokens rounded to FP16): see the design notes' ML rows.
+    // B200, gemm_pb_f16w M = 64 (HS): W 4096 x 4096 38.3 -> 28.6 us; W 11008 x 4096 unchanged at 46.6 us.
     int ks = 1;
     if (!pair && type == GEN9BLAS_HS && count == 1 && !(peers && npeers > 0) && !c_t) {
         const long long t1 = (long long)((M + TC_BM - 1) / TC_BM) * ((N + TC_BN - 1) / TC_BN);

@@ -1015,8 +1015,8 @@ __global__ void __launch_bounds__(AT2_WARPS * 32, 3) attn_tc_k(AttnArgs a) {
                     if (j < nsl) wm[j * G + h] = w;
                     float ls = lj > 0.0f ? lj * w : 0.0f;
                     for (int o = 16; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
-                    // slots of earlier rounds were weighted against M: rescale them to Mn (rows of > 32 slots only)
-                    __syncwarp();   // this round's weights are in shared memory for every lane
+                    // slots of earlier passes were weighted against M: rescale them to Mn (rows of > 32 slots only)
+                    __syncwarp();   // this pass's weights are in shared memory for every lane
                     if (j0 > 0 && Mn > M) {
                         const float f = exp2f(M - Mn);
                         for (int q = lane; q < j0; q += 32)
