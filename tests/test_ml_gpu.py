@@ -642,6 +642,26 @@ def test_attn_dec_nan_past_visible(gpu_lib):
             assert _close_attn(got[s_], want), (s_, np.max(np.abs(got[s_] - want)))
 
 
+@pytest.mark.parametrize("nk,vis", [(20000, 19999), (20000, 12345)])
+def test_attn_dec_one_row_many_slots(gpu_lib, nk, vis):
+    """One (stream, KV head) row split over the whole grid: the merging CTA combines hundreds of slots, more than a
+    warp's 32 lanes take in one pass (the weights of earlier passes are rescaled to the running maximum)."""
+    D, H, HKV, ns, nq = 64, 8, 1, 1, 1
+    Q = dev(rng.standard_normal((ns, nq, H, D)).astype(np.float32))
+    Kc = rng.standard_normal((ns, nk, HKV, D)).astype(np.float16)
+    Vc = rng.standard_normal((ns, nk, HKV, D)).astype(np.float16)
+    Kc[0, 7777] *= 3   # a few keys far above the rest: the running maximum moves between passes
+    Kd, Vd = dev(Kc), dev(Vc)
+    O = dev(np.full((ns, nq, H, D), np.nan, np.float32))
+    vv = np.array([vis], np.int32)
+    kk, kh, ks, scale = HKV * D, D, nk * HKV * D, 0.125
+    assert gpu_lib.attn_dec(D, H, HKV, ns, nq, nk, ptr(Q), H * D, D, nq * H * D, ptr(Kd), kk, kh, ks, Kd.numel() * 2,
+                            ptr(Vd), kk, kh, ks, Vd.numel() * 2, ptr(O), scale, ptr(vv), 0, 64, 1) == 0, gpu_lib.error()
+    got = host(O, gpu_lib)
+    want = ml_ref.attention(Q.cpu().numpy()[0], Kc[0], Vc[0], scale, [vis])
+    assert _close_attn(got[0], want), np.max(np.abs(got[0] - want))
+
+
 def test_attn_dec_long_chunks(gpu_lib):
     """Enough (stream, KV head) rows that the planner gives each warp several 32-key steps (the copy of the next
     step's rows overlapping this step's MMAs), with visible counts that end inside a step, a warp and a chunk."""
