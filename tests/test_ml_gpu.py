@@ -119,10 +119,12 @@ def test_gemm_pb_f16w_ex_equals_unfused_ops(gpu_lib):
         gpu_lib.packed_b_free(P)
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 4096, 2048), (5, 3000, 2304), (16, 2500, 4104), (9, 4096, 2048)])
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 2048), (5, 3000, 2304), (16, 2500, 4104), (9, 4096, 2048),
+                                   (16, 11008, 4096), (12, 5000, 4096)])
 def test_gemm_pb_f16w_single_kernel_shapes(gpu_lib, M, N, K):
-    """Shapes that run the FP16-weight product as one kernel (M <= 16, at least 16 weight rows per SM, K >= 2048):
-    the same bits as the FP16-accumulating-in-FP32 GEMM (gen9blas_gemm, GEN9BLAS_HS) of the FP16-rounded activations,
+    """Shapes that run the FP16-weight product as one kernel (M <= 16, at least 16 weight rows per SM, K >= 2048; the
+    last two over several waves, the F32 activations rounded ahead of the kernel for the wider one): the same bits as
+    the FP16-accumulating-in-FP32 GEMM (gen9blas_gemm, GEN9BLAS_HS) of the FP16-rounded activations,
     as the FP16-activation entry point, and as the unfused bias / GELU / residual chain; the oracle's bound; a
     non-finite result flagged."""
     A = rng.standard_normal((M, K)).astype(np.float32)

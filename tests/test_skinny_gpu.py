@@ -48,11 +48,13 @@ def test_reference_skinny_cases(g9, dt, usm):
 
 @pytest.mark.parametrize("M,N,K", [(1, 3000, 2100), (3, 4100, 2056), (8, 2380, 4104), (5, 4736, 2048), (2, 4096, 8),
                                    (4, 9000, 3000), (7, 14000, 2304), (1, 6000, 5000), (9, 3000, 2100),
-                                   (16, 4100, 2056), (12, 9000, 4096)])
+                                   (16, 4100, 2056), (12, 9000, 4096), (16, 5000, 4096), (9, 4800, 6144),
+                                   (13, 11000, 4104)])
 def test_whole_blocks_per_cta_plan(g9, M, N, K):
     """At least one 16-row block per SM and K of at least 8 chunks of 256 take the kernel with one row block per CTA
     (one or two token tiles, one or several waves): K off the chunk, edge rows past N, alpha/beta into a slice of C,
-    both operand orders (K = 8 stays on the stream-K kernel)."""
+    both operand orders (K = 8 stays on the stream-K kernel). The last three leave a partly filled last wave of
+    blocks."""
     A = tab(g9, (M, K), np.float16, True)
     W = tab(g9, (N, K), np.float16, True)
     ref = A.astype(np.float64) @ W.astype(np.float64).T
