@@ -115,3 +115,19 @@ def test_tensor_peak_follows_the_sampled_clocks():
     assert p == sust and "1357" in note
     p, note, _ = bench.tensor_peak(None)
     assert p == burst and "no clock samples" in note
+
+
+def test_no_function_shadows_the_type_constants():
+    """bench.py's functions read the module's GEMM type constants (H, S, HS, D); a function that also assigns one of
+    those names makes it local for the whole function, and the earlier reads then fail (UnboundLocalError) only when
+    the workload that reads them runs. Checked on the source: no function assigns them."""
+    import ast
+    src = open(os.path.join(ROOT, "bench.py")).read()
+    tree = ast.parse(src)
+    consts = {"H", "S", "HS", "D"}
+    bad = []
+    for fn in [n for n in ast.walk(tree) if isinstance(n, (ast.FunctionDef, ast.AsyncFunctionDef))]:
+        for node in ast.walk(fn):
+            if isinstance(node, ast.Name) and isinstance(node.ctx, ast.Store) and node.id in consts:
+                bad.append((fn.name, node.id, node.lineno))
+    assert not bad, bad
