@@ -718,8 +718,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
                         continue;
                     }
                     if (!have || col0 >= p.N || !row_ok) continue;
+                    // destinations in an order rotated by CTA and chunk, so that at any moment the CTAs of all
+                    // ranks write into different ranks' C rather than all into the same one
+                    const int rot = (int)(blockIdx.x >> 1) + c;
                     if (w.part < 0) {
-                        for (int q = 0; q < p.ndst; q++) store_chunk<F16ACC>(p, r, p.dst[q] + roff, col0, row_ok);
+                        for (int qq = 0; qq < p.ndst; qq++) {
+                            const int q = (qq + rot) % p.ndst;
+                            store_chunk<F16ACC>(p, r, p.dst[q] + roff, col0, row_ok);
+                        }
                     } else {
                         float v[32];
                         acc_to_f32<F16ACC>(r, v);
@@ -733,7 +739,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
                                 v[4 * e] += t.x; v[4 * e + 1] += t.y; v[4 * e + 2] += t.z; v[4 * e + 3] += t.w;
                             }
                         }
-                        for (int q = 0; q < p.ndst; q++) store_vals(p, v, p.dst[q] + roff, col0);
+                        for (int qq = 0; qq < p.ndst; qq++) store_vals(p, v, p.dst[(qq + rot) % p.ndst] + roff, col0);
                     }
                 }
                 if (p.ndst > 1) __threadfence_system();   // peer stores ordered before the ranks' next barrier
