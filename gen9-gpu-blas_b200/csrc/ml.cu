@@ -254,12 +254,15 @@ __global__ void gelu_tab_k() {
     if (i < 65536) g_gelu_tab[i] = __float2half_rn(gelu_ggml(__half2float(__ushort_as_half((unsigned short)i))));
 }
 
+// OP 0: GELU by the table; 1: GELU (erf form); 2: ReLU; 3: GELU computed (gelu_ggml, the table's own values).
 template <int OP>
 __device__ __forceinline__ float unary_f(float v, const __half *tab) {
     if (OP == 0) {
         if (v <= -10.0f) return 0.0f;
         if (v >= 10.0f) return v;
         return __half2float(tab[__half_as_ushort(__float2half_rn(v))]);
+    } else if (OP == 3) {
+        return gelu_ggml(v);
     } else if (OP == 1) {
         return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, erff(__fmul_rn(v, 0.70710678118654752440f))));
     }
@@ -1267,7 +1270,12 @@ static int unary(int op, size_t n, const float *X, float *Y, int sync) {
         G9_TRY(c.big(Y, n * 4, false, true, &y));
     }
     if (((uintptr_t)x & 15) == 0 && ((uintptr_t)y & 15) == 0) {
-        if (op == 0) {
+        // the table kernel copies 128 KB into every SM first: worth it from a few million elements on (a decode-sized
+        // call computes instead; both give the same bits)
+        if (op == 0 && n < ((size_t)1 << 22)) {
+            unary_v_k<3><<<grid_n((long long)(n + 3) / 4, d->sm_count), 256, 0, st>>>((long long)n, (const float *)x,
+                                                                                      (float *)y);
+        } else if (op == 0) {
             static bool tab[kMaxDevices] = {}, attr[kMaxDevices] = {};
             if (!tab[d->dev]) {
                 gelu_tab_k<<<64, 1024, 0, st>>>();
