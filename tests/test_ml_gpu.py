@@ -572,7 +572,8 @@ def _close_attn(got, want):
 
 
 @pytest.mark.parametrize("pad", [5, 8])
-@pytest.mark.parametrize("D,H,HKV", [(128, 32, 8), (128, 8, 8), (64, 12, 2), (96, 16, 2), (128, 36, 4)])
+@pytest.mark.parametrize("D,H,HKV", [(128, 32, 8), (128, 8, 8), (64, 12, 2), (96, 16, 2), (128, 36, 4), (80, 32, 32),
+                                     (112, 16, 2), (16, 8, 1)])
 def test_attn_dec_streams(gpu_lib, D, H, HKV, pad):
     """Row padding 8 (16-byte rows, D a multiple of 16, at most 8 query heads per KV head) takes the tensor-core
     kernel, padding 5 and the 9-heads-per-KV-head case the per-head one."""
