@@ -1440,8 +1440,8 @@ GEN9BLAS_API int gen9blas_cpy_any(const void *src, int tin, const int64_t sne[4]
         return fail(GEN9BLAS_ERR_UNSUPPORTED, "cpy_any: types F32 / F16 only");
     if (!sne || !snb || !dne || !dnb) return fail(GEN9BLAS_ERR_INVALID_ARG, "cpy_any: four ne / nb each");
     Shape4 s, dd;
-    long long ns, ndd;
-    size_t sspan, dspan;
+    long long ns = 0, ndd = 0;
+    size_t sspan = 0, dspan = 0;
     bool es, ed;
     G9_TRY(shape4(sne, snb, tin == GEN9BLAS_S ? 4 : 2, &s, &ns, &sspan, &es));
     G9_TRY(shape4(dne, dnb, tout == GEN9BLAS_S ? 4 : 2, &dd, &ndd, &dspan, &ed));
@@ -1464,8 +1464,8 @@ GEN9BLAS_API int gen9blas_upscale_f32(const float *src, const int64_t sne[4], co
     if (int e = begin_op()) return e;
     if (!sne || !snb || !dne || !dnb) return fail(GEN9BLAS_ERR_INVALID_ARG, "upscale_f32: four ne / nb each");
     Shape4 s, dd;
-    long long ns, ndd;
-    size_t sspan, dspan;
+    long long ns = 0, ndd = 0;
+    size_t sspan = 0, dspan = 0;
     bool es, ed;
     G9_TRY(shape4(sne, snb, 4, &s, &ns, &sspan, &es));
     G9_TRY(shape4(dne, dnb, 4, &dd, &ndd, &dspan, &ed));

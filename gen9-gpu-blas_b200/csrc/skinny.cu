@@ -222,6 +222,7 @@ constexpr int SK_PRE_BYTES = WK_WARPS * 16 * SK_PRE_ROWB;
 // no more shared memory than the regions (73,728 bytes), so a CTA of the next call still fits beside two of this one.
 static_assert(SK_PRE_ROWB == SK_ROWB && SK_ROWB - 8 * 32 * 2 == 64, "pad of 16 floats per staging row");
 constexpr int SK_SMEM_BYTES = WK_WARPS * 16 * SK_ROWB;
+static_assert(SK_PRE_BYTES == SK_SMEM_BYTES && sk_stage_bytes(true) == SK_SMEM_BYTES, "both regions fill the launch");
 __device__ __forceinline__ float *sk_pad_row(uint8_t *smem, int warp_local, int r) {
     return reinterpret_cast<float *>(smem + (warp_local * 16 + r) * SK_ROWB + 8 * 32 * 2);
 }
