@@ -816,6 +816,11 @@ extern "C" GEN9BLAS_API int gen9blas_gemv_noalloc(int type, int trans, int M, in
                                    (__half *)y + oy, incy, sm_count, P, st);
     }
     if (r < 0) return r;
+    // On a stream that is being captured the launches were recorded into the caller's graph and nothing ran; waiting
+    // for that stream would fail and invalidate the capture.
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    G9_CU(cudaStreamIsCapturing(st, &cap));
+    if (cap == cudaStreamCaptureStatusActive) return 0;
     if (!G.nowait || st == cudaStreamPerThread) {
         G9_CU(cudaStreamSynchronize(st));
     } else if (ds) {   // queued on the library's stream: later calls that read y early must know

@@ -233,7 +233,7 @@ GEN9BLAS_API int gen9blas_selftest_wait(double limit_ms);
  *   threads) race on it. Every partial sum is written before it is read, so nothing needs clearing between calls.
  * - Runs on the stream set with gen9blas_set_stream, else on the library's own stream of the device, so it is
  *   ordered with the other entry points' work and gen9blas_flush waits for it; waits for that stream unless no-wait
- *   mode is on. On a device where no other entry point has run yet, the library has no stream of its own (creating
+ *   mode is on or the stream is being captured into a CUDA graph (the launches are then only recorded). On a device where no other entry point has run yet, the library has no stream of its own (creating
  *   it would allocate): the call then runs on the per-thread default stream and always waits for it.
  * - Calls no cudaMalloc, cudaFree or other allocating routine. */
 GEN9BLAS_API int gen9blas_gemv_noalloc(int type, int trans, int M, int N, double alpha, const void *A, int lda,

@@ -93,6 +93,40 @@ def test_noalloc_nowait_orders_after_gemm_and_flush_waits(gpu_lib, torch):
         assert scaled_error(y.cpu().numpy(), ref, scale) <= 1e-5, rep
 
 
+def test_noalloc_records_into_a_cuda_graph(gpu_lib, torch):
+    """Called on a stream that is being captured (set with gen9blas_set_stream, no-wait mode off), the call records
+    its launches and returns without waiting; each replay of the graph then computes y from the buffers' contents
+    at replay time."""
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(17)
+    M, N = 3000, 2000
+    A = torch.empty(M, N, device="cuda", dtype=torch.float32).uniform_(-1, 1, generator=gen)
+    x = torch.empty(M, device="cuda", dtype=torch.float32).uniform_(-1, 1, generator=gen)
+    y = torch.zeros(N, device="cuda", dtype=torch.float32)
+    torch.cuda.synchronize()
+    # the first call looks up the fixed scratch array's address, which must happen before any capture
+    assert gpu_lib.gemv_noalloc(abi.S, 1, M, N, 1.0, A.data_ptr(), N, x.data_ptr(), 1, 0.0, y.data_ptr(), 1) == 0
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, capture_error_mode="relaxed"):
+        assert gpu_lib.set_stream(torch.cuda.current_stream().cuda_stream) == 0
+        try:
+            r = gpu_lib.gemv_noalloc(abi.S, 1, M, N, 0.5, A.data_ptr(), N, x.data_ptr(), 1, 0.0, y.data_ptr(), 1)
+        finally:
+            gpu_lib.set_stream(None)
+    assert r == 0, gpu_lib.error()
+    for rep in range(2):
+        A.uniform_(-1, 1, generator=gen)
+        x.uniform_(-1, 1, generator=gen)
+        y.fill_(float("nan"))
+        g.replay()
+        torch.cuda.synchronize()
+        Ad, xs = A.double().cpu().numpy(), x.double().cpu().numpy()
+        ref = 0.5 * (Ad.T @ xs)
+        scale = 0.5 * (np.abs(Ad.T) @ np.abs(xs))
+        assert scaled_error(y.cpu().numpy(), ref, scale) <= TOL[abi.S], rep
+    del g
+
+
 def test_noalloc_uses_no_new_device_memory(gpu_lib, torch):
     """After the first call (which loads the library's device image, fixed array included) larger transposed
     problems, which would grow gen9blas_gemv's scratch, leave the free device memory unchanged."""
