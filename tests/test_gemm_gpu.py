@@ -233,6 +233,36 @@ def test_sgemm_large_grid_all_layouts(gpu_lib):
                 assert (C[:, N:] == C0[:, N:]).all()
 
 
+def test_sgemm_stream_k_ragged_all_layouts(gpu_lib):
+    """SGEMM grids of less than one wave with K >= 256 (the stream-K kernel: tile × K-chunk iterations spread over one
+    wave, partial tiles handed over between CTAs): ragged M, N and K (K not a multiple of the chunk), all four
+    transposes, pitches that are and are not multiples of 4 floats, alpha / beta, bytes past N untouched; each shape
+    twice, so the hand-over flags of a later call carry a new epoch."""
+    rng = np.random.default_rng(41)
+    for (M, N, K) in ((1000, 900, 1000), (3000, 100, 2001)):
+        for ta in (0, 1):
+            for tb in (0, 1):
+                for pad in (0, 1):
+                    ra, ca = (K, M) if ta else (M, K)
+                    rb, cb = (N, K) if tb else (K, N)
+                    lda, ldb, ldc = ca + pad, cb + pad, N + 3
+                    A = rng.uniform(-1, 1, (ra, lda)).astype(np.float32)
+                    B = rng.uniform(-1, 1, (rb, ldb)).astype(np.float32)
+                    C0 = rng.uniform(-1, 1, (M, ldc)).astype(np.float32)
+                    a64 = (A[:, :ca].T if ta else A[:, :ca]).astype(np.float64)
+                    b64 = (B[:, :cb].T if tb else B[:, :cb]).astype(np.float64)
+                    c64 = C0[:, :N].astype(np.float64)
+                    ref = 1.5 * a64 @ b64 + 0.5 * c64
+                    scale = 1.5 * np.abs(a64) @ np.abs(b64) + 0.5 * np.abs(c64)
+                    for _ in range(2):
+                        C = C0.copy()
+                        assert gpu_lib.gemm(abi.S, ta, tb, M, N, K, 1.5, A.ctypes.data, lda, B.ctypes.data, ldb, 0.5,
+                                            C.ctypes.data, ldc) == 0
+                        avg, mx = gemm_error(C[:, :N], ref, scale)
+                        assert avg <= 1e-6 and mx <= 1e-5, (M, N, K, ta, tb, pad, avg, mx)
+                        assert (C[:, N:] == C0[:, N:]).all()
+
+
 @pytest.mark.parametrize("t,dt", [(abi.H, np.float16), (abi.S, np.float32)])
 def test_host_operands_banded_pipeline(gpu_lib, t, dt):
     """Host A and C large enough for the banded pipeline (row bands of A cross to the device while earlier bands are
