@@ -12,7 +12,8 @@ import os
 import re
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-SKIP_DIRS = {".git", "_work", "_build", "baseline", "gpurun_out", "__pycache__", "_ref", ".pytest_cache"}
+SOURCE_DIRS = ("gen9-gpu-blas_b200", "include", "oracle", "profiles", "tests")   # plus the files at the top level
+SKIP_DIRS = {"_build", "_ref", "__pycache__"}
 SOURCE_EXT = {".cu", ".cuh", ".h", ".hpp", ".c", ".cc", ".cpp", ".py", ".sh", ".txt", ".json", ".mk"}
 
 BATCH_COPY = re.compile("cu(?:da)?Memcpy(?:3D)?Batch" + "Async")
@@ -20,13 +21,20 @@ MULTICAST = re.compile("multi" + "cast::cluster")
 BULK_COPY, MC_WORD = "cp.async" + ".bulk", "multi" + "cast"
 
 
+def is_source(f):
+    return os.path.splitext(f)[1] in SOURCE_EXT or f == "Makefile"
+
+
 def source_files():
-    for dirpath, dirnames, filenames in os.walk(ROOT):
-        dirnames[:] = [d for d in dirnames if d not in SKIP_DIRS]
-        for f in filenames:
-            ext = os.path.splitext(f)[1]
-            if ext in SOURCE_EXT or f == "Makefile":
-                yield os.path.join(dirpath, f)
+    for f in os.listdir(ROOT):
+        if os.path.isfile(os.path.join(ROOT, f)) and is_source(f):
+            yield os.path.join(ROOT, f)
+    for top in SOURCE_DIRS:
+        for dirpath, dirnames, filenames in os.walk(os.path.join(ROOT, top)):
+            dirnames[:] = [d for d in dirnames if d not in SKIP_DIRS]
+            for f in filenames:
+                if is_source(f):
+                    yield os.path.join(dirpath, f)
 
 
 def read(path):
@@ -61,7 +69,7 @@ def test_product_does_not_reach_the_oracle():
     for dirpath, dirnames, filenames in os.walk(pkg):
         dirnames[:] = [d for d in dirnames if d not in SKIP_DIRS]
         for f in filenames:
-            if os.path.splitext(f)[1] not in SOURCE_EXT and f != "Makefile":
+            if not is_source(f):
                 continue
             p = os.path.join(dirpath, f)
             for i, line in enumerate(read(p).splitlines(), 1):
